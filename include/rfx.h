@@ -1,0 +1,298 @@
+/*
+ * rfx.h — C ABI of librfx_b200, the sm_100a (B200) implementation of Reflex's
+ * streaming denoising hot path (PI0.5 / PI0 action expert over a partitioned,
+ * int8-quantized KV context).
+ *
+ * Conventions
+ *   - Every entry point returns an int status (RFX_OK on success) and never
+ *     throws; rfx_last_error() gives the calling thread's last message.
+ *   - All pointers are device pointers unless stated otherwise; the caller
+ *     owns every buffer (the library allocates only small host-side objects:
+ *     tensor-map caches, plans and CUDA graphs).
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy stream.
+ *   - bf16 = IEEE bfloat16 stored as uint16; "fp32" = IEEE binary32.
+ *   - Device-side waits are bounded (about one second). A wait that gives up
+ *     records a code in a device status word; rfx_device_status() reads and
+ *     clears it.
+ *
+ * Each declaration cites the reference interface (path:line inside 9yc/Reflex)
+ * whose behaviour it replaces.
+ */
+#ifndef RFX_H_
+#define RFX_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ------------------------------------------------------------ status ---- */
+#define RFX_OK 0
+#define RFX_E_INVAL 1       /* bad argument (shape, alignment, null pointer) */
+#define RFX_E_CUDA 2        /* a CUDA runtime call failed */
+#define RFX_E_DEVICE 3      /* a bounded device-side wait gave up */
+#define RFX_E_UNSUPPORTED 4 /* configuration not supported by these kernels */
+#define RFX_E_STATE 5       /* call out of order (e.g. replay before capture) */
+
+#define RFX_DTYPE_F32 0
+#define RFX_DTYPE_BF16 1
+
+/* KV quantization schemes.
+ * RFX_QUANT_I8_SYM: int8, per token per head over head_dim:
+ *     scale = absmax / 127 (fp32), q = clamp(rne(x / scale), -127, 127);
+ *     absmax == 0 gives scale 0 and q 0.
+ * RFX_QUANT_U8_REF: the reference's uint8 asymmetric scheme
+ *     (reflex/layers/streaming_attention.py:211-218), every op rounded to the
+ *     activation dtype: range = clamp(max-min, min=1e-5); scale = range/255;
+ *     zp = -min/scale; q = clamp(round_half_even(x/scale + zp), 0, 255);
+ *     scale and zp are stored in the activation dtype. */
+#define RFX_QUANT_I8_SYM 0
+#define RFX_QUANT_U8_REF 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int rfx_version(void);
+
+/* Message of the calling thread's last failing call ("" if none). */
+const char* rfx_last_error(void);
+
+/* Reads and clears the device status word of the current device after
+ * synchronizing `stream`. *out receives 0 or a non-zero device error code. */
+int rfx_device_status(void* stream, int* out);
+
+/* Enables (1) or disables (0) programmatic dependent launch for kernels
+ * launched afterwards by this process. Default: enabled. */
+int rfx_set_pdl(int enable);
+
+/* Number of streaming multiprocessors of the current device. */
+int rfx_num_sms(int* out);
+
+/* ------------------------------------------------- KV quantize-append ---- */
+/* Quantizes new K and V rows and writes them into ring-buffer slots.
+ * Replaces reflex/layers/quantize_kernel.py:58 (fused_quantize_store) and the
+ * quantized branch of StreamingAttention.prefill_source
+ * (reflex/layers/streaming_attention.py:346-362).
+ * Input rows x[b][h][l][0..D) at element strides (xs_b, xs_h, xs_l); D = 256.
+ * Token l of the call goes to slot region_base + (region_off + l) % region_len
+ * of q[b][h][slot][0..D) (byte strides qs_*), scale/zp[b][h][slot] (element
+ * strides ss_*). Eviction of the oldest frame is overwriting its slots. */
+typedef struct rfx_kv_quant_desc {
+  int mode;     /* RFX_QUANT_* */
+  int in_dtype; /* RFX_DTYPE_BF16 or RFX_DTYPE_F32 */
+  const void* k;
+  const void* v;
+  long xs_b, xs_h, xs_l;
+  int B, H, L, D;
+  void* k_q;
+  void* v_q;
+  long qs_b, qs_h, qs_c;
+  int capacity; /* slots per (b, h) */
+  void* k_scale;
+  void* v_scale;
+  void* k_zp; /* U8_REF only */
+  void* v_zp;
+  long ss_b, ss_h, ss_c;
+  int region_base, region_off, region_len;
+} rfx_kv_quant_desc;
+int rfx_kv_quant_append(const rfx_kv_quant_desc* desc, void* stream);
+
+/* ------------------------------------------------------ fused linear ---- */
+/* y = epilogue(prologue(x) · Wᵀ) for a small token count T, streaming the bf16
+ * weight W[O][K] from HBM once (tcgen05 MMA, TMA-staged weight tiles, split-K
+ * across a thread-block cluster with a DSMEM reduction).
+ * Replaces QKVLinear.forward (reflex/layers/linear.py:72-98) with the AdaRMSNorm
+ * in front of it (reflex/policies/pi05/modeling_pi05.py:73-99,587) and RoPE after
+ * it (reflex/layers/rope.py:104-132); MergedColumnLinear.forward
+ * (reflex/layers/linear.py:138-148) with GELU-tanh(gate)*up
+ * (modeling_pi05.py:526-531); o_proj/down_proj with the gated residual
+ * (modeling_pi05.py:491,532,598,619). */
+#define RFX_PRO_LOAD 0 /* X = x (bf16 [T][ldx]) */
+#define RFX_PRO_NORM 1 /* X[t][k] = bf16(((x[t][k]*rstd[t]) * a1[k]) * a2[b][k] + b2[b][k]),
+                          rstd[t] = rsqrt(mean_k x[t][k]^2 + eps); a2 = 1 / b2 = 0 when null */
+#define RFX_EPI_STORE 0    /* y[t][o] = bf16(acc + bias[o]) */
+#define RFX_EPI_SILU 1     /* y[t][o] = bf16(silu(bf16(acc + bias[o]))) */
+#define RFX_EPI_QKV_ROPE 2 /* q/k/v split of a packed QKV weight (rfx_pack_weight RFX_PACK_QKV_ROPE),
+                              RoPE on q and k at positions[t], head-major q, token-major k/v */
+#define RFX_EPI_RESIDUAL 3 /* y[t][o] = bf16(y[t][o] + bf16(gate[b][o] * bf16(acc))); gate null -> 1 */
+#define RFX_EPI_GEGLU 4    /* y[t][f] = bf16(bf16(gelu_tanh(bf16(gate_f))) * bf16(up_f)) on a weight
+                              packed with rfx_pack_weight RFX_PACK_GATE_UP */
+typedef struct rfx_linear_desc {
+  int T;                /* tokens */
+  int O;                /* rows of the (packed) weight; multiple of 128 */
+  int K;                /* reduction length; multiple of 64 */
+  int tokens_per_batch; /* S: token t belongs to stream t / S */
+  int prologue;         /* RFX_PRO_* */
+  int epilogue;         /* RFX_EPI_* */
+  const void* w;        /* bf16 [O][K] */
+  const void* x;        /* bf16 [T][ldx] */
+  int ldx;
+  const float* norm_a1; /* [K] (RFX_PRO_NORM) */
+  const float* norm_a2; /* [B][K] at stride norm_ab_stride, or NULL */
+  const float* norm_b2; /* [B][K] at stride norm_ab_stride, or NULL */
+  long norm_ab_stride;
+  float eps;
+  void* y; /* bf16 [T][ldy] */
+  int ldy;
+  const float* bias; /* [O] or NULL */
+  const float* gate; /* [B][O] at stride gate_stride, or NULL (RFX_EPI_RESIDUAL) */
+  long gate_stride;
+  const float* rope_table; /* [rope_max_pos][256]: cos(0..127) | sin(0..127) */
+  int rope_max_pos;
+  const int* positions; /* [T] */
+  void* q_out;          /* bf16 [B][num_q_heads][S][256] */
+  void* k_out;          /* bf16 [T][256] */
+  void* v_out;          /* bf16 [T][256] */
+  int num_q_heads;
+  int n_tile; /* tokens per MMA tile: 0 (auto), 64, 128 or 256 */
+  int splits; /* CTAs per cluster along K: 0 (auto) or 1..8 */
+} rfx_linear_desc;
+int rfx_linear(const rfx_linear_desc* desc, void* stream);
+
+/* Weight repacks for the fused epilogues (one-time, at load). */
+#define RFX_PACK_QKV_ROPE 0 /* [Wq; Wk; Wv] ((Hq+2)*256 rows, modeling_pi05.py:864-866) -> RoPE pair tiles */
+#define RFX_PACK_GATE_UP 1  /* [Wgate; Wup] (2F rows, modeling_pi05.py:913-914) -> gate/up pair tiles */
+int rfx_pack_weight(int kind, const void* src, void* dst, int rows, int K, void* stream);
+
+/* ------------------------------------------------ partitioned attention ---- */
+/* Attention of S new tokens per stream (all num_q_heads heads stacked along
+ * the MMA M dimension; one shared KV head) over the quantized context ring
+ * plus the S new keys. Replaces StreamingAttention.forward's decode branch
+ * (reflex/layers/streaming_attention.py:585-627) with merge_caches /
+ * _dequantize (:472-550) fused in, and the attention math of
+ * reflex/layers/attention.py:98-164 / mixed_precision_attention.py:74-171.
+ * Mask: every valid context slot is visible; new key j is visible to query i
+ * iff new_block[j] <= new_block[i] (the block-causal cumsum rule of
+ * reflex/policies/pi05/utils.py:210-215 restricted to the suffix). */
+typedef struct rfx_attn_desc {
+  int B, num_q_heads, head_dim, S;
+  int capacity;   /* ring slots per stream */
+  int n_ctx;      /* valid slots [0, n_ctx) */
+  int quant_mode; /* RFX_QUANT_* */
+  int scale_dtype; /* dtype of k/v scale and zp in U8_REF mode (I8_SYM scales are fp32) */
+  const void* q;      /* bf16 [B][Hq][S][D] */
+  const void* k_new;  /* bf16 [B*S][D] */
+  const void* v_new;  /* bf16 [B*S][D] */
+  const void* k_ring; /* int8/uint8 [B][capacity][D] */
+  const void* v_ring;
+  const void* k_scale; /* [B][capacity] */
+  const void* v_scale;
+  const void* k_zp; /* [B][capacity] (U8_REF) */
+  const void* v_zp;
+  const unsigned char* ctx_valid; /* [B][capacity] 0/1 or NULL */
+  const int* new_block;           /* [S] or NULL */
+  float softmax_scale;
+  void* out; /* bf16 [B*S][Hq*D] */
+  void* workspace;
+  size_t workspace_bytes;
+  int kv_splits; /* 0 = auto */
+} rfx_attn_desc;
+int rfx_attention(const rfx_attn_desc* desc, void* stream);
+/* Workspace needed by rfx_attention for this descriptor (0 if none). */
+int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes);
+
+/* ----------------------------------------- timestep conditioning + heads ---- */
+/* cond[i] = silu(W_out · silu(W_in · bf16(sinusoid(t[i])) + b_in) + b_out), bf16.
+ * Replaces PI05SuffixEmbedder's time path (modeling_pi05.py:322-339) with
+ * create_sinusoidal_pos_embedding (reflex/policies/pi05/utils.py:72-121, fp64). */
+typedef struct rfx_time_cond_desc {
+  int n_t;
+  const float* t; /* [n_t] */
+  int width;
+  float min_period, max_period;
+  const void* w_in; /* bf16 [width][width] */
+  const void* b_in; /* bf16 [width] */
+  const void* w_out;
+  const void* b_out;
+  void* hidden; /* bf16 [n_t][width] scratch */
+  void* cond;   /* bf16 [n_t][width] */
+} rfx_time_cond_desc;
+int rfx_time_cond(const rfx_time_cond_desc* desc, void* stream);
+
+/* AdaRMSNorm modulation for n_rows conditioning rows and n_norms norms:
+ * m = W_n · fp32(cond_r) + b_n (fp32, modeling_pi05.py:86-88).
+ * RFX_ADARMS_GATE (in-tree AdaRMSNorm, modeling_pi05.py:50-99): a2 = m,
+ *     b2 = 0, gate = bf16(m).
+ * RFX_ADARMS_SSG (scale/shift/gate adaRMS): m = [scale|shift|gate],
+ *     a2 = 1 + scale, b2 = shift, gate = bf16(gate).
+ * Outputs are [n_rows][n_norms][width] fp32 (gate values bf16-rounded). */
+#define RFX_ADARMS_GATE 0
+#define RFX_ADARMS_SSG 1
+typedef struct rfx_modulation_desc {
+  int mode;
+  int n_rows; /* conditioning rows (timesteps x streams) */
+  int n_norms;
+  int width;
+  const float* w;  /* fp32 [n_norms][out][width], out = width (GATE) or 3*width (SSG) */
+  const float* b;  /* fp32 [n_norms][out] */
+  const void* cond; /* bf16 [n_rows][width] */
+  float* a2;
+  float* b2;
+  float* gate;
+} rfx_modulation_desc;
+int rfx_modulation(const rfx_modulation_desc* desc, void* stream);
+
+/* Action projections around the expert (modeling_pi05.py:292,342,1234-1241,1417):
+ * rfx_action_in:   h_next[row(b,s)] = bf16(W_in · bf16(x[b][s]) + b_in)
+ * rfx_euler_tail:  v = bf16(W_out · norm(h[b*S_total + h_row_offset + s]) + b_out),
+ *                  x = x + fp32(bf16(dt * v)) (PyTorch promotes the 0-dim fp32
+ *                  dt times the bf16 velocity to bf16), then (if h_next) the
+ *                  action-in projection of the updated x into h_next. */
+typedef struct rfx_action_io_desc {
+  int B, S, S_total, action_dim, width;
+  int h_row_offset; /* first action row inside a stream's S_total rows */
+  const void* h;    /* bf16 [B*S_total][width] */
+  const float* norm_a1;
+  const float* norm_a2;
+  const float* norm_b2;
+  long norm_ab_stride;
+  float eps;
+  const void* w_out; /* bf16 [action_dim][width] */
+  const void* b_out; /* bf16 [action_dim] */
+  float* x;          /* fp32 [B][S][action_dim] */
+  float dt;
+  const void* w_in; /* bf16 [width][action_dim] */
+  const void* b_in; /* bf16 [width] */
+  void* h_next;     /* bf16 rows of the next step's input, or NULL */
+  int h_next_ld;    /* row stride of h_next in elements (>= width) */
+  int h_next_rows_per_stream; /* h_next row of (b, s) = b*rows_per_stream + row_offset + s */
+  int h_next_row_offset;
+} rfx_action_io_desc;
+int rfx_action_in(const rfx_action_io_desc* desc, void* stream);
+int rfx_euler_tail(const rfx_action_io_desc* desc, void* stream);
+
+/* ---------------------------------------------------- execution plans ---- */
+/* A plan is an ordered list of the launches above, validated and with their
+ * TMA descriptors encoded once. rfx_plan_run launches them in order;
+ * rfx_plan_capture records them into a CUDA graph that rfx_plan_replay
+ * launches as one unit. Replaces torch.compile(mode="max-autotune") of
+ * sample_actions (modeling_pi05.py:812-814) and the CUDAGraphWrapper pattern
+ * (reflex/optimizations/single_frame_optimizer.py:157-235). */
+typedef struct rfx_plan rfx_plan;
+int rfx_plan_create(rfx_plan** out);
+int rfx_plan_destroy(rfx_plan* plan);
+int rfx_plan_add_linear(rfx_plan* plan, const rfx_linear_desc* desc);
+int rfx_plan_add_attention(rfx_plan* plan, const rfx_attn_desc* desc);
+int rfx_plan_add_kv_quant(rfx_plan* plan, const rfx_kv_quant_desc* desc);
+int rfx_plan_add_time_cond(rfx_plan* plan, const rfx_time_cond_desc* desc);
+int rfx_plan_add_modulation(rfx_plan* plan, const rfx_modulation_desc* desc);
+int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc);
+int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc);
+/* Number of kernel launches one run of the plan performs. */
+int rfx_plan_num_launches(const rfx_plan* plan, int* out);
+int rfx_plan_run(rfx_plan* plan, void* stream);
+int rfx_plan_capture(rfx_plan* plan, void* stream);
+int rfx_plan_replay(rfx_plan* plan, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RFX_H_ */

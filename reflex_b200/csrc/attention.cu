@@ -1,0 +1,585 @@
+// Partitioned attention of the new (suffix) tokens over a quantized context
+// ring plus the new tokens' own bf16 K/V, on tcgen05 tensor cores.
+//
+// Work decomposition
+//   rows  = num_q_heads x S query rows of one stream, stacked head-major (MQA:
+//           every head shares the single KV head, so heads become MMA rows);
+//           tiles of 128 rows (MMA M = 128).
+//   keys  = ceil(n_ctx/64) context blocks of 64 ring slots, then ceil(S/64)
+//           blocks of new keys.  Grid (q_tiles, kv_splits, B); split sp owns
+//           a contiguous range of key blocks and runs an online softmax over
+//           them; with kv_splits > 1 the partial (O, m, l) go to a workspace
+//           and a combine kernel merges them (log-sum-exp weights).
+//
+// Per key block (64 keys):
+//   TMA  : int8/uint8 K and V rows [64 x 256] -> shared staging
+//   conv : int8 -> bf16 K tile (exact; per-token scale applied to the fp32
+//          scores) and int8 -> f16 V tile (exact; per-token scale folded into
+//          the probabilities), or, for the reference uint8 scheme, the
+//          reference's dequantize ((q - zp) * scale, rounded per op to the
+//          scale dtype) -> bf16 K / f16 V.  New keys are copied from bf16.
+//   MMA1 : S[128 x 64] = Q[128 x 256] · Kᵀ  (bf16, fp32 in TMEM)
+//   soft : tcgen05.ld rows, mask, online max / sum, P = p * v_scale -> f16
+//          shared tile (conditional rescale of O in TMEM when the running max
+//          grows by more than 2^8)
+//   MMA2 : O[128 x 256] += P[128 x 64] · V[64 x 256]  (f16, V MN-major)
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2-5 convert / softmax / epilogue (warp w reads TMEM lanes
+// 32*(w%4) .. +31, i.e. one query row per thread).
+#include "rfx_internal.h"
+
+#include <algorithm>
+
+namespace rfx {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kKB = 64;
+constexpr int kQR = 128;
+constexpr int kThreads = 192;
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int kOffQ = 0;                     // 4 x [128 x 64] bf16, 64 KB
+constexpr int kOffK = kOffQ + 4 * 16384;     // 4 x [64 x 64] bf16, 32 KB
+constexpr int kOffV = kOffK + 4 * 8192;      // 4 x [64 x 64] f16 (MN-major blocks), 32 KB
+constexpr int kOffP = kOffV + 4 * 8192;      // [128 x 64] f16, 16 KB
+constexpr int kOffSK = kOffP + 16384;        // int8 K staging [64 x 256], 16 KB
+constexpr int kOffSV = kOffSK + 16384;       // int8 V staging, 16 KB
+constexpr int kOffScale = kOffSV + 16384;    // ks, vs, kdq, vdq, kzp, vzp: 6 x 64 fp32
+constexpr int kOffBar = kOffScale + 6 * 64 * 4;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+
+struct AttnParams {
+  int B, Hq, S, cap, n_ctx, mode, scale_bf16;
+  int q_tiles, splits, n_ctx_blocks, n_blocks;
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  const void* k_scale;
+  const void* v_scale;
+  const void* k_zp;
+  const void* v_zp;
+  const unsigned char* ctx_valid;
+  const int* new_block;
+  float scale_log2;
+  __nv_bfloat16* out;
+  float* ws_o;
+  float2* ws_ml;
+  int* status;
+};
+
+__device__ __forceinline__ float load_scalar(const void* p, long i, bool bf16) {
+  return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]) : static_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ float round_to(float x, bool bf16) { return bf16 ? bf16_round(x) : x; }
+
+// Converts 16 consecutive quantized values of one key row into bf16 (K) or
+// f16 (V) and stores them as two 16-byte chunks of a 128-byte-swizzled tile.
+template <bool IS_K>
+__device__ __forceinline__ void convert16(const uint8_t* src, uint8_t* tile_base, int key, int g, int mode,
+                                          bool sbf16, float sc, float zp) {
+  uint4 raw = *reinterpret_cast<const uint4*>(src);
+  const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&raw);
+  float f[16];
+  if (mode == kQuantI8Sym) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = static_cast<float>(static_cast<int8_t>(b8[e]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float t = round_to(__fsub_rn(static_cast<float>(b8[e]), zp), sbf16);
+      f[e] = round_to(__fmul_rn(t, sc), sbf16);
+    }
+  }
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = IS_K ? pack_bf16x2(f[2 * e], f[2 * e + 1]) : pack_f16x2(f[2 * e], f[2 * e + 1]);
+  uint8_t* atom = tile_base + (g >> 2) * 8192;
+  const int c0 = (g & 3) * 2;
+  *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  const int blk_begin = sp * p.n_blocks / p.splits;
+  const int blk_end = (sp + 1) * p.n_blocks / p.splits;
+  const int nbl = blk_end - blk_begin;
+
+  uint8_t* sQ = smem + kOffQ;
+  uint8_t* sK = smem + kOffK;
+  uint8_t* sV = smem + kOffV;
+  uint8_t* sP = smem + kOffP;
+  uint8_t* stK = smem + kOffSK;
+  uint8_t* stV = smem + kOffSV;
+  float* ks_s = reinterpret_cast<float*>(smem + kOffScale);
+  float* vs_s = ks_s + 64;
+  float* kdq_s = vs_s + 64;  // reference-scheme dequant scales and zero points
+  float* vdq_s = kdq_s + 64;
+  float* kzp_s = vdq_s + 64;
+  float* vzp_s = kzp_s + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* stage_free = bars + 2;
+  uint64_t* conv_done = bars + 3;
+  uint64_t* s_full = bars + 4;
+  uint64_t* p_ready = bars + 5;
+  uint64_t* o_full = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(kv_full, 1);
+    mbar_init(stage_free, 4);
+    mbar_init(conv_done, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 4);
+    mbar_init(o_full, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmO = tmem, tmS = tmem + 256;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
+  int issued_ctx = 0;
+
+  if (warp == 0) {
+    if (lane == 0 && nbl > 0) {
+      mbar_arrive_expect_tx(q_full, 4 * 16384);
+      for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
+      for (int jl = 0; jl < nbl; ++jl) {
+        const int j = blk_begin + jl;
+        if (j >= p.n_ctx_blocks) break;
+        if (issued_ctx > 0 && !mbar_wait(stage_free, (issued_ctx - 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
+        mbar_arrive_expect_tx(kv_full, 2 * 16384);
+        const int row = b * p.cap + j * kKB;
+        tma_load_2d(stK, &tmK, kv_full, 0, row);
+        tma_load_2d(stV, &tmV, kv_full, 0, row);
+        ++issued_ctx;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nbl > 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
+      constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
+      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutTmaFull);
+      for (int jl = 0; jl < nbl && ok; ++jl) {
+        if (!(ok = mbar_wait(conv_done, jl & 1, p.status, kDevTimeoutConvert))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const int a = ks >> 2, kk = ks & 3;
+          const uint64_t ad = make_sdesc_sw128(smem_u32(sQ + a * 16384) + kk * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(smem_u32(sK + a * 8192) + kk * 32, 16, 1024);
+          umma_f16_ss(tmS, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!(ok = mbar_wait(p_ready, jl & 1, p.status, kDevTimeoutConvert))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kKB / 16; ++ks) {
+          const uint64_t ad = make_sdesc_sw128(smem_u32(sP) + ks * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(smem_u32(sV) + ks * 2048, 8192, 1024);
+          umma_f16_ss(tmO, ad, bd, idesc_o, (jl > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(o_full);
+      }
+    }
+  } else {
+    const int et = threadIdx.x - 64;  // 0..127
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row inside the tile == TMEM lane
+    const int R = qt * kQR + r;      // stacked row inside the stream
+    const bool row_valid = R < p.Hq * p.S;
+    const int s_row = row_valid ? R % p.S : 0;
+    const int h_row = row_valid ? R / p.S : 0;
+    const int my_block = (row_valid && p.new_block) ? p.new_block[s_row] : 0;
+    const bool sbf16 = p.scale_bf16 != 0;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    int ctx_iter = 0;
+    bool ok = true;
+
+    for (int jl = 0; jl < nbl && ok; ++jl) {
+      const int j = blk_begin + jl;
+      const bool is_ctx = j < p.n_ctx_blocks;
+      if (jl > 0) ok = mbar_wait(o_full, (jl - 1) & 1, p.status, kDevTimeoutMmaDone);
+      if (!ok) break;
+      // ---- convert block j into sK / sV ----
+      if (is_ctx) {
+        if (et < 64) {
+          const long slot = static_cast<long>(j) * kKB + et;
+          const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
+          bool valid = slot < p.n_ctx;
+          if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
+          if (p.mode == kQuantI8Sym) {
+            ks_s[et] = valid ? static_cast<const float*>(p.k_scale)[gi] : -INFINITY;  // -inf masks the key
+            vs_s[et] = valid ? static_cast<const float*>(p.v_scale)[gi] : 0.f;
+          } else {
+            ks_s[et] = valid ? 1.f : -INFINITY;
+            vs_s[et] = 1.f;
+            kdq_s[et] = load_scalar(p.k_scale, gi, sbf16);
+            vdq_s[et] = load_scalar(p.v_scale, gi, sbf16);
+            kzp_s[et] = load_scalar(p.k_zp, gi, sbf16);
+            vzp_s[et] = load_scalar(p.v_zp, gi, sbf16);
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!(ok = mbar_wait(kv_full, ctx_iter & 1, p.status, kDevTimeoutTmaFull))) break;
+        ++ctx_iter;
+        for (int it = et; it < 2 * kKB * 16; it += 128) {
+          const bool isv = it >= kKB * 16;
+          const int w = isv ? it - kKB * 16 : it;
+          const int key = w >> 4, g = w & 15;
+          float sc = 0.f, zp = 0.f;
+          if (p.mode != kQuantI8Sym) {
+            sc = isv ? vdq_s[key] : kdq_s[key];
+            zp = isv ? vzp_s[key] : kzp_s[key];
+          }
+          if (isv)
+            convert16<false>(stV + key * kD + g * 16, sV, key, g, p.mode, sbf16, sc, zp);
+          else
+            convert16<true>(stK + key * kD + g * 16, sK, key, g, p.mode, sbf16, sc, zp);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stage_free);
+      } else {
+        const int nb0 = (j - p.n_ctx_blocks) * kKB;
+        if (et < 64) {
+          const int kk = nb0 + et;
+          ks_s[et] = kk < p.S ? 1.f : -INFINITY;  // block-causal visibility is applied per row
+          vs_s[et] = 1.f;
+        }
+        for (int it = et; it < 2 * kKB * 32; it += 128) {
+          const bool isv = it >= kKB * 32;
+          const int w = isv ? it - kKB * 32 : it;
+          const int key = w >> 5, c = w & 31;  // 32 chunks of 8 elements per key
+          const int kk = nb0 + key;
+          uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+          if (kk < p.S) {
+            const __nv_bfloat16* src = (isv ? p.v_new : p.k_new) + (static_cast<long>(b) * p.S + kk) * kD + c * 8;
+            raw = *reinterpret_cast<const uint4*>(src);
+          }
+          uint8_t* atom = (isv ? sV : sK) + (c >> 3) * 8192;
+          if (isv) {
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 f = __bfloat1622float2(h2[e]);
+              w4[e] = pack_f16x2(f.x, f.y);
+            }
+            raw = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+          *reinterpret_cast<uint4*>(atom + sw128_offset(key, c & 7)) = raw;
+        }
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (lane == 0) mbar_arrive(conv_done);
+
+      // ---- softmax on S ----
+      if (!(ok = mbar_wait(s_full, jl & 1, p.status, kDevTimeoutMmaDone))) break;
+      tc_fence_after();
+      float z[kKB];
+#pragma unroll
+      for (int c = 0; c < kKB / 16; ++c) {
+        uint32_t rr[16];
+        tmem_ld16(tmS + lane_base + c * 16, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[e]);
+      }
+      float bmax = -INFINITY;
+#pragma unroll
+      for (int kk = 0; kk < kKB; ++kk) {
+        const float ksc = ks_s[kk];
+        bool valid = ksc != -INFINITY;
+        if (!is_ctx && valid && p.new_block) {
+          const int nk = (j - p.n_ctx_blocks) * kKB + kk;
+          valid = p.new_block[nk] <= my_block;
+        }
+        z[kk] = valid ? z[kk] * ksc * p.scale_log2 : -INFINITY;
+        bmax = fmaxf(bmax, z[kk]);
+      }
+      float m_new = fmaxf(m_run, bmax);
+      bool need = false;
+      float m_use;
+      if (m_run == -INFINITY) {
+        m_use = m_new;
+      } else if (m_new > m_run + 8.f) {
+        need = true;
+        m_use = m_new;
+      } else {
+        m_use = m_run;
+      }
+      const float alpha = need ? exp2f(m_run - m_use) : 1.f;
+      float psum = 0.f;
+      float pv[kKB];
+#pragma unroll
+      for (int kk = 0; kk < kKB; ++kk) {
+        const float e = (m_use == -INFINITY || z[kk] == -INFINITY) ? 0.f : exp2f(z[kk] - m_use);
+        psum += e;
+        pv[kk] = e * vs_s[kk];
+      }
+      l_run = l_run * alpha + psum;
+      m_run = m_use;
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < kD / 16; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(tmO + lane_base + c * 16, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+          tmem_st16(tmO + lane_base + c * 16, rr);
+        }
+        tmem_wait_st();
+      }
+      // P tile row r: 64 f16 values = 8 chunks of 16 B
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = make_uint4(pack_f16x2(pv[8 * c + 0], pv[8 * c + 1]), pack_f16x2(pv[8 * c + 2], pv[8 * c + 3]),
+                                   pack_f16x2(pv[8 * c + 4], pv[8 * c + 5]), pack_f16x2(pv[8 * c + 6], pv[8 * c + 7]));
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, c)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+
+    // ---- epilogue ----
+    if (ok && nbl > 0) ok = mbar_wait(o_full, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone);
+    tc_fence_after();
+    if (ok && nbl > 0) {
+      const bool final_out = p.splits == 1;
+      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+      const long tok = static_cast<long>(b) * p.S + s_row;
+      __nv_bfloat16* orow = p.out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
+      const long wrow = ((static_cast<long>(b) * p.q_tiles + qt) * p.splits + sp) * kQR + r;
+      float* wrow_o = p.ws_o ? p.ws_o + wrow * kD : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < kD / 16; ++c) {
+        uint32_t rr[16];
+        tmem_ld16(tmO + lane_base + c * 16, rr);
+        tmem_wait_ld();
+        if (!row_valid) continue;
+        if (final_out) {
+          uint32_t w8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            w8[e] = pack_bf16x2(__uint_as_float(rr[2 * e]) * inv_l, __uint_as_float(rr[2 * e + 1]) * inv_l);
+          *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+          *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            *reinterpret_cast<float4*>(wrow_o + c * 16 + 4 * e) =
+                make_float4(__uint_as_float(rr[4 * e]), __uint_as_float(rr[4 * e + 1]), __uint_as_float(rr[4 * e + 2]),
+                            __uint_as_float(rr[4 * e + 3]));
+        }
+      }
+      if (!final_out && row_valid) p.ws_ml[wrow] = make_float2(m_run, l_run);
+    }
+    (void)et;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // drain a producer that stopped early
+  if (warp == 0 && lane == 0 && issued_ctx > 0) mbar_wait(kv_full, (issued_ctx - 1) & 1, p.status, kDevTimeoutTmaFull);
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Merges the kv_splits partial results of every query row.
+__global__ void __launch_bounds__(128) attention_combine_kernel(const AttnParams p) {
+  pdl_wait();
+  const long g = static_cast<long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const long rows = static_cast<long>(p.B) * p.q_tiles * kQR;
+  if (g < rows) {
+    const int r = static_cast<int>(g % kQR);
+    const int qt = static_cast<int>((g / kQR) % p.q_tiles);
+    const int b = static_cast<int>(g / (static_cast<long>(kQR) * p.q_tiles));
+    const int R = qt * kQR + r;
+    if (R < p.Hq * p.S) {
+      const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.splits;
+      float M = -INFINITY;
+      for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.ws_ml[(base + s) * kQR + r].x);
+      float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < p.splits; ++s) {
+        const float2 ml = p.ws_ml[(base + s) * kQR + r];
+        if (ml.x == -INFINITY || ml.y <= 0.f) continue;
+        const float w = exp2f(ml.x - M);
+        L += w * ml.y;
+        const float* o = p.ws_o + ((base + s) * kQR + r) * kD + lane * 8;
+        const float4 a = *reinterpret_cast<const float4*>(o);
+        const float4 c = *reinterpret_cast<const float4*>(o + 4);
+        acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+        acc[4] += w * c.x; acc[5] += w * c.y; acc[6] += w * c.z; acc[7] += w * c.w;
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const int s_row = R % p.S, h_row = R / p.S;
+      __nv_bfloat16* orow =
+          p.out + (static_cast<long>(b) * p.S + s_row) * (static_cast<long>(p.Hq) * kD) + h_row * kD + lane * 8;
+      *reinterpret_cast<uint4*>(orow) = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv),
+                                                   pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                                                   pack_bf16x2(acc[4] * inv, acc[5] * inv),
+                                                   pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    }
+  }
+  pdl_launch_dependents();
+}
+
+struct Geometry {
+  int q_tiles, n_ctx_blocks, n_blocks, splits;
+};
+
+int geometry(const rfx_attn_desc& d, Geometry* g) {
+  if (d.B < 1 || d.num_q_heads < 1 || d.head_dim != kD || d.S < 1 || d.capacity < 0 || d.n_ctx < 0 ||
+      d.n_ctx > d.capacity)
+    return set_error(RFX_E_INVAL, "rfx_attention: need head_dim=256, S>=1, 0<=n_ctx<=capacity");
+  if (d.quant_mode != RFX_QUANT_I8_SYM && d.quant_mode != RFX_QUANT_U8_REF)
+    return set_error(RFX_E_INVAL, "rfx_attention: quant_mode");
+  g->q_tiles = (d.num_q_heads * d.S + kQR - 1) / kQR;
+  g->n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
+  g->n_blocks = g->n_ctx_blocks + (d.S + kKB - 1) / kKB;
+  int nsm = 148;
+  rfx_num_sms(&nsm);
+  int splits = d.kv_splits;
+  if (splits <= 0) {
+    const int ctas = d.B * g->q_tiles;
+    splits = std::max(1, std::min(g->n_blocks, nsm / std::max(1, ctas)));
+  }
+  if (splits > g->n_blocks) splits = g->n_blocks;
+  g->splits = splits;
+  return RFX_OK;
+}
+
+}  // namespace
+
+size_t attention_workspace_bytes(const rfx_attn_desc& d) {
+  Geometry g;
+  if (geometry(d, &g) != RFX_OK || g.splits == 1) return 0;
+  const size_t rows = static_cast<size_t>(d.B) * g.q_tiles * g.splits * kQR;
+  return rows * kD * sizeof(float) + rows * sizeof(float2);
+}
+
+int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV) {
+  Geometry g;
+  int rc = geometry(d, &g);
+  if (rc) return rc;
+  if (!d.q || !d.k_new || !d.v_new || !d.out) return set_error(RFX_E_INVAL, "rfx_attention: null q/k_new/v_new/out");
+  const uint64_t qrows = static_cast<uint64_t>(d.B) * d.num_q_heads * d.S;
+  rc = make_tmap_2d(tmQ, d.q, 2, kD, qrows, kD * 2, 64, kQR, true);
+  if (rc) return rc;
+  if (d.n_ctx > 0) {
+    if (!d.k_ring || !d.v_ring || !d.k_scale || !d.v_scale ||
+        (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp || !d.v_zp)))
+      return set_error(RFX_E_INVAL, "rfx_attention: null ring/scale pointers");
+    const uint64_t krows = static_cast<uint64_t>(d.B) * d.capacity;
+    rc = make_tmap_2d(tmK, d.k_ring, 1, kD, krows, kD, kD, kKB, false);
+    if (rc) return rc;
+    rc = make_tmap_2d(tmV, d.v_ring, 1, kD, krows, kD, kD, kKB, false);
+    if (rc) return rc;
+  } else {
+    *tmK = *tmQ;
+    *tmV = *tmQ;
+  }
+  return RFX_OK;
+}
+
+int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                     cudaStream_t stream, bool pdl) {
+  Geometry g;
+  int rc = geometry(d, &g);
+  if (rc) return rc;
+  const size_t need = attention_workspace_bytes(d);
+  if (need > 0 && (!d.workspace || d.workspace_bytes < need || (reinterpret_cast<uintptr_t>(d.workspace) & 15u)))
+    return set_error(RFX_E_INVAL, "rfx_attention: workspace of %zu bytes (16-byte aligned) required", need);
+  const void* fn = reinterpret_cast<const void*>(attention_kernel);
+  rc = ensure_smem_attr(fn, kSmemBytes);
+  if (rc) return rc;
+
+  AttnParams p{};
+  p.B = d.B;
+  p.Hq = d.num_q_heads;
+  p.S = d.S;
+  p.cap = d.capacity;
+  p.n_ctx = d.n_ctx;
+  p.mode = d.quant_mode;
+  p.scale_bf16 = d.scale_dtype == RFX_DTYPE_BF16;
+  p.q_tiles = g.q_tiles;
+  p.splits = g.splits;
+  p.n_ctx_blocks = g.n_ctx_blocks;
+  p.n_blocks = g.n_blocks;
+  p.k_new = static_cast<const __nv_bfloat16*>(d.k_new);
+  p.v_new = static_cast<const __nv_bfloat16*>(d.v_new);
+  p.k_scale = d.k_scale;
+  p.v_scale = d.v_scale;
+  p.k_zp = d.k_zp;
+  p.v_zp = d.v_zp;
+  p.ctx_valid = d.ctx_valid;
+  p.new_block = d.new_block;
+  p.scale_log2 = d.softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(d.out);
+  if (need > 0) {
+    p.ws_o = static_cast<float*>(d.workspace);
+    const size_t rows = static_cast<size_t>(d.B) * g.q_tiles * g.splits * kQR;
+    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(d.workspace) + rows * kD * sizeof(float));
+  }
+  p.status = device_status_ptr();
+
+  CUtensorMap q = *tmQ, k = *tmK, v = *tmV;
+  dim3 grid(g.q_tiles, g.splits, d.B);
+  rc = launch_kernel(fn, grid, dim3(kThreads), kSmemBytes, stream, pdl, 1, q, k, v, p);
+  if (rc || g.splits == 1) return rc;
+  const long rows = static_cast<long>(d.B) * g.q_tiles * kQR;
+  dim3 cgrid(static_cast<unsigned>((rows + 3) / 4));
+  return launch_kernel(reinterpret_cast<const void*>(attention_combine_kernel), cgrid, dim3(128), 0, stream, pdl, 1,
+                       p);
+}
+
+}  // namespace rfx
+
+extern "C" int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes) {
+  using namespace rfx;
+  if (!desc || !bytes) return set_error(RFX_E_INVAL, "rfx_attention_workspace_size: null argument");
+  Geometry g;
+  int rc = geometry(*desc, &g);
+  if (rc) return rc;
+  *bytes = attention_workspace_bytes(*desc);
+  return RFX_OK;
+}
+
+extern "C" int rfx_attention(const rfx_attn_desc* desc, void* stream) {
+  using namespace rfx;
+  if (!desc) return set_error(RFX_E_INVAL, "rfx_attention: null descriptor");
+  CUtensorMap q, k, v;
+  int rc = build_attention_maps(*desc, &q, &k, &v);
+  if (rc) return rc;
+  return launch_attention(*desc, &q, &k, &v, static_cast<cudaStream_t>(stream), pdl_enabled());
+}

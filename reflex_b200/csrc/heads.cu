@@ -1,0 +1,400 @@
+// Small kernels around the action expert: timestep conditioning, AdaRMSNorm
+// modulation, action in-projection and the fused Euler tail.  All of them are
+// HBM- or latency-bound; weights are read with 128-bit coalesced loads, one
+// warp per output row, and reduced with warp shuffles.
+#include "rfx_internal.h"
+
+namespace rfx {
+namespace {
+
+constexpr int kMaxRows = 16;  // conditioning rows (timesteps x streams) per launch
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+
+// emb[i][j]: sin for j < W/2, cos for j >= W/2, of t[i] * 2*pi / period_j with
+// period_j = min_period * (max_period/min_period)^(j/(W/2-1)), all in fp64,
+// rounded once to bf16 (reflex/policies/pi05/utils.py:109-121).
+__global__ void sinusoid_kernel(const float* __restrict__ t, int n_t, int width, double min_period,
+                                double max_period, __nv_bfloat16* __restrict__ emb) {
+  pdl_wait();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int half = width / 2;
+  if (idx < n_t * half) {
+    const int i = idx / half, j = idx % half;
+    // torch.linspace(0, 1, half) in fp64: start + step*j for the first half,
+    // end - step*(half-1-j) for the second half
+    const double step = half > 1 ? 1.0 / static_cast<double>(half - 1) : 0.0;
+    const double frac = j < half / 2 ? step * j : 1.0 - step * (half - 1 - j);
+    const double period = min_period * pow(max_period / min_period, frac);
+    const double x = (1.0 / period * 2.0 * 3.141592653589793) * static_cast<double>(t[i]);
+    double s, c;
+    sincos(x, &s, &c);
+    emb[static_cast<long>(i) * width + j] = __double2bfloat16(s);
+    emb[static_cast<long>(i) * width + half + j] = __double2bfloat16(c);
+  }
+  pdl_launch_dependents();
+}
+
+// out[i][o] = bf16(silu(bf16(sum_k in[i][k] * W[o][k] + b[o]))) for bf16 W.
+__global__ void __launch_bounds__(256) gemv_bf16_silu_kernel(const __nv_bfloat16* __restrict__ in, int n_rows,
+                                                             int width, const __nv_bfloat16* __restrict__ W,
+                                                             const __nv_bfloat16* __restrict__ bias, int n_out,
+                                                             __nv_bfloat16* __restrict__ out) {
+  extern __shared__ float xin[];  // [n_rows][width]
+  pdl_wait();
+  for (int i = threadIdx.x; i < n_rows * width; i += blockDim.x) xin[i] = __bfloat162float(in[i]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.x * 8 + warp;
+  if (o < n_out) {
+    float acc[kMaxRows];
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
+    const __nv_bfloat16* wr = W + static_cast<long>(o) * width;
+    for (int k = lane * 8; k < width; k += 256) {
+      uint4 raw = *reinterpret_cast<const uint4*>(wr + k);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(w2[e]);
+        w[2 * e] = f.x;
+        w[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxRows; ++r) {
+        if (r < n_rows) {
+          const float* xr = xin + r * width + k;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r] = fmaf(w[e], xr[e], acc[r]);
+        }
+      }
+    }
+    const float bo = bias ? __bfloat162float(bias[o]) : 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) {
+      if (r < n_rows) {
+        const float s = warp_sum(acc[r]);
+        if (lane == 0) out[static_cast<long>(r) * n_out + o] = __float2bfloat16_rn(silu(bf16_round(s + bo)));
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// AdaRMSNorm modulation: fp32 W [n_norms * out][width], one warp per output
+// row, all conditioning rows at once.
+__global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict__ W, const float* __restrict__ bias,
+                                                         const __nv_bfloat16* __restrict__ cond, int n_rows, int width,
+                                                         int n_norms, int out_per_norm, int mode,
+                                                         float* __restrict__ a2, float* __restrict__ b2,
+                                                         float* __restrict__ gate) {
+  extern __shared__ float cin[];  // [n_rows][width]
+  pdl_wait();
+  for (int i = threadIdx.x; i < n_rows * width; i += blockDim.x) cin[i] = __bfloat162float(cond[i]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = static_cast<long>(blockIdx.x) * 8 + warp;  // over n_norms * out_per_norm
+  if (row < static_cast<long>(n_norms) * out_per_norm) {
+    float acc[kMaxRows];
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
+    const float* wr = W + row * width;
+    for (int k = lane * 4; k < width; k += 128) {
+      const float4 w = __ldcs(reinterpret_cast<const float4*>(wr + k));  // streamed once per chunk
+#pragma unroll
+      for (int r = 0; r < kMaxRows; ++r) {
+        if (r < n_rows) {
+          const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
+          acc[r] = fmaf(w.x, x.x, acc[r]);
+          acc[r] = fmaf(w.y, x.y, acc[r]);
+          acc[r] = fmaf(w.z, x.z, acc[r]);
+          acc[r] = fmaf(w.w, x.w, acc[r]);
+        }
+      }
+    }
+    const int n = static_cast<int>(row / out_per_norm);
+    const int o = static_cast<int>(row % out_per_norm);
+    const float bo = bias[row];
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) {
+      if (r < n_rows) {
+        const float m = __fadd_rn(warp_sum(acc[r]), bo);
+        if (lane == 0) {
+          const long base = (static_cast<long>(r) * n_norms + n) * width;
+          if (mode == RFX_ADARMS_GATE) {
+            a2[base + o] = m;
+            if (b2) b2[base + o] = 0.f;
+            gate[base + o] = bf16_round(m);
+          } else {
+            const int part = o / width, f = o % width;
+            if (part == 0) a2[base + f] = __fadd_rn(1.f, m);
+            else if (part == 1) b2[base + f] = m;
+            else gate[base + f] = bf16_round(m);
+          }
+        }
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// h_next[row(b,s)][o] = bf16(sum_a bf16(x[b][s][a]) * W_in[o][a] + b_in[o]); one CTA per (b, s).
+__device__ __forceinline__ void action_in_row(const float* xs, int A, int width, const __nv_bfloat16* __restrict__ W_in,
+                                              const __nv_bfloat16* __restrict__ b_in, __nv_bfloat16* __restrict__ dst) {
+  for (int o = threadIdx.x; o < width; o += blockDim.x) {
+    const __nv_bfloat16* wr = W_in + static_cast<long>(o) * A;
+    float acc = 0.f;
+    for (int a = 0; a < A; a += 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(wr + a);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(w2[e]);
+        acc = fmaf(f.x, xs[a + 2 * e], acc);
+        acc = fmaf(f.y, xs[a + 2 * e + 1], acc);
+      }
+    }
+    dst[o] = __float2bfloat16_rn(acc + (b_in ? __bfloat162float(b_in[o]) : 0.f));
+  }
+}
+
+struct IoParams {
+  int B, S, S_total, A, width, h_row_offset;
+  const __nv_bfloat16* h;
+  const float* a1;
+  const float* a2;
+  const float* b2;
+  long ab_stride;
+  float eps;
+  const __nv_bfloat16* w_out;
+  const __nv_bfloat16* b_out;
+  float* x;
+  float dt;
+  const __nv_bfloat16* w_in;
+  const __nv_bfloat16* b_in;
+  __nv_bfloat16* h_next;
+  int h_next_ld, h_next_rps, h_next_off;
+};
+
+__global__ void __launch_bounds__(256) action_in_kernel(const IoParams p) {
+  __shared__ float xs[256];
+  pdl_wait();
+  const int b = blockIdx.x / p.S, s = blockIdx.x % p.S;
+  for (int a = threadIdx.x; a < p.A; a += blockDim.x)
+    xs[a] = bf16_round(p.x[(static_cast<long>(b) * p.S + s) * p.A + a]);
+  __syncthreads();
+  action_in_row(xs, p.A, p.width, p.w_in, p.b_in,
+                p.h_next + (static_cast<long>(b) * p.h_next_rps + p.h_next_off + s) * p.h_next_ld);
+  pdl_launch_dependents();
+}
+
+// Final norm -> action_out_proj -> Euler update -> next step's action_in_proj,
+// all per action token (tokens are independent in these three ops).
+__global__ void __launch_bounds__(256) euler_tail_kernel(const IoParams p) {
+  extern __shared__ float ysh[];  // [width] normalized row, then [A] velocity / new x
+  __shared__ float red[8];
+  __shared__ float xs[256];
+  pdl_wait();
+  const int b = blockIdx.x / p.S, s = blockIdx.x % p.S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __nv_bfloat16* hr = p.h + (static_cast<long>(b) * p.S_total + p.h_row_offset + s) * p.width;
+  float ss = 0.f;
+  for (int k = threadIdx.x * 8; k < p.width; k += blockDim.x * 8) {
+    uint4 raw = *reinterpret_cast<const uint4*>(hr + k);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(h2[e]);
+      ysh[k + 2 * e] = f.x;
+      ysh[k + 2 * e + 1] = f.y;
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];
+  const float rstd = rsqrtf(tot / static_cast<float>(p.width) + p.eps);
+  for (int k = threadIdx.x; k < p.width; k += blockDim.x) {
+    float v = __fmul_rn(__fmul_rn(ysh[k], rstd), p.a1[k]);
+    if (p.a2) v = __fmul_rn(v, p.a2[b * p.ab_stride + k]);
+    if (p.b2) v = __fadd_rn(v, p.b2[b * p.ab_stride + k]);
+    ysh[k] = bf16_round(v);
+  }
+  __syncthreads();
+  // velocity v[a] = bf16(y · W_out[a] + b_out[a]); x += fp32(bf16(dt * v))
+  for (int a = warp; a < p.A; a += blockDim.x >> 5) {
+    const __nv_bfloat16* wr = p.w_out + static_cast<long>(a) * p.width;
+    float acc = 0.f;
+    for (int k = lane * 8; k < p.width; k += 256) {
+      uint4 raw = *reinterpret_cast<const uint4*>(wr + k);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(w2[e]);
+        acc = fmaf(f.x, ysh[k + 2 * e], acc);
+        acc = fmaf(f.y, ysh[k + 2 * e + 1], acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const float v = bf16_round(acc + (p.b_out ? __bfloat162float(p.b_out[a]) : 0.f));
+      float* xp = p.x + (static_cast<long>(b) * p.S + s) * p.A + a;
+      const float xn = __fadd_rn(*xp, bf16_round(__fmul_rn(p.dt, v)));
+      *xp = xn;
+      xs[a] = bf16_round(xn);
+    }
+  }
+  if (p.h_next) {
+    __syncthreads();
+    action_in_row(xs, p.A, p.width, p.w_in, p.b_in,
+                  p.h_next + (static_cast<long>(b) * p.h_next_rps + p.h_next_off + s) * p.h_next_ld);
+  }
+  pdl_launch_dependents();
+}
+
+IoParams io_params(const rfx_action_io_desc& d) {
+  IoParams p{};
+  p.B = d.B;
+  p.S = d.S;
+  p.S_total = d.S_total;
+  p.A = d.action_dim;
+  p.width = d.width;
+  p.h_row_offset = d.h_row_offset;
+  p.h = static_cast<const __nv_bfloat16*>(d.h);
+  p.a1 = d.norm_a1;
+  p.a2 = d.norm_a2;
+  p.b2 = d.norm_b2;
+  p.ab_stride = d.norm_ab_stride;
+  p.eps = d.eps;
+  p.w_out = static_cast<const __nv_bfloat16*>(d.w_out);
+  p.b_out = static_cast<const __nv_bfloat16*>(d.b_out);
+  p.x = d.x;
+  p.dt = d.dt;
+  p.w_in = static_cast<const __nv_bfloat16*>(d.w_in);
+  p.b_in = static_cast<const __nv_bfloat16*>(d.b_in);
+  p.h_next = static_cast<__nv_bfloat16*>(d.h_next);
+  p.h_next_ld = d.h_next_ld;
+  p.h_next_rps = d.h_next_rows_per_stream;
+  p.h_next_off = d.h_next_row_offset;
+  return p;
+}
+
+bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate_io(const rfx_action_io_desc& d, bool tail) {
+  if (d.B < 1 || d.S < 1 || d.action_dim < 8 || d.action_dim % 8 || d.action_dim > 256 || d.width < 256 ||
+      d.width % 256 || !d.x)
+    return set_error(RFX_E_INVAL, "action io: need B,S>=1, action_dim%%8==0 (<=256), width%%256==0");
+  if (tail) {
+    if (!d.h || !d.w_out || !d.norm_a1 || d.S_total < d.S || d.h_row_offset < 0 ||
+        d.h_row_offset + d.S > d.S_total || !a16(d.h) || !a16(d.w_out))
+      return set_error(RFX_E_INVAL, "rfx_euler_tail: h/w_out/norm_a1 and row layout");
+  }
+  if (d.h_next || !tail) {
+    if (!d.h_next || !d.w_in || !a16(d.w_in) || d.h_next_ld < d.width || d.h_next_rows_per_stream < d.S ||
+        d.h_next_row_offset < 0 || d.h_next_row_offset + d.S > d.h_next_rows_per_stream)
+      return set_error(RFX_E_INVAL, "action in-proj: h_next/w_in layout");
+  }
+  return RFX_OK;
+}
+
+}  // namespace
+
+int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl) {
+  if (d.n_t < 1 || d.n_t > kMaxRows || d.width < 256 || d.width % 256 || !d.t || !d.w_in || !d.w_out || !d.hidden ||
+      !d.cond || !a16(d.w_in) || !a16(d.w_out))
+    return set_error(RFX_E_INVAL, "rfx_time_cond: need 1<=n_t<=16, width%%256==0, aligned weights");
+  if (!(d.min_period > 0.f) || !(d.max_period > 0.f)) return set_error(RFX_E_INVAL, "rfx_time_cond: periods");
+  __nv_bfloat16* emb = static_cast<__nv_bfloat16*>(d.cond);  // the embedding is staged in `cond`
+  const int half = d.width / 2;
+  const float* t = d.t;
+  int n_t = d.n_t, width = d.width;
+  double minp = d.min_period, maxp = d.max_period;
+  int rc = launch_kernel(reinterpret_cast<const void*>(sinusoid_kernel), dim3((n_t * half + 255) / 256), dim3(256), 0,
+                         stream, pdl, 1, t, n_t, width, minp, maxp, emb);
+  if (rc) return rc;
+  const size_t smem = static_cast<size_t>(n_t) * width * sizeof(float);
+  const void* gemv = reinterpret_cast<const void*>(gemv_bf16_silu_kernel);
+  rc = ensure_smem_attr(gemv, 200 * 1024);
+  if (rc) return rc;
+  if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_time_cond: n_t*width too large");
+  const __nv_bfloat16* in0 = emb;
+  const __nv_bfloat16* w_in = static_cast<const __nv_bfloat16*>(d.w_in);
+  const __nv_bfloat16* b_in = static_cast<const __nv_bfloat16*>(d.b_in);
+  __nv_bfloat16* hid = static_cast<__nv_bfloat16*>(d.hidden);
+  int n_out = width;
+  dim3 grid((width + 7) / 8);
+  rc = launch_kernel(gemv, grid, dim3(256), smem, stream, pdl, 1, in0, n_t, width, w_in, b_in, n_out, hid);
+  if (rc) return rc;
+  const __nv_bfloat16* in1 = hid;
+  const __nv_bfloat16* w_out = static_cast<const __nv_bfloat16*>(d.w_out);
+  const __nv_bfloat16* b_out = static_cast<const __nv_bfloat16*>(d.b_out);
+  __nv_bfloat16* cond = static_cast<__nv_bfloat16*>(d.cond);
+  return launch_kernel(gemv, grid, dim3(256), smem, stream, pdl, 1, in1, n_t, width, w_out, b_out, n_out, cond);
+}
+
+int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pdl) {
+  const int out = d.mode == RFX_ADARMS_SSG ? 3 * d.width : d.width;
+  if ((d.mode != RFX_ADARMS_GATE && d.mode != RFX_ADARMS_SSG) || d.n_rows < 1 || d.n_rows > kMaxRows ||
+      d.n_norms < 1 || d.width < 128 || d.width % 128 || !d.w || !d.b || !d.cond || !d.a2 || !d.gate ||
+      (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w))
+    return set_error(RFX_E_INVAL, "rfx_modulation: bad descriptor");
+  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(float);
+  if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
+  const void* fn = reinterpret_cast<const void*>(modulation_kernel);
+  int rc = ensure_smem_attr(fn, 200 * 1024);
+  if (rc) return rc;
+  const long rows = static_cast<long>(d.n_norms) * out;
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  const float* w = d.w;
+  const float* bias = d.b;
+  const __nv_bfloat16* cond = static_cast<const __nv_bfloat16*>(d.cond);
+  int n_rows = d.n_rows, width = d.width, n_norms = d.n_norms, opn = out, mode = d.mode;
+  float* a2 = d.a2;
+  float* b2 = d.b2;
+  float* gate = d.gate;
+  return launch_kernel(fn, grid, dim3(256), smem, stream, pdl, 1, w, bias, cond, n_rows, width, n_norms, opn, mode, a2,
+                       b2, gate);
+}
+
+int launch_action_in(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_io(d, false);
+  if (rc) return rc;
+  IoParams p = io_params(d);
+  return launch_kernel(reinterpret_cast<const void*>(action_in_kernel), dim3(d.B * d.S), dim3(256), 0, stream, pdl, 1,
+                       p);
+}
+
+int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_io(d, true);
+  if (rc) return rc;
+  IoParams p = io_params(d);
+  const size_t smem = static_cast<size_t>(d.width) * sizeof(float);
+  const void* fn = reinterpret_cast<const void*>(euler_tail_kernel);
+  rc = ensure_smem_attr(fn, static_cast<int>(smem > 48 * 1024 ? smem : 48 * 1024));
+  if (rc) return rc;
+  return launch_kernel(fn, dim3(d.B * d.S), dim3(256), smem, stream, pdl, 1, p);
+}
+
+}  // namespace rfx
+
+extern "C" int rfx_time_cond(const rfx_time_cond_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_time_cond: null descriptor");
+  return rfx::launch_time_cond(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}
+extern "C" int rfx_modulation(const rfx_modulation_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_modulation: null descriptor");
+  return rfx::launch_modulation(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}
+extern "C" int rfx_action_in(const rfx_action_io_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_action_in: null descriptor");
+  return rfx::launch_action_in(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}
+extern "C" int rfx_euler_tail(const rfx_action_io_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_euler_tail: null descriptor");
+  return rfx::launch_euler_tail(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}

@@ -1,0 +1,194 @@
+// KV quantize-append into a ring buffer.
+//
+// Replaces the reference's per-(batch, head, token) quantizers:
+//   * reflex/layers/streaming_attention.py:211-218  (StreamingAttention._quantize,
+//     uint8 asymmetric min/max with zero-point, every op in the activation dtype)
+//   * reflex/layers/quantize_kernel.py:6-79         (Triton _quantize_store_kernel,
+//     same scheme, cache offset = l_offset + token)
+// and adds the int8 symmetric per-token/per-head scheme (scale = absmax/127 in
+// fp32, q = clamp(rne(x/scale), -127, 127)).
+//
+// Layout: one warp per (b, h, token) row of D = 256 elements; each lane owns 8
+// contiguous elements (one 16-byte bf16 vector or two fp32 vectors) and
+// reductions are warp shuffles.  The destination slot of token l is
+//   region_base + (region_off + l) % region_len
+// so an append that wraps around the ring window is one launch, and eviction
+// of the oldest frame is simply overwriting its slots (no data movement).
+// Grid: x = row blocks, y = {K, V}.
+#include "rfx_internal.h"
+
+namespace rfx {
+
+namespace {
+
+constexpr int kD = 256;
+constexpr int kWarpsPerBlock = 8;
+
+template <typename T>
+struct Vec8 {
+  float v[8];
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Rounds an fp32 intermediate to the activation dtype (identity for fp32).
+template <typename T>
+__device__ __forceinline__ float to_act(float x);
+template <>
+__device__ __forceinline__ float to_act<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_act<__nv_bfloat16>(float x) { return bf16_round(x); }
+
+template <typename T>
+__device__ __forceinline__ void store_act(T* p, float x);
+template <>
+__device__ __forceinline__ void store_act<float>(float* p, float x) { *p = x; }
+template <>
+__device__ __forceinline__ void store_act<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+
+struct QuantArgs {
+  const void* x[2];      // K and V inputs, [B][H][L][D]
+  long xs_b, xs_h, xs_l;  // element strides
+  void* q[2];             // ring payload, [B][H][C][D] (int8 or uint8)
+  long qs_b, qs_h, qs_c;
+  void* scale[2];         // [B][H][C]: fp32 (i8 mode) or activation dtype (u8 mode)
+  void* zp[2];            // [B][H][C] activation dtype (u8 mode only)
+  long ss_b, ss_h, ss_c;
+  int B, H, L;
+  int region_base, region_off, region_len;
+};
+
+template <typename Tin, int MODE>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) kv_quant_append_kernel(const QuantArgs a) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = static_cast<long>(blockIdx.x) * kWarpsPerBlock + warp;
+  const long rows = static_cast<long>(a.B) * a.H * a.L;
+  const int which = blockIdx.y;  // 0 = K, 1 = V
+  if (row < rows) {
+    const int l = static_cast<int>(row % a.L);
+    const int h = static_cast<int>((row / a.L) % a.H);
+    const int b = static_cast<int>(row / (static_cast<long>(a.L) * a.H));
+    const Tin* src = static_cast<const Tin*>(a.x[which]) + b * a.xs_b + h * a.xs_h + l * a.xs_l + lane * 8;
+    float v[8];
+    load8(src, v);
+    const long slot = a.region_base + (static_cast<long>(a.region_off) + l) % a.region_len;
+    uint8_t* dst = static_cast<uint8_t*>(a.q[which]) + b * a.qs_b + h * a.qs_h + slot * a.qs_c + lane * 8;
+    const long sidx = b * a.ss_b + h * a.ss_h + slot * a.ss_c;
+    uint32_t packed[2] = {0u, 0u};
+    if (MODE == kQuantI8Sym) {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      amax = warp_max(amax);
+      const float scale = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int qi = 0;
+        if (amax > 0.f) {
+          float r = rintf(__fdiv_rn(v[i], scale));
+          r = fminf(fmaxf(r, -127.f), 127.f);
+          qi = static_cast<int>(r);
+        }
+        packed[i >> 2] |= (static_cast<uint32_t>(qi) & 0xFFu) << (8 * (i & 3));
+      }
+      if (lane == 0) static_cast<float*>(a.scale[which])[sidx] = scale;
+    } else {
+      // Reference scheme, each op rounded to the activation dtype:
+      //   range = clamp(max - min, min=1e-5); scale = range / 255;
+      //   zp = -min / scale; q = clamp(round(x / scale + zp), 0, 255)
+      float mn = v[0], mx = v[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) {
+        mn = fminf(mn, v[i]);
+        mx = fmaxf(mx, v[i]);
+      }
+      mn = warp_min(mn);
+      mx = warp_max(mx);
+      float range = to_act<Tin>(mx - mn);
+      const float kMinRange = to_act<Tin>(1e-5f);
+      if (range < 1e-5f) range = kMinRange;
+      const float scale = to_act<Tin>(__fdiv_rn(range, 255.0f));
+      const float zp = to_act<Tin>(__fdiv_rn(-mn, scale));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float t1 = to_act<Tin>(__fdiv_rn(v[i], scale));
+        const float t2 = to_act<Tin>(__fadd_rn(t1, zp));
+        float r = rintf(t2);
+        r = fminf(fmaxf(r, 0.f), 255.f);
+        packed[i >> 2] |= (static_cast<uint32_t>(r) & 0xFFu) << (8 * (i & 3));
+      }
+      if (lane == 0) {
+        store_act<Tin>(static_cast<Tin*>(a.scale[which]) + sidx, scale);
+        store_act<Tin>(static_cast<Tin*>(a.zp[which]) + sidx, zp);
+      }
+    }
+    *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace
+
+int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) {
+  if (d.D != kD) return set_error(RFX_E_INVAL, "kv_quant_append: head_dim must be 256");
+  if (d.B <= 0 || d.H <= 0 || d.L < 0) return set_error(RFX_E_INVAL, "kv_quant_append: bad B/H/L");
+  if (d.L == 0) return RFX_OK;
+  if (d.region_len <= 0 || d.region_base < 0 || d.region_off < 0 || d.L > d.region_len)
+    return set_error(RFX_E_INVAL, "kv_quant_append: bad ring region");
+  if (static_cast<long>(d.region_base) + d.region_len > d.capacity)
+    return set_error(RFX_E_INVAL, "kv_quant_append: ring region exceeds capacity");
+  if (d.mode != kQuantI8Sym && d.mode != kQuantU8Ref) return set_error(RFX_E_INVAL, "kv_quant_append: bad mode");
+  if (d.in_dtype != kDtypeBF16 && d.in_dtype != kDtypeF32)
+    return set_error(RFX_E_INVAL, "kv_quant_append: input dtype must be bf16 or f32");
+  for (int w = 0; w < 2; ++w) {
+    if (!d.x[w] || !d.q[w] || !d.scale[w] || (d.mode == kQuantU8Ref && !d.zp[w]))
+      return set_error(RFX_E_INVAL, "kv_quant_append: null pointer");
+    if ((reinterpret_cast<uintptr_t>(d.x[w]) & 15u) || (reinterpret_cast<uintptr_t>(d.q[w]) & 7u))
+      return set_error(RFX_E_INVAL, "kv_quant_append: misaligned input/ring pointer");
+  }
+  const int esz = d.in_dtype == kDtypeBF16 ? 2 : 4;
+  if (((d.xs_b | d.xs_h | d.xs_l) * esz) % 16 || (d.qs_b | d.qs_h | d.qs_c) % 8)
+    return set_error(RFX_E_INVAL, "kv_quant_append: strides must keep 16-byte rows");
+
+  QuantArgs a{};
+  for (int w = 0; w < 2; ++w) {
+    a.x[w] = d.x[w];
+    a.q[w] = d.q[w];
+    a.scale[w] = d.scale[w];
+    a.zp[w] = d.zp[w];
+  }
+  a.xs_b = d.xs_b; a.xs_h = d.xs_h; a.xs_l = d.xs_l;
+  a.qs_b = d.qs_b; a.qs_h = d.qs_h; a.qs_c = d.qs_c;
+  a.ss_b = d.ss_b; a.ss_h = d.ss_h; a.ss_c = d.ss_c;
+  a.B = d.B; a.H = d.H; a.L = d.L;
+  a.region_base = d.region_base; a.region_off = d.region_off; a.region_len = d.region_len;
+
+  const long rows = static_cast<long>(d.B) * d.H * d.L;
+  dim3 grid(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock), 2);
+  dim3 block(kWarpsPerBlock * 32);
+  void (*kern)(QuantArgs) = nullptr;
+  if (d.in_dtype == kDtypeBF16)
+    kern = d.mode == kQuantI8Sym ? kv_quant_append_kernel<__nv_bfloat16, kQuantI8Sym>
+                                 : kv_quant_append_kernel<__nv_bfloat16, kQuantU8Ref>;
+  else
+    kern = d.mode == kQuantI8Sym ? kv_quant_append_kernel<float, kQuantI8Sym> : kv_quant_append_kernel<float, kQuantU8Ref>;
+  return launch_kernel(reinterpret_cast<const void*>(kern), grid, block, 0, stream, pdl, 1, a);
+}
+
+}  // namespace rfx

@@ -1,0 +1,234 @@
+"""Kernel-level parity of the CUDA path (through the C ABI) against the oracle.
+
+Bit-exact for the KV quantizers; the bf16 GEMMs and attention against an
+fp32 torch computation on the same bf16 inputs with the tolerance stated in
+each test.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle.attention import partitioned_attention
+from oracle.bf16 import bf16_round
+
+pytestmark = pytest.mark.gpu
+
+# Tolerance of a bf16 kernel output against the fp32 computation of the same
+# bf16 inputs: 1e-2 absolute + 1e-2 relative (one bf16 ulp is 2^-8 relative).
+ATOL, RTOL = 1e-2, 1e-2
+
+
+@pytest.fixture(scope="module")
+def K():
+    from reflex_b200 import kernels
+    return kernels
+
+
+@pytest.fixture(scope="module")
+def L():
+    from reflex_b200 import _lib
+    return _lib
+
+
+def gen(seed):
+    g = torch.Generator().manual_seed(seed)
+    return lambda *shape, std=1.0: torch.randn(*shape, generator=g) * std
+
+
+# ------------------------------------------------------------- quantizers ---
+def _edge_rows(D=256):
+    rows = [np.zeros(D), np.full(D, 3.25), np.linspace(-1e-6, 1e-6, D), -np.abs(np.linspace(0.1, 7, D)),
+            np.linspace(-2.5, 2.5, D), np.r_[np.full(D - 1, 0.5), 127.0], np.r_[np.full(D - 1, -1.0), 1e4]]
+    return np.stack(rows).astype(np.float32)
+
+
+@pytest.mark.parametrize("mode", ["i8", "u8"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_kv_quant_bit_exact(K, L, mode, dtype):
+    B, H, Lnew, D, cap = 2, 1, 77, 256, 160
+    r = gen(1)
+    k = r(B, H, Lnew, D) * 3
+    v = r(B, H, Lnew, D)
+    k[0, 0, :7] = torch.from_numpy(_edge_rows())
+    k = k.to(dtype).cuda()
+    v = v.to(dtype).cuda()
+    qm = L.RFX_QUANT_I8_SYM if mode == "i8" else L.RFX_QUANT_U8_REF
+    ring = K.KVRing.allocate(B, H, cap, D, qm, scale_dtype=dtype)
+    # window region [32, 160) with an append that wraps around its end
+    base, off, rlen = 32, 100, 128
+    K.kv_quant_append(k, v, ring, base, off, rlen)
+    torch.cuda.synchronize()
+    slots = base + (off + np.arange(Lnew)) % rlen
+    for src, q, s, z in ((k, ring.k_q, ring.k_scale, ring.k_zp), (v, ring.v_q, ring.v_scale, ring.v_zp)):
+        x = src.float().cpu().numpy()
+        if mode == "i8":
+            eq, es = oq.quant_i8_sym(x)
+        else:
+            eq, es, ez = oq.quant_u8_ref(x, act_bf16=dtype == torch.bfloat16)
+            np.testing.assert_array_equal(z.float().cpu().numpy()[:, :, slots], ez[..., 0])
+        np.testing.assert_array_equal(q.cpu().numpy()[:, :, slots], eq)
+        np.testing.assert_array_equal(s.float().cpu().numpy()[:, :, slots], es[..., 0])
+
+
+# ------------------------------------------------------------------ linear ---
+def _mm(x, w):
+    return x.float() @ w.float().t()
+
+
+@pytest.mark.parametrize("T,n_tile,splits", [(50, 0, 0), (1, 64, 1), (50, 64, 2), (50, 64, 8), (50, 64, 16),
+                                             (100, 128, 4), (200, 256, 2), (400, 0, 0)])
+def test_linear_store(K, T, n_tile, splits):
+    r = gen(2)
+    O, Kd = 512, 1024
+    x = r(T, Kd).bfloat16().cuda()
+    w = r(O, Kd, std=0.03).bfloat16().cuda()
+    bias = r(O, std=0.1).cuda()
+    y = torch.empty(T, O, dtype=torch.bfloat16, device="cuda")
+    K.linear(w=w, x=x, T=T, S=T, y=y, bias=bias, n_tile=n_tile, splits=splits)
+    ref = _mm(x, w).cpu() + bias.cpu()
+    torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+
+
+def _norm_ref(x, a1, a2, b2, S, eps=1e-6):
+    xf = x.float().cpu()
+    rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    b = torch.arange(x.shape[0]) // S
+    y = (xf * rstd) * a1.cpu()
+    if a2 is not None:
+        y = y * a2.cpu()[b]
+    if b2 is not None:
+        y = y + b2.cpu()[b]
+    return y.bfloat16()
+
+
+@pytest.mark.parametrize("epi", ["residual", "geglu", "silu"])
+def test_linear_norm_prologue_epilogues(K, L, epi):
+    r = gen(3)
+    B, S, Kd = 2, 50, 1024
+    T = B * S
+    x = r(T, Kd).bfloat16().cuda()
+    a1 = (1 + r(Kd, std=0.1)).cuda()
+    a2 = (1 + r(B, Kd, std=0.2)).cuda()
+    b2 = r(B, Kd, std=0.1).cuda()
+    xn = _norm_ref(x, a1, a2, b2, S)
+    if epi == "residual":
+        O = 1024
+        w = r(O, Kd, std=0.03).bfloat16().cuda()
+        gate = bf16_round(r(B, O).numpy())
+        gate = torch.from_numpy(gate).cuda()
+        y = r(T, O).bfloat16().cuda()
+        y0 = y.clone().cpu().float()
+        K.linear(w=w, x=x, T=T, S=S, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_RESIDUAL, y=y, norm_a1=a1,
+                 norm_a2=a2, norm_b2=b2, norm_ab_stride=Kd, gate=gate, gate_stride=O)
+        acc = _mm(xn, w.cpu()).bfloat16().float()
+        g = gate.cpu()[torch.arange(T) // S]
+        ref = (y0 + (g * acc).bfloat16().float())
+    elif epi == "geglu":
+        F = 2048
+        wg = r(F, Kd, std=0.03).bfloat16()
+        wu = r(F, Kd, std=0.03).bfloat16()
+        w = K.pack_weight(L.RFX_PACK_GATE_UP, torch.cat([wg, wu]).cuda())
+        y = torch.empty(T, F, dtype=torch.bfloat16, device="cuda")
+        K.linear(w=w, x=x, T=T, S=S, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_GEGLU, y=y, norm_a1=a1,
+                 norm_a2=a2, norm_b2=b2, norm_ab_stride=Kd)
+        gg = _mm(xn, wg).bfloat16().float()
+        uu = _mm(xn, wu).bfloat16().float()
+        ref = torch.nn.functional.gelu(gg, approximate="tanh").bfloat16().float() * uu
+    else:
+        O = 1024
+        w = r(O, Kd, std=0.03).bfloat16().cuda()
+        bias = r(O, std=0.1).cuda()
+        y = torch.empty(T, O, dtype=torch.bfloat16, device="cuda")
+        K.linear(w=w, x=x, T=T, S=S, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_SILU, y=y, norm_a1=a1,
+                 norm_a2=a2, norm_b2=b2, norm_ab_stride=Kd, bias=bias)
+        ref = torch.nn.functional.silu((_mm(xn, w.cpu()) + bias.cpu()).bfloat16().float())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+
+
+def rope_table(max_pos=8192, D=256, base=10000.0):
+    inv = 1.0 / (base ** (torch.arange(0, D, 2, dtype=torch.float) / D))
+    t = torch.arange(max_pos, dtype=torch.float)
+    f = torch.einsum("i,j->ij", t, inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1)
+
+
+def test_linear_qkv_rope(K, L):
+    r = gen(4)
+    B, S, Kd, Hq, D = 2, 50, 1024, 8, 256
+    T = B * S
+    x = r(T, Kd).bfloat16().cuda()
+    a1 = (1 + r(Kd, std=0.1)).cuda()
+    wqkv = r((Hq + 2) * D, Kd, std=0.03).bfloat16()
+    w = K.pack_weight(L.RFX_PACK_QKV_ROPE, wqkv.cuda())
+    tab = rope_table().cuda()
+    pos = (818 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
+    q = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device="cuda")
+    k = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+    v = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+    K.linear(w=w, x=x, T=T, S=S, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_QKV_ROPE, norm_a1=a1,
+             rope_table=tab, positions=pos, q_out=q, k_out=k, v_out=v, num_q_heads=Hq)
+    torch.cuda.synchronize()
+    xn = _norm_ref(x, a1, None, None, S)
+    out = _mm(xn, wqkv).bfloat16().view(T, Hq + 2, D)
+    cs = tab.cpu()[pos.cpu().long()]
+    cos, sin = cs[:, None, :128], cs[:, None, 128:]
+
+    def rope(t):
+        t1, t2 = t.float().chunk(2, -1)
+        return torch.cat([t1 * cos - t2 * sin, t2 * cos + t1 * sin], -1)
+
+    qr = rope(out[:, :Hq]).view(B, S, Hq, D).permute(0, 2, 1, 3)
+    kr = rope(out[:, Hq:Hq + 1])[:, 0]
+    torch.testing.assert_close(q.float().cpu(), qr, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(k.float().cpu(), kr, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(v.float().cpu(), out[:, Hq + 1].float(), atol=ATOL, rtol=RTOL)
+
+
+# --------------------------------------------------------------- attention ---
+@pytest.mark.parametrize("mode", ["i8", "u8"])
+@pytest.mark.parametrize("n_ctx,S,splits", [(576, 50, 0), (818, 50, 1), (818, 50, 3), (100, 50, 0), (0, 50, 0),
+                                            (1584, 51, 0)])
+def test_attention_partitioned(K, L, mode, n_ctx, S, splits):
+    r = gen(5)
+    B, Hq, D, cap = 2, 8, 256, max(64, n_ctx + 64)
+    qm = L.RFX_QUANT_I8_SYM if mode == "i8" else L.RFX_QUANT_U8_REF
+    ring = K.KVRing.allocate(B, 1, cap, D, qm, scale_dtype=torch.bfloat16)
+    kc = r(B, 1, n_ctx, D).bfloat16()
+    vc = r(B, 1, n_ctx, D).bfloat16()
+    if n_ctx:
+        K.kv_quant_append(kc.cuda(), vc.cuda(), ring, 0, 0, cap)
+    q = r(B, Hq, S, D).bfloat16()
+    ks = r(B, S, D).bfloat16()
+    vs = r(B, S, D).bfloat16()
+    # PI0-style suffix block ids: first token its own block when S == 51
+    blk = torch.zeros(S, dtype=torch.int32)
+    blk[1:] = 1 if S == 51 else 0
+    out = torch.empty(B * S, Hq * D, dtype=torch.bfloat16, device="cuda")
+    K.attention(q=q.cuda(), k_new=ks.cuda(), v_new=vs.cuda(), ring=ring, n_ctx=n_ctx, out=out,
+                softmax_scale=1 / 16, new_block=blk.cuda(), kv_splits=splits)
+    torch.cuda.synchronize()
+    # oracle: dequantize what the GPU stored, then fp32 attention
+    if mode == "i8":
+        kd = oq.dequant_i8_sym(ring.k_q.cpu().numpy(), ring.k_scale.cpu().numpy()[..., None])
+        vd = oq.dequant_i8_sym(ring.v_q.cpu().numpy(), ring.v_scale.cpu().numpy()[..., None])
+    else:
+        kd = oq.dequant_u8_ref(ring.k_q.cpu().numpy(), ring.k_scale.float().cpu().numpy()[..., None],
+                               ring.k_zp.float().cpu().numpy()[..., None], True)
+        vd = oq.dequant_u8_ref(ring.v_q.cpu().numpy(), ring.v_scale.float().cpu().numpy()[..., None],
+                               ring.v_zp.float().cpu().numpy()[..., None], True)
+    kd = torch.from_numpy(kd)[:, :, :n_ctx]
+    vd = torch.from_numpy(vd)[:, :, :n_ctx]
+    att = torch.zeros(S, dtype=torch.int64)
+    att[0] = 1
+    if S == 51:
+        att[1] = 1
+    ref = partitioned_attention(q, kd, vd, ks[:, None], vs[:, None], torch.ones(B, n_ctx, dtype=torch.bool), att,
+                                1 / 16)
+    ref = ref.permute(0, 2, 1, 3).reshape(B * S, Hq * D)
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 2e-2, f"max abs err {err}"
+    assert K.device_status() == 0
