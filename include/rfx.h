@@ -148,7 +148,11 @@ typedef struct rfx_linear_desc {
   void* v_out;          /* bf16 [T][256] */
   int num_q_heads;
   int n_tile; /* tokens per MMA tile: 0 (auto), 64, 128 or 256 */
-  int splits; /* CTAs per cluster along K: 0 (auto) or 1..8 */
+  int splits; /* CTAs per cluster along K: 0 (auto), 1, 2, 4, 8 or 16 */
+  /* Output row of token t for STORE/SILU/RESIDUAL/GEGLU:
+   * (t / S) * y_rows_per_batch + y_row_offset + t % S; 0/0 means row t. */
+  int y_rows_per_batch;
+  int y_row_offset;
 } rfx_linear_desc;
 int rfx_linear(const rfx_linear_desc* desc, void* stream);
 
@@ -196,6 +200,7 @@ int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes);
 
 /* ----------------------------------------- timestep conditioning + heads ---- */
 /* cond[i] = silu(W_out · silu(W_in · bf16(sinusoid(t[i])) + b_in) + b_out), bf16.
+ * With w_in == NULL only the embedding is computed: cond[i] = bf16(sinusoid(t[i])).
  * Replaces PI05SuffixEmbedder's time path (modeling_pi05.py:322-339) with
  * create_sinusoidal_pos_embedding (reflex/policies/pi05/utils.py:72-121, fp64). */
 typedef struct rfx_time_cond_desc {
@@ -264,6 +269,19 @@ typedef struct rfx_action_io_desc {
 int rfx_action_in(const rfx_action_io_desc* desc, void* stream);
 int rfx_euler_tail(const rfx_action_io_desc* desc, void* stream);
 
+/* Row copy / broadcast of bf16 rows (suffix assembly, modeling_pi0.py:163-200):
+ * for r in [0, rows): dst[(r / group) * dst_rows_per_group + dst_row_offset + r % group][0..width)
+ *                     = src[r * src_ld + 0..width)   (src_ld = 0 broadcasts one row). */
+typedef struct rfx_copy_rows_desc {
+  void* dst;
+  long dst_ld;
+  int dst_rows_per_group, dst_row_offset, group;
+  const void* src;
+  long src_ld;
+  int rows, width;
+} rfx_copy_rows_desc;
+int rfx_copy_rows(const rfx_copy_rows_desc* desc, void* stream);
+
 /* ---------------------------------------------------- execution plans ---- */
 /* A plan is an ordered list of the launches above, validated and with their
  * TMA descriptors encoded once. rfx_plan_run launches them in order;
@@ -281,6 +299,7 @@ int rfx_plan_add_time_cond(rfx_plan* plan, const rfx_time_cond_desc* desc);
 int rfx_plan_add_modulation(rfx_plan* plan, const rfx_modulation_desc* desc);
 int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc);
+int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc);
 /* Number of kernel launches one run of the plan performs. */
 int rfx_plan_num_launches(const rfx_plan* plan, int* out);
 int rfx_plan_run(rfx_plan* plan, void* stream);

@@ -76,6 +76,7 @@ class LinearDesc(Structure):
         ("rope_table", c_void_p), ("rope_max_pos", c_int), ("positions", c_void_p),
         ("q_out", c_void_p), ("k_out", c_void_p), ("v_out", c_void_p), ("num_q_heads", c_int),
         ("n_tile", c_int), ("splits", c_int),
+        ("y_rows_per_batch", c_int), ("y_row_offset", c_int),
     ]
 
 
@@ -122,6 +123,14 @@ class ActionIoDesc(Structure):
     ]
 
 
+class CopyRowsDesc(Structure):
+    _fields_ = [
+        ("dst", c_void_p), ("dst_ld", c_long),
+        ("dst_rows_per_group", c_int), ("dst_row_offset", c_int), ("group", c_int),
+        ("src", c_void_p), ("src_ld", c_long), ("rows", c_int), ("width", c_int),
+    ]
+
+
 # Every entry point declared in include/rfx.h: name -> (argtypes, restype).
 SIGNATURES = {
     "rfx_version": ([], c_int),
@@ -138,6 +147,7 @@ SIGNATURES = {
     "rfx_modulation": ([POINTER(ModulationDesc), c_void_p], c_int),
     "rfx_action_in": ([POINTER(ActionIoDesc), c_void_p], c_int),
     "rfx_euler_tail": ([POINTER(ActionIoDesc), c_void_p], c_int),
+    "rfx_copy_rows": ([POINTER(CopyRowsDesc), c_void_p], c_int),
     "rfx_plan_create": ([POINTER(c_void_p)], c_int),
     "rfx_plan_destroy": ([c_void_p], c_int),
     "rfx_plan_add_linear": ([c_void_p, POINTER(LinearDesc)], c_int),
@@ -147,6 +157,7 @@ SIGNATURES = {
     "rfx_plan_add_modulation": ([c_void_p, POINTER(ModulationDesc)], c_int),
     "rfx_plan_add_action_in": ([c_void_p, POINTER(ActionIoDesc)], c_int),
     "rfx_plan_add_euler_tail": ([c_void_p, POINTER(ActionIoDesc)], c_int),
+    "rfx_plan_add_copy_rows": ([c_void_p, POINTER(CopyRowsDesc)], c_int),
     "rfx_plan_num_launches": ([c_void_p, POINTER(c_int)], c_int),
     "rfx_plan_run": ([c_void_p, c_void_p], c_int),
     "rfx_plan_capture": ([c_void_p, c_void_p], c_int),
@@ -190,6 +201,6 @@ def ptr(t) -> int | None:
 
 
 __all__ = [n for n in dir() if n.startswith(("RFX_", "Rfx"))] + [
-    "KvQuantDesc", "LinearDesc", "AttnDesc", "TimeCondDesc", "ModulationDesc", "ActionIoDesc",
+    "KvQuantDesc", "LinearDesc", "AttnDesc", "TimeCondDesc", "ModulationDesc", "ActionIoDesc", "CopyRowsDesc",
     "SIGNATURES", "load", "check", "call", "ptr", "LIB_PATH", "c_ubyte",
 ]

@@ -4,6 +4,8 @@
 // warp per output row, and reduced with warp shuffles.
 #include "rfx_internal.h"
 
+#include <algorithm>
+
 namespace rfx {
 namespace {
 
@@ -256,6 +258,29 @@ __global__ void __launch_bounds__(256) euler_tail_kernel(const IoParams p) {
   pdl_launch_dependents();
 }
 
+struct CopyRowsParams {
+  __nv_bfloat16* dst;
+  long dst_ld;
+  int rpg, off, group;
+  const __nv_bfloat16* src;
+  long src_ld;
+  int rows, width;
+};
+
+__global__ void __launch_bounds__(256) copy_rows_kernel(const CopyRowsParams p) {
+  pdl_wait();
+  const int chunks = p.width / 8;
+  const long total = static_cast<long>(p.rows) * chunks;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / chunks), c = static_cast<int>(i % chunks);
+    const long drow = static_cast<long>(r / p.group) * p.rpg + p.off + r % p.group;
+    *reinterpret_cast<uint4*>(p.dst + drow * p.dst_ld + c * 8) =
+        *reinterpret_cast<const uint4*>(p.src + r * p.src_ld + c * 8);
+  }
+  pdl_launch_dependents();
+}
+
 IoParams io_params(const rfx_action_io_desc& d) {
   IoParams p{};
   p.B = d.B;
@@ -305,8 +330,9 @@ int validate_io(const rfx_action_io_desc& d, bool tail) {
 }  // namespace
 
 int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl) {
-  if (d.n_t < 1 || d.n_t > kMaxRows || d.width < 256 || d.width % 256 || !d.t || !d.w_in || !d.w_out || !d.hidden ||
-      !d.cond || !a16(d.w_in) || !a16(d.w_out))
+  const bool embed_only = d.w_in == nullptr;
+  if (d.n_t < 1 || d.n_t > kMaxRows || d.width < 256 || d.width % 256 || !d.t || !d.cond ||
+      (!embed_only && (!d.w_out || !d.hidden || !a16(d.w_in) || !a16(d.w_out))))
     return set_error(RFX_E_INVAL, "rfx_time_cond: need 1<=n_t<=16, width%%256==0, aligned weights");
   if (!(d.min_period > 0.f) || !(d.max_period > 0.f)) return set_error(RFX_E_INVAL, "rfx_time_cond: periods");
   __nv_bfloat16* emb = static_cast<__nv_bfloat16*>(d.cond);  // the embedding is staged in `cond`
@@ -316,7 +342,7 @@ int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl)
   double minp = d.min_period, maxp = d.max_period;
   int rc = launch_kernel(reinterpret_cast<const void*>(sinusoid_kernel), dim3((n_t * half + 255) / 256), dim3(256), 0,
                          stream, pdl, 1, t, n_t, width, minp, maxp, emb);
-  if (rc) return rc;
+  if (rc || embed_only) return rc;
   const size_t smem = static_cast<size_t>(n_t) * width * sizeof(float);
   const void* gemv = reinterpret_cast<const void*>(gemv_bf16_silu_kernel);
   rc = ensure_smem_attr(gemv, 200 * 1024);
@@ -380,7 +406,27 @@ int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl
   return launch_kernel(fn, dim3(d.B * d.S), dim3(256), smem, stream, pdl, 1, p);
 }
 
+int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl) {
+  if (!d.dst || !d.src || d.rows < 0 || d.width < 8 || d.width % 8 || d.group < 1 || d.dst_rows_per_group < 1 ||
+      d.dst_row_offset < 0 || d.dst_row_offset + d.group > d.dst_rows_per_group || d.dst_ld < d.width ||
+      d.dst_ld % 8 || d.src_ld < 0 || d.src_ld % 8 || (d.src_ld > 0 && d.src_ld < d.width) || !a16(d.dst) ||
+      !a16(d.src))
+    return set_error(RFX_E_INVAL, "rfx_copy_rows: bad layout (16-byte aligned rows of width%%8==0 required)");
+  if (d.rows == 0) return RFX_OK;
+  CopyRowsParams p{static_cast<__nv_bfloat16*>(d.dst), d.dst_ld, d.dst_rows_per_group, d.dst_row_offset, d.group,
+                   static_cast<const __nv_bfloat16*>(d.src), d.src_ld, d.rows, d.width};
+  const long total = static_cast<long>(d.rows) * (d.width / 8);
+  const unsigned blocks = static_cast<unsigned>(std::min<long>((total + 255) / 256, 1184));
+  return launch_kernel(reinterpret_cast<const void*>(copy_rows_kernel), dim3(blocks), dim3(256), 0, stream, pdl, 1,
+                       p);
+}
+
 }  // namespace rfx
+
+extern "C" int rfx_copy_rows(const rfx_copy_rows_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_copy_rows: null descriptor");
+  return rfx::launch_copy_rows(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}
 
 extern "C" int rfx_time_cond(const rfx_time_cond_desc* d, void* stream) {
   if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_time_cond: null descriptor");

@@ -74,6 +74,7 @@ struct LinParams {
   __nv_bfloat16* k_out;
   __nv_bfloat16* v_out;
   int hq;
+  int y_rps, y_off;
   int* status;
 };
 
@@ -95,6 +96,7 @@ template <int EPI>
 __device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int t, const float (&v0)[4],
                                           const float (&v1)[4]) {
   const int b = t / p.S;
+  const long yrow = static_cast<long>(b) * p.y_rps + p.y_off + (t - b * p.S);
   if (EPI == kEpiStore || EPI == kEpiSilu || EPI == kEpiResidual) {
     const int o0 = m * kBM + i, o1 = o0 + 64;
     float r0[4], r1[4];
@@ -112,8 +114,8 @@ __device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int 
       r0[j] = a;
       r1[j] = c;
     }
-    __nv_bfloat16* y0 = p.y + static_cast<long>(t) * p.ldy + o0;
-    __nv_bfloat16* y1 = p.y + static_cast<long>(t) * p.ldy + o1;
+    __nv_bfloat16* y0 = p.y + yrow * p.ldy + o0;
+    __nv_bfloat16* y1 = p.y + yrow * p.ldy + o1;
     if (EPI == kEpiResidual) {
       const float* g = p.gate ? p.gate + static_cast<long>(b) * p.gate_stride : nullptr;
       uint2 old0 = *reinterpret_cast<const uint2*>(y0);
@@ -141,7 +143,7 @@ __device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int 
       const float a = bf16_round(gelu_tanh(g));
       r[j] = __fmul_rn(a, u);
     }
-    store_bf16x4(p.y + static_cast<long>(t) * p.ldy + f, r);
+    store_bf16x4(p.y + yrow * p.ldy + f, r);
   } else {  // kEpiQkvRope
     const int head = m >> 1;
     const int d0 = (m & 1) * 64 + i;
@@ -494,6 +496,8 @@ int validate(const rfx_linear_desc& d) {
   } else {
     if (!d.y || d.ldy < d.O || d.ldy % 4) return set_error(RFX_E_INVAL, "rfx_linear: output y/ldy");
   }
+  if (d.y_rows_per_batch > 0 && (d.y_row_offset < 0 || d.y_row_offset + d.tokens_per_batch > d.y_rows_per_batch))
+    return set_error(RFX_E_INVAL, "rfx_linear: y_row_offset + tokens_per_batch must fit y_rows_per_batch");
   return RFX_OK;
 }
 
@@ -571,6 +575,8 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   p.k_out = static_cast<__nv_bfloat16*>(d.k_out);
   p.v_out = static_cast<__nv_bfloat16*>(d.v_out);
   p.hq = d.num_q_heads;
+  p.y_rps = d.y_rows_per_batch > 0 ? d.y_rows_per_batch : d.tokens_per_batch;
+  p.y_off = d.y_rows_per_batch > 0 ? d.y_row_offset : 0;
   p.status = device_status_ptr();
 
   dim3 grid(m_tiles * cfg.splits, n_tiles, 1);

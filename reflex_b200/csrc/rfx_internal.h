@@ -84,5 +84,6 @@ int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl)
 int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pdl);
 int launch_action_in(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
 int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
+int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl);
 
 }  // namespace rfx

@@ -283,7 +283,10 @@ struct InOp {
 struct TailOp {
   rfx_action_io_desc d;
 };
-using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp>;
+struct CopyOp {
+  rfx_copy_rows_desc d;
+};
+using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp>;
 }  // namespace
 
 struct rfx_plan {
@@ -303,6 +306,7 @@ int run_op(const Op& op, cudaStream_t s, bool pdl) {
   if (auto* o = std::get_if<ModOp>(&op)) return launch_modulation(o->d, s, pdl);
   if (auto* o = std::get_if<InOp>(&op)) return launch_action_in(o->d, s, pdl);
   if (auto* o = std::get_if<TailOp>(&op)) return launch_euler_tail(o->d, s, pdl);
+  if (auto* o = std::get_if<CopyOp>(&op)) return launch_copy_rows(o->d, s, pdl);
   return set_error(RFX_E_STATE, "plan: unknown op");
 }
 void release_graph(rfx_plan* p) {
@@ -364,7 +368,7 @@ extern "C" int rfx_plan_add_kv_quant(rfx_plan* plan, const rfx_kv_quant_desc* de
 extern "C" int rfx_plan_add_time_cond(rfx_plan* plan, const rfx_time_cond_desc* desc) {
   PLAN_GUARD(plan);
   plan->ops.emplace_back(TimeOp{*desc});
-  plan->launches += 3;
+  plan->launches += desc->w_in ? 3 : 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_modulation(rfx_plan* plan, const rfx_modulation_desc* desc) {
@@ -382,6 +386,13 @@ extern "C" int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* 
 extern "C" int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc) {
   PLAN_GUARD(plan);
   plan->ops.emplace_back(TailOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+
+extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc) {
+  PLAN_GUARD(plan);
+  plan->ops.emplace_back(CopyOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }

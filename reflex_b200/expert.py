@@ -1,0 +1,285 @@
+"""Device-resident action expert: weights, per-layer KV rings, activation
+buffers and the launch plan of one action chunk.
+
+One chunk = the per-chunk conditioning (timestep MLP for all Euler steps at
+once, AdaRMS modulation of every norm for every step in one batched GEMV) and
+then, per Euler step, 18 x [QKV+RoPE, partitioned attention, O-proj+residual,
+gate/up+GeGLU, down+residual] and a fused final-norm / out-proj / Euler /
+in-proj tail.  The dataflow follows reflex/policies/pi05/modeling_pi05.py:
+1181-1241 (denoise_step), 1403-1419 (Euler loop), 563-620 (layer) and the PI0
+equivalents in reflex/policies/pi0/modeling_pi0.py:144-206, 740-782, 827-845.
+
+The op list is built once; it runs either eagerly through the direct C entry
+points (``run_eager``, with per-op hooks for parity checks) or through a
+native rfx plan that is captured into a single CUDA graph (``capture`` /
+``run_chunk``).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from . import kernels as K
+from .config import ExpertConfig, timestep_schedule
+from .synthetic import rope_table
+
+_QUANT = {"i8_sym": L.RFX_QUANT_I8_SYM, "u8_ref": L.RFX_QUANT_U8_REF}
+
+
+class ActionExpertEngine:
+    def __init__(self, cfg: ExpertConfig, weights: dict, *, batch: int = 1, capacity: int = 1024, n_ctx: int = 0,
+                 device="cuda", kv_splits: int = 0, scale_dtype=torch.bfloat16):
+        if not torch.cuda.is_available():
+            raise RuntimeError("ActionExpertEngine needs a CUDA device (there is no CPU path)")
+        if cfg.num_kv_heads != 1 or cfg.head_dim != 256:
+            raise ValueError("the kernels serve one 256-wide KV head (MQA)")
+        self.cfg, self.B = cfg, batch
+        self.dev = torch.device(device)
+        self.kv_splits = kv_splits
+        dev = self.dev
+        bf = lambda t: t.to(dev, torch.bfloat16).contiguous()  # noqa: E731
+        f32 = lambda t: t.to(dev, torch.float32).contiguous()  # noqa: E731
+        Lh, W, H, D, F, A = cfg.num_layers, cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim, cfg.action_dim
+        S, St = cfg.chunk_size, cfg.suffix_len
+        self.S, self.St = S, St
+
+        # ---- weights (fused packs, QKV / gate-up rows permuted for the epilogues)
+        self.w_qkv, self.w_o, self.w_gu, self.w_down = [], [], [], []
+        for l in range(Lh):
+            p = f"layers.{l}."
+            qkv = torch.cat([weights[p + "q_proj.weight"], weights[p + "k_proj.weight"], weights[p + "v_proj.weight"]])
+            self.w_qkv.append(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
+            self.w_o.append(bf(weights[p + "o_proj.weight"]))
+            gu = torch.cat([weights[p + "gate_proj.weight"], weights[p + "up_proj.weight"]])
+            self.w_gu.append(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
+            self.w_down.append(bf(weights[p + "down_proj.weight"]))
+        norm_names = [f"layers.{l}.{n}" for l in range(Lh) for n in ("input_layernorm", "post_attention_layernorm")]
+        norm_names.append("norm")
+        self.norm_names = norm_names
+        if cfg.adarms == "ssg":
+            self.norm_a1 = torch.ones(len(norm_names), W, device=dev)
+        else:
+            self.norm_a1 = f32(torch.stack([weights[n + ".weight"] for n in norm_names]))
+        self.mod_w = self.mod_b = None
+        if cfg.adarms != "none":
+            self.mod_w = f32(torch.cat([weights[n + ".dense.weight"] for n in norm_names]))
+            self.mod_b = f32(torch.cat([weights[n + ".dense.bias"] for n in norm_names]))
+        self.ain_w, self.ain_b = bf(weights["action_in_proj.weight"]), bf(weights["action_in_proj.bias"])
+        self.aout_w, self.aout_b = bf(weights["action_out_proj.weight"]), bf(weights["action_out_proj.bias"])
+        if cfg.variant == "pi05":
+            self.tin_w, self.tin_b = bf(weights["time_mlp_in.weight"]), bf(weights["time_mlp_in.bias"])
+            self.tout_w, self.tout_b = bf(weights["time_mlp_out.weight"]), bf(weights["time_mlp_out.bias"])
+        else:
+            self.st_w, self.st_b = bf(weights["state_proj.weight"]), bf(weights["state_proj.bias"])
+            self.atin_w = bf(weights["action_time_mlp_in.weight"])
+            self.atin_b = f32(weights["action_time_mlp_in.bias"])
+            self.atout_w = bf(weights["action_time_mlp_out.weight"])
+            self.atout_b = f32(weights["action_time_mlp_out.bias"])
+
+        # ---- KV rings (one per layer)
+        self.quant_mode = _QUANT[cfg.quant_mode]
+        self.rings = [K.KVRing.allocate(batch, 1, capacity, D, self.quant_mode, scale_dtype=scale_dtype, device=dev)
+                      for _ in range(Lh)]
+        self.capacity = capacity
+
+        # ---- activations
+        T = batch * St
+        self.T = T
+        z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
+        self.h = z(T, W)
+        self.q = z(batch, H, St, D)
+        self.k_new, self.v_new = z(T, D), z(T, D)
+        self.attn_out = z(T, H * D)
+        self.act = z(T, F)
+        self.x = z(batch, S, A, dt=torch.float32)
+        nt = cfg.num_steps
+        self.t = torch.tensor(timestep_schedule(nt), dtype=torch.float32, device=dev)
+        self.dt = float(np.float32(-1.0 / nt))
+        self.cond = z(nt, W)
+        self.tc_hidden = z(nt, W)
+        nn_ = len(norm_names)
+        self.a2 = z(nt, nn_, W, dt=torch.float32) if cfg.adarms != "none" else None
+        self.b2 = z(nt, nn_, W, dt=torch.float32) if cfg.adarms == "ssg" else None
+        self.gate = z(nt, nn_, W, dt=torch.float32) if cfg.adarms != "none" else None
+        self.positions = torch.zeros(T, dtype=torch.int32, device=dev)
+        blk = torch.zeros(St, dtype=torch.int32)
+        if cfg.variant == "pi0":
+            blk[1:] = 1  # the state token does not see the action tokens (att row [1, 1, 0, ...])
+        self.new_block = blk.to(dev)
+        self.rope = rope_table(cfg.max_position_embeddings, D, cfg.rope_theta).to(dev)
+        if cfg.variant == "pi0":
+            self.state = z(batch, cfg.state_dim, dt=torch.float32)
+            self.state_emb = z(batch, W)
+            self.temb = z(nt, W)
+            self.at_x = z(batch * S, 2 * W)
+            self.at_hid = z(batch * S, W)
+        self.workspace = None
+        self.plan = None
+        self.set_context_length(n_ctx)
+
+    # ------------------------------------------------------------ context ---
+    def set_context_length(self, n_ctx: int) -> None:
+        """Number of valid ring slots (the same for every stream); suffix positions
+        follow (number of valid prefix tokens) + s as build_attention_mask_and_position_ids
+        gives them (reflex/policies/pi05/utils.py:234)."""
+        if not 0 <= n_ctx <= self.capacity:
+            raise ValueError(f"n_ctx {n_ctx} outside [0, {self.capacity}]")
+        self.n_ctx = n_ctx
+        pos = n_ctx + torch.arange(self.St, dtype=torch.int32)
+        self.positions.copy_(pos.repeat(self.B))
+        self._build_ops()
+
+    def load_context(self, layer: int, k: torch.Tensor, v: torch.Tensor, region_base: int = 0,
+                     region_off: int = 0, region_len: int | None = None) -> None:
+        """Quantize-appends context K/V [B, 1, L, D] (bf16) into one layer's ring."""
+        K.kv_quant_append(k.to(self.dev, torch.bfloat16).contiguous(), v.to(self.dev, torch.bfloat16).contiguous(),
+                          self.rings[layer], region_base, region_off,
+                          region_len if region_len is not None else self.capacity - region_base)
+
+    # ---------------------------------------------------------------- ops ---
+    def _build_ops(self) -> None:
+        cfg, B, S, St, T = self.cfg, self.B, self.S, self.St, self.T
+        W, H, D = cfg.width, cfg.num_heads, cfg.head_dim
+        ops = []
+        if cfg.variant == "pi05":
+            ops.append(("time", K.time_cond_desc(t=self.t, w_in=self.tin_w, b_in=self.tin_b, w_out=self.tout_w,
+                                                 b_out=self.tout_b, hidden=self.tc_hidden, cond=self.cond,
+                                                 min_period=cfg.min_period, max_period=cfg.max_period), None))
+        else:
+            d = L.TimeCondDesc()
+            d.n_t, d.t, d.width = self.t.numel(), self.t.data_ptr(), W
+            d.min_period, d.max_period = cfg.min_period, cfg.max_period
+            d.cond = self.temb.data_ptr()
+            ops.append(("time", d, None))
+        if cfg.adarms != "none":
+            mode = L.RFX_ADARMS_SSG if cfg.adarms == "ssg" else L.RFX_ADARMS_GATE
+            ops.append(("mod", K.modulation_desc(mode=mode, w=self.mod_w, b=self.mod_b, cond=self.cond, a2=self.a2,
+                                                b2=self.b2, gate=self.gate, n_norms=len(self.norm_names)), None))
+        if cfg.variant == "pi05":
+            ops.append(("in", K.action_io_desc(B=B, S=S, S_total=St, x=self.x, w_in=self.ain_w, b_in=self.ain_b,
+                                               h_next=self.h, h_next_rows_per_stream=St,
+                                               h_next_row_offset=St - S), None))
+        else:
+            ops.append(("in", K.action_io_desc(B=B, S=1, S_total=1, x=self.state.view(B, 1, -1), w_in=self.st_w,
+                                               b_in=self.st_b, h_next=self.state_emb, h_next_rows_per_stream=1),
+                        None))
+            ops.append(("in", K.action_io_desc(B=B, S=S, S_total=S, x=self.x, w_in=self.ain_w, b_in=self.ain_b,
+                                               h_next=self.at_x, h_next_rows_per_stream=S), None))
+
+        a2 = lambda tau, n: self.a2[tau, n] if self.a2 is not None else None  # noqa: E731
+        b2 = lambda tau, n: self.b2[tau, n] if self.b2 is not None else None  # noqa: E731
+        gt = lambda tau, n: self.gate[tau, n] if self.gate is not None else None  # noqa: E731
+        nl = cfg.num_layers
+        attn_descs = []
+        for tau in range(cfg.num_steps):
+            if cfg.variant == "pi0":
+                ops.append(("copy", K.copy_rows_desc(dst=self.h, src=self.state_emb, rows=B, width=W,
+                                                     dst_rows_per_group=St, dst_row_offset=0, group=1), None))
+                ops.append(("copy", K.copy_rows_desc(dst=self.at_x[:, W:], src=self.temb[tau:tau + 1], src_ld=0,
+                                                     rows=B * S, width=W, dst_rows_per_group=B * S), None))
+                ops.append(("linear", K.linear_desc(w=self.atin_w, x=self.at_x, T=B * S, S=S,
+                                                    epilogue=L.RFX_EPI_SILU, bias=self.atin_b, y=self.at_hid), None))
+                ops.append(("linear", K.linear_desc(w=self.atout_w, x=self.at_hid, T=B * S, S=S,
+                                                    epilogue=L.RFX_EPI_STORE, bias=self.atout_b, y=self.h,
+                                                    y_rows_per_batch=St, y_row_offset=1), None))
+            for l in range(nl):
+                ni, npo = 2 * l, 2 * l + 1
+                ops.append(("linear", K.linear_desc(
+                    w=self.w_qkv[l], x=self.h, T=T, S=St, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_QKV_ROPE,
+                    norm_a1=self.norm_a1[ni], norm_a2=a2(tau, ni), norm_b2=b2(tau, ni), eps=cfg.eps,
+                    rope_table=self.rope, positions=self.positions, q_out=self.q, k_out=self.k_new,
+                    v_out=self.v_new, num_q_heads=H), ("qkv", tau, l)))
+                ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l],
+                                      n_ctx=self.n_ctx, out=self.attn_out, softmax_scale=D ** -0.5,
+                                      new_block=self.new_block, kv_splits=self.kv_splits)
+                attn_descs.append(ad)
+                ops.append(("attn", ad, ("attn", tau, l)))
+                ops.append(("linear", K.linear_desc(
+                    w=self.w_o[l], x=self.attn_out, T=T, S=St, epilogue=L.RFX_EPI_RESIDUAL, y=self.h,
+                    gate=gt(tau, ni)), ("o", tau, l)))
+                ops.append(("linear", K.linear_desc(
+                    w=self.w_gu[l], x=self.h, T=T, S=St, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_GEGLU,
+                    y=self.act, norm_a1=self.norm_a1[npo], norm_a2=a2(tau, npo), norm_b2=b2(tau, npo),
+                    eps=cfg.eps), ("gu", tau, l)))
+                ops.append(("linear", K.linear_desc(
+                    w=self.w_down[l], x=self.act, T=T, S=St, epilogue=L.RFX_EPI_RESIDUAL, y=self.h,
+                    gate=gt(tau, npo)), ("layer", tau, l)))
+            nf = 2 * nl
+            last = tau == cfg.num_steps - 1
+            if cfg.variant == "pi05":
+                nxt = dict(h_next=None if last else self.h, h_next_rows_per_stream=St, h_next_row_offset=St - S)
+            else:
+                nxt = dict(h_next=None if last else self.at_x, h_next_rows_per_stream=S, h_next_row_offset=0)
+            ops.append(("tail", K.action_io_desc(B=B, S=S, S_total=St, x=self.x, w_in=self.ain_w, b_in=self.ain_b,
+                                                 h=self.h, h_row_offset=St - S, norm_a1=self.norm_a1[nf],
+                                                 norm_a2=a2(tau, nf), norm_b2=b2(tau, nf), eps=cfg.eps,
+                                                 w_out=self.aout_w, b_out=self.aout_b, dt=self.dt, **nxt),
+                        ("step", tau)))
+        # one workspace serves every attention launch (they run in sequence)
+        need = max(K.attention_workspace_bytes(d) for d in attn_descs) if attn_descs else 0
+        if need and (self.workspace is None or self.workspace.numel() < need):
+            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        for d in attn_descs:
+            if need:
+                d.workspace, d.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        self.ops = ops
+        if self.plan is not None:
+            self.plan.close()
+        self.plan = None
+
+    # ---------------------------------------------------------- execution ---
+    def _kind(self, kind):
+        return kind if kind in ("in", "tail") else None
+
+    def run_eager(self, hook=None) -> None:
+        """Runs the chunk op by op through the direct C entry points."""
+        for kind, desc, tag in self.ops:
+            K.Plan.run_direct(desc, self._kind(kind))
+            if hook is not None and tag is not None:
+                hook(tag)
+
+    def build_plan(self) -> K.Plan:
+        plan = K.Plan()
+        for kind, desc, _ in self.ops:
+            plan.add(desc, self._kind(kind))
+        self.plan = plan
+        return plan
+
+    def capture(self) -> None:
+        """Records the chunk into one CUDA graph (run once eagerly first)."""
+        if self.plan is None:
+            self.build_plan()
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.plan.run()
+            self.plan.capture(s)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+
+    @property
+    def num_launches(self) -> int:
+        if self.plan is None:
+            self.build_plan()
+        return self.plan.num_launches
+
+    def set_inputs(self, x0: torch.Tensor, state: torch.Tensor | None = None) -> None:
+        self.x.copy_(x0, non_blocking=True)
+        if self.cfg.variant == "pi0":
+            if state is None:
+                raise ValueError("PI0 needs the robot state")
+            self.state.copy_(state, non_blocking=True)
+
+    def launch_chunk(self) -> None:
+        """Enqueues one chunk on the current stream (graph replay when captured)."""
+        if self.plan is not None and self.plan.captured:
+            self.plan.replay()
+        elif self.plan is not None:
+            self.plan.run()
+        else:
+            self.run_eager()
+
+    def run_chunk(self, x0: torch.Tensor, state: torch.Tensor | None = None) -> torch.Tensor:
+        self.set_inputs(x0, state)
+        self.launch_chunk()
+        return self.x.clone()

@@ -244,6 +244,26 @@ def euler_tail(**kw) -> None:
     L.call("rfx_euler_tail", ctypes.byref(d), _stream())
 
 
+def copy_rows_desc(*, dst, src, rows, width, dst_rows_per_group, dst_row_offset=0, group=None,
+                   src_ld=None) -> L.CopyRowsDesc:
+    _need_cuda(dst, src)
+    if dst.dtype != torch.bfloat16 or src.dtype != torch.bfloat16:
+        raise ValueError("copy_rows moves bf16 rows")
+    d = L.CopyRowsDesc()
+    d.dst, d.dst_ld = dst.data_ptr(), dst.stride(0)
+    d.dst_rows_per_group, d.dst_row_offset = dst_rows_per_group, dst_row_offset
+    d.group = group if group is not None else dst_rows_per_group
+    d.src = src.data_ptr()
+    d.src_ld = src.stride(0) if src_ld is None else src_ld
+    d.rows, d.width = rows, width
+    return d
+
+
+def copy_rows(**kw) -> None:
+    d = copy_rows_desc(**kw)
+    L.call("rfx_copy_rows", ctypes.byref(d), _stream())
+
+
 def device_status() -> int:
     v = ctypes.c_int(0)
     L.call("rfx_device_status", _stream(), ctypes.byref(v))
@@ -260,7 +280,25 @@ class Plan:
         L.KvQuantDesc: "rfx_plan_add_kv_quant",
         L.TimeCondDesc: "rfx_plan_add_time_cond",
         L.ModulationDesc: "rfx_plan_add_modulation",
+        L.CopyRowsDesc: "rfx_plan_add_copy_rows",
     }
+    # direct (non-plan) entry point of each descriptor kind, for eager execution
+    DIRECT = {
+        L.LinearDesc: "rfx_linear",
+        L.AttnDesc: "rfx_attention",
+        L.KvQuantDesc: "rfx_kv_quant_append",
+        L.TimeCondDesc: "rfx_time_cond",
+        L.ModulationDesc: "rfx_modulation",
+        L.CopyRowsDesc: "rfx_copy_rows",
+    }
+
+    @classmethod
+    def run_direct(cls, desc, kind: str | None = None) -> None:
+        """Runs one descriptor through its direct C entry point on the current stream."""
+        name = cls.DIRECT.get(type(desc))
+        if isinstance(desc, L.ActionIoDesc):
+            name = {"in": "rfx_action_in", "tail": "rfx_euler_tail"}[kind]
+        L.call(name, ctypes.byref(desc), _stream())
 
     def __init__(self):
         self._h = ctypes.c_void_p()
