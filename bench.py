@@ -1,0 +1,348 @@
+"""Benchmark of the streaming denoising hot path on B200.
+
+Workload (the PI0.5 action-chunk latency config): PI0.5 action expert, one
+robot stream per GPU, 18 Gemma-300M layers (width 1024, 8x256 heads, 1 KV
+head, GeGLU 4096), scale/shift/gate adaRMS from the timestep MLP, 818 cached
+context tokens held as int8 per-token KV, 50 action tokens, 10 Euler steps.
+One "step" of this benchmark = one full 10-step action chunk, replayed as a
+single CUDA graph of the engine's kernels.
+
+Multi-GPU (torchrun): every rank serves its own independent stream (weak
+scaling, no collective on the hot path); the action chunks are gathered to
+rank 0 with NCCL after the timed region.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+--impl reference times the reference's PyTorch path for the same workload on
+the host CPU (the oracle port of reflex/policies/pi05/modeling_pi05.py).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "p50 10-step PI0.5 action-chunk latency (ms); suffix-attn tensor-pipe % / HBM GB/s"
+N_CTX = 818
+CAPACITY = 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="rfx", choices=["rfx", "reference"])
+    ap.add_argument("--layers", type=int, default=18)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cpu-sample-chunks", type=int, default=2)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload_config(args, world):
+    return {
+        "workload": "PI0.5 10-step action chunk, 1 stream/GPU, 18x(1024, 8x256 MQA, GeGLU 4096), "
+                    "818-token int8 KV context, 50 action tokens",
+        "model": "pi05-action-expert (gemma-300m shape), random-init",
+        "layers": args.layers, "context_tokens": N_CTX, "suffix_tokens": 50, "euler_steps": 10,
+        "streams_per_gpu": 1, "global_batch": world, "kv": "int8 symmetric per-token/per-head",
+        "adarms": "scale/shift/gate", "parallelism": f"dp{world} (independent streams)",
+        "l2": "no flush: each chunk streams 6.2 GB of weights + 0.47 GB of fp32 modulation weights (>> 126 MB L2)",
+    }
+
+
+# ---------------------------------------------------------------- clocks ---
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons in the background."""
+
+    def __init__(self, index: int):
+        self.index, self.rows, self._stop = index, [], threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                f = [x.strip() for x in out.stdout.strip().split(",")]
+                if len(f) >= 7:
+                    self.rows.append(f)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------- CPU legs ---
+def cpu_chunk_ms(layers: int, chunks: int):
+    """The reference's PyTorch path of the same workload on the host CPU (the
+    oracle port: reflex/policies/pi05/modeling_pi05.py:1181-1241,1403-1419 over
+    the fp32 restatement of its modules), all host threads."""
+    from oracle import quant as oq
+    from oracle.model import Context, sample_chunk
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = pi05_config(num_layers=layers, adarms="ssg")
+    wts = synthetic.expert_weights(cfg, seed=0)
+    ks, vs = synthetic.context_kv(cfg, N_CTX, seed=1)
+    kd, vd = [], []
+    for l in range(layers):
+        q, s = oq.quant_i8_sym(ks[l].numpy())
+        kd.append(torch.from_numpy(oq.dequant_i8_sym(q, s)))
+        q, s = oq.quant_i8_sym(vs[l].numpy())
+        vd.append(torch.from_numpy(oq.dequant_i8_sym(q, s)))
+    ctx = Context(kd, vd, torch.ones(1, N_CTX, dtype=torch.bool))
+    x0 = synthetic.noise(cfg, seed=2)
+    times = []
+    with torch.no_grad():
+        sample_chunk(cfg, wts, ctx, x0)  # warm-up
+        for _ in range(chunks):
+            t0 = time.perf_counter()
+            sample_chunk(cfg, wts, ctx, x0)
+            times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times), torch.get_num_threads(), times
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    med, cores, times = cpu_chunk_ms(args.layers, max(1, args.steps))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(med, 3), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": round(med, 3), "unit": "ms", "cores": cores, "kind": "port",
+                         "sample": f"{len(times)} full chunks of the workload on the host CPU (fp32 torch)"},
+        "e2e": {"value": round(med, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU leg ---
+def build_engine(args, device):
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config
+    from reflex_b200.expert import ActionExpertEngine
+
+    cfg = pi05_config(num_layers=args.layers, adarms="ssg", quant_mode="i8_sym")
+    wts = synthetic.expert_weights(cfg, seed=0, device=device)
+    eng = ActionExpertEngine(cfg, wts, batch=1, capacity=CAPACITY, n_ctx=N_CTX, device=device)
+    del wts
+    ks, vs = synthetic.context_kv(cfg, N_CTX, seed=1, device=device)
+    for l in range(cfg.num_layers):
+        eng.load_context(l, ks[l], vs[l])
+    torch.cuda.synchronize()
+    return cfg, eng
+
+
+def kernel_roofline(eng, hbm_peak, reps=3):
+    """Times the gate/up GEMM launches of one Euler step back to back (18
+    different weights, so nothing stays in L2) with CUDA events on the launching
+    stream; returns per-launch duration and achieved HBM GB/s."""
+    from reflex_b200 import kernels as K
+
+    gu = [d for kind, d, tag in eng.ops if tag is not None and tag[0] == "gu" and tag[1] == 0]
+    cfg = eng.cfg
+    # algorithmic bytes of one launch: packed gate/up weight + normed input rows + GeGLU output
+    T = eng.T
+    bytes_per = (2 * cfg.mlp_dim * cfg.width * 2) + T * cfg.width * 2 + T * cfg.mlp_dim * 2
+    st = torch.cuda.current_stream()
+    for d in gu:
+        K.Plan.run_direct(d)
+    durs = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(4_000_000)  # keeps the GPU busy while the host enqueues the launches
+        e0.record(st)
+        for d in gu:
+            K.Plan.run_direct(d)
+        e1.record(st)
+        torch.cuda.synchronize()
+        durs.append(e0.elapsed_time(e1) / len(gu))
+    avg_ms = statistics.median(durs)
+    achieved = bytes_per / (avg_ms * 1e-3) / 1e9
+    return {"kernel": "linear_kernel<64,NORM,GEGLU> (gate/up + AdaRMS prologue + GELU-tanh*up)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
+
+
+def run_gpu(args):
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        pg = dist
+    hbm_peak, _, peak_kind = peaks()
+    from reflex_b200 import kernels as K
+    from reflex_b200 import synthetic
+
+    cfg, eng = build_engine(args, device)
+    x0 = synthetic.noise(cfg, seed=2 + rank, device=device)
+    eng.set_inputs(x0)
+    if not args.no_graph:
+        eng.capture()
+    launches = eng.num_launches
+    st = torch.cuda.current_stream()
+
+    def one_chunk():
+        eng.set_inputs(x0)
+        eng.launch_chunk()
+
+    for _ in range(max(3, args.warmup)):
+        one_chunk()
+    torch.cuda.synchronize()
+    status = K.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after warm-up")
+
+    # ---- device-timed region
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_wall = time.perf_counter()
+        evs[0].record(st)
+        for i in range(args.steps):
+            one_chunk()
+            evs[i + 1].record(st)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t_wall
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    p50 = statistics.median(per)
+    if pg:
+        t = torch.tensor([p50, total_ms], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        p50, total_ms = t[0].item(), t[1].item()
+        pg.barrier()
+
+    # ---- end to end through the public API with host buffers
+    x_host = synthetic.noise(cfg, seed=2 + rank).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    e2e = []
+    for i in range(args.steps + 3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        eng.set_inputs(x_host.to(device, non_blocking=True))
+        eng.launch_chunk()
+        out_host.copy_(eng.x, non_blocking=True)
+        e1.record(st)
+        e1.synchronize()
+        if i >= 3:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_p50 = statistics.median(e2e)
+    if pg:
+        t = torch.tensor([e2e_p50], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_p50 = t.item()
+        # final gather of every stream's action chunk (not on the hot path)
+        chunks = [torch.empty_like(eng.x) for _ in range(world)]
+        pg.all_gather(chunks, eng.x)
+
+    roof = kernel_roofline(eng, hbm_peak)
+    roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    status = K.device_status()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        med, cores, times = cpu_chunk_ms(args.layers, args.cpu_sample_chunks)
+        cpu = {"value": round(med, 3), "unit": "ms", "cores": cores, "kind": "port",
+               "sample": f"{len(times)} full chunks of the same workload (fp32 torch oracle port), median"}
+
+    if rank == 0:
+        bytes_chunk = 10 * (eng.cfg.num_layers * 17301504 * 2 + eng.cfg.num_layers * N_CTX * 256 * 2) + \
+            (2 * eng.cfg.num_layers + 1) * 3 * 1024 * 1024 * 4
+        line = {
+            "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random-init weights, N(0,1) context K/V quantized to int8, x0 ~ N(0,1)",
+            "config": workload_config(args, world),
+            "chunks_per_s": round(world * 1e3 / p50, 2),
+            "chunk_roofline": {"algorithmic_bytes": bytes_chunk,
+                               "achieved_GBps": round(bytes_chunk / (p50 * 1e-3) / 1e9, 1),
+                               "peak_GBps": hbm_peak, "frac": round(bytes_chunk / (p50 * 1e-3) / 1e9 / hbm_peak, 4)},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_p50, 4), "unit": "ms", "h2d_bytes_per_step": x_host.numel() * 4,
+                    "d2h_bytes_per_step": out_host.numel() * 4},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+            "graph": not args.no_graph,
+            "device_status": status,
+            "wall_s_timed": round(wall, 3),
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        eng.plan = None
+        pg.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

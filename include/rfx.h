@@ -68,6 +68,11 @@ int rfx_device_status(void* stream, int* out);
  * launched afterwards by this process. Default: enabled. */
 int rfx_set_pdl(int enable);
 
+/* Diagnostics: when `buf` (device, 8-byte aligned, `bytes` long) is set, the
+ * linear and attention kernels record a %globaltimer stamp (ns) per phase per
+ * CTA at buf[cta * 16 + event]; NULL turns tracing off. */
+int rfx_set_trace(void* buf, size_t bytes);
+
 /* Number of streaming multiprocessors of the current device. */
 int rfx_num_sms(int* out);
 
@@ -155,6 +160,25 @@ typedef struct rfx_linear_desc {
   int y_row_offset;
 } rfx_linear_desc;
 int rfx_linear(const rfx_linear_desc* desc, void* stream);
+
+/* (Ada)RMSNorm of token rows into a bf16 GEMM input:
+ * y[t][k] = bf16(((x[t][k] * rstd[t]) * a1[k]) * a2[b][k] + b2[b][k]),
+ * rstd[t] = rsqrt(mean_k x[t][k]^2 + eps), b = t / tokens_per_batch
+ * (AdaRMSNorm.forward, reflex/policies/pi05/modeling_pi05.py:73-99; a2 = 1 and
+ * b2 = 0 when NULL). */
+typedef struct rfx_norm_desc {
+  int T, K, tokens_per_batch;
+  const void* x; /* bf16 [T][ldx] */
+  int ldx;
+  const float* norm_a1;
+  const float* norm_a2;
+  const float* norm_b2;
+  long norm_ab_stride;
+  float eps;
+  void* y; /* bf16 [T][ldy] */
+  int ldy;
+} rfx_norm_desc;
+int rfx_rms_norm(const rfx_norm_desc* desc, void* stream);
 
 /* Weight repacks for the fused epilogues (one-time, at load). */
 #define RFX_PACK_QKV_ROPE 0 /* [Wq; Wk; Wv] ((Hq+2)*256 rows, modeling_pi05.py:864-866) -> RoPE pair tiles */
@@ -300,6 +324,11 @@ int rfx_plan_add_modulation(rfx_plan* plan, const rfx_modulation_desc* desc);
 int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc);
+int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc);
+/* The next op added is launched without programmatic dependent launch: it
+ * starts only after everything before it has completed (a serialization point,
+ * e.g. after writes to the KV ring that later kernels read before waiting). */
+int rfx_plan_add_barrier(rfx_plan* plan);
 /* Number of kernel launches one run of the plan performs. */
 int rfx_plan_num_launches(const rfx_plan* plan, int* out);
 int rfx_plan_run(rfx_plan* plan, void* stream);

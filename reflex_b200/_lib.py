@@ -131,12 +131,23 @@ class CopyRowsDesc(Structure):
     ]
 
 
+class NormDesc(Structure):
+    _fields_ = [
+        ("T", c_int), ("K", c_int), ("tokens_per_batch", c_int),
+        ("x", c_void_p), ("ldx", c_int),
+        ("norm_a1", c_void_p), ("norm_a2", c_void_p), ("norm_b2", c_void_p),
+        ("norm_ab_stride", c_long), ("eps", c_float),
+        ("y", c_void_p), ("ldy", c_int),
+    ]
+
+
 # Every entry point declared in include/rfx.h: name -> (argtypes, restype).
 SIGNATURES = {
     "rfx_version": ([], c_int),
     "rfx_last_error": ([], ctypes.c_char_p),
     "rfx_device_status": ([c_void_p, POINTER(c_int)], c_int),
     "rfx_set_pdl": ([c_int], c_int),
+    "rfx_set_trace": ([c_void_p, c_size_t], c_int),
     "rfx_num_sms": ([POINTER(c_int)], c_int),
     "rfx_kv_quant_append": ([POINTER(KvQuantDesc), c_void_p], c_int),
     "rfx_linear": ([POINTER(LinearDesc), c_void_p], c_int),
@@ -148,6 +159,9 @@ SIGNATURES = {
     "rfx_action_in": ([POINTER(ActionIoDesc), c_void_p], c_int),
     "rfx_euler_tail": ([POINTER(ActionIoDesc), c_void_p], c_int),
     "rfx_copy_rows": ([POINTER(CopyRowsDesc), c_void_p], c_int),
+    "rfx_rms_norm": ([POINTER(NormDesc), c_void_p], c_int),
+    "rfx_plan_add_rms_norm": ([c_void_p, POINTER(NormDesc)], c_int),
+    "rfx_plan_add_barrier": ([c_void_p], c_int),
     "rfx_plan_create": ([POINTER(c_void_p)], c_int),
     "rfx_plan_destroy": ([c_void_p], c_int),
     "rfx_plan_add_linear": ([c_void_p, POINTER(LinearDesc)], c_int),
@@ -202,5 +216,6 @@ def ptr(t) -> int | None:
 
 __all__ = [n for n in dir() if n.startswith(("RFX_", "Rfx"))] + [
     "KvQuantDesc", "LinearDesc", "AttnDesc", "TimeCondDesc", "ModulationDesc", "ActionIoDesc", "CopyRowsDesc",
+    "NormDesc",
     "SIGNATURES", "load", "check", "call", "ptr", "LIB_PATH", "c_ubyte",
 ]

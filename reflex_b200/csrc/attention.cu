@@ -46,8 +46,8 @@ constexpr int kOffV = kOffK + 4 * 8192;      // 4 x [64 x 64] f16 (MN-major bloc
 constexpr int kOffP = kOffV + 4 * 8192;      // [128 x 64] f16, 16 KB
 constexpr int kOffSK = kOffP + 16384;        // int8 K staging [64 x 256], 16 KB
 constexpr int kOffSV = kOffSK + 16384;       // int8 V staging, 16 KB
-constexpr int kOffScale = kOffSV + 16384;    // ks, vs, kdq, vdq, kzp, vzp: 6 x 64 fp32
-constexpr int kOffBar = kOffScale + 6 * 64 * 4;
+constexpr int kOffScale = kOffSV + 16384;    // ks, vs, kdq, vdq, kzp, vzp (fp32), nb (int32): 7 x 64
+constexpr int kOffBar = kOffScale + 8 * 64 * 4;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 struct AttnParams {
@@ -66,7 +66,20 @@ struct AttnParams {
   float* ws_o;
   float2* ws_ml;
   int* status;
+  unsigned long long* trace;
 };
+
+// Trace events (one %globaltimer stamp per event per CTA, see rfx_set_trace).
+enum {
+  kTrStart = 0, kTrSetup = 1, kTrIssued = 2, kTrKv = 3, kTrConv = 4, kTrS = 5, kTrP = 6, kTrO = 7, kTrEnd = 8,
+  kTrSLoaded = 9, kTrMax = 10, kTrExp = 11, kTrOLoaded = 12, kTrOStored = 13
+};
+
+__device__ __forceinline__ void trace(const AttnParams& p, int ev) {
+  if (p.trace)
+    p.trace[((static_cast<long>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 16 + ev] =
+        globaltimer_ns();
+}
 
 __device__ __forceinline__ float load_scalar(const void* p, long i, bool bf16) {
   return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]) : static_cast<const float*>(p)[i];
@@ -123,6 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* vdq_s = kdq_s + 64;
   float* kzp_s = vdq_s + 64;
   float* vzp_s = kzp_s + 64;
+  int* nb_s = reinterpret_cast<int*>(vzp_s + 64);  // block ids of the new keys of the block
+  float* kadd_s = reinterpret_cast<float*>(nb_s + 64);  // 0 or -inf (masked key)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;
@@ -133,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_full = bars + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
 
+  if (threadIdx.x == 0) trace(p, kTrStart);
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(kv_full, 1);
@@ -156,27 +172,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmO = tmem, tmS = tmem + 256;
   pdl_launch_dependents();
-  pdl_wait();
+  if (threadIdx.x == 0) trace(p, kTrSetup);
 
+  // The quantized context (ring payload, scales, validity) is not written
+  // while a chunk runs, so its first block is fetched and converted before
+  // griddepcontrol.wait, overlapping the kernel that produces Q.  Everything
+  // that reads the new tokens' Q/K/V waits first.
   const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
   int issued_ctx = 0;
 
   if (warp == 0) {
     if (lane == 0 && nbl > 0) {
-      mbar_arrive_expect_tx(q_full, 4 * 16384);
-      for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
-      for (int jl = 0; jl < nbl; ++jl) {
-        const int j = blk_begin + jl;
-        if (j >= p.n_ctx_blocks) break;
-        if (issued_ctx > 0 && !mbar_wait(stage_free, (issued_ctx - 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
+      auto issue_kv = [&](int j) {
         mbar_arrive_expect_tx(kv_full, 2 * 16384);
         const int row = b * p.cap + j * kKB;
         tma_load_2d(stK, &tmK, kv_full, 0, row);
         tma_load_2d(stV, &tmV, kv_full, 0, row);
         ++issued_ctx;
+      };
+      if (blk_begin < p.n_ctx_blocks) issue_kv(blk_begin);
+      pdl_wait();
+      mbar_arrive_expect_tx(q_full, 4 * 16384);
+      for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
+      for (int jl = 1; jl < nbl; ++jl) {
+        const int j = blk_begin + jl;
+        if (j >= p.n_ctx_blocks) break;
+        if (!mbar_wait(stage_free, (issued_ctx - 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
+        issue_kv(j);
       }
+      trace(p, kTrIssued);
     }
+    pdl_wait();
   } else if (warp == 1) {
+    pdl_wait();
     if (lane == 0 && nbl > 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
       constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
@@ -217,12 +245,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -INFINITY, l_run = 0.f;
     int ctx_iter = 0;
     bool ok = true;
+    bool waited = false;  // griddepcontrol.wait done by this thread
 
     for (int jl = 0; jl < nbl && ok; ++jl) {
       const int j = blk_begin + jl;
       const bool is_ctx = j < p.n_ctx_blocks;
       if (jl > 0) ok = mbar_wait(o_full, (jl - 1) & 1, p.status, kDevTimeoutMmaDone);
       if (!ok) break;
+      if (!is_ctx && !waited) {
+        pdl_wait();
+        waited = true;
+      }
       // ---- convert block j into sK / sV ----
       if (is_ctx) {
         if (et < 64) {
@@ -230,11 +263,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
           bool valid = slot < p.n_ctx;
           if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
+          // score (log2 units) = acc * ks + kadd; kadd = -inf masks the key
+          kadd_s[et] = valid ? 0.f : -INFINITY;
           if (p.mode == kQuantI8Sym) {
-            ks_s[et] = valid ? static_cast<const float*>(p.k_scale)[gi] : -INFINITY;  // -inf masks the key
+            ks_s[et] = valid ? static_cast<const float*>(p.k_scale)[gi] * p.scale_log2 : 0.f;
             vs_s[et] = valid ? static_cast<const float*>(p.v_scale)[gi] : 0.f;
           } else {
-            ks_s[et] = valid ? 1.f : -INFINITY;
+            ks_s[et] = valid ? p.scale_log2 : 0.f;
             vs_s[et] = 1.f;
             kdq_s[et] = load_scalar(p.k_scale, gi, sbf16);
             vdq_s[et] = load_scalar(p.v_scale, gi, sbf16);
@@ -245,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!(ok = mbar_wait(kv_full, ctx_iter & 1, p.status, kDevTimeoutTmaFull))) break;
         ++ctx_iter;
+        if (et == 0) trace(p, kTrKv);
         for (int it = et; it < 2 * kKB * 16; it += 128) {
           const bool isv = it >= kKB * 16;
           const int w = isv ? it - kKB * 16 : it;
@@ -265,8 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb0 = (j - p.n_ctx_blocks) * kKB;
         if (et < 64) {
           const int kk = nb0 + et;
-          ks_s[et] = kk < p.S ? 1.f : -INFINITY;  // block-causal visibility is applied per row
+          ks_s[et] = kk < p.S ? p.scale_log2 : 0.f;  // block-causal visibility is applied per row
+          kadd_s[et] = kk < p.S ? 0.f : -INFINITY;
           vs_s[et] = 1.f;
+          nb_s[et] = (kk < p.S && p.new_block) ? p.new_block[kk] : 0;
         }
         for (int it = et; it < 2 * kKB * 32; it += 128) {
           const bool isv = it >= kKB * 32;
@@ -295,31 +333,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (lane == 0) mbar_arrive(conv_done);
+      if (et == 0) trace(p, kTrConv);
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
 
       // ---- softmax on S ----
       if (!(ok = mbar_wait(s_full, jl & 1, p.status, kDevTimeoutMmaDone))) break;
       tc_fence_after();
+      if (et == 0) trace(p, kTrS);
       float z[kKB];
+      {
+        uint32_t rr[kKB / 16][16];
 #pragma unroll
-      for (int c = 0; c < kKB / 16; ++c) {
-        uint32_t rr[16];
-        tmem_ld16(tmS + lane_base + c * 16, rr);
+        for (int c = 0; c < kKB / 16; ++c) tmem_ld16(tmS + lane_base + c * 16, rr[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[e]);
-      }
-      float bmax = -INFINITY;
+        for (int c = 0; c < kKB / 16; ++c)
 #pragma unroll
-      for (int kk = 0; kk < kKB; ++kk) {
-        const float ksc = ks_s[kk];
-        bool valid = ksc != -INFINITY;
-        if (!is_ctx && valid && p.new_block) {
-          const int nk = (j - p.n_ctx_blocks) * kKB + kk;
-          valid = p.new_block[nk] <= my_block;
-        }
-        z[kk] = valid ? z[kk] * ksc * p.scale_log2 : -INFINITY;
-        bmax = fmaxf(bmax, z[kk]);
+          for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[c][e]);
       }
+      if (et == 0) trace(p, kTrSLoaded);
+      // scores in log2 units: one FMA per key from float4 vectors, masked keys
+      // become -inf; the max is a 4-way tree so the chain is short
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      const bool causal = !is_ctx && p.new_block != nullptr;
+#pragma unroll
+      for (int c = 0; c < kKB / 4; ++c) {
+        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+        z[4 * c + 0] = fmaf(z[4 * c + 0], km.x, ka.x);
+        z[4 * c + 1] = fmaf(z[4 * c + 1], km.y, ka.y);
+        z[4 * c + 2] = fmaf(z[4 * c + 2], km.z, ka.z);
+        z[4 * c + 3] = fmaf(z[4 * c + 3], km.w, ka.w);
+        if (causal) {
+          const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
+          if (nb.x > my_block) z[4 * c + 0] = -INFINITY;
+          if (nb.y > my_block) z[4 * c + 1] = -INFINITY;
+          if (nb.z > my_block) z[4 * c + 2] = -INFINITY;
+          if (nb.w > my_block) z[4 * c + 3] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
+      }
+      const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       float m_new = fmaxf(m_run, bmax);
       bool need = false;
       float m_use;
@@ -332,25 +390,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_use = m_run;
       }
       const float alpha = need ? exp2f(m_run - m_use) : 1.f;
-      float psum = 0.f;
+      if (et == 0) trace(p, kTrMax);
+      // p = 2^(z - m): ex2 of -inf is +0, so masked keys need no branch
+      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
       float pv[kKB];
 #pragma unroll
-      for (int kk = 0; kk < kKB; ++kk) {
-        const float e = (m_use == -INFINITY || z[kk] == -INFINITY) ? 0.f : exp2f(z[kk] - m_use);
-        psum += e;
-        pv[kk] = e * vs_s[kk];
+      for (int c = 0; c < kKB / 4; ++c) {
+        const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
+        const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pe = ex2_approx(z[4 * c + e] - m_sub);
+          ps[e] += pe;
+          pv[4 * c + e] = pe * vv[e];
+        }
       }
+      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       l_run = l_run * alpha + psum;
+      if (et == 0) trace(p, kTrExp);
       m_run = m_use;
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c = 0; c < kD / 16; ++c) {
-          uint32_t rr[16];
-          tmem_ld16(tmO + lane_base + c * 16, rr);
+        for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-          tmem_st16(tmO + lane_base + c * 16, rr);
+          for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[q][e] = __float_as_uint(__uint_as_float(rr[q][e]) * alpha);
+            tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+          }
         }
         tmem_wait_st();
       }
@@ -365,9 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
+      if (et == 0) trace(p, kTrP);
     }
 
     // ---- epilogue ----
+    if (!waited) pdl_wait();
     if (ok && nbl > 0) ok = mbar_wait(o_full, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone);
     tc_fence_after();
     if (ok && nbl > 0) {
@@ -375,30 +449,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const long tok = static_cast<long>(b) * p.S + s_row;
       __nv_bfloat16* orow = p.out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
-      const long wrow = ((static_cast<long>(b) * p.q_tiles + qt) * p.splits + sp) * kQR + r;
-      float* wrow_o = p.ws_o ? p.ws_o + wrow * kD : nullptr;
+      const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.splits + sp;
+      const long wrow = wcta * kQR + r;
+      // partial O layout [cta][16-column chunk][row][16]: a warp's rows write
+      // consecutive 64-byte runs (coalesced)
+      float* wrow_o = p.ws_o ? p.ws_o + (wcta * (kD / 16) * kQR + r) * 16 : nullptr;
+      if (et == 0) trace(p, kTrO);
 #pragma unroll 1
-      for (int c = 0; c < kD / 16; ++c) {
-        uint32_t rr[16];
-        tmem_ld16(tmO + lane_base + c * 16, rr);
+      for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+        uint32_t rr[4][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
         tmem_wait_ld();
         if (!row_valid) continue;
-        if (final_out) {
-          uint32_t w8[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            w8[e] = pack_bf16x2(__uint_as_float(rr[2 * e]) * inv_l, __uint_as_float(rr[2 * e + 1]) * inv_l);
-          *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-          *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-        } else {
+        for (int q = 0; q < 4; ++q) {
+          const int c = c0 + q;
+          if (final_out) {
+            uint32_t w8[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            *reinterpret_cast<float4*>(wrow_o + c * 16 + 4 * e) =
-                make_float4(__uint_as_float(rr[4 * e]), __uint_as_float(rr[4 * e + 1]), __uint_as_float(rr[4 * e + 2]),
-                            __uint_as_float(rr[4 * e + 3]));
+            for (int e = 0; e < 8; ++e)
+              w8[e] = pack_bf16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+            *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              *reinterpret_cast<float4*>(wrow_o + static_cast<long>(c) * kQR * 16 + 4 * e) =
+                  make_float4(__uint_as_float(rr[q][4 * e]), __uint_as_float(rr[q][4 * e + 1]),
+                              __uint_as_float(rr[q][4 * e + 2]), __uint_as_float(rr[q][4 * e + 3]));
+          }
         }
       }
       if (!final_out && row_valid) p.ws_ml[wrow] = make_float2(m_run, l_run);
+      if (et == 0) trace(p, kTrOStored);
     }
     (void)et;
   }
@@ -412,6 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) trace(p, kTrEnd);
 }
 
 // Merges the kv_splits partial results of every query row.
@@ -427,19 +512,38 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const AttnParams
     const int R = qt * kQR + r;
     if (R < p.Hq * p.S) {
       const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.splits;
+      // all partials of this row are loaded before any is used (the loads overlap)
+      constexpr int kMaxSplits = 32;
+      float2 ml[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s)
+        if (s < p.splits) ml[s] = p.ws_ml[(base + s) * kQR + r];
       float M = -INFINITY;
-      for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.ws_ml[(base + s) * kQR + r].x);
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s)
+        if (s < p.splits && ml[s].y > 0.f) M = fmaxf(M, ml[s].x);
       float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < p.splits; ++s) {
-        const float2 ml = p.ws_ml[(base + s) * kQR + r];
-        if (ml.x == -INFINITY || ml.y <= 0.f) continue;
-        const float w = exp2f(ml.x - M);
-        L += w * ml.y;
-        const float* o = p.ws_o + ((base + s) * kQR + r) * kD + lane * 8;
-        const float4 a = *reinterpret_cast<const float4*>(o);
-        const float4 c = *reinterpret_cast<const float4*>(o + 4);
-        acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
-        acc[4] += w * c.x; acc[5] += w * c.y; acc[6] += w * c.z; acc[7] += w * c.w;
+#pragma unroll
+      for (int s0 = 0; s0 < kMaxSplits; s0 += 8) {
+        if (s0 >= p.splits) break;
+        float4 a[8], c[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (s0 + q < p.splits) {
+            const float* o = p.ws_o + (((base + s0 + q) * (kD / 16) + (lane >> 1)) * kQR + r) * 16 + (lane & 1) * 8;
+            a[q] = *reinterpret_cast<const float4*>(o);
+            c[q] = *reinterpret_cast<const float4*>(o + 4);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int s = s0 + q;
+          if (s >= p.splits || ml[s].x == -INFINITY || ml[s].y <= 0.f) continue;
+          const float w = exp2f(ml[s].x - M);
+          L += w * ml[s].y;
+          acc[0] += w * a[q].x; acc[1] += w * a[q].y; acc[2] += w * a[q].z; acc[3] += w * a[q].w;
+          acc[4] += w * c[q].x; acc[5] += w * c[q].y; acc[6] += w * c[q].z; acc[7] += w * c[q].w;
+        }
       }
       const float inv = L > 0.f ? 1.f / L : 0.f;
       const int s_row = R % p.S, h_row = R / p.S;
@@ -475,6 +579,7 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
     splits = std::max(1, std::min(g->n_blocks, nsm / std::max(1, ctas)));
   }
   if (splits > g->n_blocks) splits = g->n_blocks;
+  if (splits > 32) splits = 32;  // the combine kernel merges at most 32 partials per row
   g->splits = splits;
   return RFX_OK;
 }
@@ -552,6 +657,7 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
     p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(d.workspace) + rows * kD * sizeof(float));
   }
   p.status = device_status_ptr();
+  p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(g.q_tiles) * g.splits * d.B * 16));
 
   CUtensorMap q = *tmQ, k = *tmK, v = *tmV;
   dim3 grid(g.q_tiles, g.splits, d.B);

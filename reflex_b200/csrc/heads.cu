@@ -53,22 +53,32 @@ __global__ void __launch_bounds__(256) gemv_bf16_silu_kernel(const __nv_bfloat16
 #pragma unroll
     for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
     const __nv_bfloat16* wr = W + static_cast<long>(o) * width;
-    for (int k = lane * 8; k < width; k += 256) {
-      uint4 raw = *reinterpret_cast<const uint4*>(wr + k);
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      float w[8];
+    for (int k0 = 0; k0 < width; k0 += 1024) {
+      uint4 wv[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __bfloat1622float2(w2[e]);
-        w[2 * e] = f.x;
-        w[2 * e + 1] = f.y;
+      for (int q = 0; q < 4; ++q) {
+        const int k = k0 + q * 256 + lane * 8;
+        if (k < width) wv[q] = *reinterpret_cast<const uint4*>(wr + k);
       }
 #pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        if (r < n_rows) {
-          const float* xr = xin + r * width + k;
+      for (int q = 0; q < 4; ++q) {
+        const int k = k0 + q * 256 + lane * 8;
+        if (k >= width) continue;
+        const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[q]);
+        float w[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r] = fmaf(w[e], xr[e], acc[r]);
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __bfloat1622float2(w2[e]);
+          w[2 * e] = f.x;
+          w[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) {
+          if (r < n_rows) {
+            const float* xr = xin + r * width + k;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[r] = fmaf(w[e], xr[e], acc[r]);
+          }
         }
       }
     }
@@ -102,16 +112,28 @@ __global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict
 #pragma unroll
     for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
     const float* wr = W + row * width;
-    for (int k = lane * 4; k < width; k += 128) {
-      const float4 w = __ldcs(reinterpret_cast<const float4*>(wr + k));  // streamed once per chunk
+    for (int k0 = 0; k0 < width; k0 += 1024) {
+      // the whole 4 KB slice of the row is requested before any of it is used
+      float4 wv[8];
 #pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        if (r < n_rows) {
-          const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
-          acc[r] = fmaf(w.x, x.x, acc[r]);
-          acc[r] = fmaf(w.y, x.y, acc[r]);
-          acc[r] = fmaf(w.z, x.z, acc[r]);
-          acc[r] = fmaf(w.w, x.w, acc[r]);
+      for (int q = 0; q < 8; ++q) {
+        const int k = k0 + q * 128 + lane * 4;
+        if (k < width) wv[q] = __ldcs(reinterpret_cast<const float4*>(wr + k));  // streamed once per chunk
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int k = k0 + q * 128 + lane * 4;
+        if (k >= width) continue;
+        const float4 w = wv[q];
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) {
+          if (r < n_rows) {
+            const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
+            acc[r] = fmaf(w.x, x.x, acc[r]);
+            acc[r] = fmaf(w.y, x.y, acc[r]);
+            acc[r] = fmaf(w.z, x.z, acc[r]);
+            acc[r] = fmaf(w.w, x.w, acc[r]);
+          }
         }
       }
     }
@@ -254,6 +276,83 @@ __global__ void __launch_bounds__(256) euler_tail_kernel(const IoParams p) {
     __syncthreads();
     action_in_row(xs, p.A, p.width, p.w_in, p.b_in,
                   p.h_next + (static_cast<long>(b) * p.h_next_rps + p.h_next_off + s) * p.h_next_ld);
+  }
+  pdl_launch_dependents();
+}
+
+// y[t][k] = bf16(((x[t][k] * rstd[t]) * a1[k]) * a2[b][k] + b2[b][k]),
+// rstd[t] = rsqrt(mean_k x[t][k]^2 + eps): the (Ada)RMSNorm of
+// reflex/policies/pi05/modeling_pi05.py:73-99 in fp32 with one rounding to
+// bf16, one CTA per token row.
+struct NormParams {
+  const __nv_bfloat16* x;
+  int ldx, T, K, S;
+  const float* a1;
+  const float* a2;
+  const float* b2;
+  long ab_stride;
+  float eps;
+  __nv_bfloat16* y;
+  int ldy;
+};
+
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const NormParams p) {
+  constexpr int kMaxChunks = 4;  // K <= 4096
+  __shared__ float red[4];
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int b = t / p.S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint4 raw[kMaxChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int k = (c * 128 + threadIdx.x) * 8;
+    if (k < p.K) raw[c] = *reinterpret_cast<const uint4*>(p.x + static_cast<long>(t) * p.ldx + k);
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int k = (c * 128 + threadIdx.x) * 8;
+    if (k >= p.K) continue;
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h2[e]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  const float rstd = rsqrtf((red[0] + red[1] + red[2] + red[3]) / static_cast<float>(p.K) + p.eps);
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int k = (c * 128 + threadIdx.x) * 8;
+    if (k >= p.K) continue;
+    const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&raw[c]);
+    float a1[8], a2[8], b2[8];
+    *reinterpret_cast<float4*>(a1) = *reinterpret_cast<const float4*>(p.a1 + k);
+    *reinterpret_cast<float4*>(a1 + 4) = *reinterpret_cast<const float4*>(p.a1 + k + 4);
+    const long bo = static_cast<long>(b) * p.ab_stride + k;
+    if (p.a2) {
+      *reinterpret_cast<float4*>(a2) = *reinterpret_cast<const float4*>(p.a2 + bo);
+      *reinterpret_cast<float4*>(a2 + 4) = *reinterpret_cast<const float4*>(p.a2 + bo + 4);
+    }
+    if (p.b2) {
+      *reinterpret_cast<float4*>(b2) = *reinterpret_cast<const float4*>(p.b2 + bo);
+      *reinterpret_cast<float4*>(b2 + 4) = *reinterpret_cast<const float4*>(p.b2 + bo + 4);
+    }
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = __fmul_rn(__fmul_rn(__bfloat162float(xv[e]), rstd), a1[e]);
+      if (p.a2) v = __fmul_rn(v, a2[e]);
+      if (p.b2) v = __fadd_rn(v, b2[e]);
+      y[e] = v;
+    }
+    *reinterpret_cast<uint4*>(p.y + static_cast<long>(t) * p.ldy + k) =
+        make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
   }
   pdl_launch_dependents();
 }
@@ -406,6 +505,16 @@ int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl
   return launch_kernel(fn, dim3(d.B * d.S), dim3(256), smem, stream, pdl, 1, p);
 }
 
+int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl) {
+  if (d.T < 1 || d.K < 8 || d.K % 8 || d.K > 4096 || d.tokens_per_batch < 1 || !d.x || !d.y || !d.norm_a1 ||
+      d.ldx < d.K || d.ldx % 8 || d.ldy < d.K || d.ldy % 8 || !a16(d.x) || !a16(d.y) || !a16(d.norm_a1) ||
+      (d.norm_a2 && !a16(d.norm_a2)) || (d.norm_b2 && !a16(d.norm_b2)) || d.norm_ab_stride % 4)
+    return set_error(RFX_E_INVAL, "rfx_rms_norm: need K%%8==0 (<=4096), 16-byte aligned rows and vectors");
+  NormParams p{static_cast<const __nv_bfloat16*>(d.x), d.ldx, d.T, d.K, d.tokens_per_batch, d.norm_a1, d.norm_a2,
+               d.norm_b2, d.norm_ab_stride, d.eps, static_cast<__nv_bfloat16*>(d.y), d.ldy};
+  return launch_kernel(reinterpret_cast<const void*>(rmsnorm_kernel), dim3(d.T), dim3(128), 0, stream, pdl, 1, p);
+}
+
 int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl) {
   if (!d.dst || !d.src || d.rows < 0 || d.width < 8 || d.width % 8 || d.group < 1 || d.dst_rows_per_group < 1 ||
       d.dst_row_offset < 0 || d.dst_row_offset + d.group > d.dst_rows_per_group || d.dst_ld < d.width ||
@@ -422,6 +531,11 @@ int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl)
 }
 
 }  // namespace rfx
+
+extern "C" int rfx_rms_norm(const rfx_norm_desc* d, void* stream) {
+  if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_rms_norm: null descriptor");
+  return rfx::launch_rms_norm(*d, static_cast<cudaStream_t>(stream), rfx::pdl_enabled());
+}
 
 extern "C" int rfx_copy_rows(const rfx_copy_rows_desc* d, void* stream) {
   if (!d) return rfx::set_error(RFX_E_INVAL, "rfx_copy_rows: null descriptor");

@@ -10,13 +10,16 @@
 //     issued *before* griddepcontrol.wait, so under programmatic dependent
 //     launch the weight stream overlaps the previous kernel's tail.
 //   * Split-K across a thread-block cluster: every CTA of the cluster
-//     accumulates a K-slice in its own TMEM, parks the fp32 partial tile in its
-//     shared memory, and after a cluster barrier each CTA reduces a disjoint
+//     accumulates a K-slice in its own TMEM and parks the fp32 partial tile in
+//     its shared memory; after a cluster barrier each CTA reduces a disjoint
 //     set of rows over all CTAs' partials through DSMEM in a fixed order
-//     (deterministic), then runs the fused epilogue for those rows.
-//   * Prologues: TMA load of a bf16 activation, or the RMS/AdaRMS norm
-//     computed in-kernel from the residual stream and written to shared memory
-//     in the UMMA layout.
+//     (deterministic), with the remote loads batched so their latencies
+//     overlap, then runs the fused epilogue for those rows.
+//   * Prologues: TMA load of a bf16 activation tile, or the RMS / AdaRMS norm:
+//     the raw activation K-slice is TMA-loaded into the UMMA tile, every CTA
+//     sums x^2 over its slice, the cluster exchanges the partial sums through
+//     DSMEM (the cluster holds the full rows), and the tile is normalized in
+//     place in shared memory.
 //   * Epilogues work on row pairs (r, r+64) of a tile so RoPE (dims d, d+128)
 //     and GELU-tanh(gate)*up see both operands; the weight rows are permuted
 //     once at load time (rfx_pack_weight) to put the pairs in one tile.
@@ -48,6 +51,23 @@ enum {
   kEpiGeglu = RFX_EPI_GEGLU
 };
 
+// Trace events (one 8-byte %globaltimer stamp per event per CTA).
+enum {
+  kTrStart = 0,
+  kTrSetup = 1,
+  kTrWIssued = 2,
+  kTrPdl = 3,
+  kTrFirstFull = 4,
+  kTrMmaIssued = 5,
+  kTrXFull = 6,
+  kTrXReady = 7,
+  kTrAcc = 8,
+  kTrRed = 9,
+  kTrCluster = 10,
+  kTrEpi = 11,
+  kTrEnd = 12
+};
+
 struct LinParams {
   int T, O, K, S;
   int k_chunks;
@@ -75,8 +95,16 @@ struct LinParams {
   __nv_bfloat16* v_out;
   int hq;
   int y_rps, y_off;
+  int stage_off; // byte offset of the staged epilogue operands (0: fetched in the epilogue)
+  int push;      // split-K partials are pushed into the owner CTA's receive buffer
+  int recv_off;  // byte offset of the receive buffer [splits][2*pairs][NT] fp32
   int* status;
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void trace(const LinParams& p, int ev) {
+  if (p.trace) p.trace[(static_cast<long>(blockIdx.y) * gridDim.x + blockIdx.x) * 16 + ev] = globaltimer_ns();
+}
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
@@ -90,49 +118,85 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* p, const float (&v)[
   uint2 u = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
   *reinterpret_cast<uint2*>(p) = u;
 }
+__device__ __forceinline__ void unpack_bf16x4(uint2 u, float (&v)[4]) {
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = __bfloat162float(h[j]);
+}
+
+// Global operands of one epilogue item, fetched before the reduction so their
+// latency overlaps the DSMEM loads.
+struct EpiIn {
+  float r0[4], r1[4];  // residual (RESIDUAL) or bias (STORE/SILU)
+  float g0[4], g1[4];  // gates (RESIDUAL)
+  float c[4], s[4];    // RoPE cos / sin (QKV_ROPE)
+};
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_fetch(const LinParams& p, int m, int i, int t, EpiIn& in) {
+  const int b = t / p.S;
+  if (EPI == kEpiResidual) {
+    const long yrow = static_cast<long>(b) * p.y_rps + p.y_off + (t - b * p.S);
+    const int o0 = m * kBM + i;
+    unpack_bf16x4(*reinterpret_cast<const uint2*>(p.y + yrow * p.ldy + o0), in.r0);
+    unpack_bf16x4(*reinterpret_cast<const uint2*>(p.y + yrow * p.ldy + o0 + 64), in.r1);
+    if (p.gate) {
+      const float* g = p.gate + static_cast<long>(b) * p.gate_stride + o0;
+      const float4 a = *reinterpret_cast<const float4*>(g);
+      const float4 c = *reinterpret_cast<const float4*>(g + 64);
+      in.g0[0] = a.x; in.g0[1] = a.y; in.g0[2] = a.z; in.g0[3] = a.w;
+      in.g1[0] = c.x; in.g1[1] = c.y; in.g1[2] = c.z; in.g1[3] = c.w;
+    }
+  } else if (EPI == kEpiStore || EPI == kEpiSilu) {
+    const int o0 = m * kBM + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      in.r0[j] = p.bias ? p.bias[o0 + j] : 0.f;
+      in.r1[j] = p.bias ? p.bias[o0 + 64 + j] : 0.f;
+    }
+  } else if (EPI == kEpiQkvRope) {
+    const int head = m >> 1;
+    if (head <= p.hq) {
+      int pos = p.pos[t];
+      pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
+      const float* cs = p.rope + static_cast<long>(pos) * 256 + (m & 1) * 64 + i;
+      const float4 a = *reinterpret_cast<const float4*>(cs);
+      const float4 c = *reinterpret_cast<const float4*>(cs + 128);
+      in.c[0] = a.x; in.c[1] = a.y; in.c[2] = a.z; in.c[3] = a.w;
+      in.s[0] = c.x; in.s[1] = c.y; in.s[2] = c.z; in.s[3] = c.w;
+    }
+  }
+}
 
 // Fused epilogue for rows (i..i+3) and (i+64..i+67) of tile `m` at token t.
 template <int EPI>
-__device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int t, const float (&v0)[4],
-                                          const float (&v1)[4]) {
+__device__ __forceinline__ void epilogue_store(const LinParams& p, int m, int i, int t, const float (&v0)[4],
+                                               const float (&v1)[4], const EpiIn& in) {
   const int b = t / p.S;
   const long yrow = static_cast<long>(b) * p.y_rps + p.y_off + (t - b * p.S);
   if (EPI == kEpiStore || EPI == kEpiSilu || EPI == kEpiResidual) {
-    const int o0 = m * kBM + i, o1 = o0 + 64;
+    const int o0 = m * kBM + i;
     float r0[4], r1[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float a = v0[j], c = v1[j];
-      if (EPI != kEpiResidual && p.bias) {
-        a += p.bias[o0 + j];
-        c += p.bias[o1 + j];
-      }
-      if (EPI == kEpiSilu) {
-        a = silu(bf16_round(a));
-        c = silu(bf16_round(c));
-      }
-      r0[j] = a;
-      r1[j] = c;
-    }
-    __nv_bfloat16* y0 = p.y + yrow * p.ldy + o0;
-    __nv_bfloat16* y1 = p.y + yrow * p.ldy + o1;
-    if (EPI == kEpiResidual) {
-      const float* g = p.gate ? p.gate + static_cast<long>(b) * p.gate_stride : nullptr;
-      uint2 old0 = *reinterpret_cast<const uint2*>(y0);
-      uint2 old1 = *reinterpret_cast<const uint2*>(y1);
-      const __nv_bfloat16* h0 = reinterpret_cast<const __nv_bfloat16*>(&old0);
-      const __nv_bfloat16* h1 = reinterpret_cast<const __nv_bfloat16*>(&old1);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float a = bf16_round(r0[j]), c = bf16_round(r1[j]);
-        const float ga = g ? bf16_round(__fmul_rn(g[o0 + j], a)) : a;
-        const float gc = g ? bf16_round(__fmul_rn(g[o1 + j], c)) : c;
-        r0[j] = __fadd_rn(__bfloat162float(h0[j]), ga);
-        r1[j] = __fadd_rn(__bfloat162float(h1[j]), gc);
+      if (EPI == kEpiResidual) {
+        const float a = bf16_round(v0[j]), c = bf16_round(v1[j]);
+        const float ga = p.gate ? bf16_round(__fmul_rn(in.g0[j], a)) : a;
+        const float gc = p.gate ? bf16_round(__fmul_rn(in.g1[j], c)) : c;
+        r0[j] = __fadd_rn(in.r0[j], ga);
+        r1[j] = __fadd_rn(in.r1[j], gc);
+      } else {
+        float a = v0[j] + in.r0[j], c = v1[j] + in.r1[j];
+        if (EPI == kEpiSilu) {
+          a = silu(bf16_round(a));
+          c = silu(bf16_round(c));
+        }
+        r0[j] = a;
+        r1[j] = c;
       }
     }
-    store_bf16x4(y0, r0);
-    store_bf16x4(y1, r1);
+    store_bf16x4(p.y + yrow * p.ldy + o0, r0);
+    store_bf16x4(p.y + yrow * p.ldy + o0 + 64, r1);
   } else if (EPI == kEpiGeglu) {
     const int f = m * 64 + i;
     float r[4];
@@ -150,16 +214,12 @@ __device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int 
     const int s = t - b * p.S;
     float r0[4], r1[4];
     if (head <= p.hq) {
-      int pos = p.pos[t];
-      pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
-      const float* cs = p.rope + static_cast<long>(pos) * 256;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float x1 = bf16_round(v0[j]);
         const float x2 = bf16_round(v1[j]);
-        const float c = cs[d0 + j], sn = cs[128 + d0 + j];
-        r0[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
-        r1[j] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+        r0[j] = __fsub_rn(__fmul_rn(x1, in.c[j]), __fmul_rn(x2, in.s[j]));
+        r1[j] = __fadd_rn(__fmul_rn(x2, in.c[j]), __fmul_rn(x1, in.s[j]));
       }
     } else {
 #pragma unroll
@@ -180,6 +240,14 @@ __device__ __forceinline__ void epilogue4(const LinParams& p, int m, int i, int 
   }
 }
 
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release_na() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_na() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
 template <int NT, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const LinParams p) {
@@ -194,17 +262,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int c_begin = split * p.k_chunks / p.splits;
   const int nch = (split + 1) * p.k_chunks / p.splits - c_begin;
   const int S = p.stages;
+  const bool clustered = p.splits > 1;
 
   uint8_t* w_ring = smem;
   uint8_t* x_region = smem + S * kWTileBytes;
   float* red = reinterpret_cast<float*>(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.small_off);
+  float* recv = reinterpret_cast<float*>(smem + p.recv_off);
+  uint8_t* small = smem + p.small_off;
+  uint64_t* full = reinterpret_cast<uint64_t*>(small);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* acc_bar = empty + kMaxStages;
+  uint64_t* acc_bar = reinterpret_cast<uint64_t*>(small + 128);
   uint64_t* x_ready = acc_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_ready + 1);
-  float* rstd_s = reinterpret_cast<float*>(tmem_slot + 4);
+  uint64_t* x_full = acc_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + 160);
+  float* ss_part = reinterpret_cast<float*>(small + 176);
+  float* rstd_s = ss_part + NT;
+  float* vec_s = rstd_s + NT;  // [3][x_slots*64]: a1, a2, b2 of this CTA's K-slice
 
+  if (threadIdx.x == 0) trace(p, kTrStart);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
@@ -212,9 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(acc_bar, 1);
     mbar_init(x_ready, 4);
+    mbar_init(x_full, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
-    if (PRO == kProLoad) tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, NT);
@@ -225,6 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
+  if (threadIdx.x == 0) trace(p, kTrSetup);
+  // the norm prologue exchanges partial sums over the cluster; the producer and
+  // MMA warps take part in that barrier phase without waiting for it here
+  if (PRO == kProNorm && clustered && warp < 2) cluster_arrive_relaxed();
 
   int issued = 0;  // chunks whose TMA the producer issued
   if (warp == 0) {
@@ -236,9 +316,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[i], bytes);
         tma_load_2d_hint(w_ring + i * kWTileBytes, &tmW, &full[i], (c_begin + i) * kBK, m_tile * kBM, pol);
       }
+      trace(p, kTrWIssued);
       pdl_wait();
-      if (PRO == kProLoad)
+      trace(p, kTrPdl);
+      if (PRO == kProLoad) {
         for (int i = 0; i < first; ++i) tma_load_2d(x_region + i * XT, &tmX, &full[i], (c_begin + i) * kBK, n0);
+      } else {
+        mbar_arrive_expect_tx(x_full, nch * XT);
+        for (int j = 0; j < nch; ++j) tma_load_2d(x_region + j * XT, &tmX, x_full, (c_begin + j) * kBK, n0);
+      }
       issued = first;
       for (int i = first; i < nch; ++i) {
         const int s = i % S;
@@ -257,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < nch && ok; ++i) {
         const int s = i % S;
         if (!mbar_wait(&full[s], (i / S) & 1, p.status, kDevTimeoutTmaFull)) break;
+        if (i == 0) trace(p, kTrFirstFull);
         tc_fence_after();
         const uint32_t a_base = smem_u32(w_ring + s * kWTileBytes);
         const uint32_t b_base = smem_u32(x_region + (PRO == kProLoad ? s : i) * XT);
@@ -269,85 +356,185 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(acc_bar);
+      trace(p, kTrMmaIssued);
     }
   } else {
     const int et = threadIdx.x - 64;  // 0..127
+    const int wq = warp - 2;
+    pdl_wait();
+    if (p.stage_off > 0) {
+      // while the weights stream, fetch the epilogue's global operands of every
+      // item of this CTA into shared memory (4 items' loads in flight per thread)
+      const int pairs = 64 / p.splits;
+      const int quads = pairs / 4;
+      const int items = quads * NT;
+      EpiIn* stage = reinterpret_cast<EpiIn*>(smem + p.stage_off);
+      for (int it0 = et; it0 < items; it0 += 4 * 128) {
+        EpiIn in[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int it = it0 + u * 128;
+          const int t = n0 + it / quads;
+          if (it < items && t < p.T) epilogue_fetch<EPI>(p, m_tile, split * pairs + (it % quads) * 4, t, in[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (it0 + u * 128 < items) stage[it0 + u * 128] = in[u];
+      }
+    }
     if (PRO == kProNorm) {
-      pdl_wait();
-      const int wq = warp - 2;
+      // norm vectors of this CTA's K-slice -> shared memory
+      const int kw4 = nch * kBK / 4;  // float4s per vector (<= 256)
+      const bool shared_vec = p.ab_stride == 0;
+      {
+        float4 va[2], vb[2], vc[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int e = et + q * 128;
+          if (e < kw4) {
+            const int k = c_begin * kBK + 4 * e;
+            va[q] = *reinterpret_cast<const float4*>(p.a1 + k);
+            vb[q] = (shared_vec && p.a2) ? *reinterpret_cast<const float4*>(p.a2 + k) : make_float4(1.f, 1.f, 1.f, 1.f);
+            vc[q] = (shared_vec && p.b2) ? *reinterpret_cast<const float4*>(p.b2 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int e = et + q * 128;
+          if (e < kw4) {
+            reinterpret_cast<float4*>(vec_s)[e] = va[q];
+            reinterpret_cast<float4*>(vec_s + p.x_slots * kBK)[e] = vb[q];
+            reinterpret_cast<float4*>(vec_s + 2 * p.x_slots * kBK)[e] = vc[q];
+          }
+        }
+      }
+      const bool ok = mbar_wait(x_full, 0, p.status, kDevTimeoutTmaFull);
+      if (et == 0) trace(p, kTrXFull);
+      // partial sum of squares of every token over this CTA's K-slice
       for (int tt = wq; tt < NT; tt += 4) {
-        const int t = n0 + tt;
         float ss = 0.f;
-        if (t < p.T) {
-          const __nv_bfloat16* xr = p.x + static_cast<long>(t) * p.ldx;
-          for (int k = lane * 8; k < p.K; k += 256) {
-            uint4 raw = *reinterpret_cast<const uint4*>(xr + k);
+        if (ok) {
+          for (int c = lane; c < nch * 8; c += 32) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(x_region + (c >> 3) * XT + sw128_offset(tt, c & 7));
             const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              float2 f = __bfloat1622float2(h2[j]);
+              const float2 f = __bfloat1622float2(h2[j]);
               ss = fmaf(f.x, f.x, ss);
               ss = fmaf(f.y, f.y, ss);
             }
           }
-          ss = warp_sum(ss);
         }
-        if (lane == 0) rstd_s[tt] = t < p.T ? rsqrtf(ss / static_cast<float>(p.K) + p.eps) : 0.f;
+        ss = warp_sum(ss);
+        if (lane == 0) ss_part[tt] = ss;
+      }
+      if (clustered) {
+        cluster_arrive_release_na();
+        cluster_wait_na();
+      } else {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      // rstd from the partial sums of every CTA in the cluster (fixed order)
+      for (int tt = et; tt < NT; tt += 128) {
+        float tot = 0.f;
+        if (clustered) {
+          float part[16];
+          const uint32_t a = smem_u32(ss_part + tt);
+#pragma unroll
+          for (int r = 0; r < 16; ++r)
+            if (r < p.splits) part[r] = ld_dsmem_f32(mapa_shared(a, r));
+#pragma unroll
+          for (int r = 0; r < 16; ++r)
+            if (r < p.splits) tot += part[r];
+        } else {
+          tot = ss_part[tt];
+        }
+        rstd_s[tt] = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      // normalize the tile in place
       const int items = nch * NT * 8;
       for (int it = et; it < items; it += 128) {
         const int cc = it & 7;
         const int tt = (it >> 3) % NT;
         const int j = it / (8 * NT);
         const int t = n0 + tt;
+        uint4* cell = reinterpret_cast<uint4*>(x_region + j * XT + sw128_offset(tt, cc));
         uint4 outv = make_uint4(0u, 0u, 0u, 0u);
         if (t < p.T) {
-          const int k = (c_begin + j) * kBK + cc * 8;
-          const int b = t / p.S;
-          uint4 raw = *reinterpret_cast<const uint4*>(p.x + static_cast<long>(t) * p.ldx + k);
+          const uint4 raw = *cell;
           const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&raw);
           const float r = rstd_s[tt];
+          const int e0 = j * kBK + cc * 8;
+          const long bo = static_cast<long>(t / p.S) * p.ab_stride + c_begin * kBK + e0;
           float y[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            float v = __fmul_rn(__fmul_rn(__bfloat162float(xv[e]), r), p.a1[k + e]);
-            if (p.a2) v = __fmul_rn(v, p.a2[b * p.ab_stride + k + e]);
-            if (p.b2) v = __fadd_rn(v, p.b2[b * p.ab_stride + k + e]);
+            const float a1 = vec_s[e0 + e];
+            const float a2 = shared_vec ? vec_s[p.x_slots * kBK + e0 + e] : (p.a2 ? p.a2[bo + e] : 1.f);
+            const float b2 = shared_vec ? vec_s[2 * p.x_slots * kBK + e0 + e] : (p.b2 ? p.b2[bo + e] : 0.f);
+            float v = __fmul_rn(__fmul_rn(__bfloat162float(xv[e]), r), a1);
+            if (p.a2) v = __fmul_rn(v, a2);
+            if (p.b2) v = __fadd_rn(v, b2);
             y[e] = v;
           }
           outv = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
                             pack_bf16x2(y[6], y[7]));
         }
-        *reinterpret_cast<uint4*>(x_region + j * XT + sw128_offset(tt, cc)) = outv;
+        *cell = outv;
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(x_ready);
-    } else {
-      pdl_wait();  // the epilogue reads tensors written by earlier kernels
+      if (et == 0) trace(p, kTrXReady);
     }
     // accumulator -> shared partial tile red[t][row]
     const bool ok = mbar_wait(acc_bar, 0, p.status, kDevTimeoutMmaDone);
     tc_fence_after();
+    if (et == 0) trace(p, kTrAcc);
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     if (ok) {
-#pragma unroll 1
-      for (int c = 0; c < NT / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r);
+      // push mode: this row's partial goes to the CTA that reduces its pair
+      const int pairs = 64 / p.splits;
+      const int pr = row & 63;
+      const int owner = pr / pairs;
+      const int lr = (pr - owner * pairs) + (row >= 64 ? pairs : 0);
+      const uint32_t dst =
+          p.push ? mapa_shared(smem_u32(recv + static_cast<long>(split * 2 * pairs + lr) * NT), owner) : 0u;
+#pragma unroll
+      for (int c0 = 0; c0 < NT / 16; c0 += 4) {
+        uint32_t r[4][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (c0 + q < NT / 16) tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + (c0 + q) * 16, r[q]);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) red[(c * 16 + j) * kRedLd + row] = __uint_as_float(r[j]);
+        for (int q = 0; q < 4; ++q) {
+          if (c0 + q >= NT / 16) continue;
+          if (p.push) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_dsmem_f4(dst + static_cast<uint32_t>(((c0 + q) * 16 + 4 * j) * 4), __uint_as_float(r[q][4 * j]),
+                          __uint_as_float(r[q][4 * j + 1]), __uint_as_float(r[q][4 * j + 2]),
+                          __uint_as_float(r[q][4 * j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) red[((c0 + q) * 16 + j) * kRedLd + row] = __uint_as_float(r[q][j]);
+          }
+        }
       }
     }
-    (void)et;
+    if (et == 0) trace(p, kTrRed);
   }
-  if (warp == 0) pdl_wait();
+  pdl_wait();
   tc_fence_before();
   __syncthreads();
-  if (p.splits > 1) cluster_sync();
+  if (clustered) {
+    if (PRO == kProNorm && warp < 2) cluster_wait_na();  // completes the prologue phase
+    cluster_sync();
+  }
+  if (threadIdx.x == 64) trace(p, kTrCluster);
 
   // ---- reduction over the cluster + fused epilogue (all threads) ----
   {
@@ -362,27 +549,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = n0 + tt;
       if (t >= p.T) continue;
       const int i = pair0 + qd * 4;
+      EpiIn in;
+      if (p.stage_off > 0)
+        in = reinterpret_cast<const EpiIn*>(smem + p.stage_off)[it];
+      else
+        epilogue_fetch<EPI>(p, m_tile, i, t, in);
       float v0[4] = {0.f, 0.f, 0.f, 0.f}, v1[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t off0 = red_s + static_cast<uint32_t>((tt * kRedLd + i) * 4);
-      const uint32_t off1 = off0 + 64 * 4;
-      if (p.splits == 1) {
+      if (p.push) {
+        // every CTA of the cluster pushed its partial of these rows here: local sums, fixed order
+        const int lr0 = qd * 4;
+        for (int src = 0; src < p.splits; ++src) {
+          const float* base = recv + static_cast<long>(src * 2 * pairs) * NT + tt;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v0[j] += base[(lr0 + j) * NT];
+            v1[j] += base[(pairs + lr0 + j) * NT];
+          }
+        }
+      } else if (!clustered) {
         const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + i);
         const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + i + 64);
         v0[0] = a.x; v0[1] = a.y; v0[2] = a.z; v0[3] = a.w;
         v1[0] = c.x; v1[1] = c.y; v1[2] = c.z; v1[3] = c.w;
       } else {
-        for (int r = 0; r < p.splits; ++r) {
-          const float4 a = ld_dsmem_f4(mapa_shared(off0, r));
-          const float4 c = ld_dsmem_f4(mapa_shared(off1, r));
-          v0[0] += a.x; v0[1] += a.y; v0[2] += a.z; v0[3] += a.w;
-          v1[0] += c.x; v1[1] += c.y; v1[2] += c.z; v1[3] += c.w;
+        const uint32_t off0 = red_s + static_cast<uint32_t>((tt * kRedLd + i) * 4);
+        const uint32_t off1 = off0 + 64 * 4;
+        for (int r0 = 0; r0 < p.splits; r0 += 8) {
+          float4 a[8], c[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (r0 + q < p.splits) {
+              a[q] = ld_dsmem_f4(mapa_shared(off0, r0 + q));
+              c[q] = ld_dsmem_f4(mapa_shared(off1, r0 + q));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (r0 + q < p.splits) {
+              v0[0] += a[q].x; v0[1] += a[q].y; v0[2] += a[q].z; v0[3] += a[q].w;
+              v1[0] += c[q].x; v1[1] += c[q].y; v1[2] += c[q].z; v1[3] += c[q].w;
+            }
+          }
         }
       }
-      epilogue4<EPI>(p, m_tile, i, t, v0, v1);
+      epilogue_store<EPI>(p, m_tile, i, t, v0, v1, in);
     }
   }
+  if (threadIdx.x == 64) trace(p, kTrEpi);
 
-  if (p.splits > 1) cluster_sync();
+  // pull mode reads peers' shared memory: keep it alive until every CTA is done
+  if (clustered && !p.push) cluster_sync();
   // drain: a producer that stopped early waits (bounded) for its TMA writes
   if (warp == 0 && lane == 0) {
     for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
@@ -395,23 +611,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, NT);
   }
+  if (threadIdx.x == 0) trace(p, kTrEnd);
 }
 
 struct Config {
-  int nt, splits, stages, x_slots, small_off, smem;
+  int nt, splits, stages, x_slots, small_off, smem, push, recv_off, stage_off;
 };
+
+int small_bytes(int nt, bool norm, int x_slots) {
+  const int b = 176 + 8 * nt + (norm ? 3 * x_slots * kBK * 4 : 0);
+  return (b + 127) & ~127;
+}
 
 int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
   int nt = d.n_tile;
   if (nt == 0) nt = d.T <= 64 ? 64 : (d.T <= 128 ? 128 : 256);
   if (nt != 64 && nt != 128 && nt != 256) return set_error(RFX_E_INVAL, "rfx_linear: n_tile must be 64, 128 or 256");
+  const bool norm = d.prologue == RFX_PRO_NORM;
   const int m_tiles = d.O / kBM;
   const int n_tiles = (d.T + nt - 1) / nt;
   const int chunks = d.K / kBK;
   int splits = d.splits;
   if (splits == 0) {
     splits = 1;
-    for (int s : {2, 4, 8, 16}) {
+    // clusters of at most 8 CTAs: larger ones wait for whole free GPCs, which
+    // kernels overlapping under programmatic dependent launch rarely leave
+    for (int s : {2, 4, 8}) {
       if (s > chunks) break;
       if (m_tiles * n_tiles * s <= num_sms) splits = s;
     }
@@ -419,30 +644,53 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
   if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16)
     return set_error(RFX_E_INVAL, "rfx_linear: splits must be 1, 2, 4, 8 or 16");
   if (splits > chunks) return set_error(RFX_E_INVAL, "rfx_linear: splits exceeds K/64");
-  const int max_nch = (chunks + splits - 1) / splits;
   const int xt = nt * 128;
-  const int small = 2 * kMaxStages * 8 + 16 + 16 + nt * 4 + 64;
-  const int budget = kSmemLimit - 1024 - small;
+  auto budget_for = [&](int xs) { return kSmemLimit - 1024 - small_bytes(nt, norm, xs); };
+  if (norm && d.splits == 0) {
+    // the normalized K-slice of a CTA stays resident: split K further (or
+    // shrink the token tile) until it fits next to one weight stage
+    auto fits = [&](int s) {
+      const int xs = (chunks + s - 1) / s;
+      return xs * xt <= budget_for(xs) - kWTileBytes;
+    };
+    while (!fits(splits) && splits < 16 && splits * 2 <= chunks) splits *= 2;
+    if (!fits(splits) && d.n_tile == 0 && nt > 64) {
+      rfx_linear_desc smaller = d;
+      smaller.n_tile = nt / 2;
+      return pick_config(smaller, num_sms, cfg);
+    }
+  }
+  const int max_nch = (chunks + splits - 1) / splits;
+  // split-K partials are pushed into a dedicated receive buffer (TMA-fed X only)
+  const int push = (!norm && splits > 1) ? 1 : 0;
+  const int recv_bytes = push ? 128 * nt * 4 : 0;
+  // epilogue operands staged in shared memory during the mainloop
+  const int items = (16 / splits) * nt;
+  int stage_bytes = (!norm && d.epilogue != RFX_EPI_GEGLU) ? items * static_cast<int>(sizeof(EpiIn)) : 0;
+  if (stage_bytes > 48 * 1024) stage_bytes = 0;
   int stages, x_slots;
-  if (d.prologue == RFX_PRO_NORM) {
+  if (norm) {
     x_slots = max_nch;
-    const int left = budget - x_slots * xt;
+    const int left = budget_for(x_slots) - x_slots * xt;
     stages = std::min({max_nch, kMaxStages, left / kWTileBytes});
     if (stages < 1) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: K slice too long for the norm prologue; raise splits");
   } else {
-    stages = std::min({max_nch, kMaxStages, budget / (kWTileBytes + xt)});
+    stages = std::min({max_nch, kMaxStages, (budget_for(0) - recv_bytes - stage_bytes) / (kWTileBytes + xt)});
     x_slots = stages;
     if (stages < 1) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: tile does not fit in shared memory");
   }
   int body = stages * kWTileBytes + x_slots * xt;
-  body = std::max(body, nt * kRedLd * 4);
+  if (!push) body = std::max(body, nt * kRedLd * 4);
   body = (body + 127) & ~127;
   cfg->nt = nt;
   cfg->splits = splits;
   cfg->stages = stages;
   cfg->x_slots = x_slots;
-  cfg->small_off = body;
-  cfg->smem = body + small + 1024;
+  cfg->push = push;
+  cfg->recv_off = body;
+  cfg->stage_off = stage_bytes ? body + recv_bytes : 0;
+  cfg->small_off = body + recv_bytes + stage_bytes;
+  cfg->smem = cfg->small_off + small_bytes(nt, norm, x_slots) + 1024;
   if (cfg->smem > kSmemLimit) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: shared memory %d too large", cfg->smem);
   return RFX_OK;
 }
@@ -486,10 +734,15 @@ int validate(const rfx_linear_desc& d) {
   if (d.epilogue < RFX_EPI_STORE || d.epilogue > RFX_EPI_GEGLU) return set_error(RFX_E_INVAL, "rfx_linear: epilogue");
   if (!d.w || !d.x || !aligned16(d.w) || !aligned16(d.x) || d.ldx < d.K || d.ldx % 8)
     return set_error(RFX_E_INVAL, "rfx_linear: w/x must be 16-byte aligned and ldx>=K, ldx%%8==0");
-  if (d.prologue == RFX_PRO_NORM && !d.norm_a1) return set_error(RFX_E_INVAL, "rfx_linear: norm_a1 required");
+  if (d.prologue == RFX_PRO_NORM &&
+      (!d.norm_a1 || !aligned16(d.norm_a1) || (d.norm_a2 && !aligned16(d.norm_a2)) ||
+       (d.norm_b2 && !aligned16(d.norm_b2)) || d.norm_ab_stride % 4))
+    return set_error(RFX_E_INVAL, "rfx_linear: norm vectors must be 16-byte aligned (norm_a1 required)");
+  if (d.gate && (reinterpret_cast<uintptr_t>(d.gate) & 15u || d.gate_stride % 4))
+    return set_error(RFX_E_INVAL, "rfx_linear: gate must be 16-byte aligned with gate_stride%%4==0");
   if (d.epilogue == RFX_EPI_QKV_ROPE) {
     if (d.O != (d.num_q_heads + 2) * 256 || !d.q_out || !d.k_out || !d.v_out || !d.rope_table || !d.positions ||
-        d.rope_max_pos < 1)
+        d.rope_max_pos < 1 || !aligned16(d.rope_table))
       return set_error(RFX_E_INVAL, "rfx_linear: QKV_ROPE needs O=(Hq+2)*256 and q/k/v/rope/positions");
   } else if (d.epilogue == RFX_EPI_GEGLU) {
     if (!d.y || d.ldy < d.O / 2 || d.ldy % 4) return set_error(RFX_E_INVAL, "rfx_linear: GEGLU output");
@@ -513,11 +766,7 @@ int build_linear_maps(const rfx_linear_desc& d, CUtensorMap* tmW, CUtensorMap* t
   if (rc) return rc;
   rc = make_tmap_2d(tmW, d.w, 2, d.K, d.O, static_cast<uint64_t>(d.K) * 2, kBK, kBM, true);
   if (rc) return rc;
-  if (d.prologue == RFX_PRO_LOAD)
-    rc = make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, cfg.nt, true);
-  else
-    *tmX = *tmW;  // unused by the norm prologue
-  return rc;
+  return make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, cfg.nt, true);
 }
 
 int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, cudaStream_t stream,
@@ -577,7 +826,11 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   p.hq = d.num_q_heads;
   p.y_rps = d.y_rows_per_batch > 0 ? d.y_rows_per_batch : d.tokens_per_batch;
   p.y_off = d.y_rows_per_batch > 0 ? d.y_row_offset : 0;
+  p.push = cfg.push;
+  p.recv_off = cfg.recv_off;
+  p.stage_off = cfg.stage_off;
   p.status = device_status_ptr();
+  p.trace = static_cast<unsigned long long*>(trace_buffer(m_tiles * cfg.splits * n_tiles * 16));
 
   dim3 grid(m_tiles * cfg.splits, n_tiles, 1);
   CUtensorMap w = *tmW, x = *tmX;

@@ -18,6 +18,10 @@ int check_cuda(cudaError_t e, const char* what);
 // Device address of the library's status word on the current device.
 int* device_status_ptr();
 
+// Device buffer for per-CTA phase timestamps (rfx_set_trace), or nullptr when
+// tracing is off or the buffer holds fewer than n_events 8-byte slots.
+void* trace_buffer(size_t n_events);
+
 // Whether kernels are launched with programmatic dependent launch.
 bool pdl_enabled();
 
@@ -85,5 +89,6 @@ int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pd
 int launch_action_in(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
 int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
 int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl);
+int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl);
 
 }  // namespace rfx

@@ -34,6 +34,17 @@ int check_cuda(cudaError_t e, const char* what) {
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 
+// ------------------------------------------------------------ tracing ---
+namespace {
+std::atomic<void*> g_trace_buf{nullptr};
+std::atomic<size_t> g_trace_bytes{0};
+}  // namespace
+
+void* trace_buffer(size_t n_events) {
+  void* b = g_trace_buf.load();
+  return (b && n_events * 8 <= g_trace_bytes.load()) ? b : nullptr;
+}
+
 // ------------------------------------------------------------ status word ---
 namespace {
 __device__ int g_device_status = 0;
@@ -91,6 +102,11 @@ int ensure_smem_attr(const void* func, int bytes, bool nonportable_cluster) {
   if (it != done.end() && it->second >= bytes) return RFX_OK;
   int rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                       "cudaFuncSetAttribute(smem)");
+  if (rc) return rc;
+  // one carveout (all shared memory) for every kernel of the library, so the
+  // SMs are not re-partitioned between consecutive launches
+  rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+                  "cudaFuncSetAttribute(carveout)");
   if (rc) return rc;
   if (nonportable_cluster) {
     rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
@@ -183,6 +199,13 @@ using namespace rfx;
 extern "C" int rfx_version(void) { return 100; }
 
 extern "C" const char* rfx_last_error(void) { return g_last_error; }
+
+extern "C" int rfx_set_trace(void* buf, size_t bytes) {
+  if (buf && (reinterpret_cast<uintptr_t>(buf) & 7u)) return set_error(RFX_E_INVAL, "rfx_set_trace: 8-byte alignment");
+  g_trace_bytes.store(buf ? bytes : 0);
+  g_trace_buf.store(buf);
+  return RFX_OK;
+}
 
 extern "C" int rfx_set_pdl(int enable) {
   g_pdl.store(enable != 0);
@@ -286,7 +309,11 @@ struct TailOp {
 struct CopyOp {
   rfx_copy_rows_desc d;
 };
-using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp>;
+struct NormOp {
+  rfx_norm_desc d;
+};
+struct BarrierOp {};
+using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp, NormOp, BarrierOp>;
 }  // namespace
 
 struct rfx_plan {
@@ -307,7 +334,22 @@ int run_op(const Op& op, cudaStream_t s, bool pdl) {
   if (auto* o = std::get_if<InOp>(&op)) return launch_action_in(o->d, s, pdl);
   if (auto* o = std::get_if<TailOp>(&op)) return launch_euler_tail(o->d, s, pdl);
   if (auto* o = std::get_if<CopyOp>(&op)) return launch_copy_rows(o->d, s, pdl);
+  if (auto* o = std::get_if<NormOp>(&op)) return launch_rms_norm(o->d, s, pdl);
   return set_error(RFX_E_STATE, "plan: unknown op");
+}
+// Launches every op in order; an op that follows a BarrierOp runs without PDL.
+int run_ops(const std::vector<Op>& ops, cudaStream_t s, bool pdl) {
+  bool serialize = false;
+  for (const Op& op : ops) {
+    if (std::holds_alternative<BarrierOp>(op)) {
+      serialize = true;
+      continue;
+    }
+    int rc = run_op(op, s, pdl && !serialize);
+    if (rc) return rc;
+    serialize = false;
+  }
+  return RFX_OK;
 }
 void release_graph(rfx_plan* p) {
   if (p->exec) cudaGraphExecDestroy(p->exec);
@@ -397,6 +439,20 @@ extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* 
   return RFX_OK;
 }
 
+extern "C" int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc) {
+  PLAN_GUARD(plan);
+  plan->ops.emplace_back(NormOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+
+extern "C" int rfx_plan_add_barrier(rfx_plan* plan) {
+  if (!plan) return set_error(RFX_E_INVAL, "plan: null argument");
+  if (plan->exec) return set_error(RFX_E_STATE, "plan: already captured");
+  plan->ops.emplace_back(BarrierOp{});
+  return RFX_OK;
+}
+
 extern "C" int rfx_plan_num_launches(const rfx_plan* plan, int* out) {
   if (!plan || !out) return set_error(RFX_E_INVAL, "rfx_plan_num_launches: null");
   *out = plan->launches;
@@ -406,12 +462,7 @@ extern "C" int rfx_plan_num_launches(const rfx_plan* plan, int* out) {
 extern "C" int rfx_plan_run(rfx_plan* plan, void* stream) {
   if (!plan) return set_error(RFX_E_INVAL, "rfx_plan_run: null plan");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool pdl = pdl_enabled();
-  for (const Op& op : plan->ops) {
-    int rc = run_op(op, s, pdl);
-    if (rc) return rc;
-  }
-  return RFX_OK;
+  return run_ops(plan->ops, s, pdl_enabled());
 }
 
 extern "C" int rfx_plan_capture(rfx_plan* plan, void* stream) {
@@ -421,12 +472,7 @@ extern "C" int rfx_plan_capture(rfx_plan* plan, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = check_cuda(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
   if (rc) return rc;
-  const bool pdl = pdl_enabled();
-  int run_rc = RFX_OK;
-  for (const Op& op : plan->ops) {
-    run_rc = run_op(op, s, pdl);
-    if (run_rc) break;
-  }
+  const int run_rc = run_ops(plan->ops, s, pdl_enabled());
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (run_rc) {

@@ -88,6 +88,7 @@ class ActionExpertEngine:
         self.T = T
         z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
         self.h = z(T, W)
+        self.xn = z(T, W)  # normalized GEMM input (input / post-attention norm)
         self.q = z(batch, H, St, D)
         self.k_new, self.v_new = z(T, D), z(T, D)
         self.attn_out = z(T, H * D)
@@ -141,7 +142,9 @@ class ActionExpertEngine:
     def _build_ops(self) -> None:
         cfg, B, S, St, T = self.cfg, self.B, self.S, self.St, self.T
         W, H, D = cfg.width, cfg.num_heads, cfg.head_dim
-        ops = []
+        # the chunk starts after everything before it has completed: kernels of
+        # the chunk read the KV ring before waiting on their predecessor
+        ops = [("barrier", None, None)]
         if cfg.variant == "pi05":
             ops.append(("time", K.time_cond_desc(t=self.t, w_in=self.tin_w, b_in=self.tin_b, w_out=self.tout_w,
                                                  b_out=self.tout_b, hidden=self.tc_hidden, cond=self.cond,
@@ -185,23 +188,27 @@ class ActionExpertEngine:
                                                     y_rows_per_batch=St, y_row_offset=1), None))
             for l in range(nl):
                 ni, npo = 2 * l, 2 * l + 1
+                ops.append(("norm", K.norm_desc(x=self.h, y=self.xn, S=St, norm_a1=self.norm_a1[ni],
+                                                norm_a2=a2(tau, ni), norm_b2=b2(tau, ni), eps=cfg.eps),
+                            ("norm_in", tau, l)))
                 ops.append(("linear", K.linear_desc(
-                    w=self.w_qkv[l], x=self.h, T=T, S=St, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_QKV_ROPE,
-                    norm_a1=self.norm_a1[ni], norm_a2=a2(tau, ni), norm_b2=b2(tau, ni), eps=cfg.eps,
+                    w=self.w_qkv[l], x=self.xn, T=T, S=St, epilogue=L.RFX_EPI_QKV_ROPE,
                     rope_table=self.rope, positions=self.positions, q_out=self.q, k_out=self.k_new,
                     v_out=self.v_new, num_q_heads=H), ("qkv", tau, l)))
                 ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l],
                                       n_ctx=self.n_ctx, out=self.attn_out, softmax_scale=D ** -0.5,
-                                      new_block=self.new_block, kv_splits=self.kv_splits)
+                                      new_block=self.new_block if cfg.variant == "pi0" else None,
+                                      kv_splits=self.kv_splits)
                 attn_descs.append(ad)
                 ops.append(("attn", ad, ("attn", tau, l)))
                 ops.append(("linear", K.linear_desc(
                     w=self.w_o[l], x=self.attn_out, T=T, S=St, epilogue=L.RFX_EPI_RESIDUAL, y=self.h,
                     gate=gt(tau, ni)), ("o", tau, l)))
+                ops.append(("norm", K.norm_desc(x=self.h, y=self.xn, S=St, norm_a1=self.norm_a1[npo],
+                                                norm_a2=a2(tau, npo), norm_b2=b2(tau, npo), eps=cfg.eps),
+                            ("norm_post", tau, l)))
                 ops.append(("linear", K.linear_desc(
-                    w=self.w_gu[l], x=self.h, T=T, S=St, prologue=L.RFX_PRO_NORM, epilogue=L.RFX_EPI_GEGLU,
-                    y=self.act, norm_a1=self.norm_a1[npo], norm_a2=a2(tau, npo), norm_b2=b2(tau, npo),
-                    eps=cfg.eps), ("gu", tau, l)))
+                    w=self.w_gu[l], x=self.xn, T=T, S=St, epilogue=L.RFX_EPI_GEGLU, y=self.act), ("gu", tau, l)))
                 ops.append(("linear", K.linear_desc(
                     w=self.w_down[l], x=self.act, T=T, S=St, epilogue=L.RFX_EPI_RESIDUAL, y=self.h,
                     gate=gt(tau, npo)), ("layer", tau, l)))
@@ -230,11 +237,13 @@ class ActionExpertEngine:
 
     # ---------------------------------------------------------- execution ---
     def _kind(self, kind):
-        return kind if kind in ("in", "tail") else None
+        return kind if kind in ("in", "tail", "barrier") else None
 
     def run_eager(self, hook=None) -> None:
         """Runs the chunk op by op through the direct C entry points."""
         for kind, desc, tag in self.ops:
+            if kind == "barrier":
+                continue
             K.Plan.run_direct(desc, self._kind(kind))
             if hook is not None and tag is not None:
                 hook(tag)

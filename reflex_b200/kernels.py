@@ -108,7 +108,7 @@ def pack_weight(kind: int, w: torch.Tensor) -> torch.Tensor:
 def linear_desc(*, w, x, T, S, prologue=L.RFX_PRO_LOAD, epilogue=L.RFX_EPI_STORE, y=None, norm_a1=None,
                 norm_a2=None, norm_b2=None, norm_ab_stride=0, eps=1e-6, bias=None, gate=None, gate_stride=0,
                 rope_table=None, positions=None, q_out=None, k_out=None, v_out=None, num_q_heads=0,
-                n_tile=0, splits=0) -> L.LinearDesc:
+                n_tile=0, splits=0, y_rows_per_batch=0, y_row_offset=0) -> L.LinearDesc:
     _need_cuda(w, x, y)
     for t in (w, x, y, q_out, k_out, v_out):
         if t is not None and t.dtype != torch.bfloat16:
@@ -133,6 +133,7 @@ def linear_desc(*, w, x, T, S, prologue=L.RFX_PRO_LOAD, epilogue=L.RFX_EPI_STORE
     d.q_out, d.k_out, d.v_out = L.ptr(q_out), L.ptr(k_out), L.ptr(v_out)
     d.num_q_heads = num_q_heads
     d.n_tile, d.splits = n_tile, splits
+    d.y_rows_per_batch, d.y_row_offset = y_rows_per_batch, y_row_offset
     return d
 
 
@@ -244,6 +245,28 @@ def euler_tail(**kw) -> None:
     L.call("rfx_euler_tail", ctypes.byref(d), _stream())
 
 
+def norm_desc(*, x, y, S, norm_a1, norm_a2=None, norm_b2=None, norm_ab_stride=0, eps=1e-6, T=None) -> L.NormDesc:
+    _need_cuda(x, y, norm_a1)
+    if x.dtype != torch.bfloat16 or y.dtype != torch.bfloat16:
+        raise ValueError("rms_norm maps bf16 rows to bf16 rows")
+    for t in (norm_a1, norm_a2, norm_b2):
+        if t is not None and t.dtype != torch.float32:
+            raise ValueError("norm vectors are fp32")
+    d = L.NormDesc()
+    d.T = x.shape[0] if T is None else T
+    d.K, d.tokens_per_batch = x.shape[1], S
+    d.x, d.ldx = x.data_ptr(), x.stride(0)
+    d.norm_a1, d.norm_a2, d.norm_b2 = L.ptr(norm_a1), L.ptr(norm_a2), L.ptr(norm_b2)
+    d.norm_ab_stride, d.eps = norm_ab_stride, eps
+    d.y, d.ldy = y.data_ptr(), y.stride(0)
+    return d
+
+
+def rms_norm(**kw) -> None:
+    d = norm_desc(**kw)
+    L.call("rfx_rms_norm", ctypes.byref(d), _stream())
+
+
 def copy_rows_desc(*, dst, src, rows, width, dst_rows_per_group, dst_row_offset=0, group=None,
                    src_ld=None) -> L.CopyRowsDesc:
     _need_cuda(dst, src)
@@ -281,6 +304,7 @@ class Plan:
         L.TimeCondDesc: "rfx_plan_add_time_cond",
         L.ModulationDesc: "rfx_plan_add_modulation",
         L.CopyRowsDesc: "rfx_plan_add_copy_rows",
+        L.NormDesc: "rfx_plan_add_rms_norm",
     }
     # direct (non-plan) entry point of each descriptor kind, for eager execution
     DIRECT = {
@@ -290,6 +314,7 @@ class Plan:
         L.TimeCondDesc: "rfx_time_cond",
         L.ModulationDesc: "rfx_modulation",
         L.CopyRowsDesc: "rfx_copy_rows",
+        L.NormDesc: "rfx_rms_norm",
     }
 
     @classmethod
@@ -306,6 +331,9 @@ class Plan:
         self.captured = False
 
     def add(self, desc, kind: str | None = None) -> None:
+        if kind == "barrier":
+            L.call("rfx_plan_add_barrier", self._h)
+            return
         name = self._ADD.get(type(desc))
         if isinstance(desc, L.ActionIoDesc):
             name = {"in": "rfx_plan_add_action_in", "tail": "rfx_plan_add_euler_tail"}[kind]

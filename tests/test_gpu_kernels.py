@@ -149,6 +149,28 @@ def test_linear_norm_prologue_epilogues(K, L, epi):
     torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("K_,shared", [(1024, True), (2048, False)])
+def test_rms_norm_exact(K, K_, shared):
+    """The norm kernel rounds once to bf16 like AdaRMSNorm (reflex/policies/pi05/modeling_pi05.py:73-99);
+    against the fp32 torch computation it may differ by one bf16 ulp (summation order of mean(x^2))."""
+    r = gen(8)
+    B, S = 3, 50
+    x = (r(B * S, K_) * 2).bfloat16().cuda()
+    a1 = (1 + r(K_, std=0.1)).cuda()
+    a2 = (1 + r(1 if shared else B, K_, std=0.2)).cuda()
+    b2 = r(1 if shared else B, K_, std=0.1).cuda()
+    y = torch.empty_like(x)
+    K.rms_norm(x=x, y=y, S=S, norm_a1=a1, norm_a2=a2, norm_b2=b2, norm_ab_stride=0 if shared else K_)
+    torch.cuda.synchronize()
+    xf = x.float().cpu()
+    rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    bidx = torch.zeros(B * S, dtype=torch.long) if shared else torch.arange(B * S) // S
+    ref = ((xf * rstd) * a1.cpu()) * a2.cpu()[bidx] + b2.cpu()[bidx]
+    diff = (y.float().cpu() - ref.bfloat16().float()).abs()
+    ulp = ref.abs().clamp_min(1e-30) * 2 ** -7
+    assert (diff <= ulp + 1e-6).all()
+
+
 def rope_table(max_pos=8192, D=256, base=10000.0):
     inv = 1.0 / (base ** (torch.arange(0, D, 2, dtype=torch.float) / D))
     t = torch.arange(max_pos, dtype=torch.float)
