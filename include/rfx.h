@@ -153,7 +153,7 @@ typedef struct rfx_linear_desc {
   void* v_out;          /* bf16 [T][256] */
   int num_q_heads;
   int n_tile; /* tokens per MMA tile: 0 (auto), 64, 128 or 256 */
-  int splits; /* CTAs per cluster along K: 0 (auto), 1, 2, 4, 8 or 16 */
+  int splits; /* CTAs per cluster along K: 0 (auto), 1, 2, 4 or 8 */
   /* Output row of token t for STORE/SILU/RESIDUAL/GEGLU:
    * (t / S) * y_rows_per_batch + y_row_offset + t % S; 0/0 means row t. */
   int y_rows_per_batch;

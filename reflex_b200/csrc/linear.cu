@@ -641,8 +641,8 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
       if (m_tiles * n_tiles * s <= num_sms) splits = s;
     }
   }
-  if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16)
-    return set_error(RFX_E_INVAL, "rfx_linear: splits must be 1, 2, 4, 8 or 16");
+  if (splits != 1 && splits != 2 && splits != 4 && splits != 8)
+    return set_error(RFX_E_INVAL, "rfx_linear: splits must be 1, 2, 4 or 8");
   if (splits > chunks) return set_error(RFX_E_INVAL, "rfx_linear: splits exceeds K/64");
   const int xt = nt * 128;
   auto budget_for = [&](int xs) { return kSmemLimit - 1024 - small_bytes(nt, norm, xs); };
@@ -653,7 +653,7 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
       const int xs = (chunks + s - 1) / s;
       return xs * xt <= budget_for(xs) - kWTileBytes;
     };
-    while (!fits(splits) && splits < 16 && splits * 2 <= chunks) splits *= 2;
+    while (!fits(splits) && splits < 8 && splits * 2 <= chunks) splits *= 2;
     if (!fits(splits) && d.n_tile == 0 && nt > 64) {
       rfx_linear_desc smaller = d;
       smaller.n_tile = nt / 2;
@@ -661,38 +661,47 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
     }
   }
   const int max_nch = (chunks + splits - 1) / splits;
-  // split-K partials are pushed into a dedicated receive buffer (TMA-fed X only)
-  const int push = (!norm && splits > 1) ? 1 : 0;
-  const int recv_bytes = push ? 128 * nt * 4 : 0;
-  // epilogue operands staged in shared memory during the mainloop
+  // Preferred layout: split-K partials pushed into a dedicated receive buffer
+  // and the epilogue operands staged in shared memory (TMA-fed X only).  When
+  // that does not fit next to one pipeline stage, fall back to pulling the
+  // partials, then to fetching the operands in the epilogue.
   const int items = (16 / splits) * nt;
-  int stage_bytes = (!norm && d.epilogue != RFX_EPI_GEGLU) ? items * static_cast<int>(sizeof(EpiIn)) : 0;
-  if (stage_bytes > 48 * 1024) stage_bytes = 0;
-  int stages, x_slots;
-  if (norm) {
-    x_slots = max_nch;
-    const int left = budget_for(x_slots) - x_slots * xt;
-    stages = std::min({max_nch, kMaxStages, left / kWTileBytes});
-    if (stages < 1) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: K slice too long for the norm prologue; raise splits");
-  } else {
-    stages = std::min({max_nch, kMaxStages, (budget_for(0) - recv_bytes - stage_bytes) / (kWTileBytes + xt)});
-    x_slots = stages;
-    if (stages < 1) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: tile does not fit in shared memory");
+  const int want_push = (!norm && splits > 1) ? 1 : 0;
+  int want_stage = (!norm && d.epilogue != RFX_EPI_GEGLU) ? items * static_cast<int>(sizeof(EpiIn)) : 0;
+  if (want_stage > 48 * 1024) want_stage = 0;
+  const int options[4][2] = {{want_push, want_stage}, {0, want_stage}, {want_push, 0}, {0, 0}};
+  for (const auto& opt : options) {
+    const int push = opt[0], stage_bytes = opt[1];
+    const int recv_bytes = push ? 128 * nt * 4 : 0;
+    int stages, x_slots;
+    if (norm) {
+      x_slots = max_nch;
+      const int left = budget_for(x_slots) - x_slots * xt;
+      stages = std::min({max_nch, kMaxStages, left / kWTileBytes});
+      if (stages < 1)
+        return set_error(RFX_E_UNSUPPORTED, "rfx_linear: K slice too long for the norm prologue; raise splits");
+    } else {
+      stages = std::min({max_nch, kMaxStages, (budget_for(0) - recv_bytes - stage_bytes) / (kWTileBytes + xt)});
+      x_slots = stages;
+      if (stages < 1) continue;
+    }
+    int body = stages * kWTileBytes + x_slots * xt;
+    if (!push) body = std::max(body, nt * kRedLd * 4);
+    body = (body + 127) & ~127;
+    const int smem = body + recv_bytes + stage_bytes + small_bytes(nt, norm, x_slots) + 1024;
+    if (smem > kSmemLimit) continue;
+    cfg->nt = nt;
+    cfg->splits = splits;
+    cfg->stages = stages;
+    cfg->x_slots = x_slots;
+    cfg->push = push;
+    cfg->recv_off = body;
+    cfg->stage_off = stage_bytes ? body + recv_bytes : 0;
+    cfg->small_off = body + recv_bytes + stage_bytes;
+    cfg->smem = smem;
+    return RFX_OK;
   }
-  int body = stages * kWTileBytes + x_slots * xt;
-  if (!push) body = std::max(body, nt * kRedLd * 4);
-  body = (body + 127) & ~127;
-  cfg->nt = nt;
-  cfg->splits = splits;
-  cfg->stages = stages;
-  cfg->x_slots = x_slots;
-  cfg->push = push;
-  cfg->recv_off = body;
-  cfg->stage_off = stage_bytes ? body + recv_bytes : 0;
-  cfg->small_off = body + recv_bytes + stage_bytes;
-  cfg->smem = cfg->small_off + small_bytes(nt, norm, x_slots) + 1024;
-  if (cfg->smem > kSmemLimit) return set_error(RFX_E_UNSUPPORTED, "rfx_linear: shared memory %d too large", cfg->smem);
-  return RFX_OK;
+  return set_error(RFX_E_UNSUPPORTED, "rfx_linear: tile does not fit in shared memory (n_tile %d)", nt);
 }
 
 template <int NT, int PRO, int EPI>

@@ -78,7 +78,7 @@ def _mm(x, w):
     return x.float() @ w.float().t()
 
 
-@pytest.mark.parametrize("T,n_tile,splits", [(50, 0, 0), (1, 64, 1), (50, 64, 2), (50, 64, 8), (50, 64, 16),
+@pytest.mark.parametrize("T,n_tile,splits", [(50, 0, 0), (1, 64, 1), (50, 64, 2), (50, 64, 8), (100, 64, 8),
                                              (100, 128, 4), (200, 256, 2), (400, 0, 0)])
 def test_linear_store(K, T, n_tile, splits):
     r = gen(2)
