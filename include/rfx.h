@@ -221,6 +221,22 @@ typedef struct rfx_attn_desc {
 int rfx_attention(const rfx_attn_desc* desc, void* stream);
 /* Workspace needed by rfx_attention for this descriptor (0 if none). */
 int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes);
+/* rfx_attention without a caller workspace and without any allocation: the
+ * split-KV partials go to an 8 MiB scratch array in the library's device
+ * code (desc->workspace / workspace_bytes are ignored).  No counterpart in
+ * the reference; it serves callers that may not allocate device memory at
+ * call time (code under CUDA stream capture, hosts whose allocator owns all
+ * device memory).
+ *   - Make the first call on each device before any stream capture: it looks
+ *     up the scratch address (and may load the module's device code).
+ *   - Shapes whose partials need more than 8 MiB (B * q_tiles * kv_splits
+ *     above 63, at 132,096 bytes per CTA) return RFX_E_INVAL with the size
+ *     in rfx_last_error(); lower kv_splits or use rfx_attention.
+ *   - The scratch needs no zeroing; every partial read is written by the
+ *     same call.
+ *   - The scratch is shared per device: calls whose launches may overlap
+ *     (other streams, racing host threads) corrupt each other; order them. */
+int rfx_attention_noalloc(const rfx_attn_desc* desc, void* stream);
 
 /* ----------------------------------------- timestep conditioning + heads ---- */
 /* cond[i] = silu(W_out · silu(W_in · bf16(sinusoid(t[i])) + b_in) + b_out), bf16.

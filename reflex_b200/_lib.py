@@ -154,6 +154,7 @@ SIGNATURES = {
     "rfx_pack_weight": ([c_int, c_void_p, c_void_p, c_int, c_int, c_void_p], c_int),
     "rfx_attention": ([POINTER(AttnDesc), c_void_p], c_int),
     "rfx_attention_workspace_size": ([POINTER(AttnDesc), POINTER(c_size_t)], c_int),
+    "rfx_attention_noalloc": ([POINTER(AttnDesc), c_void_p], c_int),
     "rfx_time_cond": ([POINTER(TimeCondDesc), c_void_p], c_int),
     "rfx_modulation": ([POINTER(ModulationDesc), c_void_p], c_int),
     "rfx_action_in": ([POINTER(ActionIoDesc), c_void_p], c_int),

@@ -30,6 +30,8 @@
 #include "rfx_internal.h"
 
 #include <algorithm>
+#include <mutex>
+#include <unordered_map>
 
 namespace rfx {
 namespace {
@@ -669,7 +671,75 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
                        p);
 }
 
+// ------------------------------------------------- no-allocation variant ---
+// Split-KV scratch for rfx_attention_noalloc: a file-scope device array, so
+// the call never allocates.  It is for callers that may not allocate device
+// memory at call time: code running while a CUDA stream is being captured
+// (an allocation there breaks or invalidates the capture) and hosts whose
+// allocator owns every device byte and hands the kernel library none.
+// 8 MiB holds the partials of B * q_tiles * kv_splits <= 63 CTAs (each CTA
+// needs 128 rows * (256 + 2) fp32 = 132,096 bytes), e.g. 4 streams of
+// 10 actions x 8 heads at up to 15 splits.  Nothing in it has to start at
+// zero: the attention launch writes every partial (O, m, l) that the combine
+// launch of the same call reads.  The array is shared by all calls on a
+// device, so two calls whose launches can overlap (different streams, or
+// host threads racing on one device) corrupt each other's partials; the
+// caller orders them.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+std::mutex g_scratch_mu;
+std::unordered_map<int, void*> g_scratch_ptrs;
+
+// Device address of the scratch array on the current device, looked up once
+// per device.  The first call on a device can load the module's device code
+// (lazy loading), so it belongs before any stream capture.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "rfx_attention_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  auto it = g_scratch_ptrs.find(dev);
+  if (it != g_scratch_ptrs.end()) {
+    *out = it->second;
+    return RFX_OK;
+  }
+  void* p = nullptr;
+  rc = check_cuda(cudaGetSymbolAddress(&p, g_attn_scratch), "rfx_attention_noalloc: cudaGetSymbolAddress(scratch)");
+  if (rc) return rc;
+  g_scratch_ptrs[dev] = p;
+  *out = p;
+  return RFX_OK;
+}
+}  // namespace
+
 }  // namespace rfx
+
+extern "C" int rfx_attention_noalloc(const rfx_attn_desc* desc, void* stream) {
+  using namespace rfx;
+  if (!desc) return set_error(RFX_E_INVAL, "rfx_attention_noalloc: null descriptor");
+  Geometry g;
+  int rc = geometry(*desc, &g);
+  if (rc) return rc;
+  rfx_attn_desc d = *desc;
+  const size_t need = attention_workspace_bytes(d);
+  if (need > kNoAllocScratchBytes)
+    return set_error(RFX_E_INVAL,
+                     "rfx_attention_noalloc: this shape needs %zu bytes of split-KV scratch, the static scratch "
+                     "holds %zu; lower kv_splits or call rfx_attention with a workspace",
+                     need, kNoAllocScratchBytes);
+  d.workspace = nullptr;
+  d.workspace_bytes = 0;
+  if (need > 0) {
+    rc = noalloc_scratch(&d.workspace);
+    if (rc) return rc;
+    d.workspace_bytes = kNoAllocScratchBytes;
+  }
+  CUtensorMap q, k, v;
+  rc = build_attention_maps(d, &q, &k, &v);
+  if (rc) return rc;
+  return launch_attention(d, &q, &k, &v, static_cast<cudaStream_t>(stream), pdl_enabled());
+}
 
 extern "C" int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes) {
   using namespace rfx;
