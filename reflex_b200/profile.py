@@ -1,11 +1,14 @@
 """Runs the kernels of one denoising layer in isolation, for profilers.
 
     python -m reflex_b200.profile [--layers 2] [--reps 3] [--ops qkv,attn,o,gu,down,tail]
+    python -m reflex_b200.profile --layers 18 --chunk   # one eager chunk, then one graph replay
 
 Builds the PI0.5 engine at the benchmark's shapes (width 1024, 8x256 heads,
 818-token int8 context, 50 action tokens) with a few layers, runs one chunk to
 warm up, then launches the requested ops of step 0 / layer 0 `reps` times each
-through the direct C entry points, in the order given.  Device memory stays
+through the direct C entry points, in the order given.  Only the measured
+launches sit inside cudaProfilerStart/Stop (profile with
+`ncu --profile-from-start off`).  Device memory stays
 well under 1 GB, so a profiler capture of a handful of launches ends quickly.
 """
 from __future__ import annotations
@@ -27,6 +30,7 @@ def main():
     ap.add_argument("--ops", default="qkv,attn,o,gu,down,tail")
     ap.add_argument("--n-ctx", type=int, default=818)
     ap.add_argument("--streams", type=int, default=1)
+    ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
     args = ap.parse_args()
     cfg = pi05_config(num_layers=args.layers, adarms="ssg")
     wts = synthetic.expert_weights(cfg, seed=0, device="cuda")
@@ -37,16 +41,28 @@ def main():
     eng.set_inputs(synthetic.noise(cfg, B=args.streams, seed=2, device="cuda"))
     eng.run_eager()
     torch.cuda.synchronize()
+    if args.chunk:
+        print("launches per chunk", eng.num_launches)
+        eng.capture()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        eng.launch_chunk()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("ok", K.device_status())
+        return
     by_tag = {}
     for kind, desc, tag in eng.ops:
         if tag is not None and tag[1] == 0 and (len(tag) < 3 or tag[2] == 0):
             by_tag[tag[0]] = (kind, desc)
     names = {"qkv": "qkv", "attn": "attn", "o": "o", "gu": "gu", "down": "layer", "tail": "step"}
+    torch.cuda.profiler.start()
     for op in args.ops.split(","):
         kind, desc = by_tag[names[op]]
         for _ in range(args.reps):
             K.Plan.run_direct(desc, kind if kind in ("in", "tail") else None)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     print("ok", K.device_status())
 
 

@@ -1,0 +1,79 @@
+"""The C ABI without a GPU: the library loads, exports every function that
+include/rfx.h declares, the ctypes mirror matches the C struct layouts
+(checked by compiling the header with gcc), and argument checks that need no
+device return RFX_E_INVAL.
+"""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from reflex_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "rfx.h")
+
+STRUCTS = {
+    "rfx_kv_quant_desc": "KvQuantDesc", "rfx_linear_desc": "LinearDesc", "rfx_norm_desc": "NormDesc",
+    "rfx_attn_desc": "AttnDesc", "rfx_time_cond_desc": "TimeCondDesc", "rfx_modulation_desc": "ModulationDesc",
+    "rfx_action_io_desc": "ActionIoDesc", "rfx_copy_rows_desc": "CopyRowsDesc",
+}
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_]+\s*\**\s*(rfx_[a-z0-9_]+)\s*\(", src, flags=re.M)))
+
+
+def test_library_exports_every_declared_function():
+    lib = _lib.load()
+    names = header_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    assert sorted(_lib.SIGNATURES) == names, "ctypes signatures and header disagree"
+    assert lib.rfx_version() >= 100
+
+
+def test_ctypes_structs_match_c_layout(tmp_path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "rfx.h"', "int main(void) {"]
+    for c_name, py_name in STRUCTS.items():
+        lines.append(f'  printf("{py_name} size %zu\\n", sizeof({c_name}));')
+        for field, _ in getattr(_lib, py_name)._fields_:
+            lines.append(f'  printf("{py_name} {field} %zu\\n", offsetof({c_name}, {field}));')
+    lines.append("  return 0; }")
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.dirname(HEADER), str(c), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    for line in filter(None, out):
+        py_name, key, val = line.split()
+        cls = getattr(_lib, py_name)
+        got = ctypes.sizeof(cls) if key == "size" else getattr(cls, key).offset
+        assert got == int(val), f"{py_name}.{key}: ctypes {got}, C {val}"
+
+
+@pytest.mark.parametrize("name", ["rfx_linear", "rfx_attention", "rfx_attention_noalloc", "rfx_kv_quant_append",
+                                  "rfx_rms_norm", "rfx_time_cond", "rfx_modulation", "rfx_action_in",
+                                  "rfx_euler_tail", "rfx_copy_rows"])
+def test_null_descriptor_is_rejected(name):
+    lib = _lib.load()
+    rc = getattr(lib, name)(None, None)
+    assert rc == _lib.RFX_E_INVAL
+    assert lib.rfx_last_error()
+
+
+def test_plan_calls_out_of_order():
+    lib = _lib.load()
+    plan = ctypes.c_void_p()
+    assert lib.rfx_plan_create(ctypes.byref(plan)) == _lib.RFX_OK
+    try:
+        assert lib.rfx_plan_replay(plan, None) == _lib.RFX_E_STATE
+        n = ctypes.c_int(-1)
+        assert lib.rfx_plan_num_launches(plan, ctypes.byref(n)) == _lib.RFX_OK and n.value == 0
+    finally:
+        assert lib.rfx_plan_destroy(plan) == _lib.RFX_OK
