@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=2)
+    ap.add_argument("--streams-per-gpu", type=int, default=1,
+                    help="independent robot streams served per GPU, batched along B (multi-stream sweep)")
     return ap.parse_args()
 
 
@@ -58,11 +60,11 @@ def dist_env():
 
 def workload_config(args, world):
     return {
-        "workload": "PI0.5 10-step action chunk, 1 stream/GPU, 18x(1024, 8x256 MQA, GeGLU 4096), "
-                    "818-token int8 KV context, 50 action tokens",
+        "workload": f"PI0.5 10-step action chunk, {args.streams_per_gpu} stream(s)/GPU, "
+                    "18x(1024, 8x256 MQA, GeGLU 4096), 818-token int8 KV context per stream, 50 action tokens",
         "model": "pi05-action-expert (gemma-300m shape), random-init",
         "layers": args.layers, "context_tokens": N_CTX, "suffix_tokens": 50, "euler_steps": 10,
-        "streams_per_gpu": 1, "global_batch": world, "kv": "int8 symmetric per-token/per-head",
+        "streams_per_gpu": args.streams_per_gpu, "global_batch": world * args.streams_per_gpu, "kv": "int8 symmetric per-token/per-head",
         "adarms": "scale/shift/gate", "parallelism": f"dp{world} (independent streams)",
         "l2": "no flush: each chunk streams 6.2 GB of weights + 0.47 GB of fp32 modulation weights (>> 126 MB L2)",
     }
@@ -70,34 +72,41 @@ def workload_config(args, world):
 
 # ---------------------------------------------------------------- clocks ---
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons in the background."""
+    """Samples SM clocks and throttle reasons every 100 ms during the timed
+    region (one `nvidia-smi -lms` process, ended when the region ends)."""
 
     def __init__(self, index: int):
-        self.index, self.rows, self._stop = index, [], threading.Event()
-        self._t = threading.Thread(target=self._run, daemon=True)
+        self.index, self.rows, self.proc = index, [], None
+        self._t = threading.Thread(target=self._read, daemon=True)
 
-    def _run(self):
+    def _read(self):
+        for line in self.proc.stdout:
+            f = [x.strip() for x in line.strip().split(",")]
+            if len(f) >= 7:
+                self.rows.append(f)
+
+    def __enter__(self):
         q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                f = [x.strip() for x in out.stdout.strip().split(",")]
-                if len(f) >= 7:
-                    self.rows.append(f)
-            except Exception:
-                pass
-            self._stop.wait(0.2)
-
-    def __enter__(self):
-        self._t.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t.start()
+            time.sleep(0.3)  # first sample lands before the timed launches start
+        except OSError:
+            self.proc = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._t.join(timeout=5)
 
     def summary(self):
         if not self.rows:
@@ -176,9 +185,10 @@ def build_engine(args, device):
 
     cfg = pi05_config(num_layers=args.layers, adarms="ssg", quant_mode="i8_sym")
     wts = synthetic.expert_weights(cfg, seed=0, device=device)
-    eng = ActionExpertEngine(cfg, wts, batch=1, capacity=CAPACITY, n_ctx=N_CTX, device=device)
+    B = args.streams_per_gpu
+    eng = ActionExpertEngine(cfg, wts, batch=B, capacity=CAPACITY, n_ctx=N_CTX, device=device)
     del wts
-    ks, vs = synthetic.context_kv(cfg, N_CTX, seed=1, device=device)
+    ks, vs = synthetic.context_kv(cfg, N_CTX, B=B, seed=1, device=device)
     for l in range(cfg.num_layers):
         eng.load_context(l, ks[l], vs[l])
     torch.cuda.synchronize()
@@ -211,9 +221,18 @@ def kernel_roofline(eng, hbm_peak, reps=3):
         durs.append(e0.elapsed_time(e1) / len(gu))
     avg_ms = statistics.median(durs)
     achieved = bytes_per / (avg_ms * 1e-3) / 1e9
-    return {"kernel": "linear_kernel<64,NORM,GEGLU> (gate/up + AdaRMS prologue + GELU-tanh*up)",
+    traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and shape
+    try:
+        with open(os.path.join(ROOT, "profiles", "linear_gate_up_pi05_b1.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1])
+    except OSError:
+        pass
+    return {"kernel": "linear_kernel<64,LOAD,GEGLU> (gate/up projection + GELU-tanh(gate)*up)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/linear_gate_up_pi05_b1.md",
             "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
 
 
@@ -233,7 +252,8 @@ def run_gpu(args):
     from reflex_b200 import synthetic
 
     cfg, eng = build_engine(args, device)
-    x0 = synthetic.noise(cfg, seed=2 + rank, device=device)
+    B = args.streams_per_gpu
+    x0 = synthetic.noise(cfg, B=B, seed=2 + rank, device=device)
     eng.set_inputs(x0)
     if not args.no_graph:
         eng.capture()
@@ -274,7 +294,7 @@ def run_gpu(args):
         pg.barrier()
 
     # ---- end to end through the public API with host buffers
-    x_host = synthetic.noise(cfg, seed=2 + rank).pin_memory()
+    x_host = synthetic.noise(cfg, B=B, seed=2 + rank).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
     e2e = []
     for i in range(args.steps + 3):
@@ -293,8 +313,9 @@ def run_gpu(args):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_p50 = t.item()
         # final gather of every stream's action chunk (not on the hot path)
-        chunks = [torch.empty_like(eng.x) for _ in range(world)]
-        pg.all_gather(chunks, eng.x)
+        from reflex_b200.streams import gather_chunks
+        gathered = gather_chunks(eng.x, world * B, pg)
+        assert gathered.shape[0] == world * B
 
     roof = kernel_roofline(eng, hbm_peak)
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
@@ -307,7 +328,9 @@ def run_gpu(args):
                "sample": f"{len(times)} full chunks of the same workload (fp32 torch oracle port), median"}
 
     if rank == 0:
-        bytes_chunk = 10 * (eng.cfg.num_layers * 17301504 * 2 + eng.cfg.num_layers * N_CTX * 256 * 2) + \
+        # weights once per step, each stream's int8 K+V context and fp32 scales per step, and the fp32
+        # scale/shift/gate modulation weights once per chunk
+        bytes_chunk = 10 * (eng.cfg.num_layers * 17301504 * 2 + B * eng.cfg.num_layers * N_CTX * (256 + 4) * 2) + \
             (2 * eng.cfg.num_layers + 1) * 3 * 1024 * 1024 * 4
         line = {
             "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
@@ -315,7 +338,7 @@ def run_gpu(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded random-init weights, N(0,1) context K/V quantized to int8, x0 ~ N(0,1)",
             "config": workload_config(args, world),
-            "chunks_per_s": round(world * 1e3 / p50, 2),
+            "chunks_per_s": round(world * B * 1e3 / p50, 2),
             "chunk_roofline": {"algorithmic_bytes": bytes_chunk,
                                "achieved_GBps": round(bytes_chunk / (p50 * 1e-3) / 1e9, 1),
                                "peak_GBps": hbm_peak, "frac": round(bytes_chunk / (p50 * 1e-3) / 1e9 / hbm_peak, 4)},

@@ -247,7 +247,7 @@ typedef struct rfx_time_cond_desc {
   int n_t;
   const float* t; /* [n_t] */
   int width;
-  float min_period, max_period;
+  double min_period, max_period; /* fp64, as the reference passes Python floats */
   const void* w_in; /* bf16 [width][width] */
   const void* b_in; /* bf16 [width] */
   const void* w_out;

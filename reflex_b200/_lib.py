@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, Structure, c_float, c_int, c_long, c_size_t, c_ubyte, c_void_p
+from ctypes import POINTER, Structure, c_double, c_float, c_int, c_long, c_size_t, c_ubyte, c_void_p
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "librfx_b200.so")
@@ -96,7 +96,7 @@ class AttnDesc(Structure):
 class TimeCondDesc(Structure):
     _fields_ = [
         ("n_t", c_int), ("t", c_void_p), ("width", c_int),
-        ("min_period", c_float), ("max_period", c_float),
+        ("min_period", c_double), ("max_period", c_double),
         ("w_in", c_void_p), ("b_in", c_void_p), ("w_out", c_void_p), ("b_out", c_void_p),
         ("hidden", c_void_p), ("cond", c_void_p),
     ]

@@ -44,7 +44,17 @@ __global__ void __launch_bounds__(256) gemv_bf16_silu_kernel(const __nv_bfloat16
                                                              __nv_bfloat16* __restrict__ out) {
   extern __shared__ float xin[];  // [n_rows][width]
   pdl_wait();
-  for (int i = threadIdx.x; i < n_rows * width; i += blockDim.x) xin[i] = __bfloat162float(in[i]);
+  // 16-byte loads, all of a thread's loads issued before any is used
+  for (int i = threadIdx.x * 8; i < n_rows * width; i += blockDim.x * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(in + i);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h2[e]);
+      xin[i + 2 * e] = f.x;
+      xin[i + 2 * e + 1] = f.y;
+    }
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int o = blockIdx.x * 8 + warp;
@@ -94,68 +104,90 @@ __global__ void __launch_bounds__(256) gemv_bf16_silu_kernel(const __nv_bfloat16
   pdl_launch_dependents();
 }
 
-// AdaRMSNorm modulation: fp32 W [n_norms * out][width], one warp per output
-// row, all conditioning rows at once.
+// AdaRMSNorm modulation: fp32 W [n_norms * out][width]; every warp takes two
+// output rows at a time (grid-stride over all rows) against all conditioning
+// rows, which sit in shared memory as bf16 (exact: cond is bf16).
+__device__ __forceinline__ void modulation_store(long row, int r, float m, int width, int n_norms, int out_per_norm,
+                                                 int mode, float* __restrict__ a2, float* __restrict__ b2,
+                                                 float* __restrict__ gate) {
+  const int n = static_cast<int>(row / out_per_norm);
+  const int o = static_cast<int>(row % out_per_norm);
+  const long base = (static_cast<long>(r) * n_norms + n) * width;
+  if (mode == RFX_ADARMS_GATE) {
+    a2[base + o] = m;
+    if (b2) b2[base + o] = 0.f;
+    gate[base + o] = bf16_round(m);
+  } else {
+    const int part = o / width, f = o % width;
+    if (part == 0) a2[base + f] = __fadd_rn(1.f, m);
+    else if (part == 1) b2[base + f] = m;
+    else gate[base + f] = bf16_round(m);
+  }
+}
+
 __global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict__ W, const float* __restrict__ bias,
                                                          const __nv_bfloat16* __restrict__ cond, int n_rows, int width,
                                                          int n_norms, int out_per_norm, int mode,
                                                          float* __restrict__ a2, float* __restrict__ b2,
                                                          float* __restrict__ gate) {
-  extern __shared__ float cin[];  // [n_rows][width]
+  extern __shared__ __align__(16) __nv_bfloat16 cin[];  // [n_rows][width]
   pdl_wait();
-  for (int i = threadIdx.x; i < n_rows * width; i += blockDim.x) cin[i] = __bfloat162float(cond[i]);
+  for (int i = threadIdx.x * 8; i < n_rows * width; i += blockDim.x * 8)
+    *reinterpret_cast<uint4*>(cin + i) = *reinterpret_cast<const uint4*>(cond + i);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long row = static_cast<long>(blockIdx.x) * 8 + warp;  // over n_norms * out_per_norm
-  if (row < static_cast<long>(n_norms) * out_per_norm) {
-    float acc[kMaxRows];
+  const long total = static_cast<long>(n_norms) * out_per_norm;
+  for (long row0 = (static_cast<long>(blockIdx.x) * 8 + warp) * 2; row0 < total;
+       row0 += static_cast<long>(gridDim.x) * 16) {
+    const bool has1 = row0 + 1 < total;
+    float acc0[kMaxRows], acc1[kMaxRows];
 #pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
-    const float* wr = W + row * width;
+    for (int r = 0; r < kMaxRows; ++r) acc0[r] = acc1[r] = 0.f;
+    const float* w0 = W + row0 * width;
+    const float* w1 = has1 ? w0 + width : w0;
     for (int k0 = 0; k0 < width; k0 += 1024) {
-      // the whole 4 KB slice of the row is requested before any of it is used
-      float4 wv[8];
+      // both rows' 4 KB slices are requested before any of them is used
+      float4 v0[8], v1[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int k = k0 + q * 128 + lane * 4;
-        if (k < width) wv[q] = __ldcs(reinterpret_cast<const float4*>(wr + k));  // streamed once per chunk
+        if (k < width) {
+          v0[q] = __ldcs(reinterpret_cast<const float4*>(w0 + k));  // streamed once per chunk
+          v1[q] = __ldcs(reinterpret_cast<const float4*>(w1 + k));
+        }
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int k = k0 + q * 128 + lane * 4;
         if (k >= width) continue;
-        const float4 w = wv[q];
 #pragma unroll
         for (int r = 0; r < kMaxRows; ++r) {
           if (r < n_rows) {
-            const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
-            acc[r] = fmaf(w.x, x.x, acc[r]);
-            acc[r] = fmaf(w.y, x.y, acc[r]);
-            acc[r] = fmaf(w.z, x.z, acc[r]);
-            acc[r] = fmaf(w.w, x.w, acc[r]);
+            const uint2 raw = *reinterpret_cast<const uint2*>(cin + r * width + k);
+            const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+            const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+            acc0[r] = fmaf(v0[q].x, xa.x, acc0[r]);
+            acc0[r] = fmaf(v0[q].y, xa.y, acc0[r]);
+            acc0[r] = fmaf(v0[q].z, xb.x, acc0[r]);
+            acc0[r] = fmaf(v0[q].w, xb.y, acc0[r]);
+            acc1[r] = fmaf(v1[q].x, xa.x, acc1[r]);
+            acc1[r] = fmaf(v1[q].y, xa.y, acc1[r]);
+            acc1[r] = fmaf(v1[q].z, xb.x, acc1[r]);
+            acc1[r] = fmaf(v1[q].w, xb.y, acc1[r]);
           }
         }
       }
     }
-    const int n = static_cast<int>(row / out_per_norm);
-    const int o = static_cast<int>(row % out_per_norm);
-    const float bo = bias[row];
+    const float bo0 = bias[row0];
+    const float bo1 = has1 ? bias[row0 + 1] : 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxRows; ++r) {
       if (r < n_rows) {
-        const float m = __fadd_rn(warp_sum(acc[r]), bo);
+        const float m0 = __fadd_rn(warp_sum(acc0[r]), bo0);
+        const float m1 = __fadd_rn(warp_sum(acc1[r]), bo1);
         if (lane == 0) {
-          const long base = (static_cast<long>(r) * n_norms + n) * width;
-          if (mode == RFX_ADARMS_GATE) {
-            a2[base + o] = m;
-            if (b2) b2[base + o] = 0.f;
-            gate[base + o] = bf16_round(m);
-          } else {
-            const int part = o / width, f = o % width;
-            if (part == 0) a2[base + f] = __fadd_rn(1.f, m);
-            else if (part == 1) b2[base + f] = m;
-            else gate[base + f] = bf16_round(m);
-          }
+          modulation_store(row0, r, m0, width, n_norms, out_per_norm, mode, a2, b2, gate);
+          if (has1) modulation_store(row0 + 1, r, m1, width, n_norms, out_per_norm, mode, a2, b2, gate);
         }
       }
     }
@@ -431,9 +463,9 @@ int validate_io(const rfx_action_io_desc& d, bool tail) {
 int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl) {
   const bool embed_only = d.w_in == nullptr;
   if (d.n_t < 1 || d.n_t > kMaxRows || d.width < 256 || d.width % 256 || !d.t || !d.cond ||
-      (!embed_only && (!d.w_out || !d.hidden || !a16(d.w_in) || !a16(d.w_out))))
+      !a16(d.cond) || (!embed_only && (!d.w_out || !d.hidden || !a16(d.w_in) || !a16(d.w_out) || !a16(d.hidden))))
     return set_error(RFX_E_INVAL, "rfx_time_cond: need 1<=n_t<=16, width%%256==0, aligned weights");
-  if (!(d.min_period > 0.f) || !(d.max_period > 0.f)) return set_error(RFX_E_INVAL, "rfx_time_cond: periods");
+  if (!(d.min_period > 0.0) || !(d.max_period > 0.0)) return set_error(RFX_E_INVAL, "rfx_time_cond: periods");
   __nv_bfloat16* emb = static_cast<__nv_bfloat16*>(d.cond);  // the embedding is staged in `cond`
   const int half = d.width / 2;
   const float* t = d.t;
@@ -466,15 +498,17 @@ int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pd
   const int out = d.mode == RFX_ADARMS_SSG ? 3 * d.width : d.width;
   if ((d.mode != RFX_ADARMS_GATE && d.mode != RFX_ADARMS_SSG) || d.n_rows < 1 || d.n_rows > kMaxRows ||
       d.n_norms < 1 || d.width < 128 || d.width % 128 || !d.w || !d.b || !d.cond || !d.a2 || !d.gate ||
-      (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w))
+      (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w) || !a16(d.cond))
     return set_error(RFX_E_INVAL, "rfx_modulation: bad descriptor");
-  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(float);
+  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(__nv_bfloat16);
   if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
   const void* fn = reinterpret_cast<const void*>(modulation_kernel);
   int rc = ensure_smem_attr(fn, 200 * 1024);
   if (rc) return rc;
   const long rows = static_cast<long>(d.n_norms) * out;
-  dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  int nsm = 148;
+  rfx_num_sms(&nsm);
+  dim3 grid(static_cast<unsigned>(std::min<long>((rows + 15) / 16, 4L * nsm)));
   const float* w = d.w;
   const float* bias = d.b;
   const __nv_bfloat16* cond = static_cast<const __nv_bfloat16*>(d.cond);

@@ -188,12 +188,13 @@ def attention(**kw) -> None:
 
 # ----------------------------------------------------- conditioning heads ---
 def time_cond_desc(*, t, w_in, b_in, w_out, b_out, hidden, cond, min_period, max_period) -> L.TimeCondDesc:
+    """w_in = None computes the bf16 sinusoidal embedding alone (into `cond`)."""
     _need_cuda(t, w_in, cond)
     d = L.TimeCondDesc()
-    d.n_t, d.t, d.width = t.numel(), t.data_ptr(), w_in.shape[0]
+    d.n_t, d.t, d.width = t.numel(), t.data_ptr(), cond.shape[1]
     d.min_period, d.max_period = min_period, max_period
-    d.w_in, d.b_in, d.w_out, d.b_out = w_in.data_ptr(), L.ptr(b_in), w_out.data_ptr(), L.ptr(b_out)
-    d.hidden, d.cond = hidden.data_ptr(), cond.data_ptr()
+    d.w_in, d.b_in, d.w_out, d.b_out = L.ptr(w_in), L.ptr(b_in), L.ptr(w_out), L.ptr(b_out)
+    d.hidden, d.cond = L.ptr(hidden), cond.data_ptr()
     return d
 
 

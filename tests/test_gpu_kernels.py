@@ -254,3 +254,62 @@ def test_attention_partitioned(K, L, mode, n_ctx, S, splits):
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 2e-2, f"max abs err {err}"
     assert K.device_status() == 0
+
+
+# ------------------------------------------------------ conditioning heads ---
+def test_time_cond_matches_fp64_embedding_and_mlp(K):
+    from oracle.model import sinusoid
+    r = gen(11)
+    W, n_t = 1024, 10
+    t = torch.linspace(1.0, 0.1, n_t, dtype=torch.float32)
+    w_in, w_out = (r(W, W) * 0.03).bfloat16().float(), (r(W, W) * 0.03).bfloat16().float()
+    b_in, b_out = (r(W) * 0.1).bfloat16().float(), (r(W) * 0.1).bfloat16().float()
+    dev = lambda a: a.bfloat16().cuda()  # noqa: E731
+    hid = torch.empty(n_t, W, dtype=torch.bfloat16, device="cuda")
+    cond = torch.empty(n_t, W, dtype=torch.bfloat16, device="cuda")
+    # embedding alone: bf16 of the fp64 sinusoid.  fp64 pow/sin differ between
+    # libraries by an ulp, which only shows where sin/cos is ~1e-13 (t * 2pi /
+    # period a multiple of pi); everywhere else the bf16 values are identical.
+    K.time_cond(t=t.cuda(), w_in=None, b_in=None, w_out=None, b_out=None, hidden=hid, cond=cond,
+                min_period=4e-3, max_period=4.0)
+    torch.cuda.synchronize()
+    emb = sinusoid(t, W, 4e-3, 4.0).to(torch.bfloat16)
+    got = cond.cpu()
+    diff = (got.double() - emb.double()).abs()
+    assert diff.max().item() <= 1e-9
+    assert (got != emb).sum().item() <= 4
+    # full: silu(W_out silu(W_in e + b_in) + b_out), bf16 after each layer
+    K.time_cond(t=t.cuda(), w_in=dev(w_in), b_in=dev(b_in), w_out=dev(w_out), b_out=dev(b_out), hidden=hid,
+                cond=cond, min_period=4e-3, max_period=4.0)
+    torch.cuda.synchronize()
+    silu = torch.nn.functional.silu
+    h1 = silu((emb.float() @ w_in.t() + b_in).bfloat16().float()).bfloat16()
+    ref = silu((h1.float() @ w_out.t() + b_out).bfloat16().float())
+    err = (cond.float().cpu() - ref).abs().max().item()
+    assert err <= ATOL, err
+
+
+@pytest.mark.parametrize("mode", ["ssg", "gate"])
+def test_modulation_fp32_dense(K, L, mode):
+    r = gen(12)
+    W, n_rows, n_norms = 1024, 10, 5
+    m = L.RFX_ADARMS_SSG if mode == "ssg" else L.RFX_ADARMS_GATE
+    out = 3 * W if mode == "ssg" else W
+    w = r(n_norms * out, W) * 0.03
+    b = r(n_norms * out) * 0.1
+    cond = r(n_rows, W).bfloat16()
+    a2 = torch.zeros(n_rows, n_norms, W, device="cuda")
+    b2 = torch.zeros_like(a2)
+    gate = torch.zeros_like(a2)
+    K.modulation(mode=m, w=w.cuda(), b=b.cuda(), cond=cond.cuda(), a2=a2, b2=b2, gate=gate, n_norms=n_norms)
+    torch.cuda.synchronize()
+    dense = (cond.double() @ w.double().t() + b.double()).view(n_rows, n_norms, out)
+    if mode == "ssg":
+        ref_a2, ref_b2, ref_g = 1 + dense[..., :W], dense[..., W:2 * W], dense[..., 2 * W:]
+    else:
+        ref_a2, ref_b2, ref_g = dense, torch.zeros_like(dense), dense
+    assert (a2.cpu().double() - ref_a2).abs().max().item() <= 1e-4
+    assert (b2.cpu().double() - ref_b2).abs().max().item() <= 1e-4
+    # the gate is stored bf16-rounded: within half a bf16 ulp (2^-8 relative) plus the fp32 dot-product error
+    assert ((gate.cpu().double() - ref_g).abs() <= ref_g.abs() * 2.0 ** -8 + 1e-4).all()
+    assert torch.equal(gate.cpu(), gate.cpu().bfloat16().float())
