@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=2)
+    ap.add_argument("--engine", default="per-op", choices=["fused", "per-op"],
+                    help="fused: the persistent chunk executor (one launch per chunk); per-op: one launch per op")
     ap.add_argument("--streams-per-gpu", type=int, default=1,
                     help="independent robot streams served per GPU, batched along B (multi-stream sweep)")
     return ap.parse_args()
@@ -66,6 +68,8 @@ def workload_config(args, world):
         "layers": args.layers, "context_tokens": N_CTX, "suffix_tokens": 50, "euler_steps": 10,
         "streams_per_gpu": args.streams_per_gpu, "global_batch": world * args.streams_per_gpu, "kv": "int8 symmetric per-token/per-head",
         "adarms": "scale/shift/gate", "parallelism": f"dp{world} (independent streams)",
+        "engine": "persistent chunk executor" if args.engine == "fused" and args.streams_per_gpu * 50 <= 64
+                  else "one launch per op",
         "l2": "no flush: each chunk streams 6.2 GB of weights + 0.47 GB of fp32 modulation weights (>> 126 MB L2)",
     }
 
@@ -186,13 +190,57 @@ def build_engine(args, device):
     cfg = pi05_config(num_layers=args.layers, adarms="ssg", quant_mode="i8_sym")
     wts = synthetic.expert_weights(cfg, seed=0, device=device)
     B = args.streams_per_gpu
-    eng = ActionExpertEngine(cfg, wts, batch=B, capacity=CAPACITY, n_ctx=N_CTX, device=device)
+    fused = args.engine == "fused" and B * cfg.suffix_len <= 64
+    # int8 symmetric KV keeps fp32 per-token scales (absmax / 127)
+    eng = ActionExpertEngine(cfg, wts, batch=B, capacity=CAPACITY, n_ctx=N_CTX, device=device,
+                             scale_dtype=torch.float32, fused=fused)
     del wts
     ks, vs = synthetic.context_kv(cfg, N_CTX, B=B, seed=1, device=device)
     for l in range(cfg.num_layers):
         eng.load_context(l, ks[l], vs[l])
     torch.cuda.synchronize()
     return cfg, eng
+
+
+def chunk_kernel_roofline(eng, hbm_peak, reps=3):
+    """Times the persistent chunk executor alone (counter clear + one launch)
+    with CUDA events on the launching stream; returns per-launch duration and
+    achieved HBM GB/s over its algorithmic bytes."""
+    import ctypes
+
+    from reflex_b200 import _lib as L
+    from reflex_b200 import kernels as K
+
+    cfg = eng.cfg
+    # per Euler step: every layer's bf16 weights once, each stream's int8 K+V context and fp32 scales
+    per_step = cfg.num_layers * 17301504 * 2 + eng.B * cfg.num_layers * N_CTX * (256 + 4) * 2
+    bytes_per = cfg.num_steps * per_step
+    st = torch.cuda.current_stream()
+    L.call("rfx_chunk_run", eng.chunk, K._stream())
+    durs = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        L.call("rfx_chunk_run", eng.chunk, K._stream())
+        e1.record(st)
+        torch.cuda.synchronize()
+        durs.append(e0.elapsed_time(e1))
+    avg_ms = statistics.median(durs)
+    achieved = bytes_per / (avg_ms * 1e-3) / 1e9
+    traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and workload
+    try:
+        with open(os.path.join(ROOT, "profiles", "chunk_kernel_pi05_818ctx.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1])
+    except OSError:
+        pass
+    del ctypes
+    return {"kernel": "chunk_kernel (persistent executor of the whole 10-step chunk, 1 CTA per SM)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/chunk_kernel_pi05_818ctx.md",
+            "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
 
 
 def kernel_roofline(eng, hbm_peak, reps=3):
@@ -317,7 +365,7 @@ def run_gpu(args):
         gathered = gather_chunks(eng.x, world * B, pg)
         assert gathered.shape[0] == world * B
 
-    roof = kernel_roofline(eng, hbm_peak)
+    roof = chunk_kernel_roofline(eng, hbm_peak) if eng.fused else kernel_roofline(eng, hbm_peak)
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
     status = K.device_status()
 

@@ -322,6 +322,59 @@ typedef struct rfx_copy_rows_desc {
 } rfx_copy_rows_desc;
 int rfx_copy_rows(const rfx_copy_rows_desc* desc, void* stream);
 
+/* ------------------------------------------------ fused chunk executor ---- */
+/* The whole PI0.5 denoising loop of one chunk (all Euler steps x layers:
+ * input norm, QKV+RoPE, partitioned attention over the context ring,
+ * o_proj + gated residual, post-attention norm, gate/up + GeGLU, down_proj +
+ * gated residual, and the Euler tail) in ONE persistent kernel launch with one
+ * CTA per SM; phases hand over through global counters instead of kernel
+ * boundaries. Same dataflow and roundings as the per-op entry points above
+ * (modeling_pi05.py:1181-1241 per step, 1403-1419 the Euler loop); partial
+ * sums of split GEMMs are added in a fixed order. The timestep embedding and
+ * the modulation vectors (rfx_time_cond, rfx_modulation) are computed before.
+ * Limits: B*S <= 64 tokens, width 1024, head_dim 256 with one KV head. */
+typedef struct rfx_chunk rfx_chunk;
+typedef struct rfx_chunk_desc {
+  int B, S;                   /* streams, action tokens per stream */
+  int num_layers, num_steps;
+  int width, num_q_heads, mlp_dim, action_dim;
+  float eps, dt, softmax_scale;
+  const void* w_qkv;          /* bf16 [L][(Hq+2)*256][width], rfx_pack_weight RFX_PACK_QKV_ROPE per layer */
+  const void* w_o;            /* bf16 [L][width][Hq*256] */
+  const void* w_gu;           /* bf16 [L][2*mlp_dim][width], rfx_pack_weight RFX_PACK_GATE_UP per layer */
+  const void* w_down;         /* bf16 [L][width][mlp_dim] */
+  const float* norm_a1;       /* [2L+1][width]: input / post-attention norms per layer, then the final norm */
+  const float* mod_a2;        /* [num_steps][2L+1][width] or NULL (rfx_modulation outputs) */
+  const float* mod_b2;
+  const float* mod_gate;
+  const void* w_in;           /* bf16 [width][action_dim], action_in_proj */
+  const void* b_in;           /* bf16 [width] */
+  const void* w_out;          /* bf16 [action_dim][width], action_out_proj */
+  const void* b_out;          /* bf16 [action_dim] */
+  const float* rope_table;    /* [rope_max_pos][256] */
+  int rope_max_pos;
+  const int* positions;       /* [B*S] */
+  int capacity, n_ctx, quant_mode, scale_dtype;
+  int kv_splits;              /* key-block splits of the attention, 0 = one per 64-key block */
+  const void* const* k_ring;  /* HOST array of num_layers device pointers: int8/uint8 [B][capacity][256] */
+  const void* const* v_ring;
+  const void* const* k_scale; /* HOST arrays of device pointers: [B][capacity] */
+  const void* const* v_scale;
+  const void* const* k_zp;    /* RFX_QUANT_U8_REF only */
+  const void* const* v_zp;
+  const unsigned char* ctx_valid; /* [B][capacity] or NULL */
+  float* x;                   /* fp32 [B][S][action_dim]: x0 in, denoised actions out */
+} rfx_chunk_desc;
+/* Device workspace the executor needs (activations, partial sums, counters,
+ * task tables); 256-byte aligned, owned by the caller. */
+int rfx_chunk_workspace_size(const rfx_chunk_desc* desc, size_t* bytes);
+/* Builds the per-SM task lists and tensor maps and copies the tables into the
+ * workspace (synchronous copies: create before any stream capture). */
+int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, size_t workspace_bytes, rfx_chunk** out);
+/* Clears the counters and launches the executor on `stream`. */
+int rfx_chunk_run(rfx_chunk* chunk, void* stream);
+int rfx_chunk_destroy(rfx_chunk* chunk);
+
 /* ---------------------------------------------------- execution plans ---- */
 /* A plan is an ordered list of the launches above, validated and with their
  * TMA descriptors encoded once. rfx_plan_run launches them in order;
@@ -341,6 +394,8 @@ int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc);
 int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc);
+/* The chunk (not owned by the plan) is run at this point: counter clear + one launch. */
+int rfx_plan_add_chunk(rfx_plan* plan, rfx_chunk* chunk);
 /* The next op added is launched without programmatic dependent launch: it
  * starts only after everything before it has completed (a serialization point,
  * e.g. after writes to the KV ring that later kernels read before waiting). */

@@ -141,6 +141,23 @@ class NormDesc(Structure):
     ]
 
 
+class ChunkDesc(Structure):
+    _fields_ = [
+        ("B", c_int), ("S", c_int), ("num_layers", c_int), ("num_steps", c_int),
+        ("width", c_int), ("num_q_heads", c_int), ("mlp_dim", c_int), ("action_dim", c_int),
+        ("eps", c_float), ("dt", c_float), ("softmax_scale", c_float),
+        ("w_qkv", c_void_p), ("w_o", c_void_p), ("w_gu", c_void_p), ("w_down", c_void_p),
+        ("norm_a1", c_void_p), ("mod_a2", c_void_p), ("mod_b2", c_void_p), ("mod_gate", c_void_p),
+        ("w_in", c_void_p), ("b_in", c_void_p), ("w_out", c_void_p), ("b_out", c_void_p),
+        ("rope_table", c_void_p), ("rope_max_pos", c_int), ("positions", c_void_p),
+        ("capacity", c_int), ("n_ctx", c_int), ("quant_mode", c_int), ("scale_dtype", c_int), ("kv_splits", c_int),
+        ("k_ring", POINTER(c_void_p)), ("v_ring", POINTER(c_void_p)),
+        ("k_scale", POINTER(c_void_p)), ("v_scale", POINTER(c_void_p)),
+        ("k_zp", POINTER(c_void_p)), ("v_zp", POINTER(c_void_p)),
+        ("ctx_valid", c_void_p), ("x", c_void_p),
+    ]
+
+
 # Every entry point declared in include/rfx.h: name -> (argtypes, restype).
 SIGNATURES = {
     "rfx_version": ([], c_int),
@@ -162,6 +179,11 @@ SIGNATURES = {
     "rfx_copy_rows": ([POINTER(CopyRowsDesc), c_void_p], c_int),
     "rfx_rms_norm": ([POINTER(NormDesc), c_void_p], c_int),
     "rfx_plan_add_rms_norm": ([c_void_p, POINTER(NormDesc)], c_int),
+    "rfx_plan_add_chunk": ([c_void_p, c_void_p], c_int),
+    "rfx_chunk_workspace_size": ([POINTER(ChunkDesc), POINTER(c_size_t)], c_int),
+    "rfx_chunk_create": ([POINTER(ChunkDesc), c_void_p, c_size_t, POINTER(c_void_p)], c_int),
+    "rfx_chunk_run": ([c_void_p, c_void_p], c_int),
+    "rfx_chunk_destroy": ([c_void_p], c_int),
     "rfx_plan_add_barrier": ([c_void_p], c_int),
     "rfx_plan_create": ([POINTER(c_void_p)], c_int),
     "rfx_plan_destroy": ([c_void_p], c_int),
@@ -217,6 +239,6 @@ def ptr(t) -> int | None:
 
 __all__ = [n for n in dir() if n.startswith(("RFX_", "Rfx"))] + [
     "KvQuantDesc", "LinearDesc", "AttnDesc", "TimeCondDesc", "ModulationDesc", "ActionIoDesc", "CopyRowsDesc",
-    "NormDesc",
+    "NormDesc", "ChunkDesc",
     "SIGNATURES", "load", "check", "call", "ptr", "LIB_PATH", "c_ubyte",
 ]

@@ -1,0 +1,1673 @@
+// Persistent executor of one whole PI0.5 action chunk: all Euler steps, all
+// layers and the Euler tails run inside ONE kernel launch with one CTA per SM.
+//
+// Why: at one robot stream the chunk is a chain of ~1,450 small dependent
+// operations.  As separate launches each pays launch + setup + teardown
+// (3-4 us) on top of its useful time; here each dependency costs one release
+// / acquire of a global counter instead, and every CTA keeps streaming the
+// weights of its next GEMM tile while the rest of the GPU works on the
+// current phase.
+//
+// Work decomposition (T = B*S <= 64 tokens; per layer, in phase order):
+//   QKV   20 row tiles x 2 K-splits: tcgen05 GEMM of the packed [Wq;Wk;Wv]
+//         against the normed input; the second split to finish sums the two
+//         fp32 partials and applies RoPE (rows r / r+64 of a tile are the
+//         rotary pair) -> q (head-major), k_new, v_new (bf16).
+//   ATTN  (stream, 128-row query tile, key-block split): the partitioned
+//         attention of the new tokens over the int8 context ring + the new
+//         keys, on tcgen05 with TMEM accumulators (context rows are loaded and
+//         converted int8 -> bf16 K / f16 V in shared memory; per-token scales
+//         folded into the scores / probabilities) -> fp32 partial (O, m, l).
+//   COMB  rows of a query tile: log-sum-exp merge of the partials -> bf16.
+//   O     8 row tiles x 8 K-splits -> fp32 partials.
+//   FIN_O per token: h += gate * bf16(sum of O partials); post-attention
+//         (Ada)RMSNorm -> GEMM input.
+//   GU    64 row tiles x 2 K-splits, last split: GELU-tanh(gate) * up.
+//   DOWN  8 row tiles x 8 K-splits -> fp32 partials.
+//   FIN_D per token: h += gate * bf16(sum of down partials); next layer's
+//         input norm, or after the last layer the Euler tail (final norm,
+//         action_out_proj, x += dt*v, next step's action_in_proj, norm).
+//
+// Every phase counts its finished items on a global counter (release); the
+// consumers of the phase wait for the count of the current use (acquire).
+// Counters only grow within a chunk and are cleared before each chunk.
+// Partials are summed in a fixed order, so results do not depend on timing.
+//
+// Roles (192 threads, as in the standalone kernels): warp 0 lane 0 streams
+// weight / activation tiles through a 7-stage TMA ring (weights are issued
+// before the tile's input is ready), warp 1 lane 0 issues tcgen05.mma, warps
+// 2-5 do everything else.  The attention tiles reuse the ring's shared memory;
+// the producer drains the ring before an attention item and resumes after it.
+//
+// Every wait is bounded (about one second); a wait that runs out records a
+// device status code and raises a chunk-wide abort flag, after which every
+// role leaves its loop, in-flight copies are drained and TMEM is freed.
+#include "rfx_internal.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace rfx {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kNT = 64;  // token tile: T <= 64
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 7;
+constexpr int kWBytes = kBM * kBK * 2;  // 16 KB weight tile
+constexpr int kXBytes = kNT * kBK * 2;  // 8 KB activation tile
+constexpr int kOffX = kStages * kWBytes;
+constexpr int kOffRed = kOffX + kStages * kXBytes;  // 168 KB
+constexpr int kRedBytes = kNT * kBM * 4;            // [t][128] fp32
+constexpr int kOffSmall = kOffRed + kRedBytes;      // 200 KB
+constexpr int kSmallBytes = 8192;
+constexpr int kSmemBytes = kOffSmall + kSmallBytes + 1024;
+
+// attention overlay on the ring region
+constexpr int kD = 256, kKB = 64, kQR = 128;
+constexpr int kOffAQ = 0;        // 4 x [128 x 64] bf16
+constexpr int kOffAK = 65536;    // 4 x [64 x 64] bf16
+constexpr int kOffAV = 98304;    // 4 x [64 x 64] f16, MN-major blocks
+constexpr int kOffAP = 131072;   // [128 x 64] f16
+static_assert(kOffAP + 16384 <= kOffRed, "attention tiles must fit in the ring region");
+
+// small region (byte offsets)
+constexpr int kSmFull = 0;         // 8 mbarriers
+constexpr int kSmEmpty = 64;       // 8 mbarriers
+constexpr int kSmAccFull = 128;
+constexpr int kSmAccFree = 136;
+constexpr int kSmQFull = 144;
+constexpr int kSmConv = 152;
+constexpr int kSmSFull = 160;
+constexpr int kSmPReady = 168;
+constexpr int kSmOFull = 176;
+constexpr int kSmAttnDone = 184;
+constexpr int kSmTmem = 192;
+constexpr int kSmBcast = 256;      // 16 ints
+constexpr int kSmRed4 = 320;       // 8 floats
+constexpr int kSmScales = 512;     // 8 x 64 floats (2 KB)
+constexpr int kSmRow = 2560;       // 1024 floats
+constexpr int kSmXs = 6656;        // 64 floats
+static_assert(kSmXs + 256 <= kSmallBytes, "small region");
+
+enum TaskType : int { kTInit = 0, kTQkv = 1, kTO = 2, kTGu = 3, kTDown = 4, kTAttn = 5, kTComb = 6, kTFinO = 7, kTFinD = 8 };
+enum Op : int { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3 };
+// counter lines (32 u32 = 128 B apart)
+enum CtrLine : int { kCXn = 0, kCQkv = 1, kCAttn = 2, kCComb = 3, kCPo = 4, kCXn2 = 5, kCAct = 6, kCPd = 7, kCAbort = 8,
+                     kCTileQkv = 16, kCTileGu = 48, kNumCtrLines = 176 };
+
+
+enum ChunkError : int { kDevTimeoutDependency = 8 };
+
+struct OpCfg {
+  int rows;    // weight rows per layer
+  int K;       // reduction length
+  int m_tiles;
+  int splits;
+  int kb;      // k-blocks per split
+  float* part; // [m_tiles][splits][kNT][128] fp32
+};
+
+struct ChunkParams {
+  int T, S, B, NL, steps, W, Hq, F, A, NN;
+  int n_ctx, cap, mode, scale_bf16;
+  int q_tiles, attn_splits, n_ctx_blocks, n_blocks;
+  int n_attn, n_comb, n_fin;
+  float eps, dt, scale_log2;
+  OpCfg op[4];
+  const float* a1;    // [NN][W]
+  const float* a2;    // [steps][NN][W] or null
+  const float* b2;
+  const float* gate;
+  const __nv_bfloat16* w_in;   // [W][A]
+  const __nv_bfloat16* b_in;   // [W]
+  const __nv_bfloat16* w_out;  // [A][W]
+  const __nv_bfloat16* b_out;  // [A]
+  const float* rope;
+  int rope_max_pos;
+  const int* pos;              // [T]
+  const uint8_t* const* k_ring;  // [NL] -> [B][cap][256]
+  const uint8_t* const* v_ring;
+  const void* const* k_scale;    // [NL] -> [B][cap]
+  const void* const* v_scale;
+  const void* const* k_zp;
+  const void* const* v_zp;
+  const unsigned char* ctx_valid;  // [B][cap] or null
+  float* x;                    // [B][S][A]
+  __nv_bfloat16* h;            // [T][W]
+  __nv_bfloat16* xn;           // [T][W]
+  __nv_bfloat16* q;            // [B][Hq][S][256]
+  __nv_bfloat16* kn;           // [T][256]
+  __nv_bfloat16* vn;
+  __nv_bfloat16* attn_out;     // [T][Hq*256]
+  __nv_bfloat16* act;          // [T][F]
+  float* ws_o;
+  float2* ws_ml;
+  unsigned* ctr;
+  const int4* step_tasks;
+  const int* step_off;         // [grid + 1]
+  const int4* init_tasks;
+  const int* init_off;
+  int* status;
+  unsigned long long* trace;  // [grid][trace_tasks][8] stamps + task of the first step, or null
+  int trace_tasks;
+};
+
+struct Maps {
+  CUtensorMap w[4];
+  CUtensorMap x[4];
+  CUtensorMap q;
+};
+
+// ------------------------------------------------------------ sync helpers ---
+__device__ __forceinline__ unsigned* ctr_ptr(const ChunkParams& p, int line) { return p.ctr + line * 32; }
+
+__device__ __forceinline__ bool aborted(const ChunkParams& p) {
+  return *reinterpret_cast<volatile unsigned*>(ctr_ptr(p, kCAbort)) != 0u;
+}
+__device__ __forceinline__ void raise_abort(const ChunkParams& p, int code) {
+  record_error(p.status, code);
+  atomicExch(ctr_ptr(p, kCAbort), 1u);
+}
+// Bounded mbarrier wait that also gives up when the chunk was aborted.
+__device__ bool bar_wait(const ChunkParams& p, uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (aborted(p)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_abort(p, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// Bounded wait until a phase counter reaches `target`.  Polls with relaxed
+// loads (an acquire load per poll would keep invalidating the SM's L1) and
+// makes the success an acquire with one fence.
+__device__ bool ctr_wait(const ChunkParams& p, int line, unsigned target) {
+  const unsigned* c = ctr_ptr(p, line);
+  if (ld_relaxed_gpu(c) >= target) {
+    fence_acq_rel_gpu();
+    return true;
+  }
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 16; ++i) {
+      if (ld_relaxed_gpu(c) >= target) {
+        fence_acq_rel_gpu();
+        return true;
+      }
+      __nanosleep(32);
+    }
+    if (aborted(p)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_abort(p, kDevTimeoutDependency);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void ctr_signal(const ChunkParams& p, int line) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr_ptr(p, line)) : "memory");
+}
+__device__ __forceinline__ unsigned ctr_fetch_add(const ChunkParams& p, int line) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr_ptr(p, line)) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// named barrier 1 over the 128 worker threads
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool workers_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+// One worker waits for the counter (acquire); the barrier that follows orders
+// every worker's later reads after it.  All workers agree on the outcome.
+__device__ __forceinline__ bool workers_ctr_wait(const ChunkParams& p, int et, int line, unsigned target) {
+  bool ok = true;
+  if (et == 0) ok = ctr_wait(p, line, target);
+  return workers_all(ok);
+}
+// All workers' global writes are ordered before the barrier; one worker then
+// releases the phase counter (cumulative release at GPU scope).
+__device__ __forceinline__ void workers_publish(const ChunkParams& p, int et, int line) {
+  workers_sync();
+  if (et == 0) {
+    fence_acq_rel_gpu();
+    ctr_signal(p, line);
+  }
+}
+
+__device__ __forceinline__ void stamp(unsigned long long* slot, int k) {
+  if (slot) slot[k] = globaltimer_ns();
+}
+
+// ---------------------------------------------------------------- math ---
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  const float inner = kBeta * (x + kKappa * x * x * x);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
+__device__ __forceinline__ void unpack8_bf16(uint4 raw, float (&f)[8]) {
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 v = __bfloat1622float2(h2[e]);
+    f[2 * e] = v.x;
+    f[2 * e + 1] = v.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8_bf16(const float (&y)[8]) {
+  return make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+}
+__device__ __forceinline__ float load_scalar(const void* ptr, long i, bool bf16) {
+  return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(ptr)[i]) : static_cast<const float*>(ptr)[i];
+}
+__device__ __forceinline__ float round_to(float x, bool bf16) { return bf16 ? bf16_round(x) : x; }
+
+// Per-op GEMM configuration; a switch keeps the parameter accesses static
+// (a runtime index into the kernel parameters would copy them to local memory).
+__device__ __forceinline__ OpCfg op_cfg(const ChunkParams& p, int op) {
+  switch (op) {
+    case kOpQkv: return p.op[kOpQkv];
+    case kOpO: return p.op[kOpO];
+    case kOpGu: return p.op[kOpGu];
+    default: return p.op[kOpDown];
+  }
+}
+
+// Modulation vectors of norm n at Euler step tau ([steps][NN][W]).
+__device__ __forceinline__ long mod_off(const ChunkParams& p, int tau, int n) {
+  return (static_cast<long>(tau) * p.NN + n) * p.W;
+}
+
+// Norm vectors of one norm for the worker's 8 features (f0 = et*8).
+struct NormVec {
+  float a1[8], a2[8], b2[8];
+};
+__device__ __forceinline__ void load8(const float* src, float (&dst)[8]) {
+  *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+  *reinterpret_cast<float4*>(dst + 4) = *reinterpret_cast<const float4*>(src + 4);
+}
+__device__ __forceinline__ void load_norm_vec(const ChunkParams& p, int et, int tau, int n, NormVec& v) {
+  const int f0 = et * 8;
+  load8(p.a1 + static_cast<long>(n) * p.W + f0, v.a1);
+  if (p.a2) load8(p.a2 + mod_off(p, tau, n) + f0, v.a2);
+  if (p.b2) load8(p.b2 + mod_off(p, tau, n) + f0, v.b2);
+}
+
+// (Ada)RMSNorm of one token row held as 8 features per worker thread:
+// y = ((x*rstd)*a1)*a2 + b2 (fp32, rounded by the caller), rstd =
+// rsqrt(mean(x^2) + eps).  The reduction order matches the standalone norm
+// kernel (per thread, then warp, then the four warps in order).
+__device__ void norm_row(const ChunkParams& p, int et, const float (&hv)[8], const NormVec& v, float* red4,
+                         float (&y)[8]) {
+  const int lane = et & 31, wq = et >> 5;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss = fmaf(hv[e], hv[e], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) red4[wq] = ss;
+  workers_sync();
+  const float rstd = rsqrtf((red4[0] + red4[1] + red4[2] + red4[3]) / static_cast<float>(p.W) + p.eps);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float x = __fmul_rn(__fmul_rn(hv[e], rstd), v.a1[e]);
+    if (p.a2) x = __fmul_rn(x, v.a2[e]);
+    if (p.b2) x = __fadd_rn(x, v.b2[e]);
+    y[e] = x;
+  }
+  workers_sync();  // red4 is reused by the next row
+}
+
+// h_row[o] = bf16(sum_a xs[a] * W_in[o][a] + b_in[o]) for the worker's 8 features.
+__device__ __forceinline__ void action_in8(const ChunkParams& p, int et, const float* xs, float (&hv)[8]) {
+#pragma unroll 1
+  for (int e = 0; e < 8; ++e) {
+    const int o = et * 8 + e;
+    const __nv_bfloat16* wr = p.w_in + static_cast<long>(o) * p.A;
+    float acc = 0.f;
+    for (int a = 0; a < p.A; a += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(wr + a);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(w2[q]);
+        acc = fmaf(f.x, xs[a + 2 * q], acc);
+        acc = fmaf(f.y, xs[a + 2 * q + 1], acc);
+      }
+    }
+    hv[e] = bf16_round(acc + (p.b_in ? __bfloat162float(p.b_in[o]) : 0.f));
+  }
+}
+
+// ------------------------------------------------------- worker: GEMM tile ---
+// Accumulator (row = TMEM lane, 64 token columns) -> fp32 partial in global
+// memory; for QKV / gate-up the split that finishes last sums the partials
+// and runs the epilogue.  Returns false when the chunk was aborted.
+__device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int op,
+                            int layer, int m, int split, uint32_t& acc_cnt, unsigned long long* ts) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3;
+  const int row = quad * 32 + lane;
+  uint64_t* acc_full = reinterpret_cast<uint64_t*>(small + kSmAccFull);
+  uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
+  int* bcast = reinterpret_cast<int*>(small + kSmBcast);
+  const OpCfg oc = op_cfg(p, op);
+  bool ok = true;
+  if (lane == 0) ok = bar_wait(p, acc_full, acc_cnt & 1, kDevTimeoutMmaDone);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  ++acc_cnt;
+  ok = workers_all(ok);
+  if (!ok) return false;
+  if (et == 0) stamp(ts, 1);
+  tc_fence_after();
+  // accumulator row (this thread's TMEM lane), 16 token columns at a time ->
+  // fp32 partial [t][128] in global memory
+  float* part = oc.part + (static_cast<long>(m) * oc.splits + split) * kNT * kBM;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[16];
+    tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int t = c * 16 + e;
+      if (t < p.T) __stcg(part + t * kBM + row, __uint_as_float(r[e]));
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acc_free);
+  if (et == 0) stamp(ts, 6);
+  const bool last_arriver = op == kOpQkv || op == kOpGu;
+  if (!last_arriver) {
+    workers_publish(p, et, op == kOpO ? kCPo : kCPd);
+    if (et == 0) stamp(ts, 7);
+    return true;
+  }
+  workers_sync();
+  if (et == 0) {
+    const int line = (op == kOpQkv ? kCTileQkv : kCTileGu) + m;
+    fence_acq_rel_gpu();
+    const unsigned old = ctr_fetch_add(p, line);  // releases this split's partial, acquires the others'
+    bcast[0] = ((old + 1) % static_cast<unsigned>(oc.splits)) == 0u ? 1 : 0;
+  }
+  workers_sync();
+  if (bcast[0] == 0) return true;
+  // last split of this tile.  RoPE cos / sin of this thread's epilogue items
+  // (item k: it = et + 128 k, token it / 16, rows (it % 16) * 4) are requested
+  // together with the partial sums.
+  constexpr int kItems = kNT * 16 / 128;
+  float4 rc[kItems], rsn[kItems];
+  const bool rotary = op == kOpQkv && (m >> 1) <= p.Hq;
+  if (rotary) {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = et + 128 * k;
+      if (it < p.T * 16) {
+        int pos = p.pos[it >> 4];
+        pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
+        const float* cs = p.rope + static_cast<long>(pos) * 256 + (m & 1) * 64 + (it & 15) * 4;
+        rc[k] = *reinterpret_cast<const float4*>(cs);
+        rsn[k] = *reinterpret_cast<const float4*>(cs + 128);
+      }
+    }
+  }
+  // sum all splits in split order -> red[t][row]
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  const float* pm = oc.part + static_cast<long>(m) * oc.splits * kNT * kBM;
+#pragma unroll
+  for (int t0 = 0; t0 < kNT; t0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = (t0 + e < p.T) ? __ldcg(pm + (t0 + e) * kBM + row) : 0.f;
+    for (int s = 1; s < oc.splits; ++s) {
+      float w[16];
+      const float* ps = pm + static_cast<long>(s) * kNT * kBM;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) w[e] = (t0 + e < p.T) ? __ldcg(ps + (t0 + e) * kBM + row) : 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] += w[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) red[(t0 + e) * kBM + row] = v[e];
+  }
+  workers_sync();
+  // epilogue on row pairs (i, i+64), 4 rows per item
+  const int items = p.T * 16;
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const int it = et + 128 * k;
+    if (it >= items) break;
+    const int t = it >> 4;
+    const int i = (it & 15) * 4;
+    const float4 va = *reinterpret_cast<const float4*>(red + t * kBM + i);
+    const float4 vc = *reinterpret_cast<const float4*>(red + t * kBM + i + 64);
+    const float v0[4] = {va.x, va.y, va.z, va.w};
+    const float v1[4] = {vc.x, vc.y, vc.z, vc.w};
+    const int b = t / p.S, s = t - b * p.S;
+    if (op == kOpGu) {
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float g = bf16_round(v0[j]);
+        const float u = bf16_round(v1[j]);
+        y[j] = __fmul_rn(bf16_round(gelu_tanh(g)), u);
+      }
+      *reinterpret_cast<uint2*>(p.act + static_cast<long>(t) * p.F + m * 64 + i) =
+          make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+    } else {
+      const int head = m >> 1;
+      const int d0 = (m & 1) * 64 + i;
+      float r0[4], r1[4];
+      if (rotary) {
+        const float cc[4] = {rc[k].x, rc[k].y, rc[k].z, rc[k].w};
+        const float sn[4] = {rsn[k].x, rsn[k].y, rsn[k].z, rsn[k].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float x1 = bf16_round(v0[j]);
+          const float x2 = bf16_round(v1[j]);
+          r0[j] = __fsub_rn(__fmul_rn(x1, cc[j]), __fmul_rn(x2, sn[j]));
+          r1[j] = __fadd_rn(__fmul_rn(x2, cc[j]), __fmul_rn(x1, sn[j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          r0[j] = v0[j];
+          r1[j] = v1[j];
+        }
+      }
+      __nv_bfloat16* dst;
+      if (head < p.Hq)
+        dst = p.q + ((static_cast<long>(b) * p.Hq + head) * p.S + s) * 256;
+      else if (head == p.Hq)
+        dst = p.kn + static_cast<long>(t) * 256;
+      else
+        dst = p.vn + static_cast<long>(t) * 256;
+      *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_bf16x2(r0[0], r0[1]), pack_bf16x2(r0[2], r0[3]));
+      *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_bf16x2(r1[0], r1[1]), pack_bf16x2(r1[2], r1[3]));
+    }
+  }
+  workers_publish(p, et, op == kOpQkv ? kCQkv : kCAct);
+  return true;
+}
+
+// ----------------------------------------------------- worker: attention ---
+// Converts 16 quantized values (one 16-byte chunk of a key row) into bf16 (K)
+// or f16 (V) and stores them into a 128-byte-swizzled tile.
+template <bool IS_K>
+__device__ __forceinline__ void convert16r(uint4 raw, uint8_t* tile_base, int key, int g, int mode, bool sbf16,
+                                           float sc, float zp) {
+  const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&raw);
+  float f[16];
+  if (mode == kQuantI8Sym) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = static_cast<float>(static_cast<int8_t>(b8[e]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float t = round_to(__fsub_rn(static_cast<float>(b8[e]), zp), sbf16);
+      f[e] = round_to(__fmul_rn(t, sc), sbf16);
+    }
+  }
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = IS_K ? pack_bf16x2(f[2 * e], f[2 * e + 1]) : pack_f16x2(f[2 * e], f[2 * e + 1]);
+  uint8_t* atom = tile_base + (g >> 2) * 8192;
+  const int c0 = (g & 3) * 2;
+  *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int layer,
+                            unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, unsigned long long* ts) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3;
+  uint8_t* sK = smem + kOffAK;
+  uint8_t* sV = smem + kOffAV;
+  uint8_t* sP = smem + kOffAP;
+  float* ks_s = reinterpret_cast<float*>(small + kSmScales);
+  float* vs_s = ks_s + 64;
+  float* kdq_s = vs_s + 64;
+  float* vdq_s = kdq_s + 64;
+  float* kzp_s = vdq_s + 64;
+  float* vzp_s = kzp_s + 64;
+  int* nb_s = reinterpret_cast<int*>(vzp_s + 64);
+  float* kadd_s = reinterpret_cast<float*>(nb_s + 64);
+  uint64_t* conv_done = reinterpret_cast<uint64_t*>(small + kSmConv);
+  uint64_t* s_full = reinterpret_cast<uint64_t*>(small + kSmSFull);
+  uint64_t* p_ready = reinterpret_cast<uint64_t*>(small + kSmPReady);
+  uint64_t* o_full = reinterpret_cast<uint64_t*>(small + kSmOFull);
+  uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
+  uint64_t* attn_done = reinterpret_cast<uint64_t*>(small + kSmAttnDone);
+  const uint32_t tmO = tmem, tmS = tmem + 256;
+  const int blk_begin = sp * p.n_blocks / p.attn_splits;
+  const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk_begin;
+  const int r = quad * 32 + lane;
+  const int R = qt * kQR + r;
+  const bool row_valid = R < p.Hq * p.S;
+  const int s_row = row_valid ? R % p.S : 0;
+  const int h_row = row_valid ? R / p.S : 0;
+  const bool sbf16 = p.scale_bf16 != 0;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+  const uint8_t* kring = p.k_ring[layer];
+  const uint8_t* vring = p.v_ring[layer];
+  const void* kscale = p.k_scale[layer];
+  const void* vscale = p.v_scale[layer];
+  const void* kzp = p.k_zp[layer];
+  const void* vzp = p.v_zp[layer];
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  bool new_ready = false;
+
+  for (int jl = 0; jl < nbl && ok; ++jl) {
+    const int j = blk_begin + jl;
+    const bool is_ctx = j < p.n_ctx_blocks;
+    if (jl > 0) {
+      bool w = true;
+      if (lane == 0) w = bar_wait(p, o_full, (blk_cnt - 1) & 1, kDevTimeoutMmaDone);
+      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+      if (!ok) break;
+    }
+    if (is_ctx) {
+      // int8 rows straight from the ring (no dependency on this chunk's work);
+      // the first half of this thread's 16-byte chunks is requested here, the
+      // second half while the first is converted
+      auto ctx_chunk = [&](int q) {
+        const int it = et + q * 128;  // 0..2047: K chunks then V chunks
+        const bool isv = it >= kKB * 16;
+        const int w = isv ? it - kKB * 16 : it;
+        const int key = w >> 4, g = w & 15;
+        long slot = static_cast<long>(j) * kKB + key;
+        if (slot >= p.cap) slot = p.cap - 1;
+        return *reinterpret_cast<const uint4*>((isv ? vring : kring) + (static_cast<long>(b) * p.cap + slot) * kD +
+                                               g * 16);
+      };
+      uint4 raw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) raw[q] = ctx_chunk(q);
+      if (et < 64) {
+        const long slot = static_cast<long>(j) * kKB + et;
+        const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
+        bool valid = slot < p.n_ctx;
+        if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
+        kadd_s[et] = valid ? 0.f : -INFINITY;
+        if (p.mode == kQuantI8Sym) {
+          ks_s[et] = valid ? static_cast<const float*>(kscale)[gi] * p.scale_log2 : 0.f;
+          vs_s[et] = valid ? static_cast<const float*>(vscale)[gi] : 0.f;
+        } else {
+          ks_s[et] = valid ? p.scale_log2 : 0.f;
+          vs_s[et] = 1.f;
+          kdq_s[et] = load_scalar(kscale, gi, sbf16);
+          vdq_s[et] = load_scalar(vscale, gi, sbf16);
+          kzp_s[et] = load_scalar(kzp, gi, sbf16);
+          vzp_s[et] = load_scalar(vzp, gi, sbf16);
+        }
+      }
+      workers_sync();
+#pragma unroll
+      for (int quarter = 0; quarter < 4; ++quarter) {
+        uint4 nxt[4];
+        if (quarter < 3) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) nxt[q] = ctx_chunk(4 * (quarter + 1) + q);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int it = et + (quarter * 4 + q) * 128;
+          const bool isv = it >= kKB * 16;
+          const int w = isv ? it - kKB * 16 : it;
+          const int key = w >> 4, g = w & 15;
+          float sc = 0.f, zp = 0.f;
+          if (p.mode != kQuantI8Sym) {
+            sc = isv ? vdq_s[key] : kdq_s[key];
+            zp = isv ? vzp_s[key] : kzp_s[key];
+          }
+          if (isv)
+            convert16r<false>(raw[q], sV, key, g, p.mode, sbf16, sc, zp);
+          else
+            convert16r<true>(raw[q], sK, key, g, p.mode, sbf16, sc, zp);
+        }
+        if (quarter < 3) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) raw[q] = nxt[q];
+        }
+      }
+    } else {
+      if (!new_ready) {
+        ok = workers_ctr_wait(p, et, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles) * (use + 1));
+        if (!ok) break;
+        new_ready = true;
+      }
+      const int nb0 = (j - p.n_ctx_blocks) * kKB;
+      if (et < 64) {
+        const int kk = nb0 + et;
+        ks_s[et] = kk < p.S ? p.scale_log2 : 0.f;
+        kadd_s[et] = kk < p.S ? 0.f : -INFINITY;
+        vs_s[et] = 1.f;
+        nb_s[et] = 0;
+      }
+#pragma unroll 2
+      for (int it = et; it < 2 * kKB * 32; it += 128) {
+        const bool isv = it >= kKB * 32;
+        const int w = isv ? it - kKB * 32 : it;
+        const int key = w >> 5, c = w & 31;
+        const int kk = nb0 + key;
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+        if (kk < p.S) {
+          const __nv_bfloat16* src = (isv ? p.vn : p.kn) + (static_cast<long>(b) * p.S + kk) * kD + c * 8;
+          raw = __ldcg(reinterpret_cast<const uint4*>(src));
+        }
+        uint8_t* atom = (isv ? sV : sK) + (c >> 3) * 8192;
+        if (isv) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h2[e]);
+            w4[e] = pack_f16x2(f.x, f.y);
+          }
+          raw = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+        *reinterpret_cast<uint4*>(atom + sw128_offset(key, c & 7)) = raw;
+      }
+    }
+    fence_proxy_async_smem();
+    workers_sync();
+    if (lane == 0) mbar_arrive(conv_done);
+
+    // ---- softmax on S ----
+    {
+      bool w = true;
+      if (lane == 0) w = bar_wait(p, s_full, blk_cnt & 1, kDevTimeoutMmaDone);
+      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+      if (!ok) break;
+    }
+    ++blk_cnt;
+    if (et == 0 && jl == 0) stamp(ts, 1);
+    tc_fence_after();
+    // two passes over the scores in TMEM (16 columns at a time): the block
+    // max, then p = 2^(z - m) -> P tile; scores in log2 units, one FMA per key
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int q = 0; q < kKB / 16; ++q) {
+      uint32_t rr[16];
+      tmem_ld16(tmS + lane_base + q * 16, rr);
+      tmem_wait_ld();
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = 4 * q + cc;
+        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+        mx[0] = fmaxf(mx[0], fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x));
+        mx[1] = fmaxf(mx[1], fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y));
+        mx[2] = fmaxf(mx[2], fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z));
+        mx[3] = fmaxf(mx[3], fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w));
+      }
+    }
+    const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    const float m_new = fmaxf(m_run, bmax);
+    bool need = false;
+    float m_use;
+    if (m_run == -INFINITY) {
+      m_use = m_new;
+    } else if (m_new > m_run + 8.f) {
+      need = true;
+      m_use = m_new;
+    } else {
+      m_use = m_run;
+    }
+    const float alpha = need ? exp2f(m_run - m_use) : 1.f;
+    const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < kKB / 16; ++q) {
+      uint32_t rr[16];
+      tmem_ld16(tmS + lane_base + q * 16, rr);
+      tmem_wait_ld();
+      float pvq[16];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = 4 * q + cc;
+        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+        const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
+        const float zz[4] = {fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x),
+                             fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y),
+                             fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z),
+                             fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w)};
+        const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pe = ex2_approx(zz[e] - m_sub);
+          ps[e] += pe;
+          pvq[4 * cc + e] = pe * vv[e];
+        }
+      }
+      // keys 16q .. 16q+15 of row r: two 16-byte chunks of the P tile
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const uint4 v = make_uint4(pack_f16x2(pvq[8 * h2 + 0], pvq[8 * h2 + 1]),
+                                   pack_f16x2(pvq[8 * h2 + 2], pvq[8 * h2 + 3]),
+                                   pack_f16x2(pvq[8 * h2 + 4], pvq[8 * h2 + 5]),
+                                   pack_f16x2(pvq[8 * h2 + 6], pvq[8 * h2 + 7]));
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, 2 * q + h2)) = v;
+      }
+    }
+    const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+    l_run = l_run * alpha + psum;
+    m_run = m_use;
+    if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < kD / 16; c0 += 2) {
+        uint32_t rr[2][16];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) rr[q][e] = __float_as_uint(__uint_as_float(rr[q][e]) * alpha);
+          tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+        }
+      }
+      tmem_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_ready);
+  }
+
+  // ---- epilogue: partial (O, m, l) of this split ----
+  if (ok && nbl > 0) {
+    bool w = true;
+    if (lane == 0) w = bar_wait(p, o_full, (blk_cnt - 1) & 1, kDevTimeoutMmaDone);
+    ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+  }
+  if (ok && nbl > 0) {
+    tc_fence_after();
+    const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits + sp;
+    const bool final_out = p.attn_splits == 1;
+    const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+    const long tok = static_cast<long>(b) * p.S + s_row;
+    __nv_bfloat16* orow = p.attn_out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
+    float* wrow_o = p.ws_o + (wcta * (kD / 16) * kQR + r) * 16;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kD / 16; c0 += 2) {
+      uint32_t rr[2][16];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+      tmem_wait_ld();
+      if (!row_valid) continue;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int c = c0 + q;
+        if (final_out) {
+          uint32_t w8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            w8[e] = pack_bf16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
+          *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+          *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            __stcg(reinterpret_cast<float4*>(wrow_o + static_cast<long>(c) * kQR * 16 + 4 * e),
+                   make_float4(__uint_as_float(rr[q][4 * e]), __uint_as_float(rr[q][4 * e + 1]),
+                               __uint_as_float(rr[q][4 * e + 2]), __uint_as_float(rr[q][4 * e + 3])));
+        }
+      }
+    }
+    if (!final_out && row_valid) __stcg(p.ws_ml + wcta * kQR + r, make_float2(m_run, l_run));
+  }
+  // TMEM and the ring's shared memory are free again
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_arrive(acc_free);
+    mbar_arrive(attn_done);
+  }
+  if (!ok) return false;
+  workers_publish(p, et, kCAttn);
+  return true;
+}
+
+// ------------------------------------------------------ worker: combine ---
+__device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsigned use, int b, int qt, int r0, int r1,
+                            unsigned long long* ts) {
+  if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
+  if (et == 0) stamp(ts, 1);
+  const int wq = et >> 5, lane = et & 31;
+  constexpr int kBatch = 8;  // partials whose loads are in flight together
+  for (int r = r0 + wq; r < r1; r += 4) {
+    const int R = qt * kQR + r;
+    if (R >= p.Hq * p.S) continue;
+    const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < p.attn_splits; ++s) {
+      const float2 v = __ldcg(p.ws_ml + (base + s) * kQR + r);
+      if (v.y > 0.f) M = fmaxf(M, v.x);
+    }
+    float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < p.attn_splits; s0 += kBatch) {
+      float4 a[kBatch], c[kBatch];
+      float2 ml[kBatch];
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        if (s0 + q < p.attn_splits) {
+          const float* o = p.ws_o + (((base + s0 + q) * (kD / 16) + (lane >> 1)) * kQR + r) * 16 + (lane & 1) * 8;
+          a[q] = __ldcg(reinterpret_cast<const float4*>(o));
+          c[q] = __ldcg(reinterpret_cast<const float4*>(o + 4));
+          ml[q] = __ldcg(p.ws_ml + (base + s0 + q) * kQR + r);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        if (s0 + q >= p.attn_splits || ml[q].x == -INFINITY || ml[q].y <= 0.f) continue;
+        const float w = exp2f(ml[q].x - M);
+        L += w * ml[q].y;
+        acc[0] += w * a[q].x; acc[1] += w * a[q].y; acc[2] += w * a[q].z; acc[3] += w * a[q].w;
+        acc[4] += w * c[q].x; acc[5] += w * c[q].y; acc[6] += w * c[q].z; acc[7] += w * c[q].w;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int s_row = R % p.S, h_row = R / p.S;
+    __nv_bfloat16* orow =
+        p.attn_out + (static_cast<long>(b) * p.S + s_row) * (static_cast<long>(p.Hq) * kD) + h_row * kD + lane * 8;
+    *reinterpret_cast<uint4*>(orow) = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv),
+                                                 pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                                                 pack_bf16x2(acc[4] * inv, acc[5] * inv),
+                                                 pack_bf16x2(acc[6] * inv, acc[7] * inv));
+  }
+  workers_publish(p, et, kCComb);
+  return true;
+}
+
+// ------------------------------------------ worker: per-token finalization ---
+// kind kTInit: h = action_in_proj(x) at the first step; kTFinO / kTFinD: the
+// gated residual of o_proj / down_proj.  Then the next norm (or the Euler tail
+// after the last layer).
+__device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small, int et, int kind, int tau, int layer, int t,
+                           unsigned long long* ts) {
+  const int lane = et & 31, wq = et >> 5;
+  float* red4 = reinterpret_cast<float*>(small + kSmRed4);
+  float* row = reinterpret_cast<float*>(small + kSmRow);
+  float* xs = reinterpret_cast<float*>(small + kSmXs);
+  const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
+  const int f0 = et * 8;
+  const int b = t / p.S, s = t - b * p.S;
+  const bool tail = kind == kTFinD && layer == p.NL - 1;
+  const bool next_step = tail && tau + 1 < p.steps;
+  // everything that does not depend on the phase input is requested first
+  NormVec nv1;
+  const int n1 = kind == kTInit ? 0 : (kind == kTFinO ? 2 * layer + 1 : (tail ? 2 * p.NL : 2 * (layer + 1)));
+  load_norm_vec(p, et, tau, n1, nv1);
+  float g[8];
+  if (kind != kTInit && p.gate) load8(p.gate + mod_off(p, tau, kind == kTFinO ? 2 * layer : 2 * layer + 1) + f0, g);
+  float hv[8];
+  if (kind == kTInit) {
+    if (et < p.A) xs[et] = bf16_round(p.x[(static_cast<long>(b) * p.S + s) * p.A + et]);
+    workers_sync();
+    action_in8(p, et, xs, hv);
+  } else {
+    const int op = kind == kTFinO ? kOpO : kOpDown;
+    const OpCfg oc = op_cfg(p, op);
+    if (!workers_ctr_wait(p, et, kind == kTFinO ? kCPo : kCPd,
+                          static_cast<unsigned>(oc.m_tiles * oc.splits) * (use + 1)))
+      return false;
+    if (et == 0) stamp(ts, 1);
+    const int m = f0 / kBM, r0 = f0 % kBM;
+    uint4 hraw = __ldcg(reinterpret_cast<const uint4*>(p.h + static_cast<long>(t) * p.W + f0));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < oc.splits; s0 += 8) {
+      float4 a[8], c[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (s0 + q < oc.splits) {
+          const float* ps = oc.part + ((static_cast<long>(m) * oc.splits + s0 + q) * kNT + t) * kBM + r0;
+          a[q] = __ldcg(reinterpret_cast<const float4*>(ps));
+          c[q] = __ldcg(reinterpret_cast<const float4*>(ps + 4));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (s0 + q < oc.splits) {
+          acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
+          acc[4] += c[q].x; acc[5] += c[q].y; acc[6] += c[q].z; acc[7] += c[q].w;
+        }
+      }
+    }
+    float hres[8];
+    unpack8_bf16(hraw, hres);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = bf16_round(acc[e]);
+      const float ga = p.gate ? bf16_round(__fmul_rn(g[e], a)) : a;
+      hv[e] = bf16_round(__fadd_rn(hres[e], ga));
+    }
+  }
+  if (tail) {
+    // final norm -> action_out_proj -> x += bf16(dt * v) -> next step's action_in_proj
+    float y[8];
+    norm_row(p, et, hv, nv1, red4, y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) row[f0 + e] = bf16_round(y[e]);
+    workers_sync();
+#pragma unroll 1
+    for (int a = wq; a < p.A; a += 4) {
+      const __nv_bfloat16* wr = p.w_out + static_cast<long>(a) * p.W;
+      float acc = 0.f;
+      for (int k = lane * 8; k < p.W; k += 256) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(wr + k);
+        const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(w2[e]);
+          acc = fmaf(f.x, row[k + 2 * e], acc);
+          acc = fmaf(f.y, row[k + 2 * e + 1], acc);
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        const float v = bf16_round(acc + (p.b_out ? __bfloat162float(p.b_out[a]) : 0.f));
+        float* xp = p.x + (static_cast<long>(b) * p.S + s) * p.A + a;
+        const float xn = __fadd_rn(*xp, bf16_round(__fmul_rn(p.dt, v)));
+        *xp = xn;
+        xs[a] = bf16_round(xn);
+      }
+    }
+    workers_sync();
+    if (!next_step) {
+      workers_publish(p, et, kCXn);
+      return true;
+    }
+    load_norm_vec(p, et, tau + 1, 0, nv1);  // the next step's first input norm
+    action_in8(p, et, xs, hv);
+  }
+  *reinterpret_cast<uint4*>(p.h + static_cast<long>(t) * p.W + f0) = pack8_bf16(hv);
+  float y[8];
+  norm_row(p, et, hv, nv1, red4, y);
+  *reinterpret_cast<uint4*>(p.xn + static_cast<long>(t) * p.W + f0) = pack8_bf16(y);
+  workers_publish(p, et, (kind == kTFinO) ? kCXn2 : kCXn);
+  return true;
+}
+
+// --------------------------------------------------------------- kernel ---
+// Tensor maps of a GEMM op, selected with constant indices (a runtime index
+// into the kernel parameters would copy them to local memory).
+__device__ __forceinline__ const CUtensorMap* wmap(const Maps& maps, int op) {
+  return op == kOpQkv ? &maps.w[kOpQkv] : op == kOpO ? &maps.w[kOpO] : op == kOpGu ? &maps.w[kOpGu] : &maps.w[kOpDown];
+}
+__device__ __forceinline__ const CUtensorMap* xmap(const Maps& maps, int op) {
+  return op == kOpQkv ? &maps.x[kOpQkv] : op == kOpO ? &maps.x[kOpO] : op == kOpGu ? &maps.x[kOpGu] : &maps.x[kOpDown];
+}
+
+__device__ __forceinline__ int task_type(int4 t) { return t.x & 0xff; }
+__device__ __forceinline__ int task_layer(int4 t) { return (t.x >> 8) & 0xff; }
+
+// input counter of a GEMM op at use u
+__device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigned use, int* line, unsigned* target) {
+  switch (op) {
+    case kOpQkv: *line = kCXn; *target = static_cast<unsigned>(p.n_fin) * (use + 1); break;
+    case kOpO:
+      if (p.attn_splits > 1) {
+        *line = kCComb;
+        *target = static_cast<unsigned>(p.n_comb) * (use + 1);
+      } else {
+        *line = kCAttn;
+        *target = static_cast<unsigned>(p.n_attn) * (use + 1);
+      }
+      break;
+    case kOpGu: *line = kCXn2; *target = static_cast<unsigned>(p.n_fin) * (use + 1); break;
+    default: *line = kCAct; *target = static_cast<unsigned>(p.op[kOpGu].m_tiles) * (use + 1); break;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_kernel(const __grid_constant__ Maps maps, const __grid_constant__ ChunkParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* small = smem + kOffSmall;
+  uint64_t* full = reinterpret_cast<uint64_t*>(small + kSmFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(small + kSmEmpty);
+  uint64_t* acc_full = reinterpret_cast<uint64_t*>(small + kSmAccFull);
+  uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(small + kSmQFull);
+  uint64_t* conv_done = reinterpret_cast<uint64_t*>(small + kSmConv);
+  uint64_t* s_full = reinterpret_cast<uint64_t*>(small + kSmSFull);
+  uint64_t* p_ready = reinterpret_cast<uint64_t*>(small + kSmPReady);
+  uint64_t* o_full = reinterpret_cast<uint64_t*>(small + kSmOFull);
+  uint64_t* attn_done = reinterpret_cast<uint64_t*>(small + kSmAttnDone);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + kSmTmem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_free, 4);
+    mbar_init(q_full, 1);
+    mbar_init(conv_done, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 4);
+    mbar_init(o_full, 1);
+    mbar_init(attn_done, 4);
+    fence_mbar_init();
+    for (int i = 0; i < 4; ++i) {
+      tma_prefetch_desc(&maps.w[i]);
+      tma_prefetch_desc(&maps.x[i]);
+    }
+    tma_prefetch_desc(&maps.q);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // modulation vectors and inputs of this chunk are written by earlier kernels
+
+  const int cta = blockIdx.x;
+  const int4* itasks = p.init_tasks + p.init_off[cta];
+  const int n_init = p.init_off[cta + 1] - p.init_off[cta];
+  const int4* stasks = p.step_tasks + p.step_off[cta];
+  const int n_step = p.step_off[cta + 1] - p.step_off[cta];
+  uint32_t issued = 0;  // ring stages issued by the producer
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      uint32_t attn_cnt = 0;
+      bool ok = true;
+      for (int tau = 0; tau < p.steps && ok; ++tau) {
+        for (int i = 0; i < n_step && ok; ++i) {
+          const int4 tk = stasks[i];
+          const int ty = task_type(tk), layer = task_layer(tk);
+          const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
+          if (ty >= kTQkv && ty <= kTDown) {
+            const int op = ty - kTQkv;
+            const OpCfg oc = op_cfg(p, op);
+            const int m = tk.y, kb0 = tk.w >> 16, kb1 = tk.w & 0xffff;
+            const int nkb = kb1 - kb0;
+            const int wrow = layer * oc.rows + m * kBM;
+            const int nw = nkb < kStages ? nkb : kStages;
+            int armed = 0;  // stages whose weight tile is in flight
+            for (int j = 0; j < nw && ok; ++j) {
+              const uint32_t ii = issued + j;
+              const int s = ii % kStages;
+              if (ii >= kStages) ok = bar_wait(p, &empty[s], ((ii / kStages) - 1) & 1, kDevTimeoutStageEmpty);
+              if (!ok) break;
+              mbar_arrive_expect_tx(&full[s], kWBytes + kXBytes);
+              tma_load_2d_hint(smem + s * kWBytes, wmap(maps, op), &full[s], (kb0 + j) * kBK, wrow, pol);
+              ++armed;
+            }
+            int line;
+            unsigned target;
+            gemm_input(p, op, use, &line, &target);
+            if (ok) ok = ctr_wait(p, line, target);
+            if (p.trace && tau == 0 && i < p.trace_tasks)
+              p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 8 + 3] = globaltimer_ns();
+            fence_proxy_async_global();
+            // armed stages get their activation tile even after a failed wait,
+            // so that every stage in flight completes and can be drained
+            for (int j = 0; j < armed; ++j) {
+              const int s = (issued + j) % kStages;
+              tma_load_2d(smem + kOffX + s * kXBytes, xmap(maps, op), &full[s], (kb0 + j) * kBK, 0);
+            }
+            issued += armed;
+            for (int j = nw; j < nkb && ok; ++j) {
+              const uint32_t ii = issued;
+              const int s = ii % kStages;
+              ok = bar_wait(p, &empty[s], ((ii / kStages) - 1) & 1, kDevTimeoutStageEmpty);
+              if (!ok) break;
+              mbar_arrive_expect_tx(&full[s], kWBytes + kXBytes);
+              tma_load_2d_hint(smem + s * kWBytes, wmap(maps, op), &full[s], (kb0 + j) * kBK, wrow, pol);
+              tma_load_2d(smem + kOffX + s * kXBytes, xmap(maps, op), &full[s], (kb0 + j) * kBK, 0);
+              ++issued;
+            }
+          } else if (ty == kTAttn) {
+            // the ring's shared memory becomes the attention tiles: wait until
+            // the MMA has consumed every stage issued so far
+            for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued && ok; ++ii)
+              ok = bar_wait(p, &empty[ii % kStages], (ii / kStages) & 1, kDevTimeoutStageEmpty);
+            if (!ok) break;
+            ok = ctr_wait(p, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles) * (use + 1));
+            if (!ok) break;
+            fence_proxy_async_global();
+            const int b = tk.y, qt = tk.z;
+            const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
+            mbar_arrive_expect_tx(q_full, 4 * 16384);
+            for (int a = 0; a < 4; ++a)
+              tma_load_2d(smem + kOffAQ + a * 16384, &maps.q, q_full, a * 64, static_cast<int>(q_row0));
+            ok = bar_wait(p, attn_done, attn_cnt & 1, kDevTimeoutConvert);
+            ++attn_cnt;
+          }
+        }
+      }
+      if (!ok) raise_abort(p, kDevTimeoutStageEmpty);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_g = make_idesc_f16(kBM, kNT, true);
+      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
+      constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
+      uint32_t consumed = 0, tmem_uses = 0, q_cnt = 0, conv_cnt = 0, p_cnt = 0;
+      bool ok = true;
+      for (int tau = 0; tau < p.steps && ok; ++tau) {
+        for (int i = 0; i < n_step && ok; ++i) {
+          const int4 tk = stasks[i];
+          const int ty = task_type(tk);
+          if (ty >= kTQkv && ty <= kTDown) {
+            const int nkb = (tk.w & 0xffff) - (tk.w >> 16);
+            if (tmem_uses > 0) ok = bar_wait(p, acc_free, (tmem_uses - 1) & 1, kDevTimeoutMmaDone);
+            if (!ok) break;
+            ++tmem_uses;
+            tc_fence_after();
+            for (int j = 0; j < nkb && ok; ++j) {
+              const uint32_t ii = consumed + j;
+              const int s = ii % kStages;
+              ok = bar_wait(p, &full[s], (ii / kStages) & 1, kDevTimeoutTmaFull);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t a_base = smem_u32(smem + s * kWBytes);
+              const uint32_t b_base = smem_u32(smem + kOffX + s * kXBytes);
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const uint64_t ad = make_sdesc_sw128(a_base + kk * 32, 16, 1024);
+                const uint64_t bd = make_sdesc_sw128(b_base + kk * 32, 16, 1024);
+                umma_f16_ss(tmem, ad, bd, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+              }
+              umma_commit(&empty[s]);
+            }
+            consumed += nkb;
+            if (ok) umma_commit(acc_full);
+          } else if (ty == kTAttn) {
+            const int sp = tk.w;
+            const int blk_begin = sp * p.n_blocks / p.attn_splits;
+            const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk_begin;
+            if (tmem_uses > 0) ok = bar_wait(p, acc_free, (tmem_uses - 1) & 1, kDevTimeoutMmaDone);
+            if (!ok) break;
+            ++tmem_uses;
+            ok = bar_wait(p, q_full, q_cnt & 1, kDevTimeoutTmaFull);
+            ++q_cnt;
+            for (int jl = 0; jl < nbl && ok; ++jl) {
+              ok = bar_wait(p, conv_done, conv_cnt & 1, kDevTimeoutConvert);
+              ++conv_cnt;
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int ks = 0; ks < kD / 16; ++ks) {
+                const int a = ks >> 2, kk = ks & 3;
+                const uint64_t ad = make_sdesc_sw128(smem_u32(smem + kOffAQ + a * 16384) + kk * 32, 16, 1024);
+                const uint64_t bd = make_sdesc_sw128(smem_u32(smem + kOffAK + a * 8192) + kk * 32, 16, 1024);
+                umma_f16_ss(tmem + 256, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+              }
+              umma_commit(s_full);
+              ok = bar_wait(p, p_ready, p_cnt & 1, kDevTimeoutConvert);
+              ++p_cnt;
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int ks = 0; ks < kKB / 16; ++ks) {
+                const uint64_t ad = make_sdesc_sw128(smem_u32(smem + kOffAP) + ks * 32, 16, 1024);
+                const uint64_t bd = make_sdesc_sw128(smem_u32(smem + kOffAV) + ks * 2048, 8192, 1024);
+                umma_f16_ss(tmem, ad, bd, idesc_o, (jl > 0 || ks > 0) ? 1u : 0u);
+              }
+              umma_commit(o_full);
+            }
+          }
+        }
+      }
+    }
+  } else {
+    const int et = threadIdx.x - 64;
+    uint32_t acc_cnt = 0, blk_cnt = 0;
+    bool ok = true;
+    for (int i = 0; i < n_init && ok; ++i) ok = worker_fin(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
+    for (int tau = 0; tau < p.steps && ok; ++tau) {
+      for (int i = 0; i < n_step && ok; ++i) {
+        const int4 tk = stasks[i];
+        const int ty = task_type(tk), layer = task_layer(tk);
+        const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
+        unsigned long long* ts =
+            (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 8
+                                                       : nullptr;
+        if (et == 0) {
+          stamp(ts, 0);
+          if (ts) {
+            ts[4] = static_cast<unsigned long long>(static_cast<unsigned>(tk.x)) |
+                    (static_cast<unsigned long long>(static_cast<unsigned>(tk.y)) << 32);
+            ts[5] = static_cast<unsigned long long>(static_cast<unsigned>(tk.z)) |
+                    (static_cast<unsigned long long>(static_cast<unsigned>(tk.w)) << 32);
+          }
+        }
+        switch (ty) {
+          case kTQkv: case kTO: case kTGu: case kTDown:
+            ok = worker_gemm(p, smem, small, tmem, et, ty - kTQkv, layer, tk.y, tk.z, acc_cnt, ts);
+            break;
+          case kTAttn: ok = worker_attn(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, ts); break;
+          case kTComb: ok = worker_comb(p, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
+          case kTFinO: case kTFinD: ok = worker_fin(p, small, et, ty, tau, layer, tk.y, ts); break;
+          default: break;
+        }
+        if (et == 0) stamp(ts, 2);
+      }
+    }
+  }
+
+  // ---- teardown: bounded drain of copies in flight, then free TMEM ----
+  __syncthreads();
+  if (warp == 0 && lane == 0) {
+    for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued; ++ii)
+      mbar_wait(&full[ii % kStages], (ii / kStages) & 1, p.status, kDevTimeoutTmaFull);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+}  // namespace rfx
+
+// ================================================================= host ===
+namespace rfx {
+namespace {
+
+constexpr int kSplitsQkv = 2, kSplitsO = 8, kSplitsGu = 2, kSplitsDown = 8;
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Layout {
+  int T, q_tiles, n_ctx_blocks, n_blocks, splits, n_attn, n_comb;
+  OpCfg op[4];
+  size_t off_ctr, off_part[4], off_ws_o, off_ws_ml, off_h, off_xn, off_q, off_kn, off_vn, off_attn, off_act,
+      off_ptrs, off_tasks, total;
+};
+
+int validate(const rfx_chunk_desc& d) {
+  const int T = d.B * d.S;
+  if (d.B < 1 || d.S < 1 || T > kNT || d.num_layers < 1 || d.num_layers > 255 || d.num_steps < 1 ||
+      d.width != 1024 || d.num_q_heads < 1 || (d.num_q_heads + 2) * 256 % kBM || d.mlp_dim < kBM ||
+      d.mlp_dim % 64 || d.action_dim < 8 || d.action_dim > 64 || d.action_dim % 8)
+    return set_error(RFX_E_UNSUPPORTED,
+                     "rfx_chunk: needs B*S <= 64 tokens, width 1024, head_dim 256, mlp_dim %% 64 == 0, action_dim "
+                     "8..64 (multiple of 8)");
+  if (!d.w_qkv || !d.w_o || !d.w_gu || !d.w_down || !d.norm_a1 || !d.w_in || !d.w_out || !d.rope_table ||
+      !d.positions || !d.x || !d.k_ring || !d.v_ring || !d.k_scale || !d.v_scale)
+    return set_error(RFX_E_INVAL, "rfx_chunk: null pointer in the descriptor");
+  if (d.quant_mode != RFX_QUANT_I8_SYM && d.quant_mode != RFX_QUANT_U8_REF)
+    return set_error(RFX_E_INVAL, "rfx_chunk: quant_mode");
+  if (d.quant_mode == RFX_QUANT_I8_SYM && d.scale_dtype != RFX_DTYPE_F32)
+    return set_error(RFX_E_INVAL, "rfx_chunk: the int8 scheme keeps fp32 scales");
+  if (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp || !d.v_zp))
+    return set_error(RFX_E_INVAL, "rfx_chunk: the uint8 scheme needs zero points");
+  if (d.n_ctx < 0 || d.capacity < 1 || d.n_ctx > d.capacity) return set_error(RFX_E_INVAL, "rfx_chunk: 0 <= n_ctx <= capacity");
+  for (int l = 0; l < d.num_layers; ++l)
+    if (!d.k_ring[l] || !d.v_ring[l] || !d.k_scale[l] || !d.v_scale[l] ||
+        (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp[l] || !d.v_zp[l])))
+      return set_error(RFX_E_INVAL, "rfx_chunk: null ring pointer of layer %d", l);
+  return RFX_OK;
+}
+
+Layout layout(const rfx_chunk_desc& d, int nct) {
+  Layout L{};
+  L.T = d.B * d.S;
+  const int hq = d.num_q_heads;
+  L.q_tiles = (hq * d.S + kQR - 1) / kQR;
+  L.n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
+  L.n_blocks = L.n_ctx_blocks + (d.S + kKB - 1) / kKB;
+  int splits = d.kv_splits > 0 ? d.kv_splits : L.n_blocks;
+  splits = std::max(1, std::min({splits, L.n_blocks, 32}));
+  L.splits = splits;
+  L.n_attn = d.B * L.q_tiles * splits;
+  L.n_comb = splits > 1 ? d.B * L.q_tiles * (kQR / 4) : 0;  // 4 query rows (one per worker warp) per item
+  const int rows[4] = {(hq + 2) * 256, d.width, 2 * d.mlp_dim, d.width};
+  const int Ks[4] = {d.width, hq * 256, d.width, d.mlp_dim};
+  const int sp[4] = {kSplitsQkv, kSplitsO, kSplitsGu, kSplitsDown};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  L.off_ctr = take(static_cast<size_t>(kNumCtrLines) * 128);
+  for (int i = 0; i < 4; ++i) {
+    OpCfg& oc = L.op[i];
+    oc.rows = rows[i];
+    oc.K = Ks[i];
+    oc.m_tiles = rows[i] / kBM;
+    const int kb_total = Ks[i] / kBK;
+    oc.splits = std::min(sp[i], kb_total);
+    while (kb_total % oc.splits) --oc.splits;
+    oc.kb = kb_total / oc.splits;
+    L.off_part[i] = take(static_cast<size_t>(oc.m_tiles) * oc.splits * kNT * kBM * 4);
+  }
+  const size_t wrows = static_cast<size_t>(d.B) * L.q_tiles * splits * kQR;
+  L.off_ws_o = take(wrows * kD * 4);
+  L.off_ws_ml = take(wrows * 8);
+  L.off_h = take(static_cast<size_t>(L.T) * d.width * 2);
+  L.off_xn = take(static_cast<size_t>(L.T) * d.width * 2);
+  L.off_q = take(static_cast<size_t>(d.B) * hq * d.S * 256 * 2);
+  L.off_kn = take(static_cast<size_t>(L.T) * 256 * 2);
+  L.off_vn = take(static_cast<size_t>(L.T) * 256 * 2);
+  L.off_attn = take(static_cast<size_t>(L.T) * hq * 256 * 2);
+  L.off_act = take(static_cast<size_t>(L.T) * d.mlp_dim * 2);
+  L.off_ptrs = take(static_cast<size_t>(6) * d.num_layers * sizeof(void*));
+  L.off_tasks = off;  // the task tables follow (size known after scheduling)
+  L.total = off;
+  return L;
+}
+
+struct Schedule {
+  std::vector<int4> step, init;
+  std::vector<int> step_off, init_off;
+};
+
+// Static task lists of every CTA, in phase order.  GEMM tiles go to the CTAs
+// with the fewest items of the phase, then the fewest weight bytes so far, so
+// the weight stream is spread over all SMs; attention items go to CTAs that
+// take no o_proj tile in that layer (their shared memory is busy meanwhile).
+Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
+  std::vector<std::vector<int4>> lst(nct), ini(nct);
+  std::vector<long> load(nct, 0);
+  int rr = 0;  // rotating start for the light tasks
+  auto enc = [](int type, int layer) { return type | (layer << 8); };
+  auto gemm_phase = [&](int layer, int op, const std::vector<char>& excl) {
+    const OpCfg& oc = L.op[op];
+    std::vector<int> cnt(nct, 0);
+    for (int m = 0; m < oc.m_tiles; ++m)
+      for (int s = 0; s < oc.splits; ++s) {
+        int best = -1;
+        for (int c = 0; c < nct; ++c) {
+          if (excl[c]) continue;
+          if (best < 0 || cnt[c] < cnt[best] || (cnt[c] == cnt[best] && load[c] < load[best])) best = c;
+        }
+        const int kb0 = s * oc.kb, kb1 = kb0 + oc.kb;
+        lst[best].push_back(make_int4(enc(kTQkv + op, layer), m, s, (kb0 << 16) | kb1));
+        cnt[best]++;
+        load[best] += static_cast<long>(oc.kb) * kWBytes;
+      }
+  };
+  auto light = [&](int4 t) {
+    lst[rr % nct].push_back(t);
+    ++rr;
+  };
+  for (int t = 0; t < L.T; ++t) ini[t % nct].push_back(make_int4(kTInit, t, 0, 0));
+  const std::vector<char> none(nct, 0);
+  for (int l = 0; l < d.num_layers; ++l) {
+    gemm_phase(l, kOpQkv, none);
+    std::vector<char> attn_cta(nct, 0);
+    int a = 0;
+    for (int b = 0; b < d.B; ++b)
+      for (int qt = 0; qt < L.q_tiles; ++qt)
+        for (int s = 0; s < L.splits; ++s) {
+          const int c = (rr + a++) % nct;
+          attn_cta[c] = 1;
+          lst[c].push_back(make_int4(enc(kTAttn, l), b, qt, s));
+        }
+    rr += a;
+    if (L.splits > 1)
+      for (int b = 0; b < d.B; ++b)
+        for (int qt = 0; qt < L.q_tiles; ++qt)
+          for (int g = 0; g < kQR / 4; ++g) light(make_int4(enc(kTComb, l), b, qt, ((g * 4) << 16) | (g * 4 + 4)));
+    int n_attn_cta = 0;
+    for (char c : attn_cta) n_attn_cta += c;
+    gemm_phase(l, kOpO, n_attn_cta < nct ? attn_cta : none);
+    for (int t = 0; t < L.T; ++t) light(make_int4(enc(kTFinO, l), t, 0, 0));
+    gemm_phase(l, kOpGu, none);
+    gemm_phase(l, kOpDown, none);
+    for (int t = 0; t < L.T; ++t) light(make_int4(enc(kTFinD, l), t, 0, 0));
+  }
+  Schedule S;
+  S.step_off.push_back(0);
+  S.init_off.push_back(0);
+  for (int c = 0; c < nct; ++c) {
+    S.step.insert(S.step.end(), lst[c].begin(), lst[c].end());
+    S.step_off.push_back(static_cast<int>(S.step.size()));
+    S.init.insert(S.init.end(), ini[c].begin(), ini[c].end());
+    S.init_off.push_back(static_cast<int>(S.init.size()));
+  }
+  return S;
+}
+
+size_t schedule_bytes(const Schedule& s) {
+  return align256(s.step.size() * sizeof(int4)) + align256(s.init.size() * sizeof(int4)) +
+         align256(s.step_off.size() * sizeof(int)) + align256(s.init_off.size() * sizeof(int));
+}
+
+int chunk_grid() {
+  int n = 148;
+  rfx_num_sms(&n);
+  return n;
+}
+
+}  // namespace
+}  // namespace rfx
+
+struct rfx_chunk {
+  rfx::Maps maps;
+  rfx::ChunkParams params;
+  size_t ctr_bytes = 0;
+  int grid = 0;
+  int max_tasks = 0;  // longest per-CTA task list of one step
+  int device = -1;
+};
+
+extern "C" int rfx_chunk_workspace_size(const rfx_chunk_desc* desc, size_t* bytes) {
+  using namespace rfx;
+  if (!desc || !bytes) return set_error(RFX_E_INVAL, "rfx_chunk_workspace_size: null argument");
+  int rc = validate(*desc);
+  if (rc) return rc;
+  const int nct = chunk_grid();
+  const Layout L = layout(*desc, nct);
+  *bytes = L.total + schedule_bytes(build_schedule(*desc, L, nct));
+  return RFX_OK;
+}
+
+extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, size_t workspace_bytes,
+                                rfx_chunk** out) {
+  using namespace rfx;
+  if (!desc || !out) return set_error(RFX_E_INVAL, "rfx_chunk_create: null argument");
+  *out = nullptr;
+  const rfx_chunk_desc& d = *desc;
+  int rc = validate(d);
+  if (rc) return rc;
+  const int nct = chunk_grid();
+  const Layout L = layout(d, nct);
+  const Schedule S = build_schedule(d, L, nct);
+  const size_t need = L.total + schedule_bytes(S);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return set_error(RFX_E_INVAL, "rfx_chunk_create: workspace of %zu bytes (256-byte aligned) required", need);
+  char* ws = static_cast<char*>(workspace);
+
+  auto* c = new (std::nothrow) rfx_chunk();
+  if (!c) return set_error(RFX_E_INVAL, "rfx_chunk_create: out of host memory");
+  cudaGetDevice(&c->device);
+  c->grid = nct;
+  for (int i = 0; i < nct; ++i) c->max_tasks = std::max(c->max_tasks, S.step_off[i + 1] - S.step_off[i]);
+  c->ctr_bytes = static_cast<size_t>(kNumCtrLines) * 128;
+  ChunkParams& p = c->params;
+  p.T = L.T;
+  p.S = d.S;
+  p.B = d.B;
+  p.NL = d.num_layers;
+  p.steps = d.num_steps;
+  p.W = d.width;
+  p.Hq = d.num_q_heads;
+  p.F = d.mlp_dim;
+  p.A = d.action_dim;
+  p.NN = 2 * d.num_layers + 1;
+  p.n_ctx = d.n_ctx;
+  p.cap = d.capacity;
+  p.mode = d.quant_mode;
+  p.scale_bf16 = d.scale_dtype == RFX_DTYPE_BF16;
+  p.q_tiles = L.q_tiles;
+  p.attn_splits = L.splits;
+  p.n_ctx_blocks = L.n_ctx_blocks;
+  p.n_blocks = L.n_blocks;
+  p.n_attn = L.n_attn;
+  p.n_comb = L.n_comb;
+  p.n_fin = L.T;
+  p.eps = d.eps;
+  p.dt = d.dt;
+  p.scale_log2 = d.softmax_scale * 1.4426950408889634f;
+  for (int i = 0; i < 4; ++i) {
+    p.op[i] = L.op[i];
+    p.op[i].part = reinterpret_cast<float*>(ws + L.off_part[i]);
+  }
+  p.a1 = d.norm_a1;
+  p.a2 = d.mod_a2;
+  p.b2 = d.mod_b2;
+  p.gate = d.mod_gate;
+  p.w_in = static_cast<const __nv_bfloat16*>(d.w_in);
+  p.b_in = static_cast<const __nv_bfloat16*>(d.b_in);
+  p.w_out = static_cast<const __nv_bfloat16*>(d.w_out);
+  p.b_out = static_cast<const __nv_bfloat16*>(d.b_out);
+  p.rope = d.rope_table;
+  p.rope_max_pos = d.rope_max_pos;
+  p.pos = d.positions;
+  p.ctx_valid = d.ctx_valid;
+  p.x = d.x;
+  p.h = reinterpret_cast<__nv_bfloat16*>(ws + L.off_h);
+  p.xn = reinterpret_cast<__nv_bfloat16*>(ws + L.off_xn);
+  p.q = reinterpret_cast<__nv_bfloat16*>(ws + L.off_q);
+  p.kn = reinterpret_cast<__nv_bfloat16*>(ws + L.off_kn);
+  p.vn = reinterpret_cast<__nv_bfloat16*>(ws + L.off_vn);
+  p.attn_out = reinterpret_cast<__nv_bfloat16*>(ws + L.off_attn);
+  p.act = reinterpret_cast<__nv_bfloat16*>(ws + L.off_act);
+  p.ws_o = reinterpret_cast<float*>(ws + L.off_ws_o);
+  p.ws_ml = reinterpret_cast<float2*>(ws + L.off_ws_ml);
+  p.ctr = reinterpret_cast<unsigned*>(ws + L.off_ctr);
+  p.status = device_status_ptr();
+
+  // per-layer context pointer tables
+  const int NL = d.num_layers;
+  std::vector<const void*> ptrs(static_cast<size_t>(6) * NL);
+  for (int l = 0; l < NL; ++l) {
+    ptrs[0 * NL + l] = d.k_ring[l];
+    ptrs[1 * NL + l] = d.v_ring[l];
+    ptrs[2 * NL + l] = d.k_scale[l];
+    ptrs[3 * NL + l] = d.v_scale[l];
+    ptrs[4 * NL + l] = d.quant_mode == RFX_QUANT_U8_REF ? d.k_zp[l] : nullptr;
+    ptrs[5 * NL + l] = d.quant_mode == RFX_QUANT_U8_REF ? d.v_zp[l] : nullptr;
+  }
+  const void** dptr = reinterpret_cast<const void**>(ws + L.off_ptrs);
+  p.k_ring = reinterpret_cast<const uint8_t* const*>(dptr);
+  p.v_ring = reinterpret_cast<const uint8_t* const*>(dptr + NL);
+  p.k_scale = dptr + 2 * NL;
+  p.v_scale = dptr + 3 * NL;
+  p.k_zp = dptr + 4 * NL;
+  p.v_zp = dptr + 5 * NL;
+  // task tables
+  size_t off = L.off_tasks;
+  auto place = [&](size_t bytes) -> char* {
+    char* dst = ws + off;
+    off += align256(bytes);
+    return dst;
+  };
+  char* st_tasks = place(S.step.size() * sizeof(int4));
+  char* in_tasks = place(S.init.size() * sizeof(int4));
+  char* st_off = place(S.step_off.size() * sizeof(int));
+  char* in_off = place(S.init_off.size() * sizeof(int));
+  p.step_tasks = reinterpret_cast<const int4*>(st_tasks);
+  p.init_tasks = reinterpret_cast<const int4*>(in_tasks);
+  p.step_off = reinterpret_cast<const int*>(st_off);
+  p.init_off = reinterpret_cast<const int*>(in_off);
+  // synchronous copies: the host vectors die with this call
+  rc = check_cuda(cudaMemcpy(dptr, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice), "rfx_chunk: copy");
+  if (!rc && !S.step.empty())
+    rc = check_cuda(cudaMemcpy(st_tasks, S.step.data(), S.step.size() * sizeof(int4), cudaMemcpyHostToDevice), "copy");
+  if (!rc && !S.init.empty())
+    rc = check_cuda(cudaMemcpy(in_tasks, S.init.data(), S.init.size() * sizeof(int4), cudaMemcpyHostToDevice), "copy");
+  if (!rc) rc = check_cuda(cudaMemcpy(st_off, S.step_off.data(), S.step_off.size() * sizeof(int), cudaMemcpyHostToDevice), "copy");
+  if (!rc) rc = check_cuda(cudaMemcpy(in_off, S.init_off.data(), S.init_off.size() * sizeof(int), cudaMemcpyHostToDevice), "copy");
+
+  // tensor maps: weights stacked over layers, activations [T][K], q rows
+  const int T = L.T;
+  const uint64_t wrows[4] = {static_cast<uint64_t>(NL) * L.op[0].rows, static_cast<uint64_t>(NL) * L.op[1].rows,
+                             static_cast<uint64_t>(NL) * L.op[2].rows, static_cast<uint64_t>(NL) * L.op[3].rows};
+  const void* wptr[4] = {d.w_qkv, d.w_o, d.w_gu, d.w_down};
+  const void* xptr[4] = {p.xn, p.attn_out, p.xn, p.act};
+  for (int i = 0; i < 4 && !rc; ++i) {
+    rc = make_tmap_2d(&c->maps.w[i], wptr[i], 2, L.op[i].K, wrows[i], static_cast<uint64_t>(L.op[i].K) * 2, kBK, kBM,
+                      true);
+    if (!rc)
+      rc = make_tmap_2d(&c->maps.x[i], xptr[i], 2, L.op[i].K, T, static_cast<uint64_t>(L.op[i].K) * 2, kBK, kNT, true);
+  }
+  if (!rc)
+    rc = make_tmap_2d(&c->maps.q, p.q, 2, kD, static_cast<uint64_t>(d.B) * d.num_q_heads * d.S, kD * 2, 64, kQR, true);
+  if (!rc) rc = ensure_smem_attr(reinterpret_cast<const void*>(chunk_kernel), kSmemBytes);
+  if (!rc) {
+    int occ = 0;
+    rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, chunk_kernel, kThreads, kSmemBytes),
+                    "rfx_chunk: occupancy");
+    if (!rc && occ < 1) rc = set_error(RFX_E_UNSUPPORTED, "rfx_chunk: the kernel does not fit on an SM");
+  }
+  if (rc) {
+    delete c;
+    return rc;
+  }
+  *out = c;
+  return RFX_OK;
+}
+
+extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
+  using namespace rfx;
+  if (!c) return set_error(RFX_E_INVAL, "rfx_chunk_run: null chunk");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = check_cuda(cudaMemsetAsync(c->params.ctr, 0, c->ctr_bytes, st), "rfx_chunk_run: clear counters");
+  if (rc) return rc;
+  // every CTA waits on work of the others: the launch must have all of them
+  // resident at once (one per SM), which the cooperative attribute guarantees
+  // trace layout: [grid][256 tasks][8] (tasks past 256 of a CTA are not recorded)
+  c->params.trace_tasks = 256;
+  c->params.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(c->grid) * 256 * 8));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(c->grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel, c->maps, c->params), "rfx_chunk_run: launch");
+}
+
+extern "C" int rfx_chunk_destroy(rfx_chunk* c) {
+  delete c;
+  return RFX_OK;
+}
+
+namespace rfx {
+int run_chunk_op(rfx_chunk* c, cudaStream_t s) { return rfx_chunk_run(c, s); }
+}  // namespace rfx

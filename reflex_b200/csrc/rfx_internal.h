@@ -90,5 +90,6 @@ int launch_action_in(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl)
 int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
 int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl);
 int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl);
+int run_chunk_op(rfx_chunk* c, cudaStream_t s);
 
 }  // namespace rfx

@@ -313,7 +313,10 @@ struct NormOp {
   rfx_norm_desc d;
 };
 struct BarrierOp {};
-using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp, NormOp, BarrierOp>;
+struct ChunkOp {
+  rfx_chunk* c;
+};
+using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp, NormOp, BarrierOp, ChunkOp>;
 }  // namespace
 
 struct rfx_plan {
@@ -335,6 +338,7 @@ int run_op(const Op& op, cudaStream_t s, bool pdl) {
   if (auto* o = std::get_if<TailOp>(&op)) return launch_euler_tail(o->d, s, pdl);
   if (auto* o = std::get_if<CopyOp>(&op)) return launch_copy_rows(o->d, s, pdl);
   if (auto* o = std::get_if<NormOp>(&op)) return launch_rms_norm(o->d, s, pdl);
+  if (auto* o = std::get_if<ChunkOp>(&op)) return run_chunk_op(o->c, s);
   return set_error(RFX_E_STATE, "plan: unknown op");
 }
 // Launches every op in order; an op that follows a BarrierOp runs without PDL.
@@ -442,6 +446,14 @@ extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* 
 extern "C" int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc) {
   PLAN_GUARD(plan);
   plan->ops.emplace_back(NormOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+
+extern "C" int rfx_plan_add_chunk(rfx_plan* plan, rfx_chunk* chunk) {
+  if (!plan || !chunk) return set_error(RFX_E_INVAL, "plan: null argument");
+  if (plan->exec) return set_error(RFX_E_STATE, "plan: already captured");
+  plan->ops.emplace_back(ChunkOp{chunk});
   plan->launches += 1;
   return RFX_OK;
 }

@@ -16,6 +16,8 @@ native rfx plan that is captured into a single CUDA graph (``capture`` /
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -29,13 +31,20 @@ _QUANT = {"i8_sym": L.RFX_QUANT_I8_SYM, "u8_ref": L.RFX_QUANT_U8_REF}
 
 class ActionExpertEngine:
     def __init__(self, cfg: ExpertConfig, weights: dict, *, batch: int = 1, capacity: int = 1024, n_ctx: int = 0,
-                 device="cuda", kv_splits: int = 0, scale_dtype=torch.bfloat16):
+                 device="cuda", kv_splits: int = 0, scale_dtype=torch.bfloat16, fused: bool = False):
         if not torch.cuda.is_available():
             raise RuntimeError("ActionExpertEngine needs a CUDA device (there is no CPU path)")
         if cfg.num_kv_heads != 1 or cfg.head_dim != 256:
             raise ValueError("the kernels serve one 256-wide KV head (MQA)")
         self.cfg, self.B = cfg, batch
         self.dev = torch.device(device)
+        # fused: the whole chunk runs in the persistent executor (rfx_chunk);
+        # otherwise one launch per op
+        self.fused = fused
+        if fused and (cfg.variant != "pi05" or batch * cfg.suffix_len > 64):
+            raise ValueError("the fused chunk executor serves PI0.5 with at most 64 tokens (batch * chunk_size)")
+        if fused and cfg.quant_mode == "i8_sym" and scale_dtype != torch.float32:
+            raise ValueError("the fused chunk executor keeps fp32 scales for the int8 scheme")
         self.kv_splits = kv_splits
         dev = self.dev
         bf = lambda t: t.to(dev, torch.bfloat16).contiguous()  # noqa: E731
@@ -44,16 +53,24 @@ class ActionExpertEngine:
         S, St = cfg.chunk_size, cfg.suffix_len
         self.S, self.St = S, St
 
-        # ---- weights (fused packs, QKV / gate-up rows permuted for the epilogues)
-        self.w_qkv, self.w_o, self.w_gu, self.w_down = [], [], [], []
+        # ---- weights (fused packs, QKV / gate-up rows permuted for the epilogues),
+        # stacked over layers; self.w_*[l] are views of one layer
+        self.w_qkv_all = torch.empty(Lh, (H + 2) * D, W, dtype=torch.bfloat16, device=dev)
+        self.w_o_all = torch.empty(Lh, W, H * D, dtype=torch.bfloat16, device=dev)
+        self.w_gu_all = torch.empty(Lh, 2 * F, W, dtype=torch.bfloat16, device=dev)
+        self.w_down_all = torch.empty(Lh, W, F, dtype=torch.bfloat16, device=dev)
         for l in range(Lh):
             p = f"layers.{l}."
             qkv = torch.cat([weights[p + "q_proj.weight"], weights[p + "k_proj.weight"], weights[p + "v_proj.weight"]])
-            self.w_qkv.append(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
-            self.w_o.append(bf(weights[p + "o_proj.weight"]))
+            self.w_qkv_all[l].copy_(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
+            self.w_o_all[l].copy_(bf(weights[p + "o_proj.weight"]))
             gu = torch.cat([weights[p + "gate_proj.weight"], weights[p + "up_proj.weight"]])
-            self.w_gu.append(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
-            self.w_down.append(bf(weights[p + "down_proj.weight"]))
+            self.w_gu_all[l].copy_(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
+            self.w_down_all[l].copy_(bf(weights[p + "down_proj.weight"]))
+        self.w_qkv = list(self.w_qkv_all.unbind(0))
+        self.w_o = list(self.w_o_all.unbind(0))
+        self.w_gu = list(self.w_gu_all.unbind(0))
+        self.w_down = list(self.w_down_all.unbind(0))
         norm_names = [f"layers.{l}.{n}" for l in range(Lh) for n in ("input_layernorm", "post_attention_layernorm")]
         norm_names.append("norm")
         self.norm_names = norm_names
@@ -116,6 +133,8 @@ class ActionExpertEngine:
             self.at_x = z(batch * S, 2 * W)
             self.at_hid = z(batch * S, W)
         self.workspace = None
+        self.chunk = None
+        self.chunk_ws = None
         self.plan = None
         self.set_context_length(n_ctx)
 
@@ -159,6 +178,14 @@ class ActionExpertEngine:
             mode = L.RFX_ADARMS_SSG if cfg.adarms == "ssg" else L.RFX_ADARMS_GATE
             ops.append(("mod", K.modulation_desc(mode=mode, w=self.mod_w, b=self.mod_b, cond=self.cond, a2=self.a2,
                                                 b2=self.b2, gate=self.gate, n_norms=len(self.norm_names)), None))
+        if self.fused:
+            self._build_chunk()
+            ops.append(("chunk", self.chunk, None))
+            self.ops = ops
+            if self.plan is not None:
+                self.plan.close()
+            self.plan = None
+            return
         if cfg.variant == "pi05":
             ops.append(("in", K.action_io_desc(B=B, S=S, S_total=St, x=self.x, w_in=self.ain_w, b_in=self.ain_b,
                                                h_next=self.h, h_next_rows_per_stream=St,
@@ -235,14 +262,66 @@ class ActionExpertEngine:
             self.plan.close()
         self.plan = None
 
+    def _build_chunk(self) -> None:
+        """Descriptor, workspace and task tables of the persistent chunk executor."""
+        cfg = self.cfg
+        Lh = cfg.num_layers
+        if self.chunk is not None:
+            L.load().rfx_chunk_destroy(self.chunk)
+            self.chunk = None
+        d = L.ChunkDesc()
+        d.B, d.S, d.num_layers, d.num_steps = self.B, self.S, Lh, cfg.num_steps
+        d.width, d.num_q_heads, d.mlp_dim, d.action_dim = cfg.width, cfg.num_heads, cfg.mlp_dim, cfg.action_dim
+        d.eps, d.dt, d.softmax_scale = cfg.eps, self.dt, cfg.head_dim ** -0.5
+        d.w_qkv, d.w_o = self.w_qkv_all.data_ptr(), self.w_o_all.data_ptr()
+        d.w_gu, d.w_down = self.w_gu_all.data_ptr(), self.w_down_all.data_ptr()
+        d.norm_a1 = self.norm_a1.data_ptr()
+        d.mod_a2, d.mod_b2, d.mod_gate = L.ptr(self.a2), L.ptr(self.b2), L.ptr(self.gate)
+        d.w_in, d.b_in = self.ain_w.data_ptr(), self.ain_b.data_ptr()
+        d.w_out, d.b_out = self.aout_w.data_ptr(), self.aout_b.data_ptr()
+        d.rope_table, d.rope_max_pos, d.positions = self.rope.data_ptr(), self.rope.shape[0], self.positions.data_ptr()
+        ring0 = self.rings[0]
+        d.capacity, d.n_ctx, d.quant_mode = self.capacity, self.n_ctx, self.quant_mode
+        d.scale_dtype = K._dtype_code(ring0.k_scale)
+        d.kv_splits = self.kv_splits
+        arr = lambda ts: (ctypes.c_void_p * Lh)(*[t.data_ptr() if t is not None else None for t in ts])  # noqa: E731
+        self._chunk_ptrs = [arr([r.k_q for r in self.rings]), arr([r.v_q for r in self.rings]),
+                            arr([r.k_scale for r in self.rings]), arr([r.v_scale for r in self.rings]),
+                            arr([r.k_zp for r in self.rings]), arr([r.v_zp for r in self.rings])]
+        cast = lambda a: ctypes.cast(a, ctypes.POINTER(ctypes.c_void_p))  # noqa: E731
+        d.k_ring, d.v_ring, d.k_scale, d.v_scale, d.k_zp, d.v_zp = [cast(a) for a in self._chunk_ptrs]
+        d.ctx_valid = None
+        d.x = self.x.data_ptr()
+        n = ctypes.c_size_t(0)
+        L.call("rfx_chunk_workspace_size", ctypes.byref(d), ctypes.byref(n))
+        if self.chunk_ws is None or self.chunk_ws.numel() < n.value:
+            self.chunk_ws = torch.zeros(n.value, dtype=torch.uint8, device=self.dev)
+        h = ctypes.c_void_p()
+        L.call("rfx_chunk_create", ctypes.byref(d), self.chunk_ws.data_ptr(), self.chunk_ws.numel(), ctypes.byref(h))
+        self.chunk_desc = d
+        self.chunk = h
+
+    def __del__(self):
+        try:
+            if self.plan is not None:
+                self.plan.close()
+            if getattr(self, "chunk", None) is not None:
+                L.load().rfx_chunk_destroy(self.chunk)
+                self.chunk = None
+        except Exception:
+            pass
+
     # ---------------------------------------------------------- execution ---
     def _kind(self, kind):
-        return kind if kind in ("in", "tail", "barrier") else None
+        return kind if kind in ("in", "tail", "barrier", "chunk") else None
 
     def run_eager(self, hook=None) -> None:
         """Runs the chunk op by op through the direct C entry points."""
         for kind, desc, tag in self.ops:
             if kind == "barrier":
+                continue
+            if kind == "chunk":
+                L.call("rfx_chunk_run", desc, K._stream())
                 continue
             K.Plan.run_direct(desc, self._kind(kind))
             if hook is not None and tag is not None:

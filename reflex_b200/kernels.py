@@ -335,6 +335,9 @@ class Plan:
         if kind == "barrier":
             L.call("rfx_plan_add_barrier", self._h)
             return
+        if kind == "chunk":  # desc is an rfx_chunk handle
+            L.call("rfx_plan_add_chunk", self._h, desc)
+            return
         name = self._ADD.get(type(desc))
         if isinstance(desc, L.ActionIoDesc):
             name = {"in": "rfx_plan_add_action_in", "tail": "rfx_plan_add_euler_tail"}[kind]
