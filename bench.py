@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=2)
-    ap.add_argument("--engine", default="per-op", choices=["fused", "per-op"],
+    ap.add_argument("--engine", default="fused", choices=["fused", "per-op"],
                     help="fused: the persistent chunk executor (one launch per chunk); per-op: one launch per op")
     ap.add_argument("--streams-per-gpu", type=int, default=1,
                     help="independent robot streams served per GPU, batched along B (multi-stream sweep)")

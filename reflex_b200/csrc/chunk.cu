@@ -54,14 +54,14 @@ constexpr int kThreads = 192;
 constexpr int kNT = 64;  // token tile: T <= 64
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 7;
+constexpr int kStages = 6;
 constexpr int kWBytes = kBM * kBK * 2;  // 16 KB weight tile
 constexpr int kXBytes = kNT * kBK * 2;  // 8 KB activation tile
 constexpr int kOffX = kStages * kWBytes;
-constexpr int kOffRed = kOffX + kStages * kXBytes;  // 168 KB
-constexpr int kRedBytes = kNT * kBM * 4;            // [t][128] fp32
-constexpr int kOffSmall = kOffRed + kRedBytes;      // 200 KB
-constexpr int kSmallBytes = 8192;
+constexpr int kOffRed = kOffX + kStages * kXBytes;  // 144 KB: accumulator tile [t][128] fp32
+constexpr int kRedBytes = kNT * kBM * 4;
+constexpr int kOffSmall = kOffRed + kRedBytes;      // 176 KB
+constexpr int kSmallBytes = 3072;
 constexpr int kSmemBytes = kOffSmall + kSmallBytes + 1024;
 
 // attention overlay on the ring region
@@ -70,7 +70,9 @@ constexpr int kOffAQ = 0;        // 4 x [128 x 64] bf16
 constexpr int kOffAK = 65536;    // 4 x [64 x 64] bf16
 constexpr int kOffAV = 98304;    // 4 x [64 x 64] f16, MN-major blocks
 constexpr int kOffAP = 131072;   // [128 x 64] f16
-static_assert(kOffAP + 16384 <= kOffRed, "attention tiles must fit in the ring region");
+// the attention tiles overlay the ring and the accumulator tile (both idle
+// while an attention item runs)
+static_assert(kOffAP + 16384 <= kOffSmall, "attention tiles must fit below the small region");
 
 // small region (byte offsets)
 constexpr int kSmFull = 0;         // 8 mbarriers
@@ -84,18 +86,19 @@ constexpr int kSmPReady = 168;
 constexpr int kSmOFull = 176;
 constexpr int kSmAttnDone = 184;
 constexpr int kSmTmem = 192;
-constexpr int kSmBcast = 256;      // 16 ints
+constexpr int kSmKvnFull = 200;    // mbarrier: the new keys' K / V tiles (TMA) have landed
+constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA's partial tile is in its shared memory
+constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has finished reading this CTA's partial tile
 constexpr int kSmRed4 = 320;       // 8 floats
 constexpr int kSmScales = 512;     // 8 x 64 floats (2 KB)
-constexpr int kSmRow = 2560;       // 1024 floats
-constexpr int kSmXs = 6656;        // 64 floats
+constexpr int kSmXs = 2560;        // 64 floats
 static_assert(kSmXs + 256 <= kSmallBytes, "small region");
 
 enum TaskType : int { kTInit = 0, kTQkv = 1, kTO = 2, kTGu = 3, kTDown = 4, kTAttn = 5, kTComb = 6, kTFinO = 7, kTFinD = 8 };
 enum Op : int { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3 };
 // counter lines (32 u32 = 128 B apart)
 enum CtrLine : int { kCXn = 0, kCQkv = 1, kCAttn = 2, kCComb = 3, kCPo = 4, kCXn2 = 5, kCAct = 6, kCPd = 7, kCAbort = 8,
-                     kCTileQkv = 16, kCTileGu = 48, kNumCtrLines = 176 };
+                     kNumCtrLines = 16 };
 
 
 enum ChunkError : int { kDevTimeoutDependency = 8 };
@@ -150,7 +153,7 @@ struct ChunkParams {
   const int4* init_tasks;
   const int* init_off;
   int* status;
-  unsigned long long* trace;  // [grid][trace_tasks][8] stamps + task of the first step, or null
+  unsigned long long* trace;  // [grid][trace_tasks][16] stamps + task of the first step, or null
   int trace_tasks;
 };
 
@@ -158,6 +161,8 @@ struct Maps {
   CUtensorMap w[4];
   CUtensorMap x[4];
   CUtensorMap q;
+  CUtensorMap kn;  // the new tokens' keys, bf16 [B*S][256]
+  CUtensorMap vn;  // the new tokens' values, f16 [B*S][256]
 };
 
 // ------------------------------------------------------------ sync helpers ---
@@ -218,14 +223,40 @@ __device__ bool ctr_wait(const ChunkParams& p, int line, unsigned target) {
 __device__ __forceinline__ void ctr_signal(const ChunkParams& p, int line) {
   asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr_ptr(p, line)) : "memory");
 }
-__device__ __forceinline__ unsigned ctr_fetch_add(const ChunkParams& p, int line) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr_ptr(p, line)) : "memory");
-  return old;
-}
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
+// Arrive (release, cluster scope) on an mbarrier of the peer CTA of the pair.
+__device__ __forceinline__ void mbar_arrive_peer(uint64_t* local_bar, uint32_t peer) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mapa_shared(smem_u32(local_bar), peer))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (acquire at cluster scope) that gives up on an aborted chunk.
+__device__ bool bar_wait_cluster(const ChunkParams& p, uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (aborted(p)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_abort(p, code);
+      return false;
+    }
+  }
+}
+
 // named barrier 1 over the 128 worker threads
 __device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ bool workers_all(bool v) {
@@ -366,14 +397,36 @@ __device__ __forceinline__ void action_in8(const ChunkParams& p, int et, const f
 // memory; for QKV / gate-up the split that finishes last sums the partials
 // and runs the epilogue.  Returns false when the chunk was aborted.
 __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int op,
-                            int layer, int m, int split, uint32_t& acc_cnt, unsigned long long* ts) {
+                            int layer, int m, int split, uint32_t& acc_cnt, uint32_t& pair_cnt,
+                            unsigned long long* ts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int row = quad * 32 + lane;
   uint64_t* acc_full = reinterpret_cast<uint64_t*>(small + kSmAccFull);
   uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
-  int* bcast = reinterpret_cast<int*>(small + kSmBcast);
   const OpCfg oc = op_cfg(p, op);
+  // QKV / gate-up tiles are split along K over the two CTAs of a cluster;
+  // CTA rank h runs the epilogue of row pairs (i, i+64), i in [32h, 32h+32).
+  // RoPE cos / sin of this thread's epilogue items (item k: it = et + 128 k,
+  // token it / 8, rows 32h + (it % 8) * 4) are fetched while the MMA runs.
+  const bool paired = op == kOpQkv || op == kOpGu;
+  const int half = split;
+  constexpr int kItems = kNT * 8 / 128;
+  float4 rc[kItems], rsn[kItems];
+  const bool rotary = op == kOpQkv && (m >> 1) <= p.Hq;
+  if (rotary) {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const int it = et + 128 * k;
+      if (it < p.T * 8) {
+        int pos = p.pos[it >> 3];
+        pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
+        const float* cs = p.rope + static_cast<long>(pos) * 256 + (m & 1) * 64 + half * 32 + (it & 7) * 4;
+        rc[k] = *reinterpret_cast<const float4*>(cs);
+        rsn[k] = *reinterpret_cast<const float4*>(cs + 128);
+      }
+    }
+  }
   bool ok = true;
   if (lane == 0) ok = bar_wait(p, acc_full, acc_cnt & 1, kDevTimeoutMmaDone);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -382,90 +435,65 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   if (!ok) return false;
   if (et == 0) stamp(ts, 1);
   tc_fence_after();
-  // accumulator row (this thread's TMEM lane), 16 token columns at a time ->
-  // fp32 partial [t][128] in global memory
+  // accumulator rows (this thread's TMEM lane) -> o_proj / down_proj: fp32
+  // partial [t][128] in global memory (summed per token by the next phase);
+  // QKV / gate-up: this split's partial tile in shared memory.
+  const bool full_k = paired;
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* part = oc.part + (static_cast<long>(m) * oc.splits + split) * kNT * kBM;
+  {
+    uint32_t r[4][16];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[16];
-    tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r);
+    for (int c = 0; c < 4; ++c) tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r[c]);
     tmem_wait_ld();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(acc_free);
+    if (full_k) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int t = c * 16 + e;
-      if (t < p.T) __stcg(part + t * kBM + row, __uint_as_float(r[e]));
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kBM + row] = __uint_as_float(r[c][e]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (c * 16 + e < p.T) __stcg(part + (c * 16 + e) * kBM + row, __uint_as_float(r[c][e]));
     }
   }
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(acc_free);
   if (et == 0) stamp(ts, 6);
-  const bool last_arriver = op == kOpQkv || op == kOpGu;
-  if (!last_arriver) {
+  if (!full_k) {
     workers_publish(p, et, op == kOpO ? kCPo : kCPd);
-    if (et == 0) stamp(ts, 7);
     return true;
   }
-  workers_sync();
-  if (et == 0) {
-    const int line = (op == kOpQkv ? kCTileQkv : kCTileGu) + m;
-    fence_acq_rel_gpu();
-    const unsigned old = ctr_fetch_add(p, line);  // releases this split's partial, acquires the others'
-    bcast[0] = ((old + 1) % static_cast<unsigned>(oc.splits)) == 0u ? 1 : 0;
+  // hand the partial tile to the peer CTA and wait for the peer's
+  uint64_t* pair_ready = reinterpret_cast<uint64_t*>(small + kSmPairReady);
+  uint64_t* pair_done = reinterpret_cast<uint64_t*>(small + kSmPairDone);
+  const uint32_t peer = static_cast<uint32_t>(half ^ 1);
+  __syncwarp();
+  if (lane == 0) mbar_arrive_peer(pair_ready, peer);
+  {
+    bool w = true;
+    if (lane == 0) w = bar_wait_cluster(p, pair_ready, pair_cnt & 1, kDevTimeoutCluster);
+    if (!workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0)) return false;
   }
-  workers_sync();
-  if (bcast[0] == 0) return true;
-  // last split of this tile.  RoPE cos / sin of this thread's epilogue items
-  // (item k: it = et + 128 k, token it / 16, rows (it % 16) * 4) are requested
-  // together with the partial sums.
-  constexpr int kItems = kNT * 16 / 128;
-  float4 rc[kItems], rsn[kItems];
-  const bool rotary = op == kOpQkv && (m >> 1) <= p.Hq;
-  if (rotary) {
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      const int it = et + 128 * k;
-      if (it < p.T * 16) {
-        int pos = p.pos[it >> 4];
-        pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
-        const float* cs = p.rope + static_cast<long>(pos) * 256 + (m & 1) * 64 + (it & 15) * 4;
-        rc[k] = *reinterpret_cast<const float4*>(cs);
-        rsn[k] = *reinterpret_cast<const float4*>(cs + 128);
-      }
-    }
-  }
-  // sum all splits in split order -> red[t][row]
-  float* red = reinterpret_cast<float*>(smem + kOffRed);
-  const float* pm = oc.part + static_cast<long>(m) * oc.splits * kNT * kBM;
-#pragma unroll
-  for (int t0 = 0; t0 < kNT; t0 += 16) {
-    float v[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) v[e] = (t0 + e < p.T) ? __ldcg(pm + (t0 + e) * kBM + row) : 0.f;
-    for (int s = 1; s < oc.splits; ++s) {
-      float w[16];
-      const float* ps = pm + static_cast<long>(s) * kNT * kBM;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) w[e] = (t0 + e < p.T) ? __ldcg(ps + (t0 + e) * kBM + row) : 0.f;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) v[e] += w[e];
-    }
-#pragma unroll
-    for (int e = 0; e < 16; ++e) red[(t0 + e) * kBM + row] = v[e];
-  }
-  workers_sync();
-  // epilogue on row pairs (i, i+64), 4 rows per item
-  const int items = p.T * 16;
+  const uint32_t peer_red = mapa_shared(smem_u32(red), peer);
+  // epilogue on row pairs (i, i+64), 4 rows per item: the two splits' sums
+  // (two terms, so the order does not change the result)
+  const int items = p.T * 8;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
     const int it = et + 128 * k;
     if (it >= items) break;
-    const int t = it >> 4;
-    const int i = (it & 15) * 4;
+    const int t = it >> 3;
+    const int i = half * 32 + (it & 7) * 4;
     const float4 va = *reinterpret_cast<const float4*>(red + t * kBM + i);
     const float4 vc = *reinterpret_cast<const float4*>(red + t * kBM + i + 64);
-    const float v0[4] = {va.x, va.y, va.z, va.w};
-    const float v1[4] = {vc.x, vc.y, vc.z, vc.w};
+    const float4 pa = ld_dsmem_f4(peer_red + static_cast<uint32_t>((t * kBM + i) * 4));
+    const float4 pc = ld_dsmem_f4(peer_red + static_cast<uint32_t>((t * kBM + i + 64) * 4));
+    const float v0[4] = {va.x + pa.x, va.y + pa.y, va.z + pa.z, va.w + pa.w};
+    const float v1[4] = {vc.x + pc.x, vc.y + pc.y, vc.z + pc.z, vc.w + pc.w};
     const int b = t / p.S, s = t - b * p.S;
     if (op == kOpGu) {
       float y[4];
@@ -505,12 +533,28 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
         dst = p.kn + static_cast<long>(t) * 256;
       else
         dst = p.vn + static_cast<long>(t) * 256;
-      *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_bf16x2(r0[0], r0[1]), pack_bf16x2(r0[2], r0[3]));
-      *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_bf16x2(r1[0], r1[1]), pack_bf16x2(r1[2], r1[3]));
+      if (head <= p.Hq) {
+        *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_bf16x2(r0[0], r0[1]), pack_bf16x2(r0[2], r0[3]));
+        *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_bf16x2(r1[0], r1[1]), pack_bf16x2(r1[2], r1[3]));
+      } else {
+        // values are kept as f16 of their bf16 rounding (exact), the operand
+        // type of the P.V product, so attention loads them by TMA unchanged
+        *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_f16x2(bf16_round(r0[0]), bf16_round(r0[1])),
+                                                         pack_f16x2(bf16_round(r0[2]), bf16_round(r0[3])));
+        *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_f16x2(bf16_round(r1[0]), bf16_round(r1[1])),
+                                                               pack_f16x2(bf16_round(r1[2]), bf16_round(r1[3])));
+      }
     }
   }
+  // the peer may reuse its tile buffer once this CTA has read it, and this
+  // CTA may reuse its own once the peer has
+  __syncwarp();
+  if (lane == 0) mbar_arrive_peer(pair_done, peer);
   workers_publish(p, et, op == kOpQkv ? kCQkv : kCAct);
-  return true;
+  bool w = true;
+  if (lane == 0) w = bar_wait_cluster(p, pair_done, pair_cnt & 1, kDevTimeoutCluster);
+  ++pair_cnt;
+  return workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
 }
 
 // ----------------------------------------------------- worker: attention ---
@@ -541,7 +585,8 @@ __device__ __forceinline__ void convert16r(uint4 raw, uint8_t* tile_base, int ke
 }
 
 __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int layer,
-                            unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, unsigned long long* ts) {
+                            unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, uint32_t& kvn_cnt,
+                            unsigned long long* ts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   uint8_t* sK = smem + kOffAK;
@@ -561,6 +606,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   uint64_t* o_full = reinterpret_cast<uint64_t*>(small + kSmOFull);
   uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
   uint64_t* attn_done = reinterpret_cast<uint64_t*>(small + kSmAttnDone);
+  uint64_t* kvn_full = reinterpret_cast<uint64_t*>(small + kSmKvnFull);
   const uint32_t tmO = tmem, tmS = tmem + 256;
   const int blk_begin = sp * p.n_blocks / p.attn_splits;
   const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk_begin;
@@ -604,9 +650,9 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         return *reinterpret_cast<const uint4*>((isv ? vring : kring) + (static_cast<long>(b) * p.cap + slot) * kD +
                                                g * 16);
       };
-      uint4 raw[4];
+      uint4 raw[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) raw[q] = ctx_chunk(q);
+      for (int q = 0; q < 8; ++q) raw[q] = ctx_chunk(q);
       if (et < 64) {
         const long slot = static_cast<long>(j) * kKB + et;
         const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
@@ -627,15 +673,15 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
       }
       workers_sync();
 #pragma unroll
-      for (int quarter = 0; quarter < 4; ++quarter) {
-        uint4 nxt[4];
-        if (quarter < 3) {
+      for (int half = 0; half < 2; ++half) {
+        uint4 nxt[8];
+        if (half == 0) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) nxt[q] = ctx_chunk(4 * (quarter + 1) + q);
+          for (int q = 0; q < 8; ++q) nxt[q] = ctx_chunk(8 + q);
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int it = et + (quarter * 4 + q) * 128;
+        for (int q = 0; q < 8; ++q) {
+          const int it = et + (half * 8 + q) * 128;
           const bool isv = it >= kKB * 16;
           const int w = isv ? it - kKB * 16 : it;
           const int key = w >> 4, g = w & 15;
@@ -649,14 +695,31 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
           else
             convert16r<true>(raw[q], sK, key, g, p.mode, sbf16, sc, zp);
         }
-        if (quarter < 3) {
+        if (half == 0) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) raw[q] = nxt[q];
+          for (int q = 0; q < 8; ++q) raw[q] = nxt[q];
         }
       }
+    } else if (nbl == 1) {
+      // the split's only block holds the new keys: the producer loads its K
+      // (bf16) and V (f16) tiles by TMA once the QKV tiles are published
+      const int nb0 = (j - p.n_ctx_blocks) * kKB;
+      if (et < 64) {
+        const int kk = nb0 + et;
+        ks_s[et] = kk < p.S ? p.scale_log2 : 0.f;
+        kadd_s[et] = kk < p.S ? 0.f : -INFINITY;
+        vs_s[et] = 1.f;
+        nb_s[et] = 0;
+      }
+      bool w = true;
+      if (lane == 0) w = bar_wait(p, kvn_full, kvn_cnt & 1, kDevTimeoutTmaFull);
+      ++kvn_cnt;
+      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+      if (!ok) break;
     } else {
       if (!new_ready) {
-        ok = workers_ctr_wait(p, et, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles) * (use + 1));
+        ok = workers_ctr_wait(p, et, kCQkv,
+                              static_cast<unsigned>(p.op[kOpQkv].m_tiles * p.op[kOpQkv].splits) * (use + 1));
         if (!ok) break;
         new_ready = true;
       }
@@ -679,23 +742,14 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
           const __nv_bfloat16* src = (isv ? p.vn : p.kn) + (static_cast<long>(b) * p.S + kk) * kD + c * 8;
           raw = __ldcg(reinterpret_cast<const uint4*>(src));
         }
-        uint8_t* atom = (isv ? sV : sK) + (c >> 3) * 8192;
-        if (isv) {
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-          uint32_t w4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h2[e]);
-            w4[e] = pack_f16x2(f.x, f.y);
-          }
-          raw = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        }
+        uint8_t* atom = (isv ? sV : sK) + (c >> 3) * 8192;  // values are stored as f16 already
         *reinterpret_cast<uint4*>(atom + sw128_offset(key, c & 7)) = raw;
       }
     }
     fence_proxy_async_smem();
     workers_sync();
     if (lane == 0) mbar_arrive(conv_done);
+    if (et == 0 && jl == 0) stamp(ts, 6);
 
     // ---- softmax on S ----
     {
@@ -807,6 +861,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
   }
   if (ok && nbl > 0) {
+    if (et == 0) stamp(ts, 7);
     tc_fence_after();
     const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits + sp;
     const bool final_out = p.attn_splits == 1;
@@ -815,14 +870,14 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     __nv_bfloat16* orow = p.attn_out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
     float* wrow_o = p.ws_o + (wcta * (kD / 16) * kQR + r) * 16;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kD / 16; c0 += 2) {
-      uint32_t rr[2][16];
+    for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+      uint32_t rr[4][16];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+      for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
       tmem_wait_ld();
       if (!row_valid) continue;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < 4; ++q) {
         const int c = c0 + q;
         if (final_out) {
           uint32_t w8[8];
@@ -913,7 +968,9 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
                            unsigned long long* ts) {
   const int lane = et & 31, wq = et >> 5;
   float* red4 = reinterpret_cast<float*>(small + kSmRed4);
-  float* row = reinterpret_cast<float*>(small + kSmRow);
+  // the tail's normalized row borrows the accumulator-tile buffer (idle
+  // outside a GEMM item's epilogue)
+  float* row = reinterpret_cast<float*>(small - kOffSmall + kOffRed);
   float* xs = reinterpret_cast<float*>(small + kSmXs);
   const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
   const int f0 = et * 8;
@@ -1041,7 +1098,10 @@ __device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigne
       }
       break;
     case kOpGu: *line = kCXn2; *target = static_cast<unsigned>(p.n_fin) * (use + 1); break;
-    default: *line = kCAct; *target = static_cast<unsigned>(p.op[kOpGu].m_tiles) * (use + 1); break;
+    default:
+      *line = kCAct;
+      *target = static_cast<unsigned>(p.op[kOpGu].m_tiles * p.op[kOpGu].splits) * (use + 1);
+      break;
   }
 }
 
@@ -1076,19 +1136,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_ready, 4);
     mbar_init(o_full, 1);
     mbar_init(attn_done, 4);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmKvnFull), 1);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), 4);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), 4);
     fence_mbar_init();
     for (int i = 0; i < 4; ++i) {
       tma_prefetch_desc(&maps.w[i]);
       tma_prefetch_desc(&maps.x[i]);
     }
     tma_prefetch_desc(&maps.q);
+    tma_prefetch_desc(&maps.kn);
+    tma_prefetch_desc(&maps.vn);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // the peer CTA's barriers are initialized before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // modulation vectors and inputs of this chunk are written by earlier kernels
@@ -1132,7 +1197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             gemm_input(p, op, use, &line, &target);
             if (ok) ok = ctr_wait(p, line, target);
             if (p.trace && tau == 0 && i < p.trace_tasks)
-              p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 8 + 3] = globaltimer_ns();
+              p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 3] = globaltimer_ns();
             fence_proxy_async_global();
             // armed stages get their activation tile even after a failed wait,
             // so that every stage in flight completes and can be drained
@@ -1157,7 +1222,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued && ok; ++ii)
               ok = bar_wait(p, &empty[ii % kStages], (ii / kStages) & 1, kDevTimeoutStageEmpty);
             if (!ok) break;
-            ok = ctr_wait(p, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles) * (use + 1));
+            unsigned long long* pts =
+                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                                                           : nullptr;
+            stamp(pts, 12);
+            ok = ctr_wait(p, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles * p.op[kOpQkv].splits) * (use + 1));
+            stamp(pts, 13);
             if (!ok) break;
             fence_proxy_async_global();
             const int b = tk.y, qt = tk.z;
@@ -1165,6 +1235,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(q_full, 4 * 16384);
             for (int a = 0; a < 4; ++a)
               tma_load_2d(smem + kOffAQ + a * 16384, &maps.q, q_full, a * 64, static_cast<int>(q_row0));
+            const int sp = tk.w;
+            const int blk0 = sp * p.n_blocks / p.attn_splits;
+            const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk0;
+            if (nbl == 1 && blk0 >= p.n_ctx_blocks) {
+              // the new keys' K / V tiles (rows of the next stream, or zero
+              // fill, beyond S are masked in the softmax)
+              const int row0 = b * p.S + (blk0 - p.n_ctx_blocks) * kKB;
+              uint64_t* kvn_full = reinterpret_cast<uint64_t*>(small + kSmKvnFull);
+              mbar_arrive_expect_tx(kvn_full, 8 * 8192);
+              for (int a = 0; a < 4; ++a) {
+                tma_load_2d(smem + kOffAK + a * 8192, &maps.kn, kvn_full, a * 64, row0);
+                tma_load_2d(smem + kOffAV + a * 8192, &maps.vn, kvn_full, a * 64, row0);
+              }
+            }
             ok = bar_wait(p, attn_done, attn_cnt & 1, kDevTimeoutConvert);
             ++attn_cnt;
           }
@@ -1216,6 +1300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++tmem_uses;
             ok = bar_wait(p, q_full, q_cnt & 1, kDevTimeoutTmaFull);
             ++q_cnt;
+            unsigned long long* mts =
+                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                                                           : nullptr;
+            stamp(mts, 14);
             for (int jl = 0; jl < nbl && ok; ++jl) {
               ok = bar_wait(p, conv_done, conv_cnt & 1, kDevTimeoutConvert);
               ++conv_cnt;
@@ -1247,7 +1335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int et = threadIdx.x - 64;
-    uint32_t acc_cnt = 0, blk_cnt = 0;
+    uint32_t acc_cnt = 0, blk_cnt = 0, kvn_cnt = 0, pair_cnt = 0;
     bool ok = true;
     for (int i = 0; i < n_init && ok; ++i) ok = worker_fin(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
     for (int tau = 0; tau < p.steps && ok; ++tau) {
@@ -1256,7 +1344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ty = task_type(tk), layer = task_layer(tk);
         const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
         unsigned long long* ts =
-            (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 8
+            (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                        : nullptr;
         if (et == 0) {
           stamp(ts, 0);
@@ -1269,9 +1357,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         switch (ty) {
           case kTQkv: case kTO: case kTGu: case kTDown:
-            ok = worker_gemm(p, smem, small, tmem, et, ty - kTQkv, layer, tk.y, tk.z, acc_cnt, ts);
+            ok = worker_gemm(p, smem, small, tmem, et, ty - kTQkv, layer, tk.y, tk.z, acc_cnt, pair_cnt, ts);
             break;
-          case kTAttn: ok = worker_attn(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, ts); break;
+          case kTAttn:
+            ok = worker_attn(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, ts);
+            break;
           case kTComb: ok = worker_comb(p, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
           case kTFinO: case kTFinD: ok = worker_fin(p, small, et, ty, tau, layer, tk.y, ts); break;
           default: break;
@@ -1287,7 +1377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued; ++ii)
       mbar_wait(&full[ii % kStages], (ii / kStages) & 1, p.status, kDevTimeoutTmaFull);
   }
-  __syncthreads();
+  // the peer CTA reads this CTA's shared memory until its last paired item
+  tc_fence_before();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1301,6 +1393,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace rfx {
 namespace {
 
+// QKV and gate/up tiles are split in two along K over the two CTAs of a
+// cluster (summed through DSMEM); o_proj / down_proj tiles are split eight
+// ways and summed per token by the next phase
 constexpr int kSplitsQkv = 2, kSplitsO = 8, kSplitsGu = 2, kSplitsDown = 8;
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -1403,6 +1498,27 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
   auto gemm_phase = [&](int layer, int op, const std::vector<char>& excl) {
     const OpCfg& oc = L.op[op];
     std::vector<int> cnt(nct, 0);
+    std::vector<char> used(nct, 0);
+    if (op == kOpQkv || op == kOpGu) {
+      // split s of tile m on CTA rank s of one cluster; both CTAs of the
+      // cluster get their tiles in the same order
+      for (int m = 0; m < oc.m_tiles; ++m) {
+        int best = -1;
+        for (int c = 0; c + 1 < nct; c += 2) {
+          if (excl[c] || excl[c + 1]) continue;
+          const long lc = load[c] + load[c + 1], lb = best < 0 ? 0 : load[best] + load[best + 1];
+          if (best < 0 || cnt[c] < cnt[best] || (cnt[c] == cnt[best] && lc < lb)) best = c;
+        }
+        for (int s = 0; s < 2; ++s) {
+          const int kb0 = s * oc.kb, kb1 = kb0 + oc.kb;
+          lst[best + s].push_back(make_int4(enc(kTQkv + op, layer), m, s, (kb0 << 16) | kb1));
+          cnt[best + s]++;
+          used[best + s] = 1;
+          load[best + s] += static_cast<long>(oc.kb) * kWBytes;
+        }
+      }
+      return used;
+    }
     for (int m = 0; m < oc.m_tiles; ++m)
       for (int s = 0; s < oc.splits; ++s) {
         int best = -1;
@@ -1413,8 +1529,10 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
         const int kb0 = s * oc.kb, kb1 = kb0 + oc.kb;
         lst[best].push_back(make_int4(enc(kTQkv + op, layer), m, s, (kb0 << 16) | kb1));
         cnt[best]++;
+        used[best] = 1;
         load[best] += static_cast<long>(oc.kb) * kWBytes;
       }
+    return used;
   };
   auto light = [&](int4 t) {
     lst[rr % nct].push_back(t);
@@ -1423,17 +1541,23 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
   for (int t = 0; t < L.T; ++t) ini[t % nct].push_back(make_int4(kTInit, t, 0, 0));
   const std::vector<char> none(nct, 0);
   for (int l = 0; l < d.num_layers; ++l) {
-    gemm_phase(l, kOpQkv, none);
+    const std::vector<char> qkv_cta = gemm_phase(l, kOpQkv, none);
+    // attention items go to CTAs without a QKV tile in this layer, so they
+    // convert their context blocks while the QKV tiles run
     std::vector<char> attn_cta(nct, 0);
-    int a = 0;
+    int n_free = 0;
+    for (char c : qkv_cta) n_free += c ? 0 : 1;
+    int c = rr % nct;
     for (int b = 0; b < d.B; ++b)
       for (int qt = 0; qt < L.q_tiles; ++qt)
         for (int s = 0; s < L.splits; ++s) {
-          const int c = (rr + a++) % nct;
+          if (n_free > 0)
+            while (qkv_cta[c]) c = (c + 1) % nct;
           attn_cta[c] = 1;
           lst[c].push_back(make_int4(enc(kTAttn, l), b, qt, s));
+          c = (c + 1) % nct;
         }
-    rr += a;
+    rr = c;
     if (L.splits > 1)
       for (int b = 0; b < d.B; ++b)
         for (int qt = 0; qt < L.q_tiles; ++qt)
@@ -1466,7 +1590,7 @@ size_t schedule_bytes(const Schedule& s) {
 int chunk_grid() {
   int n = 148;
   rfx_num_sms(&n);
-  return n;
+  return n & ~1;  // CTA pairs (clusters of two)
 }
 
 }  // namespace
@@ -1624,7 +1748,16 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
   }
   if (!rc)
     rc = make_tmap_2d(&c->maps.q, p.q, 2, kD, static_cast<uint64_t>(d.B) * d.num_q_heads * d.S, kD * 2, 64, kQR, true);
+  if (!rc) rc = make_tmap_2d(&c->maps.kn, p.kn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
+  if (!rc) rc = make_tmap_2d(&c->maps.vn, p.vn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
   if (!rc) rc = ensure_smem_attr(reinterpret_cast<const void*>(chunk_kernel), kSmemBytes);
+  // the smallest shared-memory carveout that holds the kernel (164 of 228 KB),
+  // so the rest of the unified L1 caches local memory and global loads
+  if (!rc)
+    rc = check_cuda(cudaFuncSetAttribute(reinterpret_cast<const void*>(chunk_kernel),
+                                         cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (kSmemBytes * 100 + 228 * 1024 - 1) / (228 * 1024)),
+                    "rfx_chunk: carveout");
   if (!rc) {
     int occ = 0;
     rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, chunk_kernel, kThreads, kSmemBytes),
@@ -1647,19 +1780,23 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   if (rc) return rc;
   // every CTA waits on work of the others: the launch must have all of them
   // resident at once (one per SM), which the cooperative attribute guarantees
-  // trace layout: [grid][256 tasks][8] (tasks past 256 of a CTA are not recorded)
+  // trace layout: [grid][256 tasks][16] (tasks past 256 of a CTA are not recorded)
   c->params.trace_tasks = 256;
-  c->params.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(c->grid) * 256 * 8));
+  c->params.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(c->grid) * 256 * 16));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // CTA pairs share split-K tiles through DSMEM
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel, c->maps, c->params), "rfx_chunk_run: launch");
 }
 

@@ -2,6 +2,7 @@
 
     python -m reflex_b200.profile [--layers 2] [--reps 3] [--ops qkv,attn,o,gu,down,tail]
     python -m reflex_b200.profile --layers 18 --chunk   # one eager chunk, then one graph replay
+    python -m reflex_b200.profile --layers 2 --chunk --fused   # the same through the chunk executor
 
 Builds the PI0.5 engine at the benchmark's shapes (width 1024, 8x256 heads,
 818-token int8 context, 50 action tokens) with a few layers, runs one chunk to
@@ -31,10 +32,12 @@ def main():
     ap.add_argument("--n-ctx", type=int, default=818)
     ap.add_argument("--streams", type=int, default=1)
     ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
+    ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
     args = ap.parse_args()
     cfg = pi05_config(num_layers=args.layers, adarms="ssg")
     wts = synthetic.expert_weights(cfg, seed=0, device="cuda")
-    eng = ActionExpertEngine(cfg, wts, batch=args.streams, capacity=1024, n_ctx=args.n_ctx)
+    eng = ActionExpertEngine(cfg, wts, batch=args.streams, capacity=1024, n_ctx=args.n_ctx,
+                             scale_dtype=torch.float32, fused=args.chunk and args.fused)
     ks, vs = synthetic.context_kv(cfg, args.n_ctx, B=args.streams, seed=1, device="cuda")
     for l in range(cfg.num_layers):
         eng.load_context(l, ks[l], vs[l])
