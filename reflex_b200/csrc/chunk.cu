@@ -868,7 +868,9 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
     const long tok = static_cast<long>(b) * p.S + s_row;
     __nv_bfloat16* orow = p.attn_out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
-    float* wrow_o = p.ws_o + (wcta * (kD / 16) * kQR + r) * 16;
+    // partial O of the split, normalized by its own l and kept as f16 (the
+    // combine weights it by l * 2^(m - M)): [cta][16-column chunk][row][16]
+    __half* wrow_o = reinterpret_cast<__half*>(p.ws_o) + (wcta * (kD / 16) * kQR + r) * 16;
 #pragma unroll 1
     for (int c0 = 0; c0 < kD / 16; c0 += 4) {
       uint32_t rr[4][16];
@@ -887,11 +889,13 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
           *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
           *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
         } else {
+          uint32_t w8[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            __stcg(reinterpret_cast<float4*>(wrow_o + static_cast<long>(c) * kQR * 16 + 4 * e),
-                   make_float4(__uint_as_float(rr[q][4 * e]), __uint_as_float(rr[q][4 * e + 1]),
-                               __uint_as_float(rr[q][4 * e + 2]), __uint_as_float(rr[q][4 * e + 3])));
+          for (int e = 0; e < 8; ++e)
+            w8[e] = pack_f16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(wrow_o + static_cast<long>(c) * kQR * 16);
+          __stcg(dst, make_uint4(w8[0], w8[1], w8[2], w8[3]));
+          __stcg(dst + 1, make_uint4(w8[4], w8[5], w8[6], w8[7]));
         }
       }
     }
@@ -915,36 +919,48 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
   if (et == 0) stamp(ts, 1);
   const int wq = et >> 5, lane = et & 31;
-  constexpr int kBatch = 8;  // partials whose loads are in flight together
+  constexpr int kBatch = 16;  // splits whose partials are in flight together
   for (int r = r0 + wq; r < r1; r += 4) {
     const int R = qt * kQR + r;
     if (R >= p.Hq * p.S) continue;
     const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < p.attn_splits; ++s) {
-      const float2 v = __ldcg(p.ws_ml + (base + s) * kQR + r);
-      if (v.y > 0.f) M = fmaxf(M, v.x);
-    }
-    float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // lane: 8 of the row's 256 columns (chunk lane / 2, half lane % 2)
+    const __half* ob = reinterpret_cast<const __half*>(p.ws_o) + ((lane >> 1) * kQR + r) * 16 + (lane & 1) * 8;
+    float M = -INFINITY, L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int s0 = 0; s0 < p.attn_splits; s0 += kBatch) {
-      float4 a[kBatch], c[kBatch];
+      uint4 o[kBatch];
       float2 ml[kBatch];
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
         if (s0 + q < p.attn_splits) {
-          const float* o = p.ws_o + (((base + s0 + q) * (kD / 16) + (lane >> 1)) * kQR + r) * 16 + (lane & 1) * 8;
-          a[q] = __ldcg(reinterpret_cast<const float4*>(o));
-          c[q] = __ldcg(reinterpret_cast<const float4*>(o + 4));
+          o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s0 + q) * (kD / 16) * kQR * 16));
           ml[q] = __ldcg(p.ws_ml + (base + s0 + q) * kQR + r);
         }
       }
+      // running log-sum-exp merge: weights l_s * 2^(m_s - M)
+      float Mb = M;
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q)
+        if (s0 + q < p.attn_splits && ml[q].y > 0.f) Mb = fmaxf(Mb, ml[q].x);
+      if (Mb != M && M != -INFINITY) {
+        const float f = exp2f(M - Mb);
+        L *= f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] *= f;
+      }
+      M = Mb;
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
         if (s0 + q >= p.attn_splits || ml[q].x == -INFINITY || ml[q].y <= 0.f) continue;
-        const float w = exp2f(ml[q].x - M);
-        L += w * ml[q].y;
-        acc[0] += w * a[q].x; acc[1] += w * a[q].y; acc[2] += w * a[q].z; acc[3] += w * a[q].w;
-        acc[4] += w * c[q].x; acc[5] += w * c[q].y; acc[6] += w * c[q].z; acc[7] += w * c[q].w;
+        const float w = exp2f(ml[q].x - M) * ml[q].y;
+        L += w;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&o[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h2[e]);
+          acc[2 * e] = fmaf(w, f.x, acc[2 * e]);
+          acc[2 * e + 1] = fmaf(w, f.y, acc[2 * e + 1]);
+        }
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
