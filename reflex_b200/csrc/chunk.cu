@@ -54,7 +54,7 @@ constexpr int kThreads = 192;
 constexpr int kNT = 64;  // token tile: T <= 64
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 6;
+constexpr int kStages = 7;
 constexpr int kWBytes = kBM * kBK * 2;  // 16 KB weight tile
 constexpr int kXBytes = kNT * kBK * 2;  // 8 KB activation tile
 constexpr int kOffX = kStages * kWBytes;
@@ -189,26 +189,30 @@ __device__ bool bar_wait(const ChunkParams& p, uint64_t* bar, uint32_t parity, i
     }
   }
 }
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* a) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
   return v;
 }
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 // Bounded wait until a phase counter reaches `target`.  Polls with relaxed
 // loads (an acquire load per poll would keep invalidating the SM's L1) and
-// makes the success an acquire with one fence.
+// makes the success an acquire with one acquire load.
 __device__ bool ctr_wait(const ChunkParams& p, int line, unsigned target) {
   const unsigned* c = ctr_ptr(p, line);
   if (ld_relaxed_gpu(c) >= target) {
-    fence_acq_rel_gpu();
+    ld_acquire_gpu(c);
     return true;
   }
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     for (int i = 0; i < 16; ++i) {
       if (ld_relaxed_gpu(c) >= target) {
-        fence_acq_rel_gpu();
+        ld_acquire_gpu(c);  // the success becomes an acquire (one load, no full fence)
         return true;
       }
       __nanosleep(32);
@@ -279,13 +283,11 @@ __device__ __forceinline__ bool workers_ctr_wait(const ChunkParams& p, int et, i
   return workers_all(ok);
 }
 // All workers' global writes are ordered before the barrier; one worker then
-// releases the phase counter (cumulative release at GPU scope).
+// releases the phase counter (the reduction's release semantics are
+// cumulative, covering the writes the barrier ordered before it).
 __device__ __forceinline__ void workers_publish(const ChunkParams& p, int et, int line) {
   workers_sync();
-  if (et == 0) {
-    fence_acq_rel_gpu();
-    ctr_signal(p, line);
-  }
+  if (et == 0) ctr_signal(p, line);
 }
 
 __device__ __forceinline__ void stamp(unsigned long long* slot, int k) {
