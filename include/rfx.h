@@ -84,7 +84,9 @@ int rfx_num_sms(int* out);
  * Input rows x[b][h][l][0..D) at element strides (xs_b, xs_h, xs_l); D = 256.
  * Token l of the call goes to slot region_base + (region_off + l) % region_len
  * of q[b][h][slot][0..D) (byte strides qs_*), scale/zp[b][h][slot] (element
- * strides ss_*). Eviction of the oldest frame is overwriting its slots. */
+ * strides ss_*). Eviction of the oldest frame is overwriting its slots.
+ * With v, v_q, v_scale and v_zp all NULL only K is quantized (one tensor, as
+ * fused_quantize_store does). */
 typedef struct rfx_kv_quant_desc {
   int mode;     /* RFX_QUANT_* */
   int in_dtype; /* RFX_DTYPE_BF16 or RFX_DTYPE_F32 */

@@ -125,69 +125,81 @@ __device__ __forceinline__ void modulation_store(long row, int r, float m, int w
   }
 }
 
+// Every warp takes four consecutive output rows at a time (grid-stride over
+// all rows) against all KR >= n_rows conditioning rows held in shared memory
+// as fp32; one 16-byte shared load feeds 16 FMAs.  Lane l accumulates
+// k = q*128 + 4l .. 4l+3 for q = 0, 1, ... in order, then the warp sums.
+template <int KR>
 __global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict__ W, const float* __restrict__ bias,
                                                          const __nv_bfloat16* __restrict__ cond, int n_rows, int width,
                                                          int n_norms, int out_per_norm, int mode,
                                                          float* __restrict__ a2, float* __restrict__ b2,
                                                          float* __restrict__ gate) {
-  extern __shared__ __align__(16) __nv_bfloat16 cin[];  // [n_rows][width]
+  extern __shared__ __align__(16) float cin[];  // [n_rows][width]
   pdl_wait();
-  for (int i = threadIdx.x * 8; i < n_rows * width; i += blockDim.x * 8)
-    *reinterpret_cast<uint4*>(cin + i) = *reinterpret_cast<const uint4*>(cond + i);
+  for (int i = threadIdx.x * 8; i < n_rows * width; i += blockDim.x * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(cond + i);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h2[e]);
+      cin[i + 2 * e] = f.x;
+      cin[i + 2 * e + 1] = f.y;
+    }
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long total = static_cast<long>(n_norms) * out_per_norm;
-  for (long row0 = (static_cast<long>(blockIdx.x) * 8 + warp) * 2; row0 < total;
-       row0 += static_cast<long>(gridDim.x) * 16) {
-    const bool has1 = row0 + 1 < total;
-    float acc0[kMaxRows], acc1[kMaxRows];
+  constexpr int RW = 4;  // weight rows per warp iteration
+  for (long row0 = (static_cast<long>(blockIdx.x) * 8 + warp) * RW; row0 < total;
+       row0 += static_cast<long>(gridDim.x) * 8 * RW) {
+    float acc[RW][KR];
 #pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) acc0[r] = acc1[r] = 0.f;
-    const float* w0 = W + row0 * width;
-    const float* w1 = has1 ? w0 + width : w0;
-    for (int k0 = 0; k0 < width; k0 += 1024) {
-      // both rows' 4 KB slices are requested before any of them is used
-      float4 v0[8], v1[8];
+    for (int j = 0; j < RW; ++j)
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int k = k0 + q * 128 + lane * 4;
-        if (k < width) {
-          v0[q] = __ldcs(reinterpret_cast<const float4*>(w0 + k));  // streamed once per chunk
-          v1[q] = __ldcs(reinterpret_cast<const float4*>(w1 + k));
+      for (int r = 0; r < KR; ++r) acc[j][r] = 0.f;
+    const float* wr[RW];
+#pragma unroll
+    for (int j = 0; j < RW; ++j) wr[j] = W + (row0 + j < total ? row0 + j : row0) * width;
+    for (int k0 = 0; k0 < width; k0 += 512) {
+      // four rows' 2 KB slices are requested before any of them is used
+      float4 v[RW][4];
+#pragma unroll
+      for (int j = 0; j < RW; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int k = k0 + q * 128 + lane * 4;
+          if (k < width) v[j][q] = __ldcs(reinterpret_cast<const float4*>(wr[j] + k));  // streamed once per chunk
         }
-      }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         const int k = k0 + q * 128 + lane * 4;
         if (k >= width) continue;
 #pragma unroll
-        for (int r = 0; r < kMaxRows; ++r) {
+        for (int r = 0; r < KR; ++r) {
           if (r < n_rows) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(cin + r * width + k);
-            const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-            const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-            acc0[r] = fmaf(v0[q].x, xa.x, acc0[r]);
-            acc0[r] = fmaf(v0[q].y, xa.y, acc0[r]);
-            acc0[r] = fmaf(v0[q].z, xb.x, acc0[r]);
-            acc0[r] = fmaf(v0[q].w, xb.y, acc0[r]);
-            acc1[r] = fmaf(v1[q].x, xa.x, acc1[r]);
-            acc1[r] = fmaf(v1[q].y, xa.y, acc1[r]);
-            acc1[r] = fmaf(v1[q].z, xb.x, acc1[r]);
-            acc1[r] = fmaf(v1[q].w, xb.y, acc1[r]);
+            const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
+#pragma unroll
+            for (int j = 0; j < RW; ++j) {
+              acc[j][r] = fmaf(v[j][q].x, x.x, acc[j][r]);
+              acc[j][r] = fmaf(v[j][q].y, x.y, acc[j][r]);
+              acc[j][r] = fmaf(v[j][q].z, x.z, acc[j][r]);
+              acc[j][r] = fmaf(v[j][q].w, x.w, acc[j][r]);
+            }
           }
         }
       }
     }
-    const float bo0 = bias[row0];
-    const float bo1 = has1 ? bias[row0 + 1] : 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) {
-      if (r < n_rows) {
-        const float m0 = __fadd_rn(warp_sum(acc0[r]), bo0);
-        const float m1 = __fadd_rn(warp_sum(acc1[r]), bo1);
-        if (lane == 0) {
-          modulation_store(row0, r, m0, width, n_norms, out_per_norm, mode, a2, b2, gate);
-          if (has1) modulation_store(row0 + 1, r, m1, width, n_norms, out_per_norm, mode, a2, b2, gate);
+    for (int j = 0; j < RW; ++j) {
+      const long row = row0 + j;
+      if (row >= total) break;
+      const float bo = bias[row];
+#pragma unroll
+      for (int r = 0; r < KR; ++r) {
+        if (r < n_rows) {
+          const float m = __fadd_rn(warp_sum(acc[j][r]), bo);
+          if (lane == 0) modulation_store(row, r, m, width, n_norms, out_per_norm, mode, a2, b2, gate);
         }
       }
     }
@@ -500,15 +512,16 @@ int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pd
       d.n_norms < 1 || d.width < 128 || d.width % 128 || !d.w || !d.b || !d.cond || !d.a2 || !d.gate ||
       (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w) || !a16(d.cond))
     return set_error(RFX_E_INVAL, "rfx_modulation: bad descriptor");
-  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(__nv_bfloat16);
+  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(float);
   if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
-  const void* fn = reinterpret_cast<const void*>(modulation_kernel);
+  const void* fn = d.n_rows <= 8 ? reinterpret_cast<const void*>(modulation_kernel<8>)
+                                 : reinterpret_cast<const void*>(modulation_kernel<16>);
   int rc = ensure_smem_attr(fn, 200 * 1024);
   if (rc) return rc;
   const long rows = static_cast<long>(d.n_norms) * out;
   int nsm = 148;
   rfx_num_sms(&nsm);
-  dim3 grid(static_cast<unsigned>(std::min<long>((rows + 15) / 16, 4L * nsm)));
+  dim3 grid(static_cast<unsigned>(std::min<long>((rows + 31) / 32, 4L * nsm)));
   const float* w = d.w;
   const float* bias = d.b;
   const __nv_bfloat16* cond = static_cast<const __nv_bfloat16*>(d.cond);

@@ -156,7 +156,10 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   if (d.mode != kQuantI8Sym && d.mode != kQuantU8Ref) return set_error(RFX_E_INVAL, "kv_quant_append: bad mode");
   if (d.in_dtype != kDtypeBF16 && d.in_dtype != kDtypeF32)
     return set_error(RFX_E_INVAL, "kv_quant_append: input dtype must be bf16 or f32");
-  for (int w = 0; w < 2; ++w) {
+  // V pointers all null: quantize K alone (fused_quantize_store of one tensor)
+  const bool k_only = !d.x[1] && !d.q[1] && !d.scale[1] && !d.zp[1];
+  const int nw = k_only ? 1 : 2;
+  for (int w = 0; w < nw; ++w) {
     if (!d.x[w] || !d.q[w] || !d.scale[w] || (d.mode == kQuantU8Ref && !d.zp[w]))
       return set_error(RFX_E_INVAL, "kv_quant_append: null pointer");
     if ((reinterpret_cast<uintptr_t>(d.x[w]) & 15u) || (reinterpret_cast<uintptr_t>(d.q[w]) & 7u))
@@ -180,7 +183,7 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   a.region_base = d.region_base; a.region_off = d.region_off; a.region_len = d.region_len;
 
   const long rows = static_cast<long>(d.B) * d.H * d.L;
-  dim3 grid(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock), 2);
+  dim3 grid(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock), nw);
   dim3 block(kWarpsPerBlock * 32);
   void (*kern)(QuantArgs) = nullptr;
   if (d.in_dtype == kDtypeBF16)

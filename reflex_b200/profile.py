@@ -1,6 +1,6 @@
 """Runs the kernels of one denoising layer in isolation, for profilers.
 
-    python -m reflex_b200.profile [--layers 2] [--reps 3] [--ops qkv,attn,o,gu,down,tail]
+    python -m reflex_b200.profile [--layers 2] [--reps 3] [--ops qkv,attn,o,gu,down,tail,time,mod]
     python -m reflex_b200.profile --layers 18 --chunk   # one eager chunk, then one graph replay
     python -m reflex_b200.profile --layers 2 --chunk --fused   # the same through the chunk executor
 
@@ -58,7 +58,11 @@ def main():
     for kind, desc, tag in eng.ops:
         if tag is not None and tag[1] == 0 and (len(tag) < 3 or tag[2] == 0):
             by_tag[tag[0]] = (kind, desc)
-    names = {"qkv": "qkv", "attn": "attn", "o": "o", "gu": "gu", "down": "layer", "tail": "step"}
+    for kind, desc, tag in eng.ops:
+        if kind in ("time", "mod"):  # the per-chunk conditioning heads
+            by_tag[kind] = (kind, desc)
+    names = {"qkv": "qkv", "attn": "attn", "o": "o", "gu": "gu", "down": "layer", "tail": "step", "time": "time",
+             "mod": "mod"}
     torch.cuda.profiler.start()
     for op in args.ops.split(","):
         kind, desc = by_tag[names[op]]
