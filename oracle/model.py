@@ -114,7 +114,7 @@ def suffix_embed(cfg, wts, state, x_t, t, bf16):
     return embs, att, None
 
 
-def expert_layer(cfg, wts, l, h, cond, ctx: Context, pos, att, table, bf16, trace=None):
+def expert_layer(cfg, wts, l, h, cond, ctx: Context, pos, att, table, bf16, trace=None, kv_out=None):
     p = f"layers.{l}."
     B, S, W = h.shape
     H, D = cfg.num_heads, cfg.head_dim
@@ -125,6 +125,8 @@ def expert_layer(cfg, wts, l, h, cond, ctx: Context, pos, att, table, bf16, trac
     q, k, v = qkv[:, :H], qkv[:, H:H + 1], qkv[:, H + 1:]
     q = _r(rope(q, pos, table), bf16)
     k = _r(rope(k, pos, table), bf16)
+    if kv_out is not None:
+        kv_out.append((k.clone(), v.clone()))
     o = partitioned_attention(q, ctx.k[l], ctx.v[l], k, v, ctx.pad, att, D ** -0.5)
     o = _r(o, bf16).transpose(1, 2).reshape(B, S, H * D)
     if trace is not None:
@@ -174,3 +176,26 @@ def sample_chunk(cfg, wts, ctx: Context, x0, state=None, table=None, bf16=False,
         x = x + _r(dt * v, bf16)
         t = t + dt
     return x
+
+
+def prefix_frame(cfg, wts, h, ctx: Context, pos, table=None, bf16=False, hidden=None):
+    """Streaming frame update of the prefix layers: the new frame's tokens
+    [B, n, W] attend bidirectionally to each other and to the cached context
+    (pinned prefix + window), layer by layer.  The prefix layers have the
+    decoder-layer structure of the expert's (modeling_pi05.py:563-620, the
+    prefix stream of PI05ModelLayer) without conditioning.  Attention is the
+    non-streaming one (modeling_pi05.py:1379-1401 builds the full prefix
+    mask), not the streaming prefill, which returns zeros for the prefix
+    (streaming_attention.py:585-587).  Returns (hidden, [(k, v) per layer])
+    with the new frame's post-RoPE K/V that the frame appends to each ring."""
+    if table is None:
+        from reflex_b200.synthetic import rope_table
+        table = rope_table(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta)
+    att = torch.zeros(h.shape[1], dtype=torch.int64)
+    att[0] = 1
+    kvs = []
+    for l in range(cfg.num_layers):
+        h = expert_layer(cfg, wts, l, h, None, ctx, pos, att, table, bf16, kv_out=kvs)
+        if hidden is not None:
+            hidden.append(h.clone())
+    return h, kvs

@@ -64,6 +64,16 @@ def pi0_config(**kw) -> ExpertConfig:
     return ExpertConfig(variant="pi0", **kw)
 
 
+def vlm_config(**kw) -> ExpertConfig:
+    """The prefix (VLM) layers: Gemma-2B shapes (width 2048, 8 x 256 heads, one
+    KV head, GeGLU 16384, 18 layers), RMSNorm without conditioning; the
+    streaming frame update runs them over each new frame."""
+    kw.setdefault("width", 2048)
+    kw.setdefault("mlp_dim", 16384)
+    kw.setdefault("adarms", "none")
+    return ExpertConfig(variant="vlm", **kw)
+
+
 def timestep_schedule(num_steps: int) -> list[float]:
     """t_0 = 1.0, t_{k+1} = fp32(t_k + fp32(-1/num_steps)) as in
     reflex/policies/pi05/modeling_pi05.py:1403-1418 (fp32 tensors)."""

@@ -1,0 +1,133 @@
+"""Streaming frame update of the prefix (VLM) layers on the rfx kernels.
+
+Each new frame of ``frame_len`` patch embeddings runs through the prefix
+layers (Gemma-2B shapes): input norm -> QKV + RoPE -> attention of the frame
+over the cached context (pinned instruction prefix + the newest window frame;
+the frame being evicted is masked out) and over itself (bidirectional) ->
+o_proj + residual -> post-attention norm -> gate/up + GeGLU -> down_proj +
+residual; then the frame's post-RoPE K/V are quantize-appended into the
+layer's ring in the evicted frame's slots.  This is the streaming path of
+reflex/policies/pi05/modeling_pi05.py:1282-1333 (evict the oldest frame, then
+prefill the new one, streaming_attention.py:281-470) with the prefix attention
+of the non-streaming path (:1379-1401), and the rings are the ones the action
+expert reads.
+
+Ring layout per layer: slots [0, pinned) hold the instruction prefix, then
+``window_frames`` frame slots of ``frame_len`` each; frame f goes to slot
+f % window_frames.  Positions of a new frame continue after the context it
+attends to (pinned + the other window frames), as the reference's streaming
+prefill counts them (modeling_pi05.py:1301-1316).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from . import kernels as K
+from .config import ExpertConfig
+from .synthetic import rope_table
+
+
+class PrefixEngine:
+    def __init__(self, cfg: ExpertConfig, weights: dict, rings: list, *, pinned: int, frame_len: int,
+                 window_frames: int = 2, batch: int = 1, device="cuda", kv_splits: int = 0):
+        if cfg.num_kv_heads != 1 or cfg.head_dim != 256:
+            raise ValueError("the kernels serve one 256-wide KV head (MQA)")
+        if len(rings) != cfg.num_layers:
+            raise ValueError("one ring per prefix layer")
+        self.cfg, self.B, self.dev = cfg, batch, torch.device(device)
+        self.pinned, self.frame_len, self.window_frames = pinned, frame_len, window_frames
+        self.rings = rings
+        cap = pinned + window_frames * frame_len
+        if rings[0].capacity < cap:
+            raise ValueError(f"rings hold {rings[0].capacity} slots, the window needs {cap}")
+        self.n_ctx = cap
+        dev = self.dev
+        bf = lambda t: t.to(dev, torch.bfloat16).contiguous()  # noqa: E731
+        Lh, W, H, D, F = cfg.num_layers, cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim
+        self.w_qkv, self.w_o, self.w_gu, self.w_down, self.a_in, self.a_post = [], [], [], [], [], []
+        for l in range(Lh):
+            p = f"layers.{l}."
+            qkv = torch.cat([weights[p + "q_proj.weight"], weights[p + "k_proj.weight"], weights[p + "v_proj.weight"]])
+            self.w_qkv.append(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
+            self.w_o.append(bf(weights[p + "o_proj.weight"]))
+            gu = torch.cat([weights[p + "gate_proj.weight"], weights[p + "up_proj.weight"]])
+            self.w_gu.append(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
+            self.w_down.append(bf(weights[p + "down_proj.weight"]))
+            self.a_in.append(weights[p + "input_layernorm.weight"].to(dev, torch.float32).contiguous())
+            self.a_post.append(weights[p + "post_attention_layernorm.weight"].to(dev, torch.float32).contiguous())
+        T = batch * frame_len
+        self.T = T
+        z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
+        self.h = z(T, W)
+        self.xn = z(T, W)
+        self.q = z(batch, H, frame_len, D)
+        self.k_new, self.v_new = z(T, D), z(T, D)
+        self.attn_out = z(T, H * D)
+        self.act = z(T, F)
+        self.rope = rope_table(cfg.max_position_embeddings, D, cfg.rope_theta).to(dev)
+        pos = pinned + (window_frames - 1) * frame_len + torch.arange(frame_len, dtype=torch.int32)
+        self.positions = pos.repeat(batch).to(dev)
+        # context validity while frame slot s is being replaced: everything but slot s
+        self.valid = []
+        for s in range(window_frames):
+            m = torch.ones(batch, rings[0].capacity, dtype=torch.uint8)
+            m[:, cap:] = 0
+            m[:, pinned + s * frame_len: pinned + (s + 1) * frame_len] = 0
+            self.valid.append(m.to(dev))
+        self.kv_splits = kv_splits
+        self.workspace = None
+        self.frames = 0  # frames appended so far
+
+    def load_context(self, layer: int, k: torch.Tensor, v: torch.Tensor, slot_base: int = 0) -> None:
+        """Quantize-appends K/V [B, 1, L, D] at slots [slot_base, slot_base + L)."""
+        K.kv_quant_append(k.to(self.dev, torch.bfloat16).contiguous(), v.to(self.dev, torch.bfloat16).contiguous(),
+                          self.rings[layer], 0, slot_base, self.rings[layer].capacity)
+
+    def set_frame(self, emb: torch.Tensor) -> None:
+        """The new frame's embeddings [B, frame_len, width]."""
+        self.h.copy_(emb.reshape(self.T, -1), non_blocking=True)
+
+    def ops(self, slot: int) -> list:
+        """Launch list of one frame update that replaces frame slot `slot`."""
+        cfg, B, S, T = self.cfg, self.B, self.frame_len, self.T
+        H, D = cfg.num_heads, cfg.head_dim
+        base = self.pinned + slot * self.frame_len
+        out = [("barrier", None, None)]
+        attn_descs = []
+        for l in range(cfg.num_layers):
+            out.append(("norm", K.norm_desc(x=self.h, y=self.xn, S=S, norm_a1=self.a_in[l], eps=cfg.eps), None))
+            out.append(("linear", K.linear_desc(
+                w=self.w_qkv[l], x=self.xn, T=T, S=S, epilogue=L.RFX_EPI_QKV_ROPE, rope_table=self.rope,
+                positions=self.positions, q_out=self.q, k_out=self.k_new, v_out=self.v_new, num_q_heads=H), None))
+            ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l], n_ctx=self.n_ctx,
+                                  out=self.attn_out, softmax_scale=D ** -0.5, ctx_valid=self.valid[slot],
+                                  kv_splits=self.kv_splits)
+            attn_descs.append(ad)
+            out.append(("attn", ad, None))
+            out.append(("linear", K.linear_desc(w=self.w_o[l], x=self.attn_out, T=T, S=S,
+                                                epilogue=L.RFX_EPI_RESIDUAL, y=self.h), None))
+            out.append(("norm", K.norm_desc(x=self.h, y=self.xn, S=S, norm_a1=self.a_post[l], eps=cfg.eps), None))
+            out.append(("linear", K.linear_desc(w=self.w_gu[l], x=self.xn, T=T, S=S, epilogue=L.RFX_EPI_GEGLU,
+                                                y=self.act), None))
+            out.append(("linear", K.linear_desc(w=self.w_down[l], x=self.act, T=T, S=S,
+                                                epilogue=L.RFX_EPI_RESIDUAL, y=self.h), None))
+            kv = self.k_new.view(B, 1, S, D)
+            out.append(("quant", K.kv_quant_desc(kv, self.v_new.view(B, 1, S, D), self.rings[l], base, 0,
+                                                 self.frame_len), None))
+        need = max(K.attention_workspace_bytes(d) for d in attn_descs)
+        if need and (self.workspace is None or self.workspace.numel() < need):
+            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        for d in attn_descs:
+            if need:
+                d.workspace, d.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        return out
+
+    def run(self, emb: torch.Tensor | None = None) -> None:
+        """One frame update through the direct entry points (eager)."""
+        if emb is not None:
+            self.set_frame(emb)
+        for kind, desc, _ in self.ops(self.frames % self.window_frames):
+            if kind != "barrier":
+                K.Plan.run_direct(desc)
+        self.frames += 1

@@ -83,6 +83,31 @@ def expert_weights(cfg: ExpertConfig, seed: int = 0, device="cpu") -> dict[str, 
     return w
 
 
+def prefix_weights(cfg: ExpertConfig, seed: int = 10, device="cpu") -> dict[str, torch.Tensor]:
+    """Random-init prefix (VLM) layer weights, same initialisation as the
+    expert's layers; norms carry only their weight (no conditioning)."""
+    r = _Rng(seed, device)
+    W, H, D, F = cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim
+    w: dict[str, torch.Tensor] = {}
+    for l in range(cfg.num_layers):
+        p = f"layers.{l}."
+        w[p + "q_proj.weight"] = _bf16(r.normal(H * D, W, std=0.02))
+        w[p + "k_proj.weight"] = _bf16(r.normal(cfg.num_kv_heads * D, W, std=0.02))
+        w[p + "v_proj.weight"] = _bf16(r.normal(cfg.num_kv_heads * D, W, std=0.02))
+        w[p + "o_proj.weight"] = _bf16(r.normal(W, H * D, std=0.02))
+        w[p + "gate_proj.weight"] = _bf16(r.normal(F, W, std=0.02))
+        w[p + "up_proj.weight"] = _bf16(r.normal(F, W, std=0.02))
+        w[p + "down_proj.weight"] = _bf16(r.normal(W, F, std=0.02))
+        w[p + "input_layernorm.weight"] = 1.0 + r.normal(W, std=0.05)
+        w[p + "post_attention_layernorm.weight"] = 1.0 + r.normal(W, std=0.05)
+    return w
+
+
+def frame_embeddings(cfg: ExpertConfig, n: int, B: int = 1, seed: int = 11, device="cpu") -> torch.Tensor:
+    """A new frame's patch embeddings [B, n, width] ~ N(0, 1) / sqrt(width), bf16-representable."""
+    return _bf16(_Rng(seed, device).normal(B, n, cfg.width) / math.sqrt(cfg.width))
+
+
 def context_kv(cfg: ExpertConfig, n_ctx: int, B: int = 1, seed: int = 1, device="cpu"):
     """Per-layer context K/V [L][B, 1, n_ctx, D] ~ N(0, 1) (post-RoPE keys as the
     prefix layers would have cached them)."""
