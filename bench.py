@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-chunks", type=int, default=2)
+    ap.add_argument("--workload", default="chunk", choices=["chunk", "frame"],
+                    help="chunk: one 10-step chunk (the headline); frame: streaming frame update + chunk")
     ap.add_argument("--engine", default="fused", choices=["fused", "per-op"],
                     help="fused: the persistent chunk executor (one launch per chunk); per-op: one launch per op")
     ap.add_argument("--streams-per-gpu", type=int, default=1,
@@ -407,10 +409,117 @@ def run_gpu(args):
         pg.destroy_process_group()
 
 
+def run_frame(args):
+    """Streaming frame update + one chunk per control tick: a new frame of
+    3 cameras x 256 patch embeddings through the 18 prefix layers (Gemma-2B
+    shapes) over a pinned 48-token instruction prefix and a 2-frame window,
+    evicting the oldest frame and quantize-appending the new one into the
+    rings, then one 10-step PI0.5 chunk over the updated 1584-token context;
+    both in one CUDA graph (one per ring slot the frame replaces)."""
+    from reflex_b200 import kernels as K
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config, vlm_config
+    from reflex_b200.expert import ActionExpertEngine
+    from reflex_b200.prefix import PrefixEngine
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pinned, flen, win = 48, 768, 2
+    n_ctx = pinned + win * flen
+    cfg = pi05_config(num_layers=args.layers, adarms="ssg", quant_mode="i8_sym")
+    wts = synthetic.expert_weights(cfg, seed=0, device=device)
+    eng = ActionExpertEngine(cfg, wts, batch=1, capacity=n_ctx, n_ctx=n_ctx, device=device,
+                             scale_dtype=torch.float32, fused=True)
+    del wts
+    vcfg = vlm_config(num_layers=args.layers)
+    pw = synthetic.prefix_weights(vcfg, seed=10, device=device)
+    pre = PrefixEngine(vcfg, pw, eng.rings, pinned=pinned, frame_len=flen, window_frames=win)
+    del pw
+    ks, vs = synthetic.context_kv(cfg, n_ctx, seed=1, device=device)
+    for l in range(cfg.num_layers):
+        eng.load_context(l, ks[l], vs[l])
+    del ks, vs
+    plans = []
+    for slot in range(win):
+        plan = K.Plan()
+        for kind, desc, _ in pre.ops(slot) + eng.ops:
+            plan.add(desc, eng._kind(kind))
+        plans.append(plan)
+    x0 = synthetic.noise(cfg, seed=2, device=device)
+    frames = [synthetic.frame_embeddings(vcfg, flen, seed=20 + i, device=device) for i in range(2)]
+    stream = torch.cuda.Stream(device=device)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for plan in plans:
+            pre.set_frame(frames[0])
+            eng.set_inputs(x0)
+            plan.run()
+            plan.capture(stream)
+    torch.cuda.current_stream().wait_stream(stream)
+    st = torch.cuda.current_stream()
+
+    def tick(i, frame, x):
+        pre.set_frame(frame)
+        eng.set_inputs(x)
+        plans[i % win].replay()
+
+    for i in range(max(3, args.warmup)):
+        tick(i, frames[i % 2], x0)
+    torch.cuda.synchronize()
+    status = K.device_status()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        evs[0].record(st)
+        for i in range(args.steps):
+            tick(i, frames[i % 2], x0)
+            evs[i + 1].record(st)
+        torch.cuda.synchronize()
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    p50 = statistics.median(per)
+    # end to end: the frame and x0 from pinned host memory, actions back
+    fh = frames[0].cpu().pin_memory()
+    xh = x0.cpu().pin_memory()
+    out = torch.empty_like(xh).pin_memory()
+    e2e = []
+    for i in range(args.steps + 3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        tick(i, fh.to(device, non_blocking=True), xh.to(device, non_blocking=True))
+        out.copy_(eng.x, non_blocking=True)
+        e1.record(st)
+        e1.synchronize()
+        if i >= 3:
+            e2e.append(e0.elapsed_time(e1))
+    prefix_bytes = args.layers * (2560 * 2048 + 2048 * 2048 + 32768 * 2048 + 2048 * 16384) * 2
+    prefix_flops = 2.0 * flen * prefix_bytes / 2
+    line = {
+        "metric": "p50 streaming frame update + 10-step PI0.5 chunk latency (ms)", "value": round(p50, 4),
+        "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(evs[0].elapsed_time(evs[-1]) / args.steps, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded random-init prefix and expert weights, N(0,1)/sqrt(2048) frame embeddings",
+        "config": {"workload": "frame update: 3 cameras x 256 tokens through 18 Gemma-2B-shape prefix layers over "
+                               "a pinned 48-token prefix + 2-frame window (1584 tokens), evict + int8 "
+                               "quantize-append, then one 10-step PI0.5 chunk; one CUDA graph",
+                   "layers": args.layers, "frame_tokens": flen, "pinned": pinned, "window_frames": win,
+                   "context_tokens": n_ctx, "engine": "per-op prefix layers + persistent chunk executor"},
+        "prefix_weight_bytes": prefix_bytes, "prefix_gflop": round(prefix_flops / 1e9, 1),
+        "e2e": {"value": round(statistics.median(e2e), 4), "unit": "ms",
+                "h2d_bytes_per_step": fh.numel() * 2 + xh.numel() * 4, "d2h_bytes_per_step": out.numel() * 4},
+        "gpu_launches": sum(p.num_launches for p in plans) // win * args.steps,
+        "clocks": clk.summary(), "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "frame":
+        run_frame(args)
         return
     run_gpu(args)
 
