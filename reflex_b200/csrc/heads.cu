@@ -104,63 +104,69 @@ __global__ void __launch_bounds__(256) gemv_bf16_silu_kernel(const __nv_bfloat16
   pdl_launch_dependents();
 }
 
-// AdaRMSNorm modulation: fp32 W [n_norms * out][width]; every warp takes two
-// output rows at a time (grid-stride over all rows) against all conditioning
-// rows, which sit in shared memory as bf16 (exact: cond is bf16).
-__device__ __forceinline__ void modulation_store(long row, int r, float m, int width, int n_norms, int out_per_norm,
-                                                 int mode, float* __restrict__ a2, float* __restrict__ b2,
-                                                 float* __restrict__ gate) {
-  const int n = static_cast<int>(row / out_per_norm);
-  const int o = static_cast<int>(row % out_per_norm);
-  const long base = (static_cast<long>(r) * n_norms + n) * width;
-  if (mode == RFX_ADARMS_GATE) {
-    a2[base + o] = m;
-    if (b2) b2[base + o] = 0.f;
-    gate[base + o] = bf16_round(m);
-  } else {
-    const int part = o / width, f = o % width;
-    if (part == 0) a2[base + f] = __fadd_rn(1.f, m);
-    else if (part == 1) b2[base + f] = m;
-    else gate[base + f] = bf16_round(m);
-  }
+// AdaRMSNorm modulation: m[r][row] = sum_k cond[r][k] * W[row][k] + bias[row]
+// for fp32 W [n_norms * out][width] and every conditioning row r (the Euler
+// steps' timestep embeddings), in one pass over W.
+//
+// Every warp takes four consecutive output rows at a time (grid-stride over
+// all rows) against KR conditioning rows held in shared memory as fp32, rows
+// n_rows..KR-1 zero; one 16-byte shared load feeds 16 FMAs.  Lane l
+// accumulates k = q*128 + 4l .. 4l+3 for q = 0, 1, ... in order.  The 16 lane
+// partials of each row are then reduce-scattered across the warp (16 shuffles
+// per row): lanes 2i and 2i+1 end with the sum for conditioning row
+// rmap(i), and lane 2i stores it for all four rows as one float4.
+__device__ __forceinline__ float halve_slots(float keep_lo, float keep_hi, bool hi, int offset) {
+  const float keep = hi ? keep_hi : keep_lo;
+  const float send = hi ? keep_lo : keep_hi;
+  return keep + __shfl_xor_sync(0xffffffffu, send, offset);
 }
 
-// Every warp takes four consecutive output rows at a time (grid-stride over
-// all rows) against all KR >= n_rows conditioning rows held in shared memory
-// as fp32; one 16-byte shared load feeds 16 FMAs.  Lane l accumulates
-// k = q*128 + 4l .. 4l+3 for q = 0, 1, ... in order, then the warp sums.
-template <int KR>
-__global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict__ W, const float* __restrict__ bias,
-                                                         const __nv_bfloat16* __restrict__ cond, int n_rows, int width,
-                                                         int n_norms, int out_per_norm, int mode,
-                                                         float* __restrict__ a2, float* __restrict__ b2,
-                                                         float* __restrict__ gate) {
-  extern __shared__ __align__(16) float cin[];  // [n_rows][width]
-  pdl_wait();
-  for (int i = threadIdx.x * 8; i < n_rows * width; i += blockDim.x * 8) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(cond + i);
-    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+// v[0..15] per lane -> sum over the warp of v[r] where
+// r = 8*bit4(lane) + 4*bit3(lane) + 2*bit2(lane) + bit1(lane).
+__device__ __forceinline__ float reduce_scatter16(const float (&v)[16], int lane) {
+  float s8[8], s4[4], s2[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(h2[e]);
-      cin[i + 2 * e] = f.x;
-      cin[i + 2 * e + 1] = f.y;
+  for (int i = 0; i < 8; ++i) s8[i] = halve_slots(v[i], v[i + 8], lane & 16, 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s4[i] = halve_slots(s8[i], s8[i + 4], lane & 8, 8);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) s2[i] = halve_slots(s4[i], s4[i + 2], lane & 4, 4);
+  const float s1 = halve_slots(s2[0], s2[1], lane & 2, 2);
+  return s1 + __shfl_xor_sync(0xffffffffu, s1, 1);
+}
+
+template <int KR>
+__global__ void __launch_bounds__(256, 2) modulation_kernel(const float* __restrict__ W, const float* __restrict__ bias,
+                                                            const __nv_bfloat16* __restrict__ cond, int n_rows,
+                                                            int width, int n_norms, int out_per_norm, int mode,
+                                                            float* __restrict__ a2, float* __restrict__ b2,
+                                                            float* __restrict__ gate) {
+  static_assert(KR <= 16, "the reduce-scatter serves 16 conditioning rows");
+  extern __shared__ __align__(16) float cin[];  // [KR][width]
+  pdl_wait();
+  for (int i = threadIdx.x * 4; i < KR * width; i += blockDim.x * 4) {
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n_rows * width) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(cond + i);
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+      f = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
+    *reinterpret_cast<float4*>(cin + i) = f;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long total = static_cast<long>(n_norms) * out_per_norm;
+  const int total = n_norms * out_per_norm;
   constexpr int RW = 4;  // weight rows per warp iteration
-  for (long row0 = (static_cast<long>(blockIdx.x) * 8 + warp) * RW; row0 < total;
-       row0 += static_cast<long>(gridDim.x) * 8 * RW) {
+  const int r_mine = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  for (int row0 = (blockIdx.x * 8 + warp) * RW; row0 < total; row0 += gridDim.x * 8 * RW) {
     float acc[RW][KR];
 #pragma unroll
     for (int j = 0; j < RW; ++j)
 #pragma unroll
       for (int r = 0; r < KR; ++r) acc[j][r] = 0.f;
-    const float* wr[RW];
-#pragma unroll
-    for (int j = 0; j < RW; ++j) wr[j] = W + (row0 + j < total ? row0 + j : row0) * width;
+    const float* wr = W + static_cast<long>(row0) * width;
+#pragma unroll 1
     for (int k0 = 0; k0 < width; k0 += 512) {
       // four rows' 2 KB slices are requested before any of them is used
       float4 v[RW][4];
@@ -169,39 +175,52 @@ __global__ void __launch_bounds__(256) modulation_kernel(const float* __restrict
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int k = k0 + q * 128 + lane * 4;
-          if (k < width) v[j][q] = __ldcs(reinterpret_cast<const float4*>(wr[j] + k));  // streamed once per chunk
+          v[j][q] = k < width ? __ldcs(reinterpret_cast<const float4*>(wr + static_cast<long>(j) * width + k))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);  // streamed once per chunk
         }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int k = k0 + q * 128 + lane * 4;
-        if (k >= width) continue;
+        const int k = min(k0 + q * 128 + lane * 4, width - 4);
 #pragma unroll
         for (int r = 0; r < KR; ++r) {
-          if (r < n_rows) {
-            const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
+          const float4 x = *reinterpret_cast<const float4*>(cin + r * width + k);
 #pragma unroll
-            for (int j = 0; j < RW; ++j) {
-              acc[j][r] = fmaf(v[j][q].x, x.x, acc[j][r]);
-              acc[j][r] = fmaf(v[j][q].y, x.y, acc[j][r]);
-              acc[j][r] = fmaf(v[j][q].z, x.z, acc[j][r]);
-              acc[j][r] = fmaf(v[j][q].w, x.w, acc[j][r]);
-            }
+          for (int j = 0; j < RW; ++j) {
+            acc[j][r] = fmaf(v[j][q].x, x.x, acc[j][r]);
+            acc[j][r] = fmaf(v[j][q].y, x.y, acc[j][r]);
+            acc[j][r] = fmaf(v[j][q].z, x.z, acc[j][r]);
+            acc[j][r] = fmaf(v[j][q].w, x.w, acc[j][r]);
           }
         }
       }
     }
+    float m[RW];
 #pragma unroll
     for (int j = 0; j < RW; ++j) {
-      const long row = row0 + j;
-      if (row >= total) break;
-      const float bo = bias[row];
+      float vals[16];
 #pragma unroll
-      for (int r = 0; r < KR; ++r) {
-        if (r < n_rows) {
-          const float m = __fadd_rn(warp_sum(acc[j][r]), bo);
-          if (lane == 0) modulation_store(row, r, m, width, n_norms, out_per_norm, mode, a2, b2, gate);
-        }
-      }
+      for (int r = 0; r < 16; ++r) vals[r] = r < KR ? acc[j][r] : 0.f;
+      m[j] = __fadd_rn(reduce_scatter16(vals, lane), bias[row0 + j]);
+    }
+    if ((lane & 1) || r_mine >= n_rows) continue;
+    // the four rows share one norm and one part: out_per_norm and width are multiples of 4
+    const int n = row0 / out_per_norm, o = row0 - n * out_per_norm;
+    const long base = (static_cast<long>(r_mine) * n_norms + n) * width;
+    if (mode == RFX_ADARMS_GATE) {
+      *reinterpret_cast<float4*>(a2 + base + o) = make_float4(m[0], m[1], m[2], m[3]);
+      if (b2) *reinterpret_cast<float4*>(b2 + base + o) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(gate + base + o) =
+          make_float4(bf16_round(m[0]), bf16_round(m[1]), bf16_round(m[2]), bf16_round(m[3]));
+    } else {
+      const int part = o / width, f = o - part * width;
+      if (part == 0)
+        *reinterpret_cast<float4*>(a2 + base + f) =
+            make_float4(__fadd_rn(1.f, m[0]), __fadd_rn(1.f, m[1]), __fadd_rn(1.f, m[2]), __fadd_rn(1.f, m[3]));
+      else if (part == 1)
+        *reinterpret_cast<float4*>(b2 + base + f) = make_float4(m[0], m[1], m[2], m[3]);
+      else
+        *reinterpret_cast<float4*>(gate + base + f) =
+            make_float4(bf16_round(m[0]), bf16_round(m[1]), bf16_round(m[2]), bf16_round(m[3]));
     }
   }
   pdl_launch_dependents();
@@ -510,18 +529,25 @@ int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pd
   const int out = d.mode == RFX_ADARMS_SSG ? 3 * d.width : d.width;
   if ((d.mode != RFX_ADARMS_GATE && d.mode != RFX_ADARMS_SSG) || d.n_rows < 1 || d.n_rows > kMaxRows ||
       d.n_norms < 1 || d.width < 128 || d.width % 128 || !d.w || !d.b || !d.cond || !d.a2 || !d.gate ||
-      (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w) || !a16(d.cond))
+      (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w) || !a16(d.cond) || !a16(d.a2) || !a16(d.gate) ||
+      (d.b2 && !a16(d.b2)))
     return set_error(RFX_E_INVAL, "rfx_modulation: bad descriptor");
-  const size_t smem = static_cast<size_t>(d.n_rows) * d.width * sizeof(float);
-  if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
-  const void* fn = d.n_rows <= 8 ? reinterpret_cast<const void*>(modulation_kernel<8>)
-                                 : reinterpret_cast<const void*>(modulation_kernel<16>);
-  int rc = ensure_smem_attr(fn, 200 * 1024);
-  if (rc) return rc;
   const long rows = static_cast<long>(d.n_norms) * out;
+  if (rows > (1L << 30)) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: too many output rows");
+  // conditioning rows padded to the next instantiated count
+  const int kr = d.n_rows <= 4 ? 4 : d.n_rows <= 8 ? 8 : d.n_rows <= 10 ? 10 : 16;
+  const void* fn = kr == 4   ? reinterpret_cast<const void*>(modulation_kernel<4>)
+                   : kr == 8 ? reinterpret_cast<const void*>(modulation_kernel<8>)
+                   : kr == 10 ? reinterpret_cast<const void*>(modulation_kernel<10>)
+                              : reinterpret_cast<const void*>(modulation_kernel<16>);
+  const size_t smem = static_cast<size_t>(kr) * d.width * sizeof(float);
+  if (smem > 100 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
+  int rc = ensure_smem_attr(fn, 100 * 1024);
+  if (rc) return rc;
   int nsm = 148;
   rfx_num_sms(&nsm);
-  dim3 grid(static_cast<unsigned>(std::min<long>((rows + 31) / 32, 4L * nsm)));
+  // one wave at two resident blocks per SM; each warp takes 4 rows per iteration
+  dim3 grid(static_cast<unsigned>(std::min<long>((rows + 31) / 32, 2L * nsm)));
   const float* w = d.w;
   const float* bias = d.b;
   const __nv_bfloat16* cond = static_cast<const __nv_bfloat16*>(d.cond);
