@@ -54,14 +54,14 @@ constexpr int kThreads = 192;
 constexpr int kNT = 64;  // token tile: T <= 64
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 7;
+constexpr int kStages = 8;
 constexpr int kWBytes = kBM * kBK * 2;  // 16 KB weight tile
 constexpr int kXBytes = kNT * kBK * 2;  // 8 KB activation tile
 constexpr int kOffX = kStages * kWBytes;
-constexpr int kOffRed = kOffX + kStages * kXBytes;  // 144 KB: accumulator tile [t][128] fp32
+constexpr int kOffRed = kOffX + kStages * kXBytes;  // 192 KB: accumulator tile [t][128] fp32
 constexpr int kRedBytes = kNT * kBM * 4;
-constexpr int kOffSmall = kOffRed + kRedBytes;      // 176 KB
-constexpr int kSmallBytes = 3072;
+constexpr int kOffSmall = kOffRed + kRedBytes;      // 224 KB
+constexpr int kSmallBytes = 1024;
 constexpr int kSmemBytes = kOffSmall + kSmallBytes + 1024;
 
 // attention overlay on the ring region
@@ -70,9 +70,9 @@ constexpr int kOffAQ = 0;        // 4 x [128 x 64] bf16
 constexpr int kOffAK = 65536;    // 4 x [64 x 64] bf16
 constexpr int kOffAV = 98304;    // 4 x [64 x 64] f16, MN-major blocks
 constexpr int kOffAP = 131072;   // [128 x 64] f16
-// the attention tiles overlay the ring and the accumulator tile (both idle
-// while an attention item runs)
-static_assert(kOffAP + 16384 <= kOffSmall, "attention tiles must fit below the small region");
+constexpr int kOffAScales = 147456;  // 8 x 64 floats (2 KB): per-key scales, zero points, block ids
+// the attention tiles overlay the ring (idle while an attention item runs)
+static_assert(kOffAScales + 2048 <= kOffRed, "attention tiles must fit in the ring");
 
 // small region (byte offsets)
 constexpr int kSmFull = 0;         // 8 mbarriers
@@ -87,11 +87,10 @@ constexpr int kSmOFull = 176;
 constexpr int kSmAttnDone = 184;
 constexpr int kSmTmem = 192;
 constexpr int kSmKvnFull = 200;    // mbarrier: the new keys' K / V tiles (TMA) have landed
-constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA's partial tile is in its shared memory
-constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has finished reading this CTA's partial tile
+constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA has pushed its partial into this CTA's tile buffer
+constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has read its tile buffer (this CTA may push again)
 constexpr int kSmRed4 = 320;       // 8 floats
-constexpr int kSmScales = 512;     // 8 x 64 floats (2 KB)
-constexpr int kSmXs = 2560;        // 64 floats
+constexpr int kSmXs = 512;         // 64 floats
 static_assert(kSmXs + 256 <= kSmallBytes, "small region");
 
 enum TaskType : int { kTInit = 0, kTQkv = 1, kTO = 2, kTGu = 3, kTDown = 4, kTAttn = 5, kTComb = 6, kTFinO = 7, kTFinD = 8 };
@@ -395,9 +394,10 @@ __device__ __forceinline__ void action_in8(const ChunkParams& p, int et, const f
 }
 
 // ------------------------------------------------------- worker: GEMM tile ---
-// Accumulator (row = TMEM lane, 64 token columns) -> fp32 partial in global
-// memory; for QKV / gate-up the split that finishes last sums the partials
-// and runs the epilogue.  Returns false when the chunk was aborted.
+// Accumulator (row = TMEM lane, 64 token columns) -> o_proj / down_proj: fp32
+// partial in global memory.  QKV / gate-up: the tile's two K splits run on
+// the two CTAs of a cluster, which sum them through shared memory and each
+// finish half of the rows.  Returns false when the chunk was aborted.
 __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int op,
                             int layer, int m, int split, uint32_t& acc_cnt, uint32_t& pair_cnt,
                             unsigned long long* ts) {
@@ -438,11 +438,17 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   if (et == 0) stamp(ts, 1);
   tc_fence_after();
   // accumulator rows (this thread's TMEM lane) -> o_proj / down_proj: fp32
-  // partial [t][128] in global memory (summed per token by the next phase);
-  // QKV / gate-up: this split's partial tile in shared memory.
-  const bool full_k = paired;
+  // partial [t][128] in global memory (summed per token by the next phase).
+  // QKV / gate-up: the tile buffer [t][128] of the CTA that finishes a row
+  // gathers both splits of it: the rows of quads (h, h+2) at their own
+  // positions from this CTA, the peer's partial of them at row ^ 32 (rows
+  // this CTA finishes nowhere else), pushed by the peer's quads (h, h+2).
+  uint64_t* pair_ready = reinterpret_cast<uint64_t*>(small + kSmPairReady);
+  uint64_t* pair_done = reinterpret_cast<uint64_t*>(small + kSmPairDone);
+  const uint32_t peer = static_cast<uint32_t>(half ^ 1);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* part = oc.part + (static_cast<long>(m) * oc.splits + split) * kNT * kBM;
+  bool pushed = true;
   {
     uint32_t r[4][16];
 #pragma unroll
@@ -451,36 +457,50 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(acc_free);
-    if (full_k) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kBM + row] = __uint_as_float(r[c][e]);
-    } else {
+    if (!paired) {
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           if (c * 16 + e < p.T) __stcg(part + (c * 16 + e) * kBM + row, __uint_as_float(r[c][e]));
+    } else if ((quad & 1) == half) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kBM + row] = __uint_as_float(r[c][e]);
+    } else {
+      // the peer's buffer is free once the peer has read the previous tile
+      if (pair_cnt > 0) {
+        if (lane == 0) pushed = bar_wait_cluster(p, pair_done, (pair_cnt - 1) & 1, kDevTimeoutCluster);
+        pushed = __shfl_sync(0xffffffffu, pushed ? 1 : 0, 0) != 0;
+      }
+      if (pushed) {
+        const uint32_t dst = mapa_shared(smem_u32(red + (row ^ 32)), peer);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c * 16 + e < p.T) st_dsmem_f32(dst + static_cast<uint32_t>((c * 16 + e) * kBM * 4), __uint_as_float(r[c][e]));
+        __syncwarp();
+        if (lane == 0) mbar_arrive_peer(pair_ready, peer);
+      }
     }
   }
   if (et == 0) stamp(ts, 6);
-  if (!full_k) {
+  if (!paired) {
     workers_publish(p, et, op == kOpO ? kCPo : kCPd);
     return true;
   }
-  // hand the partial tile to the peer CTA and wait for the peer's
-  uint64_t* pair_ready = reinterpret_cast<uint64_t*>(small + kSmPairReady);
-  uint64_t* pair_done = reinterpret_cast<uint64_t*>(small + kSmPairDone);
-  const uint32_t peer = static_cast<uint32_t>(half ^ 1);
-  __syncwarp();
-  if (lane == 0) mbar_arrive_peer(pair_ready, peer);
+  // this CTA's own rows are in its buffer (the barrier orders them for every
+  // worker); then wait for the peer's pushed partial
+  if (!workers_all(pushed)) return false;
+  if (et == 0) stamp(ts, 8);
   {
     bool w = true;
     if (lane == 0) w = bar_wait_cluster(p, pair_ready, pair_cnt & 1, kDevTimeoutCluster);
     if (!workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0)) return false;
   }
-  const uint32_t peer_red = mapa_shared(smem_u32(red), peer);
+  if (et == 0) stamp(ts, 9);
   // epilogue on row pairs (i, i+64), 4 rows per item: the two splits' sums
   // (two terms, so the order does not change the result)
   const int items = p.T * 8;
@@ -492,8 +512,8 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
     const int i = half * 32 + (it & 7) * 4;
     const float4 va = *reinterpret_cast<const float4*>(red + t * kBM + i);
     const float4 vc = *reinterpret_cast<const float4*>(red + t * kBM + i + 64);
-    const float4 pa = ld_dsmem_f4(peer_red + static_cast<uint32_t>((t * kBM + i) * 4));
-    const float4 pc = ld_dsmem_f4(peer_red + static_cast<uint32_t>((t * kBM + i + 64) * 4));
+    const float4 pa = *reinterpret_cast<const float4*>(red + t * kBM + (i ^ 32));
+    const float4 pc = *reinterpret_cast<const float4*>(red + t * kBM + ((i + 64) ^ 32));
     const float v0[4] = {va.x + pa.x, va.y + pa.y, va.z + pa.z, va.w + pa.w};
     const float v1[4] = {vc.x + pc.x, vc.y + pc.y, vc.z + pc.z, vc.w + pc.w};
     const int b = t / p.S, s = t - b * p.S;
@@ -548,15 +568,13 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
       }
     }
   }
-  // the peer may reuse its tile buffer once this CTA has read it, and this
-  // CTA may reuse its own once the peer has
+  if (et == 0) stamp(ts, 12);
+  // this CTA has read its buffer: the peer may push its next tile into it
   __syncwarp();
   if (lane == 0) mbar_arrive_peer(pair_done, peer);
   workers_publish(p, et, op == kOpQkv ? kCQkv : kCAct);
-  bool w = true;
-  if (lane == 0) w = bar_wait_cluster(p, pair_done, pair_cnt & 1, kDevTimeoutCluster);
   ++pair_cnt;
-  return workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+  return true;
 }
 
 // ----------------------------------------------------- worker: attention ---
@@ -594,7 +612,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   uint8_t* sK = smem + kOffAK;
   uint8_t* sV = smem + kOffAV;
   uint8_t* sP = smem + kOffAP;
-  float* ks_s = reinterpret_cast<float*>(small + kSmScales);
+  float* ks_s = reinterpret_cast<float*>(smem + kOffAScales);
   float* vs_s = ks_s + 64;
   float* kdq_s = vs_s + 64;
   float* vdq_s = kdq_s + 64;
@@ -921,7 +939,7 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
   if (et == 0) stamp(ts, 1);
   const int wq = et >> 5, lane = et & 31;
-  constexpr int kBatch = 16;  // splits whose partials are in flight together
+  constexpr int kBatch = 8;  // splits whose partials are in flight together
   for (int r = r0 + wq; r < r1; r += 4) {
     const int R = qt * kQR + r;
     if (R >= p.Hq * p.S) continue;
@@ -986,8 +1004,9 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
                            unsigned long long* ts) {
   const int lane = et & 31, wq = et >> 5;
   float* red4 = reinterpret_cast<float*>(small + kSmRed4);
-  // the tail's normalized row borrows the accumulator-tile buffer (idle
-  // outside a GEMM item's epilogue)
+  // the tail's normalized row borrows the accumulator-tile buffer: the peer
+  // CTA's next push into it belongs to a paired tile of the next Euler step,
+  // whose input needs every tail of this step first
   float* row = reinterpret_cast<float*>(small - kOffSmall + kOffRed);
   float* xs = reinterpret_cast<float*>(small + kSmXs);
   const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
@@ -1016,10 +1035,10 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
     const int m = f0 / kBM, r0 = f0 % kBM;
     uint4 hraw = __ldcg(reinterpret_cast<const uint4*>(p.h + static_cast<long>(t) * p.W + f0));
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < oc.splits; s0 += 8) {
-      float4 a[8], c[8];
+    for (int s0 = 0; s0 < oc.splits; s0 += 4) {
+      float4 a[4], c[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         if (s0 + q < oc.splits) {
           const float* ps = oc.part + ((static_cast<long>(m) * oc.splits + s0 + q) * kNT + t) * kBM + r0;
           a[q] = __ldcg(reinterpret_cast<const float4*>(ps));
@@ -1027,7 +1046,7 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
         }
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 4; ++q) {
         if (s0 + q < oc.splits) {
           acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
           acc[4] += c[q].x; acc[5] += c[q].y; acc[6] += c[q].z; acc[7] += c[q].w;
@@ -1155,7 +1174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(o_full, 1);
     mbar_init(attn_done, 4);
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmKvnFull), 1);
-    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), 4);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), 2);
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), 4);
     fence_mbar_init();
     for (int i = 0; i < 4; ++i) {
@@ -1291,11 +1310,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             ++tmem_uses;
             tc_fence_after();
+            unsigned long long* mts =
+                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                                                           : nullptr;
             for (int j = 0; j < nkb && ok; ++j) {
               const uint32_t ii = consumed + j;
               const int s = ii % kStages;
               ok = bar_wait(p, &full[s], (ii / kStages) & 1, kDevTimeoutTmaFull);
               if (!ok) break;
+              if (j == 0) stamp(mts, 10);
+              if (j == nkb - 1) stamp(mts, 11);
               tc_fence_after();
               const uint32_t a_base = smem_u32(smem + s * kWBytes);
               const uint32_t b_base = smem_u32(smem + kOffX + s * kXBytes);
@@ -1395,7 +1419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued; ++ii)
       mbar_wait(&full[ii % kStages], (ii / kStages) & 1, p.status, kDevTimeoutTmaFull);
   }
-  // the peer CTA reads this CTA's shared memory until its last paired item
+  // the peer CTA writes into this CTA's shared memory until its last paired item
   tc_fence_before();
   cluster_sync();
   if (warp == 1) {
