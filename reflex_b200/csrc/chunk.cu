@@ -1299,6 +1299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
       constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
       uint32_t consumed = 0, tmem_uses = 0, q_cnt = 0, conv_cnt = 0, p_cnt = 0;
+      // ring stage 0's operand descriptors (shared-memory addresses stay below
+      // 256 KB, so start-address offsets never carry out of their field)
+      const uint64_t a_desc0 = make_sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = make_sdesc_sw128(smem_u32(smem + kOffX), 16, 1024);
       bool ok = true;
       for (int tau = 0; tau < p.steps && ok; ++tau) {
         for (int i = 0; i < n_step && ok; ++i) {
@@ -1316,19 +1320,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < nkb && ok; ++j) {
               const uint32_t ii = consumed + j;
               const int s = ii % kStages;
-              ok = bar_wait(p, &full[s], (ii / kStages) & 1, kDevTimeoutTmaFull);
+              if (!mbar_try_wait(&full[s], (ii / kStages) & 1))
+                ok = bar_wait(p, &full[s], (ii / kStages) & 1, kDevTimeoutTmaFull);
               if (!ok) break;
               if (j == 0) stamp(mts, 10);
               if (j == nkb - 1) stamp(mts, 11);
               tc_fence_after();
-              const uint32_t a_base = smem_u32(smem + s * kWBytes);
-              const uint32_t b_base = smem_u32(smem + kOffX + s * kXBytes);
+              // descriptors of stage s: the base descriptors plus the stage's
+              // byte offset >> 4 in the start-address field
+              const uint64_t ad = a_desc0 + static_cast<uint64_t>((s * kWBytes) >> 4);
+              const uint64_t bd = b_desc0 + static_cast<uint64_t>((s * kXBytes) >> 4);
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk) {
-                const uint64_t ad = make_sdesc_sw128(a_base + kk * 32, 16, 1024);
-                const uint64_t bd = make_sdesc_sw128(b_base + kk * 32, 16, 1024);
-                umma_f16_ss(tmem, ad, bd, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
-              }
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_f16_ss(tmem, ad + static_cast<uint64_t>(kk * 2), bd + static_cast<uint64_t>(kk * 2), idesc_g,
+                            (j > 0 || kk > 0) ? 1u : 0u);
               umma_commit(&empty[s]);
             }
             consumed += nkb;
