@@ -50,7 +50,8 @@
 namespace rfx {
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kWorkers = 256;  // worker threads: warps 2..9, two per TMEM lane quadrant
+constexpr int kThreads = 64 + kWorkers;
 constexpr int kNT = 64;  // token tile: T <= 64
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -71,8 +72,9 @@ constexpr int kOffAK = 65536;    // 4 x [64 x 64] bf16
 constexpr int kOffAV = 98304;    // 4 x [64 x 64] f16, MN-major blocks
 constexpr int kOffAP = 131072;   // [128 x 64] f16
 constexpr int kOffAScales = 147456;  // 8 x 64 floats (2 KB): per-key scales, zero points, block ids
+constexpr int kOffAXchg = 149504;    // 768 floats: row maxima and sums of the two column halves
 // the attention tiles overlay the ring (idle while an attention item runs)
-static_assert(kOffAScales + 2048 <= kOffRed, "attention tiles must fit in the ring");
+static_assert(kOffAXchg + 3072 <= kOffRed, "attention tiles must fit in the ring");
 
 // small region (byte offsets)
 constexpr int kSmFull = 0;         // 8 mbarriers
@@ -89,7 +91,7 @@ constexpr int kSmTmem = 192;
 constexpr int kSmKvnFull = 200;    // mbarrier: the new keys' K / V tiles (TMA) have landed
 constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA has pushed its partial into this CTA's tile buffer
 constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has read its tile buffer (this CTA may push again)
-constexpr int kSmRed4 = 320;       // 8 floats
+constexpr int kSmRed8 = 320;       // 8 floats
 constexpr int kSmXs = 512;         // 64 floats
 static_assert(kSmXs + 256 <= kSmallBytes, "small region");
 
@@ -260,14 +262,16 @@ __device__ bool bar_wait_cluster(const ChunkParams& p, uint64_t* bar, uint32_t p
   }
 }
 
-// named barrier 1 over the 128 worker threads
-__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier 1 over the 256 worker threads
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// named barrier 2 + quad over the two worker warps that share a TMEM lane quadrant
+__device__ __forceinline__ void quad_pair_sync(int quad) { asm volatile("bar.sync %0, 64;" ::"r"(2 + quad) : "memory"); }
 __device__ __forceinline__ bool workers_all(bool v) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "bar.red.and.pred q, 1, 256, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
       : "r"(v ? 1u : 0u)
@@ -300,17 +304,16 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   const float inner = kBeta * (x + kKappa * x * x * x);
   return 0.5f * x * (1.f + tanhf(inner));
 }
-__device__ __forceinline__ void unpack8_bf16(uint4 raw, float (&f)[8]) {
-  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 v = __bfloat1622float2(h2[e]);
-    f[2 * e] = v.x;
-    f[2 * e + 1] = v.y;
-  }
+__device__ __forceinline__ void unpack4_bf16(uint2 raw, float (&f)[4]) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
 }
-__device__ __forceinline__ uint4 pack8_bf16(const float (&y)[8]) {
-  return make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+__device__ __forceinline__ uint2 pack4_bf16(const float (&y)[4]) {
+  return make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
 }
 __device__ __forceinline__ float load_scalar(const void* ptr, long i, bool bf16) {
   return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(ptr)[i]) : static_cast<const float*>(ptr)[i];
@@ -333,50 +336,52 @@ __device__ __forceinline__ long mod_off(const ChunkParams& p, int tau, int n) {
   return (static_cast<long>(tau) * p.NN + n) * p.W;
 }
 
-// Norm vectors of one norm for the worker's 8 features (f0 = et*8).
+// Norm vectors of one norm for the worker's 4 features (f0 = et*4).
 struct NormVec {
-  float a1[8], a2[8], b2[8];
+  float a1[4], a2[4], b2[4];
 };
-__device__ __forceinline__ void load8(const float* src, float (&dst)[8]) {
+__device__ __forceinline__ void load4(const float* src, float (&dst)[4]) {
   *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
-  *reinterpret_cast<float4*>(dst + 4) = *reinterpret_cast<const float4*>(src + 4);
 }
 __device__ __forceinline__ void load_norm_vec(const ChunkParams& p, int et, int tau, int n, NormVec& v) {
-  const int f0 = et * 8;
-  load8(p.a1 + static_cast<long>(n) * p.W + f0, v.a1);
-  if (p.a2) load8(p.a2 + mod_off(p, tau, n) + f0, v.a2);
-  if (p.b2) load8(p.b2 + mod_off(p, tau, n) + f0, v.b2);
+  const int f0 = et * 4;
+  load4(p.a1 + static_cast<long>(n) * p.W + f0, v.a1);
+  if (p.a2) load4(p.a2 + mod_off(p, tau, n) + f0, v.a2);
+  if (p.b2) load4(p.b2 + mod_off(p, tau, n) + f0, v.b2);
 }
 
-// (Ada)RMSNorm of one token row held as 8 features per worker thread:
+// (Ada)RMSNorm of one token row held as 4 features per worker thread:
 // y = ((x*rstd)*a1)*a2 + b2 (fp32, rounded by the caller), rstd =
-// rsqrt(mean(x^2) + eps).  The reduction order matches the standalone norm
-// kernel (per thread, then warp, then the four warps in order).
-__device__ void norm_row(const ChunkParams& p, int et, const float (&hv)[8], const NormVec& v, float* red4,
-                         float (&y)[8]) {
+// rsqrt(mean(x^2) + eps); the sum of squares per thread, then per warp, then
+// over the eight warps in order.
+__device__ void norm_row(const ChunkParams& p, int et, const float (&hv)[4], const NormVec& v, float* red8,
+                         float (&y)[4]) {
   const int lane = et & 31, wq = et >> 5;
   float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ss = fmaf(hv[e], hv[e], ss);
+  for (int e = 0; e < 4; ++e) ss = fmaf(hv[e], hv[e], ss);
   ss = warp_sum(ss);
-  if (lane == 0) red4[wq] = ss;
+  if (lane == 0) red8[wq] = ss;
   workers_sync();
-  const float rstd = rsqrtf((red4[0] + red4[1] + red4[2] + red4[3]) / static_cast<float>(p.W) + p.eps);
+  float tot = 0.f;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+  for (int w = 0; w < kWorkers / 32; ++w) tot += red8[w];
+  const float rstd = rsqrtf(tot / static_cast<float>(p.W) + p.eps);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
     float x = __fmul_rn(__fmul_rn(hv[e], rstd), v.a1[e]);
     if (p.a2) x = __fmul_rn(x, v.a2[e]);
     if (p.b2) x = __fadd_rn(x, v.b2[e]);
     y[e] = x;
   }
-  workers_sync();  // red4 is reused by the next row
+  workers_sync();  // red8 is reused by the next row
 }
 
-// h_row[o] = bf16(sum_a xs[a] * W_in[o][a] + b_in[o]) for the worker's 8 features.
-__device__ __forceinline__ void action_in8(const ChunkParams& p, int et, const float* xs, float (&hv)[8]) {
+// h_row[o] = bf16(sum_a xs[a] * W_in[o][a] + b_in[o]) for the worker's 4 features.
+__device__ __forceinline__ void action_in4(const ChunkParams& p, int et, const float* xs, float (&hv)[4]) {
 #pragma unroll 1
-  for (int e = 0; e < 8; ++e) {
-    const int o = et * 8 + e;
+  for (int e = 0; e < 4; ++e) {
+    const int o = et * 4 + e;
     const __nv_bfloat16* wr = p.w_in + static_cast<long>(o) * p.A;
     float acc = 0.f;
     for (int a = 0; a < p.A; a += 8) {
@@ -404,22 +409,23 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int row = quad * 32 + lane;
+  const int ch = et >> 7;  // this warp's half of the 64 token columns
   uint64_t* acc_full = reinterpret_cast<uint64_t*>(small + kSmAccFull);
   uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
   const OpCfg oc = op_cfg(p, op);
   // QKV / gate-up tiles are split along K over the two CTAs of a cluster;
   // CTA rank h runs the epilogue of row pairs (i, i+64), i in [32h, 32h+32).
-  // RoPE cos / sin of this thread's epilogue items (item k: it = et + 128 k,
+  // RoPE cos / sin of this thread's epilogue items (item k: it = et + 256 k,
   // token it / 8, rows 32h + (it % 8) * 4) are fetched while the MMA runs.
   const bool paired = op == kOpQkv || op == kOpGu;
   const int half = split;
-  constexpr int kItems = kNT * 8 / 128;
+  constexpr int kItems = kNT * 8 / kWorkers;
   float4 rc[kItems], rsn[kItems];
   const bool rotary = op == kOpQkv && (m >> 1) <= p.Hq;
   if (rotary) {
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
-      const int it = et + 128 * k;
+      const int it = et + kWorkers * k;
       if (it < p.T * 8) {
         int pos = p.pos[it >> 3];
         pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
@@ -450,24 +456,27 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   float* part = oc.part + (static_cast<long>(m) * oc.splits + split) * kNT * kBM;
   bool pushed = true;
   {
-    uint32_t r[4][16];
+    // token columns 32 ch .. 32 ch + 31 of this thread's accumulator row
+    uint32_t r[2][16];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r[c]);
+    for (int c = 0; c < 2; ++c) tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + (2 * ch + c) * 16, r[c]);
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(acc_free);
     if (!paired) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (c * 16 + e < p.T) __stcg(part + (c * 16 + e) * kBM + row, __uint_as_float(r[c][e]));
+        for (int e = 0; e < 16; ++e) {
+          const int t = (2 * ch + c) * 16 + e;
+          if (t < p.T) __stcg(part + t * kBM + row, __uint_as_float(r[c][e]));
+        }
     } else if ((quad & 1) == half) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kBM + row] = __uint_as_float(r[c][e]);
+        for (int e = 0; e < 16; ++e) red[((2 * ch + c) * 16 + e) * kBM + row] = __uint_as_float(r[c][e]);
     } else {
       // the peer's buffer is free once the peer has read the previous tile
       if (pair_cnt > 0) {
@@ -477,10 +486,12 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
       if (pushed) {
         const uint32_t dst = mapa_shared(smem_u32(red + (row ^ 32)), peer);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (c * 16 + e < p.T) st_dsmem_f32(dst + static_cast<uint32_t>((c * 16 + e) * kBM * 4), __uint_as_float(r[c][e]));
+          for (int e = 0; e < 16; ++e) {
+            const int t = (2 * ch + c) * 16 + e;
+            if (t < p.T) st_dsmem_f32(dst + static_cast<uint32_t>(t * kBM * 4), __uint_as_float(r[c][e]));
+          }
         __syncwarp();
         if (lane == 0) mbar_arrive_peer(pair_ready, peer);
       }
@@ -506,7 +517,7 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   const int items = p.T * 8;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
-    const int it = et + 128 * k;
+    const int it = et + kWorkers * k;
     if (it >= items) break;
     const int t = it >> 3;
     const int i = half * 32 + (it & 7) * 4;
@@ -609,6 +620,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
                             unsigned long long* ts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
+  const int ch = et >> 7;  // this warp's half of the columns of its rows (S: 32 keys, O: 128 dims)
   uint8_t* sK = smem + kOffAK;
   uint8_t* sV = smem + kOffAV;
   uint8_t* sP = smem + kOffAP;
@@ -620,6 +632,10 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   float* vzp_s = kzp_s + 64;
   int* nb_s = reinterpret_cast<int*>(vzp_s + 64);
   float* kadd_s = reinterpret_cast<float*>(nb_s + 64);
+  // row maxima of the two column halves (two buffers, alternating by block)
+  // and the final row sums, exchanged between the warps of a lane quadrant
+  float* mx_x = reinterpret_cast<float*>(smem + kOffAXchg);  // [2][2][128]
+  float* l_x = mx_x + 512;                                   // [2][128]
   uint64_t* conv_done = reinterpret_cast<uint64_t*>(small + kSmConv);
   uint64_t* s_full = reinterpret_cast<uint64_t*>(small + kSmSFull);
   uint64_t* p_ready = reinterpret_cast<uint64_t*>(small + kSmPReady);
@@ -661,7 +677,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
       // the first half of this thread's 16-byte chunks is requested here, the
       // second half while the first is converted
       auto ctx_chunk = [&](int q) {
-        const int it = et + q * 128;  // 0..2047: K chunks then V chunks
+        const int it = et + q * kWorkers;  // 0..2047: K chunks then V chunks
         const bool isv = it >= kKB * 16;
         const int w = isv ? it - kKB * 16 : it;
         const int key = w >> 4, g = w & 15;
@@ -670,9 +686,9 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         return *reinterpret_cast<const uint4*>((isv ? vring : kring) + (static_cast<long>(b) * p.cap + slot) * kD +
                                                g * 16);
       };
-      uint4 raw[8];
+      uint4 raw[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) raw[q] = ctx_chunk(q);
+      for (int q = 0; q < 4; ++q) raw[q] = ctx_chunk(q);
       if (et < 64) {
         const long slot = static_cast<long>(j) * kKB + et;
         const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
@@ -694,14 +710,14 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
       workers_sync();
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint4 nxt[8];
+        uint4 nxt[4];
         if (half == 0) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) nxt[q] = ctx_chunk(8 + q);
+          for (int q = 0; q < 4; ++q) nxt[q] = ctx_chunk(4 + q);
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int it = et + (half * 8 + q) * 128;
+        for (int q = 0; q < 4; ++q) {
+          const int it = et + (half * 4 + q) * kWorkers;
           const bool isv = it >= kKB * 16;
           const int w = isv ? it - kKB * 16 : it;
           const int key = w >> 4, g = w & 15;
@@ -717,7 +733,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         }
         if (half == 0) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) raw[q] = nxt[q];
+          for (int q = 0; q < 4; ++q) raw[q] = nxt[q];
         }
       }
     } else if (nbl == 1) {
@@ -752,7 +768,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         nb_s[et] = 0;
       }
 #pragma unroll 2
-      for (int it = et; it < 2 * kKB * 32; it += 128) {
+      for (int it = et; it < 2 * kKB * 32; it += kWorkers) {
         const bool isv = it >= kKB * 32;
         const int w = isv ? it - kKB * 32 : it;
         const int key = w >> 5, c = w & 31;
@@ -781,11 +797,13 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     ++blk_cnt;
     if (et == 0 && jl == 0) stamp(ts, 1);
     tc_fence_after();
-    // two passes over the scores in TMEM (16 columns at a time): the block
-    // max, then p = 2^(z - m) -> P tile; scores in log2 units, one FMA per key
+    // two passes over this warp's 32 score columns in TMEM (16 at a time): the
+    // block max (combined with the other column half through shared memory),
+    // then p = 2^(z - m) -> P tile; scores in log2 units, one FMA per key
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int q = 0; q < kKB / 16; ++q) {
+    for (int qq = 0; qq < 2; ++qq) {
+      const int q = 2 * ch + qq;
       uint32_t rr[16];
       tmem_ld16(tmS + lane_base + q * 16, rr);
       tmem_wait_ld();
@@ -800,7 +818,10 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         mx[3] = fmaxf(mx[3], fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w));
       }
     }
-    const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    float* mxb = mx_x + (jl & 1) * 256;
+    mxb[ch * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    quad_pair_sync(quad);
+    const float bmax = fmaxf(mxb[r], mxb[128 + r]);
     const float m_new = fmaxf(m_run, bmax);
     bool need = false;
     float m_use;
@@ -816,7 +837,8 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     const float m_sub = m_use == -INFINITY ? 0.f : m_use;
     float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int q = 0; q < kKB / 16; ++q) {
+    for (int qq = 0; qq < 2; ++qq) {
+      const int q = 2 * ch + qq;
       uint32_t rr[16];
       tmem_ld16(tmS + lane_base + q * 16, rr);
       tmem_wait_ld();
@@ -854,7 +876,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     m_run = m_use;
     if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < kD / 16; c0 += 2) {
+      for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 2) {
         uint32_t rr[2][16];
 #pragma unroll
         for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
@@ -885,6 +907,9 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     tc_fence_after();
     const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits + sp;
     const bool final_out = p.attn_splits == 1;
+    l_x[ch * 128 + r] = l_run;
+    quad_pair_sync(quad);
+    l_run = l_x[r] + l_x[128 + r];
     const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
     const long tok = static_cast<long>(b) * p.S + s_row;
     __nv_bfloat16* orow = p.attn_out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
@@ -892,7 +917,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     // combine weights it by l * 2^(m - M)): [cta][16-column chunk][row][16]
     __half* wrow_o = reinterpret_cast<__half*>(p.ws_o) + (wcta * (kD / 16) * kQR + r) * 16;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+    for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 4) {
       uint32_t rr[4][16];
 #pragma unroll
       for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
@@ -919,7 +944,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         }
       }
     }
-    if (!final_out && row_valid) __stcg(p.ws_ml + wcta * kQR + r, make_float2(m_run, l_run));
+    if (!final_out && row_valid && ch == 0) __stcg(p.ws_ml + wcta * kQR + r, make_float2(m_run, l_run));
   }
   // TMEM and the ring's shared memory are free again
   tc_fence_before();
@@ -939,8 +964,8 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
   if (et == 0) stamp(ts, 1);
   const int wq = et >> 5, lane = et & 31;
-  constexpr int kBatch = 8;  // splits whose partials are in flight together
-  for (int r = r0 + wq; r < r1; r += 4) {
+  constexpr int kBatch = 4;  // splits whose partials are in flight together
+  for (int r = r0 + wq; r < r1; r += kWorkers / 32) {
     const int R = qt * kQR + r;
     if (R >= p.Hq * p.S) continue;
     const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
@@ -1003,14 +1028,14 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
 __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small, int et, int kind, int tau, int layer, int t,
                            unsigned long long* ts) {
   const int lane = et & 31, wq = et >> 5;
-  float* red4 = reinterpret_cast<float*>(small + kSmRed4);
+  float* red8 = reinterpret_cast<float*>(small + kSmRed8);
   // the tail's normalized row borrows the accumulator-tile buffer: the peer
   // CTA's next push into it belongs to a paired tile of the next Euler step,
   // whose input needs every tail of this step first
   float* row = reinterpret_cast<float*>(small - kOffSmall + kOffRed);
   float* xs = reinterpret_cast<float*>(small + kSmXs);
   const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
-  const int f0 = et * 8;
+  const int f0 = et * 4;
   const int b = t / p.S, s = t - b * p.S;
   const bool tail = kind == kTFinD && layer == p.NL - 1;
   const bool next_step = tail && tau + 1 < p.steps;
@@ -1018,13 +1043,13 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
   NormVec nv1;
   const int n1 = kind == kTInit ? 0 : (kind == kTFinO ? 2 * layer + 1 : (tail ? 2 * p.NL : 2 * (layer + 1)));
   load_norm_vec(p, et, tau, n1, nv1);
-  float g[8];
-  if (kind != kTInit && p.gate) load8(p.gate + mod_off(p, tau, kind == kTFinO ? 2 * layer : 2 * layer + 1) + f0, g);
-  float hv[8];
+  float g[4];
+  if (kind != kTInit && p.gate) load4(p.gate + mod_off(p, tau, kind == kTFinO ? 2 * layer : 2 * layer + 1) + f0, g);
+  float hv[4];
   if (kind == kTInit) {
     if (et < p.A) xs[et] = bf16_round(p.x[(static_cast<long>(b) * p.S + s) * p.A + et]);
     workers_sync();
-    action_in8(p, et, xs, hv);
+    action_in4(p, et, xs, hv);
   } else {
     const int op = kind == kTFinO ? kOpO : kOpDown;
     const OpCfg oc = op_cfg(p, op);
@@ -1033,30 +1058,28 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
       return false;
     if (et == 0) stamp(ts, 1);
     const int m = f0 / kBM, r0 = f0 % kBM;
-    uint4 hraw = __ldcg(reinterpret_cast<const uint4*>(p.h + static_cast<long>(t) * p.W + f0));
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    uint2 hraw = __ldcg(reinterpret_cast<const uint2*>(p.h + static_cast<long>(t) * p.W + f0));
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int s0 = 0; s0 < oc.splits; s0 += 4) {
-      float4 a[4], c[4];
+      float4 a[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (s0 + q < oc.splits) {
           const float* ps = oc.part + ((static_cast<long>(m) * oc.splits + s0 + q) * kNT + t) * kBM + r0;
           a[q] = __ldcg(reinterpret_cast<const float4*>(ps));
-          c[q] = __ldcg(reinterpret_cast<const float4*>(ps + 4));
         }
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (s0 + q < oc.splits) {
           acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
-          acc[4] += c[q].x; acc[5] += c[q].y; acc[6] += c[q].z; acc[7] += c[q].w;
         }
       }
     }
-    float hres[8];
-    unpack8_bf16(hraw, hres);
+    float hres[4];
+    unpack4_bf16(hraw, hres);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < 4; ++e) {
       const float a = bf16_round(acc[e]);
       const float ga = p.gate ? bf16_round(__fmul_rn(g[e], a)) : a;
       hv[e] = bf16_round(__fadd_rn(hres[e], ga));
@@ -1064,13 +1087,13 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
   }
   if (tail) {
     // final norm -> action_out_proj -> x += bf16(dt * v) -> next step's action_in_proj
-    float y[8];
-    norm_row(p, et, hv, nv1, red4, y);
+    float y[4];
+    norm_row(p, et, hv, nv1, red8, y);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) row[f0 + e] = bf16_round(y[e]);
+    for (int e = 0; e < 4; ++e) row[f0 + e] = bf16_round(y[e]);
     workers_sync();
 #pragma unroll 1
-    for (int a = wq; a < p.A; a += 4) {
+    for (int a = wq; a < p.A; a += kWorkers / 32) {
       const __nv_bfloat16* wr = p.w_out + static_cast<long>(a) * p.W;
       float acc = 0.f;
       for (int k = lane * 8; k < p.W; k += 256) {
@@ -1098,12 +1121,12 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
       return true;
     }
     load_norm_vec(p, et, tau + 1, 0, nv1);  // the next step's first input norm
-    action_in8(p, et, xs, hv);
+    action_in4(p, et, xs, hv);
   }
-  *reinterpret_cast<uint4*>(p.h + static_cast<long>(t) * p.W + f0) = pack8_bf16(hv);
-  float y[8];
-  norm_row(p, et, hv, nv1, red4, y);
-  *reinterpret_cast<uint4*>(p.xn + static_cast<long>(t) * p.W + f0) = pack8_bf16(y);
+  *reinterpret_cast<uint2*>(p.h + static_cast<long>(t) * p.W + f0) = pack4_bf16(hv);
+  float y[4];
+  norm_row(p, et, hv, nv1, red8, y);
+  *reinterpret_cast<uint2*>(p.xn + static_cast<long>(t) * p.W + f0) = pack4_bf16(y);
   workers_publish(p, et, (kind == kTFinO) ? kCXn2 : kCXn);
   return true;
 }
@@ -1166,16 +1189,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[i], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_free, 4);
+    mbar_init(acc_free, kWorkers / 32);
     mbar_init(q_full, 1);
-    mbar_init(conv_done, 4);
+    mbar_init(conv_done, kWorkers / 32);
     mbar_init(s_full, 1);
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, kWorkers / 32);
     mbar_init(o_full, 1);
-    mbar_init(attn_done, 4);
+    mbar_init(attn_done, kWorkers / 32);
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmKvnFull), 1);
-    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), 2);
-    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), 4);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), kWorkers / 64);  // the peer's pushing warps
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), kWorkers / 32);
     fence_mbar_init();
     for (int i = 0; i < 4; ++i) {
       tma_prefetch_desc(&maps.w[i]);
