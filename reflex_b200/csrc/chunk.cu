@@ -964,47 +964,42 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
   if (et == 0) stamp(ts, 1);
   const int wq = et >> 5, lane = et & 31;
-  constexpr int kBatch = 4;  // splits whose partials are in flight together
+  constexpr int kBatch = 8;  // splits whose partials are in flight together
   for (int r = r0 + wq; r < r1; r += kWorkers / 32) {
     const int R = qt * kQR + r;
     if (R >= p.Hq * p.S) continue;
     const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
     // lane: 8 of the row's 256 columns (chunk lane / 2, half lane % 2)
     const __half* ob = reinterpret_cast<const __half*>(p.ws_o) + ((lane >> 1) * kQR + r) * 16 + (lane & 1) * 8;
-    float M = -INFINITY, L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // split s's (m, l) sits in lane s (at most 32 splits): the row max M and
+    // the weights w_s = l_s * 2^(m_s - M) are warp reductions and broadcasts
+    const float2 ml = lane < p.attn_splits ? __ldcg(p.ws_ml + (base + lane) * kQR + r) : make_float2(-INFINITY, 0.f);
+    uint4 o[kBatch];
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q)
+      if (q < p.attn_splits) o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + q) * (kD / 16) * kQR * 16));
+    const bool live = ml.x != -INFINITY && ml.y > 0.f;
+    const float M = warp_max(live ? ml.x : -INFINITY);
+    const float w = live ? exp2f(ml.x - M) * ml.y : 0.f;
+    const float L = warp_sum(w);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int s0 = 0; s0 < p.attn_splits; s0 += kBatch) {
-      uint4 o[kBatch];
-      float2 ml[kBatch];
+      if (s0 > 0) {
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+          if (s0 + q < p.attn_splits)
+            o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s0 + q) * (kD / 16) * kQR * 16));
+      }
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
-        if (s0 + q < p.attn_splits) {
-          o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s0 + q) * (kD / 16) * kQR * 16));
-          ml[q] = __ldcg(p.ws_ml + (base + s0 + q) * kQR + r);
-        }
-      }
-      // running log-sum-exp merge: weights l_s * 2^(m_s - M)
-      float Mb = M;
-#pragma unroll
-      for (int q = 0; q < kBatch; ++q)
-        if (s0 + q < p.attn_splits && ml[q].y > 0.f) Mb = fmaxf(Mb, ml[q].x);
-      if (Mb != M && M != -INFINITY) {
-        const float f = exp2f(M - Mb);
-        L *= f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] *= f;
-      }
-      M = Mb;
-#pragma unroll
-      for (int q = 0; q < kBatch; ++q) {
-        if (s0 + q >= p.attn_splits || ml[q].x == -INFINITY || ml[q].y <= 0.f) continue;
-        const float w = exp2f(ml[q].x - M) * ml[q].y;
-        L += w;
+        const float ws = __shfl_sync(0xffffffffu, w, (s0 + q) & 31);
+        if (s0 + q >= p.attn_splits) continue;
         const __half2* h2 = reinterpret_cast<const __half2*>(&o[q]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __half22float2(h2[e]);
-          acc[2 * e] = fmaf(w, f.x, acc[2 * e]);
-          acc[2 * e + 1] = fmaf(w, f.y, acc[2 * e + 1]);
+          acc[2 * e] = fmaf(ws, f.x, acc[2 * e]);
+          acc[2 * e + 1] = fmaf(ws, f.y, acc[2 * e + 1]);
         }
       }
     }
