@@ -3,6 +3,7 @@
     python -m reflex_b200.profile [--layers 2] [--reps 3] [--ops qkv,attn,o,gu,down,tail,time,mod]
     python -m reflex_b200.profile --layers 18 --chunk   # one eager chunk, then one graph replay
     python -m reflex_b200.profile --layers 2 --chunk --fused   # the same through the chunk executor
+    python -m reflex_b200.profile --layers 18 --chunk --fused --trace   # per-phase timeline of the executor
 
 Builds the PI0.5 engine at the benchmark's shapes (width 1024, 8x256 heads,
 818-token int8 context, 50 action tokens) with a few layers, runs one chunk to
@@ -33,6 +34,8 @@ def main():
     ap.add_argument("--streams", type=int, default=1)
     ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
+    ap.add_argument("--trace", action="store_true",
+                    help="with --chunk --fused: %globaltimer stamps of every task of the first Euler step")
     args = ap.parse_args()
     cfg = pi05_config(num_layers=args.layers, adarms="ssg")
     wts = synthetic.expert_weights(cfg, seed=0, device="cuda")
@@ -44,6 +47,9 @@ def main():
     eng.set_inputs(synthetic.noise(cfg, B=args.streams, seed=2, device="cuda"))
     eng.run_eager()
     torch.cuda.synchronize()
+    if args.chunk and args.fused and args.trace:
+        trace_chunk(eng)
+        return
     if args.chunk:
         print("launches per chunk", eng.num_launches)
         eng.capture()
@@ -71,6 +77,68 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     print("ok", K.device_status())
+
+
+# task types and trace slots of the chunk executor (csrc/chunk.cu): per task 16
+# u64: [0] start, [1] inputs ready / accumulator ready, [2] end, [3] producer
+# saw the input, [4] task words x | y << 32, [6] accumulator read out,
+# [8] own rows stored, [9] peer partial arrived, [10] / [11] first / last
+# operand stage seen by the MMA issuer, [12] epilogue done.
+_TASKS = {1: "qkv", 2: "o", 3: "gu", 4: "down", 5: "attn", 6: "comb", 7: "fin_o", 8: "fin_d"}
+_ORDER = ["qkv", "attn", "comb", "o", "fin_o", "gu", "down", "fin_d"]
+
+
+def trace_chunk(eng, per_cta: int = 256) -> None:
+    """Runs one chunk with task tracing on and prints, for the first Euler step,
+    the per-layer phase timeline and the median segments of the GEMM tasks."""
+    import numpy as np
+
+    from . import _lib as L
+
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    buf = torch.zeros(nsm * per_cta * 16, dtype=torch.int64, device="cuda")
+    for _ in range(2):
+        eng.run_eager()
+    torch.cuda.synchronize()
+    L.call("rfx_set_trace", buf.data_ptr(), buf.numel() * 8)
+    eng.run_eager()
+    torch.cuda.synchronize()
+    L.call("rfx_set_trace", None, 0)
+    print("status", K.device_status())
+    tr = buf.view(nsm, per_cta, 16).cpu().numpy().astype(np.int64)
+    rows = []
+    for c in range(nsm):
+        for i in range(per_cta):
+            if tr[c, i, 0] == 0:
+                continue
+            w = int(tr[c, i, 4] & 0xFFFFFFFF)
+            rows.append((_TASKS.get(w & 0xFF, "?"), (w >> 8) & 0xFF, tr[c, i]))
+    t0 = min(r[2][0] for r in rows)
+    us = lambda v: (v - t0) / 1e3  # noqa: E731
+    print("layer phase  tasks  last_input_ready  last_end  median(end - ready) [us from the chunk start]")
+    ends = []
+    for layer in range(eng.cfg.num_layers):
+        for name in _ORDER:
+            rs = [r[2] for r in rows if r[0] == name and r[1] == layer]
+            if not rs:
+                continue
+            ready = [x[1] for x in rs if x[1] > 0]
+            if layer < 3:
+                print(f"{layer:5d} {name:6s} {len(rs):5d} {us(max(ready)) if ready else 0:17.2f} "
+                      f"{us(max(x[2] for x in rs)):9.2f} {np.median([(x[2] - x[1]) / 1e3 for x in rs if x[1]]):10.2f}")
+            if name == "fin_d":
+                ends.append(us(max(x[2] for x in rs)))
+    if len(ends) > 2:
+        print("layer time (us, median over layers): %.2f" % float(np.median(np.diff(ends))))
+
+    def seg(name, a, b):
+        v = [(r[2][b] - r[2][a]) / 1e3 for r in rows if r[0] == name and r[2][a] and r[2][b]]
+        return float(np.median(v)) if v else float("nan")
+
+    for name in ["qkv", "o", "gu", "down"]:
+        print(f"{name:5s} producer saw input -> first stage {seg(name, 3, 10):.2f}, first -> last stage "
+              f"{seg(name, 10, 11):.2f}, last stage -> accumulator ready {seg(name, 11, 1):.2f}, "
+              f"accumulator -> stored {seg(name, 1, 6):.2f}, stored -> end {seg(name, 6, 2):.2f} us")
 
 
 if __name__ == "__main__":
