@@ -196,7 +196,20 @@ int rfx_pack_weight(int kind, const void* src, void* dst, int rows, int K, void*
  * reflex/layers/attention.py:98-164 / mixed_precision_attention.py:74-171.
  * Mask: every valid context slot is visible; new key j is visible to query i
  * iff new_block[j] <= new_block[i] (the block-causal cumsum rule of
- * reflex/policies/pi05/utils.py:210-215 restricted to the suffix). */
+ * reflex/policies/pi05/utils.py:210-215 restricted to the suffix).
+ *
+ * kv_source selects where the kernel gets its bf16 K / f16 V tiles:
+ *   RFX_KV_RING_TILES (default): every CTA converts the quantized ring blocks
+ *     it visits (right for a few query tiles, e.g. the 8 x 50 suffix rows);
+ *   RFX_KV_DENSE: one pass first writes [context | new keys] as bf16 K and
+ *     f16 V (exact casts for the int8 scheme, the reference's dequantize for
+ *     the uint8 scheme) plus per-key score scale / mask / value scale into
+ *     the workspace, then the attention streams those tiles by TMA with two
+ *     key blocks in flight (right for many query tiles, e.g. a 768-token
+ *     frame through the prefix layers, where every query tile visits every
+ *     block).  Same results as the ring path; new_block must be NULL. */
+#define RFX_KV_RING_TILES 0
+#define RFX_KV_DENSE 1
 typedef struct rfx_attn_desc {
   int B, num_q_heads, head_dim, S;
   int capacity;   /* ring slots per stream */
@@ -219,6 +232,7 @@ typedef struct rfx_attn_desc {
   void* workspace;
   size_t workspace_bytes;
   int kv_splits; /* 0 = auto */
+  int kv_source;  /* RFX_KV_RING_TILES (0) or RFX_KV_DENSE */
 } rfx_attn_desc;
 int rfx_attention(const rfx_attn_desc* desc, void* stream);
 /* Workspace needed by rfx_attention for this descriptor (0 if none). */

@@ -24,6 +24,8 @@ RFX_DTYPE_F32 = 0
 RFX_DTYPE_BF16 = 1
 RFX_QUANT_I8_SYM = 0
 RFX_QUANT_U8_REF = 1
+RFX_KV_RING_TILES = 0
+RFX_KV_DENSE = 1
 
 RFX_PRO_LOAD = 0
 RFX_PRO_NORM = 1
@@ -89,7 +91,7 @@ class AttnDesc(Structure):
         ("k_scale", c_void_p), ("v_scale", c_void_p), ("k_zp", c_void_p), ("v_zp", c_void_p),
         ("ctx_valid", c_void_p), ("new_block", c_void_p),
         ("softmax_scale", c_float), ("out", c_void_p),
-        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("kv_splits", c_int),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("kv_splits", c_int), ("kv_source", c_int),
     ]
 
 

@@ -69,6 +69,14 @@ struct AttnParams {
   float2* ws_ml;
   int* status;
   unsigned long long* trace;
+  // dense key source (RFX_KV_DENSE): [B][Lk] per-key score scale (log2
+  // units), value scale and mask add (0 or -inf), bf16 K / f16 V [B][Lk][D]
+  float* key_ks;
+  float* key_vs;
+  float* key_add;
+  __nv_bfloat16* kd;
+  __half* vd;
+  int Lk;
 };
 
 // Trace events (one %globaltimer stamp per event per CTA, see rfx_set_trace).
@@ -501,6 +509,387 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) trace(p, kTrEnd);
 }
 
+// ------------------------------------------------------------ dense mode ---
+// Pre-pass: key block j (64 keys) of stream b -> dense bf16 K / f16 V rows and
+// per-key scales.  Context keys: the exact int8 -> bf16 / f16 casts with the
+// per-token scales moved to the scores (K) and the probabilities (V), or the
+// reference uint8 dequantize ((q - zp) * scale, rounded per op to the scale
+// dtype) with unit scales; the new keys: bf16 K as is, V as f16 of its bf16
+// value; keys past n_ctx / S (or masked by ctx_valid) get scale 0 and -inf.
+__global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ AttnParams p, const uint8_t* k_ring,
+                                                       const uint8_t* v_ring) {
+  pdl_wait();
+  const int j = blockIdx.x, b = blockIdx.y;
+  const long row0 = static_cast<long>(b) * p.Lk + static_cast<long>(j) * kKB;
+  const bool sbf16 = p.scale_bf16 != 0;
+  __shared__ float dq[4][kKB];  // reference scheme: k scale, v scale, k zp, v zp
+  if (j < p.n_ctx_blocks) {
+    if (threadIdx.x < kKB) {
+      const int t = threadIdx.x;
+      const long slot = static_cast<long>(j) * kKB + t;
+      const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
+      bool valid = slot < p.n_ctx;
+      if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
+      p.key_add[row0 + t] = valid ? 0.f : -INFINITY;
+      if (p.mode == kQuantI8Sym) {
+        p.key_ks[row0 + t] = valid ? static_cast<const float*>(p.k_scale)[gi] * p.scale_log2 : 0.f;
+        p.key_vs[row0 + t] = valid ? static_cast<const float*>(p.v_scale)[gi] : 0.f;
+      } else {
+        p.key_ks[row0 + t] = valid ? p.scale_log2 : 0.f;
+        p.key_vs[row0 + t] = 1.f;
+        dq[0][t] = load_scalar(p.k_scale, gi, sbf16);
+        dq[1][t] = load_scalar(p.v_scale, gi, sbf16);
+        dq[2][t] = load_scalar(p.k_zp, gi, sbf16);
+        dq[3][t] = load_scalar(p.v_zp, gi, sbf16);
+      }
+    }
+    __syncthreads();
+    // 64 keys x (K, V) x 16 chunks of 16 quantized values
+    for (int it = threadIdx.x; it < 2 * kKB * 16; it += blockDim.x) {
+      const bool isv = it >= kKB * 16;
+      const int w = isv ? it - kKB * 16 : it;
+      const int key = w >> 4, g = w & 15;
+      long slot = static_cast<long>(j) * kKB + key;
+      if (slot >= p.cap) slot = p.cap - 1;
+      const uint4 raw = *reinterpret_cast<const uint4*>((isv ? v_ring : k_ring) +
+                                                        (static_cast<long>(b) * p.cap + slot) * kD + g * 16);
+      const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&raw);
+      float f[16];
+      if (p.mode == kQuantI8Sym) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[e] = static_cast<float>(static_cast<int8_t>(b8[e]));
+      } else {
+        const float sc = dq[isv ? 1 : 0][key], zp = dq[isv ? 3 : 2][key];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float t = round_to(__fsub_rn(static_cast<float>(b8[e]), zp), sbf16);
+          f[e] = round_to(__fmul_rn(t, sc), sbf16);
+        }
+      }
+      uint32_t w8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w8[e] = isv ? pack_f16x2(f[2 * e], f[2 * e + 1]) : pack_bf16x2(f[2 * e], f[2 * e + 1]);
+      uint4* dst = isv ? reinterpret_cast<uint4*>(p.vd + (row0 + key) * kD + g * 16)
+                       : reinterpret_cast<uint4*>(p.kd + (row0 + key) * kD + g * 16);
+      dst[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+      dst[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+    }
+  } else {
+    const int nb0 = (j - p.n_ctx_blocks) * kKB;
+    if (threadIdx.x < kKB) {
+      const int kk = nb0 + threadIdx.x;
+      p.key_ks[row0 + threadIdx.x] = kk < p.S ? p.scale_log2 : 0.f;
+      p.key_add[row0 + threadIdx.x] = kk < p.S ? 0.f : -INFINITY;
+      p.key_vs[row0 + threadIdx.x] = 1.f;
+    }
+    // 64 keys x (K, V) x 32 chunks of 8 bf16 values
+    for (int it = threadIdx.x; it < 2 * kKB * 32; it += blockDim.x) {
+      const bool isv = it >= kKB * 32;
+      const int w = isv ? it - kKB * 32 : it;
+      const int key = w >> 5, c = w & 31;
+      const int kk = nb0 + key;
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (kk < p.S) raw = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) +
+                                                           (static_cast<long>(b) * p.S + kk) * kD + c * 8);
+      if (isv) {
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          w4[e] = pack_f16x2(f.x, f.y);
+        }
+        *reinterpret_cast<uint4*>(p.vd + (row0 + key) * kD + c * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      } else {
+        *reinterpret_cast<uint4*>(p.kd + (row0 + key) * kD + c * 8) = raw;
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Attention over the dense keys: the structure of attention_kernel with the
+// conversion gone and two key blocks in flight.  Producer: Q once, then per
+// block K (bf16) and V (f16) tiles by TMA plus the block's 3 x 64 per-key
+// floats by bulk copy into stage jl % 2.  MMA issuer: S_jl = Q K_jl^T into
+// TMEM buffer jl % 2, then P_{jl-1} V_{jl-1} into O, so the scores of the next
+// block are computed while the workers run the softmax of this one.
+constexpr int kDOffQ = 0;
+constexpr int kDOffK = 65536;        // 2 stages x 4 x [64 x 64] bf16
+constexpr int kDOffV = 131072;       // 2 stages x 4 x [64 x 64] f16 (MN-major blocks)
+constexpr int kDOffP = 196608;       // [128 x 64] f16
+constexpr int kDOffScale = 212992;   // 2 stages x (ks, vs, kadd) x 64 floats
+constexpr int kDOffBar = 214528;
+constexpr int kDSmemBytes = kDOffBar + 128 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_dense_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  const int blk_begin = sp * p.n_blocks / p.splits;
+  const int nbl = (sp + 1) * p.n_blocks / p.splits - blk_begin;
+  uint8_t* sQ = smem + kDOffQ;
+  uint8_t* sP = smem + kDOffP;
+  float* sScale = reinterpret_cast<float*>(smem + kDOffScale);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_ready = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  if (threadIdx.x == 0) trace(p, kTrStart);
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_ready, 4);
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmO = tmem, tmS = tmem + 256;  // S buffers at columns 256 and 320
+  pdl_launch_dependents();
+  const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
+  int issued = 0;
+
+  if (warp == 0) {
+    pdl_wait();
+    if (lane == 0 && nbl > 0) {
+      mbar_arrive_expect_tx(q_full, 4 * 16384);
+      for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
+      for (int jl = 0; jl < nbl; ++jl) {
+        const int st = jl & 1;
+        if (jl >= 2 && !mbar_wait(&kv_empty[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
+        const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + jl) * kKB;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * 32768 + 3 * 256);
+        for (int a = 0; a < 4; ++a) {
+          tma_load_2d(smem + kDOffK + st * 32768 + a * 8192, &tmK, &kv_full[st], a * 64, static_cast<int>(key0));
+          tma_load_2d(smem + kDOffV + st * 32768 + a * 8192, &tmV, &kv_full[st], a * 64, static_cast<int>(key0));
+        }
+        float* sc = sScale + st * 192;
+        bulk_load(sc, p.key_ks + key0, 256, &kv_full[st]);
+        bulk_load(sc + 64, p.key_vs + key0, 256, &kv_full[st]);
+        bulk_load(sc + 128, p.key_add + key0, 256, &kv_full[st]);
+        ++issued;
+      }
+      trace(p, kTrIssued);
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0 && nbl > 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
+      constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
+      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutTmaFull);
+      auto pv = [&](int jp) {  // O += P_jp V_jp
+        if (!(ok = mbar_wait(p_ready, jp & 1, p.status, kDevTimeoutConvert))) return;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(smem + kDOffV + (jp & 1) * 32768);
+#pragma unroll
+        for (int ks = 0; ks < kKB / 16; ++ks) {
+          const uint64_t ad = make_sdesc_sw128(smem_u32(sP) + ks * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(v_base + ks * 2048, 8192, 1024);
+          umma_f16_ss(tmO, ad, bd, idesc_o, (jp > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[jp & 1]);
+        umma_commit(o_done);
+      };
+      for (int jl = 0; jl < nbl && ok; ++jl) {
+        const int st = jl & 1;
+        if (!(ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
+        if (jl >= 2 && !(ok = mbar_wait(&s_free[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutConvert))) break;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + kDOffK + st * 32768);
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const int a = ks >> 2, kk = ks & 3;
+          const uint64_t ad = make_sdesc_sw128(smem_u32(sQ + a * 16384) + kk * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(k_base + a * 8192 + kk * 32, 16, 1024);
+          umma_f16_ss(tmS + st * kKB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        if (jl >= 1) pv(jl - 1);
+      }
+      if (ok) pv(nbl - 1);
+    }
+  } else {
+    pdl_wait();
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row inside the tile == TMEM lane
+    const int R = qt * kQR + r;
+    const bool row_valid = R < p.Hq * p.S;
+    const int s_row = row_valid ? R % p.S : 0;
+    const int h_row = row_valid ? R / p.S : 0;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int jl = 0; jl < nbl && ok; ++jl) {
+      const int st = jl & 1;
+      if (!(ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
+      if (!(ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone))) break;
+      tc_fence_after();
+      float z[kKB];
+      {
+        uint32_t rr[kKB / 16][16];
+#pragma unroll
+        for (int c = 0; c < kKB / 16; ++c) tmem_ld16(tmS + st * kKB + lane_base + c * 16, rr[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < kKB / 16; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[c][e]);
+      }
+      // the scores are in registers: the MMA may overwrite this S buffer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[st]);
+      const float* ks_s = sScale + st * 192;
+      const float* vs_s = ks_s + 64;
+      const float* kadd_s = ks_s + 128;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kKB / 4; ++c) {
+        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+        z[4 * c + 0] = fmaf(z[4 * c + 0], km.x, ka.x);
+        z[4 * c + 1] = fmaf(z[4 * c + 1], km.y, ka.y);
+        z[4 * c + 2] = fmaf(z[4 * c + 2], km.z, ka.z);
+        z[4 * c + 3] = fmaf(z[4 * c + 3], km.w, ka.w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
+      }
+      const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float m_new = fmaxf(m_run, bmax);
+      bool need = false;
+      float m_use;
+      if (m_run == -INFINITY) {
+        m_use = m_new;
+      } else if (m_new > m_run + 8.f) {
+        need = true;
+        m_use = m_new;
+      } else {
+        m_use = m_run;
+      }
+      const float alpha = need ? exp2f(m_run - m_use) : 1.f;
+      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      float pv[kKB];
+#pragma unroll
+      for (int c = 0; c < kKB / 4; ++c) {
+        const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
+        const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pe = ex2_approx(z[4 * c + e] - m_sub);
+          ps[e] += pe;
+          pv[4 * c + e] = pe * vv[e];
+        }
+      }
+      l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      m_run = m_use;
+      // P_{jl-1} V_{jl-1} has finished: the P tile is free and O is final
+      // for the rescale
+      if (jl > 0 && !(ok = mbar_wait(o_done, (jl - 1) & 1, p.status, kDevTimeoutMmaDone))) break;
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kD / 16; c0 += 2) {
+          uint32_t rr[2][16];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[q][e] = __float_as_uint(__uint_as_float(rr[q][e]) * alpha);
+            tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+          }
+        }
+        tmem_wait_st();
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = make_uint4(pack_f16x2(pv[8 * c + 0], pv[8 * c + 1]), pack_f16x2(pv[8 * c + 2], pv[8 * c + 3]),
+                                   pack_f16x2(pv[8 * c + 4], pv[8 * c + 5]), pack_f16x2(pv[8 * c + 6], pv[8 * c + 7]));
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, c)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    // ---- epilogue (the layout of attention_kernel's) ----
+    if (ok && nbl > 0) ok = mbar_wait(o_done, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone);
+    tc_fence_after();
+    if (ok && nbl > 0) {
+      const bool final_out = p.splits == 1;
+      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+      const long tok = static_cast<long>(b) * p.S + s_row;
+      __nv_bfloat16* orow = p.out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
+      const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.splits + sp;
+      float* wrow_o = p.ws_o ? p.ws_o + (wcta * (kD / 16) * kQR + r) * 16 : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+        uint32_t rr[4][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+        tmem_wait_ld();
+        if (!row_valid) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = c0 + q;
+          if (final_out) {
+            uint32_t w8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              w8[e] = pack_bf16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+            *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              *reinterpret_cast<float4*>(wrow_o + static_cast<long>(c) * kQR * 16 + 4 * e) =
+                  make_float4(__uint_as_float(rr[q][4 * e]), __uint_as_float(rr[q][4 * e + 1]),
+                              __uint_as_float(rr[q][4 * e + 2]), __uint_as_float(rr[q][4 * e + 3]));
+          }
+        }
+      }
+      if (!final_out && row_valid) p.ws_ml[wcta * kQR + r] = make_float2(m_run, l_run);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // drain a producer that stopped early: every issued stage completes
+  if (warp == 0 && lane == 0)
+    for (int jl = (issued > 2 ? issued - 2 : 0); jl < issued; ++jl)
+      mbar_wait(&kv_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0) trace(p, kTrEnd);
+}
+
 // Merges the kv_splits partial results of every query row.
 __global__ void __launch_bounds__(128) attention_combine_kernel(const AttnParams p) {
   pdl_wait();
@@ -570,6 +959,10 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
     return set_error(RFX_E_INVAL, "rfx_attention: need head_dim=256, S>=1, 0<=n_ctx<=capacity");
   if (d.quant_mode != RFX_QUANT_I8_SYM && d.quant_mode != RFX_QUANT_U8_REF)
     return set_error(RFX_E_INVAL, "rfx_attention: quant_mode");
+  if (d.kv_source != RFX_KV_RING_TILES && d.kv_source != RFX_KV_DENSE)
+    return set_error(RFX_E_INVAL, "rfx_attention: kv_source");
+  if (d.kv_source == RFX_KV_DENSE && d.new_block)
+    return set_error(RFX_E_UNSUPPORTED, "rfx_attention: RFX_KV_DENSE serves a bidirectional new-key block (new_block NULL)");
   g->q_tiles = (d.num_q_heads * d.S + kQR - 1) / kQR;
   g->n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
   g->n_blocks = g->n_ctx_blocks + (d.S + kKB - 1) / kKB;
@@ -588,11 +981,42 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
 
 }  // namespace
 
+namespace {
+// Workspace: the split-KV partials (O, then (m, l)), then in dense mode the
+// dense keys at 1024-byte aligned offsets: bf16 K, f16 V [B][Lk][D] and the
+// per-key ks, vs, kadd [B][Lk] fp32.
+struct WsLayout {
+  size_t partials, kd, vd, ks, vs, kadd, total;
+};
+WsLayout ws_layout(const rfx_attn_desc& d, const Geometry& g) {
+  WsLayout w{};
+  const size_t rows = static_cast<size_t>(d.B) * g.q_tiles * g.splits * kQR;
+  w.partials = g.splits > 1 ? rows * kD * sizeof(float) + rows * sizeof(float2) : 0;
+  size_t off = (w.partials + 1023) & ~size_t(1023);
+  if (d.kv_source == RFX_KV_DENSE) {
+    const size_t keys = static_cast<size_t>(d.B) * g.n_blocks * kKB;
+    auto take = [&](size_t bytes) {
+      const size_t o = off;
+      off = (off + bytes + 1023) & ~size_t(1023);
+      return o;
+    };
+    w.kd = take(keys * kD * 2);
+    w.vd = take(keys * kD * 2);
+    w.ks = take(keys * 4);
+    w.vs = take(keys * 4);
+    w.kadd = take(keys * 4);
+    w.total = off;
+  } else {
+    w.total = w.partials;
+  }
+  return w;
+}
+}  // namespace
+
 size_t attention_workspace_bytes(const rfx_attn_desc& d) {
   Geometry g;
-  if (geometry(d, &g) != RFX_OK || g.splits == 1) return 0;
-  const size_t rows = static_cast<size_t>(d.B) * g.q_tiles * g.splits * kQR;
-  return rows * kD * sizeof(float) + rows * sizeof(float2);
+  if (geometry(d, &g) != RFX_OK) return 0;
+  return ws_layout(d, g).total;
 }
 
 int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV) {
@@ -603,10 +1027,22 @@ int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* 
   const uint64_t qrows = static_cast<uint64_t>(d.B) * d.num_q_heads * d.S;
   rc = make_tmap_2d(tmQ, d.q, 2, kD, qrows, kD * 2, 64, kQR, true);
   if (rc) return rc;
+  if (d.n_ctx > 0 && (!d.k_ring || !d.v_ring || !d.k_scale || !d.v_scale ||
+                     (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp || !d.v_zp))))
+    return set_error(RFX_E_INVAL, "rfx_attention: null ring/scale pointers");
+  if (d.kv_source == RFX_KV_DENSE) {
+    // the dense keys live in the workspace: its size and alignment are checked here
+    const WsLayout w = ws_layout(d, g);
+    if (!d.workspace || d.workspace_bytes < w.total || (reinterpret_cast<uintptr_t>(d.workspace) & 1023u))
+      return set_error(RFX_E_INVAL, "rfx_attention: RFX_KV_DENSE needs a 1024-byte aligned workspace of %zu bytes",
+                       w.total);
+    const uint64_t keys = static_cast<uint64_t>(d.B) * g.n_blocks * kKB;
+    char* ws = static_cast<char*>(d.workspace);
+    rc = make_tmap_2d(tmK, ws + w.kd, 2, kD, keys, kD * 2, 64, kKB, true);
+    if (rc) return rc;
+    return make_tmap_2d(tmV, ws + w.vd, 2, kD, keys, kD * 2, 64, kKB, true);
+  }
   if (d.n_ctx > 0) {
-    if (!d.k_ring || !d.v_ring || !d.k_scale || !d.v_scale ||
-        (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp || !d.v_zp)))
-      return set_error(RFX_E_INVAL, "rfx_attention: null ring/scale pointers");
     const uint64_t krows = static_cast<uint64_t>(d.B) * d.capacity;
     rc = make_tmap_2d(tmK, d.k_ring, 1, kD, krows, kD, kD, kKB, false);
     if (rc) return rc;
@@ -624,11 +1060,17 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
   Geometry g;
   int rc = geometry(d, &g);
   if (rc) return rc;
-  const size_t need = attention_workspace_bytes(d);
-  if (need > 0 && (!d.workspace || d.workspace_bytes < need || (reinterpret_cast<uintptr_t>(d.workspace) & 15u)))
-    return set_error(RFX_E_INVAL, "rfx_attention: workspace of %zu bytes (16-byte aligned) required", need);
-  const void* fn = reinterpret_cast<const void*>(attention_kernel);
-  rc = ensure_smem_attr(fn, kSmemBytes);
+  const WsLayout wl = ws_layout(d, g);
+  const size_t need = wl.total;
+  const bool dense = d.kv_source == RFX_KV_DENSE;
+  if (need > 0 && (!d.workspace || d.workspace_bytes < need ||
+                   (reinterpret_cast<uintptr_t>(d.workspace) & (dense ? 1023u : 15u))))
+    return set_error(RFX_E_INVAL, "rfx_attention: workspace of %zu bytes (%d-byte aligned) required", need,
+                     dense ? 1024 : 16);
+  const void* fn =
+      dense ? reinterpret_cast<const void*>(attention_dense_kernel) : reinterpret_cast<const void*>(attention_kernel);
+  const int smem_bytes = dense ? kDSmemBytes : kSmemBytes;
+  rc = ensure_smem_attr(fn, smem_bytes);
   if (rc) return rc;
 
   AttnParams p{};
@@ -653,17 +1095,33 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
   p.new_block = d.new_block;
   p.scale_log2 = d.softmax_scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(d.out);
-  if (need > 0) {
+  if (wl.partials > 0) {
     p.ws_o = static_cast<float*>(d.workspace);
     const size_t rows = static_cast<size_t>(d.B) * g.q_tiles * g.splits * kQR;
     p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(d.workspace) + rows * kD * sizeof(float));
+  }
+  if (dense) {
+    char* ws = static_cast<char*>(d.workspace);
+    p.kd = reinterpret_cast<__nv_bfloat16*>(ws + wl.kd);
+    p.vd = reinterpret_cast<__half*>(ws + wl.vd);
+    p.key_ks = reinterpret_cast<float*>(ws + wl.ks);
+    p.key_vs = reinterpret_cast<float*>(ws + wl.vs);
+    p.key_add = reinterpret_cast<float*>(ws + wl.kadd);
+    p.Lk = g.n_blocks * kKB;
   }
   p.status = device_status_ptr();
   p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(g.q_tiles) * g.splits * d.B * 16));
 
   CUtensorMap q = *tmQ, k = *tmK, v = *tmV;
+  if (dense) {
+    const uint8_t* kr = static_cast<const uint8_t*>(d.k_ring);
+    const uint8_t* vr = static_cast<const uint8_t*>(d.v_ring);
+    rc = launch_kernel(reinterpret_cast<const void*>(kv_dense_kernel), dim3(g.n_blocks, d.B), dim3(256), 0, stream, pdl,
+                       1, p, kr, vr);
+    if (rc) return rc;
+  }
   dim3 grid(g.q_tiles, g.splits, d.B);
-  rc = launch_kernel(fn, grid, dim3(kThreads), kSmemBytes, stream, pdl, 1, q, k, v, p);
+  rc = launch_kernel(fn, grid, dim3(kThreads), smem_bytes, stream, pdl, 1, q, k, v, p);
   if (rc || g.splits == 1) return rc;
   const long rows = static_cast<long>(d.B) * g.q_tiles * kQR;
   dim3 cgrid(static_cast<unsigned>((rows + 3) / 4));

@@ -144,7 +144,8 @@ def linear(**kw) -> None:
 
 # ------------------------------------------------------------- attention ---
 def attention_desc(*, q, k_new, v_new, ring: KVRing | None, n_ctx: int, out, softmax_scale: float,
-                   workspace=None, ctx_valid=None, new_block=None, kv_splits=0) -> L.AttnDesc:
+                   workspace=None, ctx_valid=None, new_block=None, kv_splits=0,
+                   kv_source: int = L.RFX_KV_RING_TILES) -> L.AttnDesc:
     _need_cuda(q, k_new, v_new, out)
     B, Hq, S, D = q.shape
     d = L.AttnDesc()
@@ -166,6 +167,7 @@ def attention_desc(*, q, k_new, v_new, ring: KVRing | None, n_ctx: int, out, sof
     d.workspace = L.ptr(workspace)
     d.workspace_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     d.kv_splits = kv_splits
+    d.kv_source = kv_source
     return d
 
 
@@ -180,10 +182,15 @@ def attention(**kw) -> None:
     d = attention_desc(**kw)
     need = attention_workspace_bytes(d)
     ws = kw.get("workspace")
-    if need and (ws is None or ws.numel() * ws.element_size() < need):
-        ws = torch.empty(need, dtype=torch.uint8, device=kw["q"].device)
-        d.workspace, d.workspace_bytes = ws.data_ptr(), need
+    if need and (ws is None or ws.numel() * ws.element_size() < need or ws.data_ptr() % 1024):
+        ws = torch.empty(need + 1024, dtype=torch.uint8, device=kw["q"].device)
+        d.workspace, d.workspace_bytes = aligned_ptr(ws, 1024), need
     L.call("rfx_attention", ctypes.byref(d), _stream())
+
+
+def aligned_ptr(buf: torch.Tensor, align: int) -> int:
+    """First `align`-byte aligned address inside `buf` (allocate `align` spare bytes)."""
+    return (buf.data_ptr() + align - 1) // align * align
 
 
 # ----------------------------------------------------- conditioning heads ---

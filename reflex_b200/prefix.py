@@ -100,9 +100,11 @@ class PrefixEngine:
             out.append(("linear", K.linear_desc(
                 w=self.w_qkv[l], x=self.xn, T=T, S=S, epilogue=L.RFX_EPI_QKV_ROPE, rope_table=self.rope,
                 positions=self.positions, q_out=self.q, k_out=self.k_new, v_out=self.v_new, num_q_heads=H), None))
+            # every one of the frame's query tiles visits every key block:
+            # dequantize the context once per layer (RFX_KV_DENSE)
             ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l], n_ctx=self.n_ctx,
                                   out=self.attn_out, softmax_scale=D ** -0.5, ctx_valid=self.valid[slot],
-                                  kv_splits=self.kv_splits)
+                                  kv_splits=self.kv_splits, kv_source=L.RFX_KV_DENSE)
             attn_descs.append(ad)
             out.append(("attn", ad, None))
             out.append(("linear", K.linear_desc(w=self.w_o[l], x=self.attn_out, T=T, S=S,
@@ -116,11 +118,11 @@ class PrefixEngine:
             out.append(("quant", K.kv_quant_desc(kv, self.v_new.view(B, 1, S, D), self.rings[l], base, 0,
                                                  self.frame_len), None))
         need = max(K.attention_workspace_bytes(d) for d in attn_descs)
-        if need and (self.workspace is None or self.workspace.numel() < need):
-            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        if need and (self.workspace is None or self.workspace.numel() < need + 1024):
+            self.workspace = torch.empty(need + 1024, dtype=torch.uint8, device=self.dev)
         for d in attn_descs:
             if need:
-                d.workspace, d.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+                d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace, 1024), need
         return out
 
     def run(self, emb: torch.Tensor | None = None) -> None:

@@ -256,6 +256,53 @@ def test_attention_partitioned(K, L, mode, n_ctx, S, splits):
     assert K.device_status() == 0
 
 
+@pytest.mark.parametrize("mode", ["i8", "u8"])
+@pytest.mark.parametrize("n_ctx,S,splits", [(1584, 200, 0), (300, 100, 1), (0, 64, 0), (818, 50, 3)])
+def test_attention_dense_source_matches_ring_tiles_and_oracle(K, L, mode, n_ctx, S, splits):
+    """RFX_KV_DENSE (one dequantize pass, then TMA-fed bf16/f16 tiles with two key
+    blocks in flight) against the in-kernel conversion path on the same inputs,
+    and both against fp32 attention over the dequantized context (2e-2), with a
+    masked context range (an evicted frame) and a bidirectional new-key block."""
+    r = gen(9)
+    B, Hq, D, cap = 1, 8, 256, max(64, n_ctx + 64)
+    qm = L.RFX_QUANT_I8_SYM if mode == "i8" else L.RFX_QUANT_U8_REF
+    ring = K.KVRing.allocate(B, 1, cap, D, qm, scale_dtype=torch.float32 if mode == "i8" else torch.bfloat16)
+    kc, vc = r(B, 1, n_ctx, D).bfloat16(), r(B, 1, n_ctx, D).bfloat16()
+    if n_ctx:
+        K.kv_quant_append(kc.cuda(), vc.cuda(), ring, 0, 0, cap)
+    valid = torch.ones(B, cap, dtype=torch.uint8)
+    valid[:, n_ctx // 3: 2 * n_ctx // 3] = 0
+    q = r(B, Hq, S, D).bfloat16()
+    kn, vn = r(B, S, D).bfloat16(), r(B, S, D).bfloat16()
+    outs = []
+    for src in (L.RFX_KV_RING_TILES, L.RFX_KV_DENSE):
+        out = torch.empty(B * S, Hq * D, dtype=torch.bfloat16, device="cuda")
+        K.attention(q=q.cuda(), k_new=kn.cuda(), v_new=vn.cuda(), ring=ring, n_ctx=n_ctx, out=out,
+                    softmax_scale=1 / 16, ctx_valid=valid.cuda(), kv_splits=splits, kv_source=src)
+        torch.cuda.synchronize()
+        outs.append(out.float().cpu())
+    assert K.device_status() == 0
+    d_paths = (outs[0] - outs[1]).abs().max().item()
+    if mode == "i8":
+        kd = oq.dequant_i8_sym(ring.k_q.cpu().numpy(), ring.k_scale.cpu().numpy()[..., None])
+        vd = oq.dequant_i8_sym(ring.v_q.cpu().numpy(), ring.v_scale.cpu().numpy()[..., None])
+    else:
+        kd = oq.dequant_u8_ref(ring.k_q.cpu().numpy(), ring.k_scale.float().cpu().numpy()[..., None],
+                               ring.k_zp.float().cpu().numpy()[..., None], True)
+        vd = oq.dequant_u8_ref(ring.v_q.cpu().numpy(), ring.v_scale.float().cpu().numpy()[..., None],
+                               ring.v_zp.float().cpu().numpy()[..., None], True)
+    kd = torch.from_numpy(kd)[:, :, :n_ctx]
+    vd = torch.from_numpy(vd)[:, :, :n_ctx]
+    att = torch.zeros(S, dtype=torch.int64)
+    att[0] = 1
+    ref = partitioned_attention(q, kd, vd, kn[:, None], vn[:, None], valid[:, :n_ctx].bool(), att, 1 / 16)
+    ref = ref.permute(0, 2, 1, 3).reshape(B * S, Hq * D)
+    errs = [(o - ref).abs().max().item() for o in outs]
+    print(f"dense vs ring tiles {d_paths:.2e}; vs oracle ring {errs[0]:.2e} dense {errs[1]:.2e}")
+    assert d_paths <= 2e-3
+    assert max(errs) <= 2e-2
+
+
 # ------------------------------------------------------ conditioning heads ---
 def test_time_cond_matches_fp64_embedding_and_mlp(K):
     from oracle.model import sinusoid
