@@ -70,6 +70,7 @@ enum {
 
 struct LinParams {
   int T, O, K, S;
+  int n_tiles;
   int k_chunks;
   int splits;
   int stages;
@@ -103,7 +104,7 @@ struct LinParams {
 };
 
 __device__ __forceinline__ void trace(const LinParams& p, int ev) {
-  if (p.trace) p.trace[(static_cast<long>(blockIdx.y) * gridDim.x + blockIdx.x) * 16 + ev] = globaltimer_ns();
+  if (p.trace) p.trace[static_cast<long>(blockIdx.x) * 16 + ev] = globaltimer_ns();
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -248,8 +249,10 @@ __device__ __forceinline__ void cluster_arrive_release_na() {
 }
 __device__ __forceinline__ void cluster_wait_na() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
+// 128-token tiles run two CTAs per SM: one CTA's epilogue overlaps the
+// other's weight / activation stream.
 template <int NT, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, NT == 128 ? 2 : 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const LinParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -257,8 +260,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = p.splits > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int m_tile = blockIdx.x / p.splits;
-  const int n0 = blockIdx.y * NT;
+  // one-dimensional grid: the splits of a tile are consecutive (one cluster),
+  // and the token tiles of a weight tile follow each other, so a weight tile
+  // is fetched from HBM once and re-read from L2 by its other token tiles
+  const int m_tile = blockIdx.x / (p.splits * p.n_tiles);
+  const int n0 = (blockIdx.x / p.splits) % p.n_tiles * NT;
   const int c_begin = split * p.k_chunks / p.splits;
   const int nch = (split + 1) * p.k_chunks / p.splits - c_begin;
   const int S = p.stages;
@@ -625,8 +631,11 @@ int small_bytes(int nt, bool norm, int x_slots) {
 
 int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
   int nt = d.n_tile;
-  if (nt == 0) nt = d.T <= 64 ? 64 : (d.T <= 128 ? 128 : 256);
+  if (nt == 0) nt = d.T <= 64 ? 64 : 128;
   if (nt != 64 && nt != 128 && nt != 256) return set_error(RFX_E_INVAL, "rfx_linear: n_tile must be 64, 128 or 256");
+  // 128-token tiles: two CTAs per SM (each within half of the SM's shared memory)
+  const int per_sm = nt == 128 ? 2 : 1;
+  const int smem_limit = nt == 128 ? 113 * 1024 : kSmemLimit;
   const bool norm = d.prologue == RFX_PRO_NORM;
   const int m_tiles = d.O / kBM;
   const int n_tiles = (d.T + nt - 1) / nt;
@@ -638,14 +647,14 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
     // kernels overlapping under programmatic dependent launch rarely leave
     for (int s : {2, 4, 8}) {
       if (s > chunks) break;
-      if (m_tiles * n_tiles * s <= num_sms) splits = s;
+      if (m_tiles * n_tiles * s <= num_sms * per_sm) splits = s;
     }
   }
   if (splits != 1 && splits != 2 && splits != 4 && splits != 8)
     return set_error(RFX_E_INVAL, "rfx_linear: splits must be 1, 2, 4 or 8");
   if (splits > chunks) return set_error(RFX_E_INVAL, "rfx_linear: splits exceeds K/64");
   const int xt = nt * 128;
-  auto budget_for = [&](int xs) { return kSmemLimit - 1024 - small_bytes(nt, norm, xs); };
+  auto budget_for = [&](int xs) { return smem_limit - 1024 - small_bytes(nt, norm, xs); };
   if (norm && d.splits == 0) {
     // the normalized K-slice of a CTA stays resident: split K further (or
     // shrink the token tile) until it fits next to one weight stage
@@ -689,7 +698,7 @@ int pick_config(const rfx_linear_desc& d, int num_sms, Config* cfg) {
     if (!push) body = std::max(body, nt * kRedLd * 4);
     body = (body + 127) & ~127;
     const int smem = body + recv_bytes + stage_bytes + small_bytes(nt, norm, x_slots) + 1024;
-    if (smem > kSmemLimit) continue;
+    if (smem > smem_limit) continue;
     cfg->nt = nt;
     cfg->splits = splits;
     cfg->stages = stages;
@@ -795,7 +804,7 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   const int n_tiles = (d.T + cfg.nt - 1) / cfg.nt;
   // an automatically chosen 16-CTA cluster must be co-schedulable; else use 8
   if (d.splits == 0 && cfg.splits == 16 &&
-      !cluster_fits(fn, dim3(m_tiles * 16, n_tiles, 1), kThreads, cfg.smem, 16)) {
+      !cluster_fits(fn, dim3(m_tiles * 16 * n_tiles, 1, 1), kThreads, cfg.smem, 16)) {
     rfx_linear_desc d8 = d;
     d8.splits = 8;
     rc = pick_config(d8, nsm, &cfg);
@@ -841,7 +850,8 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   p.status = device_status_ptr();
   p.trace = static_cast<unsigned long long*>(trace_buffer(m_tiles * cfg.splits * n_tiles * 16));
 
-  dim3 grid(m_tiles * cfg.splits, n_tiles, 1);
+  p.n_tiles = n_tiles;
+  dim3 grid(m_tiles * cfg.splits * n_tiles, 1, 1);
   CUtensorMap w = *tmW, x = *tmX;
   return launch_kernel(fn, grid, dim3(kThreads), static_cast<size_t>(cfg.smem), stream, pdl, cfg.splits, w, x, p);
 }
