@@ -4,6 +4,7 @@
     python -m reflex_b200.profile --layers 18 --chunk   # one eager chunk, then one graph replay
     python -m reflex_b200.profile --layers 2 --chunk --fused   # the same through the chunk executor
     python -m reflex_b200.profile --layers 18 --chunk --fused --trace   # per-phase timeline of the executor
+    python -m reflex_b200.profile --frame --ops qkv,attn,gu,down   # frame-update ops (768 tokens, Gemma-2B layer)
 
 Builds the PI0.5 engine at the benchmark's shapes (width 1024, 8x256 heads,
 818-token int8 context, 50 action tokens) with a few layers, runs one chunk to
@@ -36,7 +37,13 @@ def main():
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
     ap.add_argument("--trace", action="store_true",
                     help="with --chunk --fused: %globaltimer stamps of every task of the first Euler step")
+    ap.add_argument("--frame", action="store_true",
+                    help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
+                         "pinned prefix and a 2-frame window)")
     args = ap.parse_args()
+    if args.frame:
+        frame_ops(args.ops, args.reps)
+        return
     cfg = pi05_config(num_layers=args.layers, adarms="ssg")
     wts = synthetic.expert_weights(cfg, seed=0, device="cuda")
     eng = ActionExpertEngine(cfg, wts, batch=args.streams, capacity=1024, n_ctx=args.n_ctx,
@@ -74,6 +81,36 @@ def main():
         kind, desc = by_tag[names[op]]
         for _ in range(args.reps):
             K.Plan.run_direct(desc, kind if kind in ("in", "tail") else None)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print("ok", K.device_status())
+
+
+def frame_ops(ops: str, reps: int) -> None:
+    """Launches the requested ops (norm, qkv, attn, o, norm2, gu, down, quant) of
+    layer 0 of a one-layer frame update `reps` times each, between
+    cudaProfilerStart/Stop, after one warm-up run of every op."""
+    from . import _lib as L
+    from .config import vlm_config
+    from .prefix import PrefixEngine
+
+    cfg = vlm_config(num_layers=1)
+    pinned, flen = 48, 768
+    wts = synthetic.prefix_weights(cfg, seed=10)
+    rings = [K.KVRing.allocate(1, 1, 2048, 256, L.RFX_QUANT_I8_SYM, scale_dtype=torch.float32)]
+    eng = PrefixEngine(cfg, wts, rings, pinned=pinned, frame_len=flen, window_frames=2, batch=1)
+    ks, vs = synthetic.context_kv(cfg, pinned + 2 * flen, B=1, seed=12)
+    eng.load_context(0, ks[0], vs[0])
+    eng.set_frame(synthetic.frame_embeddings(cfg, flen, B=1, seed=13).cuda())
+    names = ["norm", "qkv", "attn", "o", "norm2", "gu", "down", "quant"]
+    layer = [d for kind, d, _ in eng.ops(0) if kind != "barrier"]
+    for d in layer:
+        K.Plan.run_direct(d)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for op in ops.split(","):
+        for _ in range(reps):
+            K.Plan.run_direct(layer[names.index(op)])
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     print("ok", K.device_status())
