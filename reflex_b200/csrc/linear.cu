@@ -620,6 +620,189 @@ __global__ void __launch_bounds__(kThreads, NT == 128 ? 2 : 1)
   if (threadIdx.x == 0) trace(p, kTrEnd);
 }
 
+// ----------------------------------------------------- persistent tiles ---
+// Many tokens (T > 128, load prologue): one CTA per SM walks tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... in weight-tile-major order (a
+// weight tile's token tiles are adjacent, so they run at the same time and
+// the tile comes from HBM once).  The producer streams W / X k-steps through a
+// 4-stage ring without stopping at tile boundaries; the MMA issuer fills two
+// TMEM accumulators alternately; warps 2-5 drain the other one (TMEM ->
+// shared-memory transpose -> the fused epilogue), so a tile's epilogue runs
+// under the next tile's mainloop.
+constexpr int kPStages = 4;
+constexpr int kPStage = 2 * kWTileBytes;  // W [128 x 64] + X [128 x 64] bf16
+constexpr int kPOffRed = kPStages * kPStage;                   // [128 tokens][kRedLd] fp32
+constexpr int kPOffSmall = kPOffRed + 128 * kRedLd * 4;
+constexpr int kPSmemBytes = kPOffSmall + 128 + 1024;
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_tiles_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                        const LinParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* red = reinterpret_cast<float*>(smem + kPOffRed);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPOffSmall);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;  // [2]
+  uint64_t* acc_free = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
+  const int n_tiles_total = (p.O / kBM) * p.n_tiles;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_free[i], 4);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) trace(p, kTrSetup);
+  int issued = 0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      bool ok = true;
+      bool waited = false;
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+        const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * 128;
+        for (int kc = 0; kc < p.k_chunks; ++kc) {
+          const int s = issued % kPStages;
+          if (issued >= kPStages &&
+              !(ok = mbar_wait(&empty[s], ((issued / kPStages) - 1) & 1, p.status, kDevTimeoutStageEmpty)))
+            break;
+          uint8_t* st = smem + s * kPStage;
+          mbar_arrive_expect_tx(&full[s], kPStage);
+          tma_load_2d_hint(st, &tmW, &full[s], kc * kBK, m * kBM, pol);
+          if (!waited) {  // the activations come from the previous kernel
+            pdl_wait();
+            waited = true;
+          }
+          tma_load_2d(st + kWTileBytes, &tmX, &full[s], kc * kBK, n0);
+          ++issued;
+        }
+      }
+      if (!waited) pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(kBM, 128, true);
+      const uint64_t a0 = make_sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b0 = make_sdesc_sw128(smem_u32(smem + kWTileBytes), 16, 1024);
+      bool ok = true;
+      int it = 0, tl = 0;
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++tl) {
+        const int buf = tl & 1;
+        if (tl >= 2 && !(ok = mbar_wait(&acc_free[buf], ((tl >> 1) - 1) & 1, p.status, kDevTimeoutMmaDone))) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * 128;
+        for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
+          const int s = it % kPStages;
+          if (!(ok = mbar_wait(&full[s], (it / kPStages) & 1, p.status, kDevTimeoutTmaFull))) break;
+          tc_fence_after();
+          const uint64_t off = static_cast<uint64_t>((s * kPStage) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_ss(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    pdl_wait();
+    const int et = threadIdx.x - 64;  // 0..127
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++tl) {
+      const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * 128;
+      const int buf = tl & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&acc_full[buf], (tl >> 1) & 1, p.status, kDevTimeoutMmaDone);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      // every epilogue warp agrees before anyone leaves the loop
+      uint32_t all;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(all)
+          : "r"(ok ? 1u : 0u)
+          : "memory");
+      if (!all) break;
+      tc_fence_after();
+      // accumulator row `row` (128 token columns) -> red[t][row]
+#pragma unroll 1
+      for (int c0 = 0; c0 < 8; c0 += 4) {
+        uint32_t r[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_ld16(tmem + buf * 128 + (static_cast<uint32_t>(quad * 32) << 16) + (c0 + c) * 16, r[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) red[((c0 + c) * 16 + e) * kRedLd + row] = __uint_as_float(r[c][e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[buf]);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // items: 16 groups of 4 row pairs x 128 tokens; 16 consecutive threads
+      // cover one token's 64 pairs (coalesced stores); operands of 4 items in flight
+#pragma unroll 1
+      for (int it0 = et; it0 < 16 * 128; it0 += 4 * 128) {
+        EpiIn in[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int it = it0 + u * 128;
+          const int t = n0 + (it >> 4);
+          if (t < p.T) epilogue_fetch<EPI>(p, m, (it & 15) * 4, t, in[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int it = it0 + u * 128;
+          const int tt = it >> 4, i = (it & 15) * 4;
+          if (n0 + tt >= p.T) continue;
+          const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + i);
+          const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + i + 64);
+          const float v0[4] = {a.x, a.y, a.z, a.w};
+          const float v1[4] = {c.x, c.y, c.z, c.w};
+          epilogue_store<EPI>(p, m, i, n0 + tt, v0, v1, in[u]);
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // red is free for the next tile
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // drain: a producer that stopped early waits (bounded) for its TMA writes
+  if (warp == 0 && lane == 0)
+    for (int i = (issued > kPStages ? issued - kPStages : 0); i < issued; ++i)
+      mbar_wait(&full[i % kPStages], (i / kPStages) & 1, p.status, kDevTimeoutTmaFull);
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (threadIdx.x == 0) trace(p, kTrEnd);
+}
+
 struct Config {
   int nt, splits, stages, x_slots, small_off, smem, push, recv_off, stage_off;
 };
@@ -774,6 +957,77 @@ int validate(const rfx_linear_desc& d) {
 
 }  // namespace
 
+namespace {
+// Many tokens with the load prologue and automatic tiling go to the
+// persistent tile kernel.
+bool persistent_tiles(const rfx_linear_desc& d, const Config& cfg) {
+  return d.prologue == RFX_PRO_LOAD && d.splits == 0 && d.n_tile == 0 && cfg.nt == 128 && d.T > 128;
+}
+
+template <int EPI>
+const void* tiles_ptr() {
+  return reinterpret_cast<const void*>(linear_tiles_kernel<EPI>);
+}
+const void* select_tiles(int epi) {
+  switch (epi) {
+    case kEpiStore: return tiles_ptr<kEpiStore>();
+    case kEpiSilu: return tiles_ptr<kEpiSilu>();
+    case kEpiQkvRope: return tiles_ptr<kEpiQkvRope>();
+    case kEpiResidual: return tiles_ptr<kEpiResidual>();
+    case kEpiGeglu: return tiles_ptr<kEpiGeglu>();
+  }
+  return nullptr;
+}
+
+LinParams lin_params(const rfx_linear_desc& d) {
+  LinParams p{};
+  p.T = d.T;
+  p.O = d.O;
+  p.K = d.K;
+  p.S = d.tokens_per_batch;
+  p.k_chunks = d.K / kBK;
+  p.x = static_cast<const __nv_bfloat16*>(d.x);
+  p.ldx = d.ldx;
+  p.a1 = d.norm_a1;
+  p.a2 = d.norm_a2;
+  p.b2 = d.norm_b2;
+  p.ab_stride = d.norm_ab_stride;
+  p.eps = d.eps;
+  p.y = static_cast<__nv_bfloat16*>(d.y);
+  p.ldy = d.ldy;
+  p.bias = d.bias;
+  p.gate = d.gate;
+  p.gate_stride = d.gate_stride;
+  p.rope = d.rope_table;
+  p.rope_max_pos = d.rope_max_pos;
+  p.pos = d.positions;
+  p.q_out = static_cast<__nv_bfloat16*>(d.q_out);
+  p.k_out = static_cast<__nv_bfloat16*>(d.k_out);
+  p.v_out = static_cast<__nv_bfloat16*>(d.v_out);
+  p.hq = d.num_q_heads;
+  p.y_rps = d.y_rows_per_batch > 0 ? d.y_rows_per_batch : d.tokens_per_batch;
+  p.y_off = d.y_rows_per_batch > 0 ? d.y_row_offset : 0;
+  p.status = device_status_ptr();
+  return p;
+}
+
+int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, const Config& cfg,
+                        int nsm, cudaStream_t stream, bool pdl) {
+  const void* fn = select_tiles(d.epilogue);
+  if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no tile kernel for this epilogue");
+  int rc = ensure_smem_attr(fn, kPSmemBytes);
+  if (rc) return rc;
+  LinParams p = lin_params(d);
+  p.splits = 1;
+  p.n_tiles = (d.T + cfg.nt - 1) / cfg.nt;
+  const int tiles = (d.O / kBM) * p.n_tiles;
+  const int grid = std::min(tiles, nsm);
+  p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(grid) * 16));
+  CUtensorMap w = *tmW, x = *tmX;
+  return launch_kernel(fn, dim3(grid), dim3(kThreads), static_cast<size_t>(kPSmemBytes), stream, pdl, 1, w, x, p);
+}
+}  // namespace
+
 int build_linear_maps(const rfx_linear_desc& d, CUtensorMap* tmW, CUtensorMap* tmX) {
   int rc = validate(d);
   if (rc) return rc;
@@ -796,6 +1050,7 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   Config cfg;
   rc = pick_config(d, nsm, &cfg);
   if (rc) return rc;
+  if (persistent_tiles(d, cfg)) return launch_linear_tiles(d, tmW, tmX, cfg, nsm, stream, pdl);
   const void* fn = select_kernel(cfg.nt, d.prologue, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no kernel for this configuration");
   rc = ensure_smem_attr(fn, cfg.smem, cfg.splits > 8);

@@ -92,6 +92,63 @@ def test_linear_store(K, T, n_tile, splits):
     torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv"])
+@pytest.mark.parametrize("B,S", [(1, 300), (2, 384), (1, 768)])
+def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
+    """T > 128 tokens with the load prologue run the persistent tile kernel (two
+    TMEM accumulators, a tile's epilogue under the next tile's mainloop).  It
+    issues the same MMA sequence per 128 x 128 tile as the per-tile kernel with
+    n_tile=128 and no split-K, so the outputs are bit-identical to it for every
+    epilogue, with ragged last token tiles and several batches; the store
+    epilogue is also checked against the fp32 product."""
+    r = gen(6)
+    T, Kd, Hq, D = B * S, 1024, 8, 256
+    x = r(T, Kd).bfloat16().cuda()
+
+    def run(tiling):
+        kw = dict(w=w, x=x, T=T, S=S, n_tile=tiling[0], splits=tiling[1])
+        if epi == "store":
+            y = torch.empty(T, 640, dtype=torch.bfloat16, device="cuda")
+            K.linear(y=y, bias=bias, **kw)
+            return [y]
+        if epi == "residual":
+            y = y0.clone()
+            K.linear(epilogue=L.RFX_EPI_RESIDUAL, y=y, gate=gate, gate_stride=1024, **kw)
+            return [y]
+        if epi == "geglu":
+            y = torch.empty(T, 1024, dtype=torch.bfloat16, device="cuda")
+            K.linear(epilogue=L.RFX_EPI_GEGLU, y=y, **kw)
+            return [y]
+        q = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device="cuda")
+        k = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        v = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        K.linear(epilogue=L.RFX_EPI_QKV_ROPE, rope_table=tab, positions=pos, q_out=q, k_out=k, v_out=v,
+                 num_q_heads=Hq, **kw)
+        return [q, k, v]
+
+    if epi == "store":
+        w = r(640, Kd, std=0.03).bfloat16().cuda()
+        bias = r(640, std=0.1).cuda()
+    elif epi == "residual":
+        w = r(1024, Kd, std=0.03).bfloat16().cuda()
+        gate = torch.from_numpy(bf16_round(r(B, 1024).numpy())).cuda()
+        y0 = r(T, 1024).bfloat16().cuda()
+    elif epi == "geglu":
+        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(2048, Kd, std=0.03).bfloat16().cuda())
+    else:
+        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r((Hq + 2) * D, Kd, std=0.03).bfloat16().cuda())
+        tab = rope_table().cuda()
+        pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
+    got = run((0, 0))       # persistent tile kernel
+    ref = run((128, 1))     # per-tile kernel, same tiling
+    torch.cuda.synchronize()
+    assert K.device_status() == 0
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b), f"max diff {(a.float() - b.float()).abs().max().item()}"
+    if epi == "store":
+        torch.testing.assert_close(got[0].float().cpu(), _mm(x, w).cpu() + bias.cpu(), atol=ATOL, rtol=RTOL)
+
+
 def _norm_ref(x, a1, a2, b2, S, eps=1e-6):
     xf = x.float().cpu()
     rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
