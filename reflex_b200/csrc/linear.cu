@@ -629,16 +629,26 @@ __global__ void __launch_bounds__(kThreads, NT == 128 ? 2 : 1)
 // TMEM accumulators alternately; warps 2-5 drain the other one (TMEM ->
 // shared-memory transpose -> the fused epilogue), so a tile's epilogue runs
 // under the next tile's mainloop.
+// Layout per token tile NT (128 or 256): a 4-stage ring of W [128 x 64] +
+// X [NT x 64] bf16, the epilogue's transpose buffer for 64 tokens at a time.
 constexpr int kPStages = 4;
-constexpr int kPStage = 2 * kWTileBytes;  // W [128 x 64] + X [128 x 64] bf16
-constexpr int kPOffRed = kPStages * kPStage;                   // [128 tokens][kRedLd] fp32
-constexpr int kPOffSmall = kPOffRed + 128 * kRedLd * 4;
-constexpr int kPSmemBytes = kPOffSmall + 128 + 1024;
+template <int NT>
+struct TilesLayout {
+  static constexpr int kStage = kWTileBytes + NT * 128;
+  static constexpr int kOffRed = kPStages * kStage;            // [64 tokens][kRedLd] fp32
+  static constexpr int kOffSmall = kOffRed + 64 * kRedLd * 4;
+  static constexpr int kSmem = kOffSmall + 128 + 1024;
+};
+static_assert(TilesLayout<256>::kSmem <= kSmemLimit, "256-token tiles fit in shared memory");
 
-template <int EPI>
+template <int NT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tiles_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                         const LinParams p) {
+  using Lay = TilesLayout<NT>;
+  constexpr int kPStage = Lay::kStage;
+  constexpr int kPOffRed = Lay::kOffRed;
+  constexpr int kPOffSmall = Lay::kOffSmall;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -663,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 2 * NT);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -680,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool waited = false;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
-        const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * 128;
+        const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
         for (int kc = 0; kc < p.k_chunks; ++kc) {
           const int s = issued % kPStages;
           if (issued >= kPStages &&
@@ -702,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     pdl_wait();
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(kBM, 128, true);
+      constexpr uint32_t idesc = make_idesc_f16(kBM, NT, true);
       const uint64_t a0 = make_sdesc_sw128(smem_u32(smem), 16, 1024);
       const uint64_t b0 = make_sdesc_sw128(smem_u32(smem + kWTileBytes), 16, 1024);
       bool ok = true;
@@ -711,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = tl & 1;
         if (tl >= 2 && !(ok = mbar_wait(&acc_free[buf], ((tl >> 1) - 1) & 1, p.status, kDevTimeoutMmaDone))) break;
         tc_fence_after();
-        const uint32_t acc = tmem + buf * 128;
+        const uint32_t acc = tmem + buf * NT;
         for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
           const int s = it % kPStages;
           if (!(ok = mbar_wait(&full[s], (it / kPStages) & 1, p.status, kDevTimeoutTmaFull))) break;
@@ -732,7 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;
     int tl = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++tl) {
-      const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * 128;
+      const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
       const int buf = tl & 1;
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&acc_full[buf], (tl >> 1) & 1, p.status, kDevTimeoutMmaDone);
@@ -746,47 +756,53 @@ __global__ void __launch_bounds__(kThreads, 1)
           : "memory");
       if (!all) break;
       tc_fence_after();
-      // accumulator row `row` (128 token columns) -> red[t][row]
+      // parts of 64 token columns: accumulator row `row` -> red[t][row], then
+      // the fused epilogue of those tokens
 #pragma unroll 1
-      for (int c0 = 0; c0 < 8; c0 += 4) {
-        uint32_t r[4][16];
+      for (int h = 0; h < NT / 64; ++h) {
+        {
+          uint32_t r[4][16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tmem_ld16(tmem + buf * 128 + (static_cast<uint32_t>(quad * 32) << 16) + (c0 + c) * 16, r[c]);
-        tmem_wait_ld();
+          for (int c = 0; c < 4; ++c)
+            tmem_ld16(tmem + buf * NT + (static_cast<uint32_t>(quad * 32) << 16) + (4 * h + c) * 16, r[c]);
+          tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) red[((c0 + c) * 16 + e) * kRedLd + row] = __uint_as_float(r[c][e]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_free[buf]);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // items: 16 groups of 4 row pairs x 128 tokens; 16 consecutive threads
-      // cover one token's 64 pairs (coalesced stores); operands of 4 items in flight
+            for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kRedLd + row] = __uint_as_float(r[c][e]);
+        }
+        if (h == NT / 64 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_free[buf]);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        // items: 16 groups of 4 row pairs x 64 tokens; 16 consecutive threads
+        // cover one token's 64 pairs (coalesced stores); operands of 4 items in flight
+        const int t0 = n0 + 64 * h;
 #pragma unroll 1
-      for (int it0 = et; it0 < 16 * 128; it0 += 4 * 128) {
-        EpiIn in[4];
+        for (int it0 = et; it0 < 16 * 64; it0 += 4 * 128) {
+          EpiIn in[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int it = it0 + u * 128;
-          const int t = n0 + (it >> 4);
-          if (t < p.T) epilogue_fetch<EPI>(p, m, (it & 15) * 4, t, in[u]);
-        }
+          for (int u = 0; u < 4; ++u) {
+            const int it = it0 + u * 128;
+            const int t = t0 + (it >> 4);
+            if (t < p.T) epilogue_fetch<EPI>(p, m, (it & 15) * 4, t, in[u]);
+          }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int it = it0 + u * 128;
-          const int tt = it >> 4, i = (it & 15) * 4;
-          if (n0 + tt >= p.T) continue;
-          const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + i);
-          const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + i + 64);
-          const float v0[4] = {a.x, a.y, a.z, a.w};
-          const float v1[4] = {c.x, c.y, c.z, c.w};
-          epilogue_store<EPI>(p, m, i, n0 + tt, v0, v1, in[u]);
+          for (int u = 0; u < 4; ++u) {
+            const int it = it0 + u * 128;
+            const int tt = it >> 4, i = (it & 15) * 4;
+            if (t0 + tt >= p.T) continue;
+            const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + i);
+            const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + i + 64);
+            const float v0[4] = {a.x, a.y, a.z, a.w};
+            const float v1[4] = {c.x, c.y, c.z, c.w};
+            epilogue_store<EPI>(p, m, i, t0 + tt, v0, v1, in[u]);
+          }
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // red is free again
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // red is free for the next tile
     }
   }
   tc_fence_before();
@@ -798,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 2 * NT);
   }
   if (threadIdx.x == 0) trace(p, kTrEnd);
 }
@@ -958,26 +974,32 @@ int validate(const rfx_linear_desc& d) {
 }  // namespace
 
 namespace {
-// Many tokens with the load prologue and automatic tiling go to the
-// persistent tile kernel.
-bool persistent_tiles(const rfx_linear_desc& d, const Config& cfg) {
-  return d.prologue == RFX_PRO_LOAD && d.splits == 0 && d.n_tile == 0 && cfg.nt == 128 && d.T > 128;
+// Many tokens (T > 128) with the load prologue and automatic tiling go to the
+// persistent tile kernel: 256-token tiles (more FLOPs per operand byte, the
+// per-SM operand stream being the bound) when that still gives every SM at
+// least two tiles, else 128-token tiles.  0 = the per-tile kernel.
+int persistent_nt(const rfx_linear_desc& d, int nsm) {
+  if (d.prologue != RFX_PRO_LOAD || d.splits != 0 || d.n_tile != 0 || d.T <= 128) return 0;
+  const int m_tiles = d.O / kBM;
+  return m_tiles * ((d.T + 255) / 256) >= 2 * nsm ? 256 : 128;
 }
 
-template <int EPI>
+template <int NT, int EPI>
 const void* tiles_ptr() {
-  return reinterpret_cast<const void*>(linear_tiles_kernel<EPI>);
+  return reinterpret_cast<const void*>(linear_tiles_kernel<NT, EPI>);
 }
-const void* select_tiles(int epi) {
+template <int NT>
+const void* select_tiles_nt(int epi) {
   switch (epi) {
-    case kEpiStore: return tiles_ptr<kEpiStore>();
-    case kEpiSilu: return tiles_ptr<kEpiSilu>();
-    case kEpiQkvRope: return tiles_ptr<kEpiQkvRope>();
-    case kEpiResidual: return tiles_ptr<kEpiResidual>();
-    case kEpiGeglu: return tiles_ptr<kEpiGeglu>();
+    case kEpiStore: return tiles_ptr<NT, kEpiStore>();
+    case kEpiSilu: return tiles_ptr<NT, kEpiSilu>();
+    case kEpiQkvRope: return tiles_ptr<NT, kEpiQkvRope>();
+    case kEpiResidual: return tiles_ptr<NT, kEpiResidual>();
+    case kEpiGeglu: return tiles_ptr<NT, kEpiGeglu>();
   }
   return nullptr;
 }
+const void* select_tiles(int nt, int epi) { return nt == 256 ? select_tiles_nt<256>(epi) : select_tiles_nt<128>(epi); }
 
 LinParams lin_params(const rfx_linear_desc& d) {
   LinParams p{};
@@ -1011,20 +1033,21 @@ LinParams lin_params(const rfx_linear_desc& d) {
   return p;
 }
 
-int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, const Config& cfg,
-                        int nsm, cudaStream_t stream, bool pdl) {
-  const void* fn = select_tiles(d.epilogue);
+int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, int nt, int nsm,
+                        cudaStream_t stream, bool pdl) {
+  const void* fn = select_tiles(nt, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no tile kernel for this epilogue");
-  int rc = ensure_smem_attr(fn, kPSmemBytes);
+  const int smem = nt == 256 ? TilesLayout<256>::kSmem : TilesLayout<128>::kSmem;
+  int rc = ensure_smem_attr(fn, smem);
   if (rc) return rc;
   LinParams p = lin_params(d);
   p.splits = 1;
-  p.n_tiles = (d.T + cfg.nt - 1) / cfg.nt;
+  p.n_tiles = (d.T + nt - 1) / nt;
   const int tiles = (d.O / kBM) * p.n_tiles;
   const int grid = std::min(tiles, nsm);
   p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(grid) * 16));
   CUtensorMap w = *tmW, x = *tmX;
-  return launch_kernel(fn, dim3(grid), dim3(kThreads), static_cast<size_t>(kPSmemBytes), stream, pdl, 1, w, x, p);
+  return launch_kernel(fn, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), stream, pdl, 1, w, x, p);
 }
 }  // namespace
 
@@ -1038,7 +1061,8 @@ int build_linear_maps(const rfx_linear_desc& d, CUtensorMap* tmW, CUtensorMap* t
   if (rc) return rc;
   rc = make_tmap_2d(tmW, d.w, 2, d.K, d.O, static_cast<uint64_t>(d.K) * 2, kBK, kBM, true);
   if (rc) return rc;
-  return make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, cfg.nt, true);
+  const int pnt = persistent_nt(d, nsm);
+  return make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, pnt ? pnt : cfg.nt, true);
 }
 
 int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, cudaStream_t stream,
@@ -1050,7 +1074,7 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   Config cfg;
   rc = pick_config(d, nsm, &cfg);
   if (rc) return rc;
-  if (persistent_tiles(d, cfg)) return launch_linear_tiles(d, tmW, tmX, cfg, nsm, stream, pdl);
+  if (const int pnt = persistent_nt(d, nsm)) return launch_linear_tiles(d, tmW, tmX, pnt, nsm, stream, pdl);
   const void* fn = select_kernel(cfg.nt, d.prologue, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no kernel for this configuration");
   rc = ensure_smem_attr(fn, cfg.smem, cfg.splits > 8);

@@ -92,31 +92,35 @@ def test_linear_store(K, T, n_tile, splits):
     torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv"])
+@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv", "store_wide", "geglu_wide"])
 @pytest.mark.parametrize("B,S", [(1, 300), (2, 384), (1, 768)])
 def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     """T > 128 tokens with the load prologue run the persistent tile kernel (two
     TMEM accumulators, a tile's epilogue under the next tile's mainloop).  It
-    issues the same MMA sequence per 128 x 128 tile as the per-tile kernel with
-    n_tile=128 and no split-K, so the outputs are bit-identical to it for every
+    issues the same MMA sequence per tile as the per-tile kernel with the same
+    token tile and no split-K, so the outputs are bit-identical to it for every
     epilogue, with ragged last token tiles and several batches; the store
-    epilogue is also checked against the fp32 product."""
+    epilogue is also checked against the fp32 product.  The *_wide cases have
+    16384 output rows: with enough tiles the kernel uses 256-token tiles."""
     r = gen(6)
     T, Kd, Hq, D = B * S, 1024, 8, 256
     x = r(T, Kd).bfloat16().cuda()
+    wide = epi.endswith("_wide")
+    epi = epi.replace("_wide", "")
+    O = 16384 if wide else (640 if epi == "store" else 1024)  # output rows (2F for gate/up)
 
     def run(tiling):
         kw = dict(w=w, x=x, T=T, S=S, n_tile=tiling[0], splits=tiling[1])
         if epi == "store":
-            y = torch.empty(T, 640, dtype=torch.bfloat16, device="cuda")
+            y = torch.empty(T, O, dtype=torch.bfloat16, device="cuda")
             K.linear(y=y, bias=bias, **kw)
             return [y]
         if epi == "residual":
             y = y0.clone()
-            K.linear(epilogue=L.RFX_EPI_RESIDUAL, y=y, gate=gate, gate_stride=1024, **kw)
+            K.linear(epilogue=L.RFX_EPI_RESIDUAL, y=y, gate=gate, gate_stride=O, **kw)
             return [y]
         if epi == "geglu":
-            y = torch.empty(T, 1024, dtype=torch.bfloat16, device="cuda")
+            y = torch.empty(T, O // 2, dtype=torch.bfloat16, device="cuda")
             K.linear(epilogue=L.RFX_EPI_GEGLU, y=y, **kw)
             return [y]
         q = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device="cuda")
@@ -127,20 +131,23 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
         return [q, k, v]
 
     if epi == "store":
-        w = r(640, Kd, std=0.03).bfloat16().cuda()
-        bias = r(640, std=0.1).cuda()
+        w = r(O, Kd, std=0.03).bfloat16().cuda()
+        bias = r(O, std=0.1).cuda()
     elif epi == "residual":
-        w = r(1024, Kd, std=0.03).bfloat16().cuda()
-        gate = torch.from_numpy(bf16_round(r(B, 1024).numpy())).cuda()
-        y0 = r(T, 1024).bfloat16().cuda()
+        w = r(O, Kd, std=0.03).bfloat16().cuda()
+        gate = torch.from_numpy(bf16_round(r(B, O).numpy())).cuda()
+        y0 = r(T, O).bfloat16().cuda()
     elif epi == "geglu":
-        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(2048, Kd, std=0.03).bfloat16().cuda())
+        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(O, Kd, std=0.03).bfloat16().cuda())
     else:
-        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r((Hq + 2) * D, Kd, std=0.03).bfloat16().cuda())
+        O = (Hq + 2) * D
+        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r(O, Kd, std=0.03).bfloat16().cuda())
         tab = rope_table().cuda()
         pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    nt = 256 if (O // 128) * ((T + 255) // 256) >= 2 * nsm else 128
     got = run((0, 0))       # persistent tile kernel
-    ref = run((128, 1))     # per-tile kernel, same tiling
+    ref = run((nt, 1))      # per-tile kernel, same token tile
     torch.cuda.synchronize()
     assert K.device_status() == 0
     for a, b in zip(got, ref):
