@@ -977,11 +977,14 @@ namespace {
 // Many tokens (T > 128) with the load prologue and automatic tiling go to the
 // persistent tile kernel: 256-token tiles (more FLOPs per operand byte, the
 // per-SM operand stream being the bound) when that still gives every SM at
-// least two tiles, else 128-token tiles.  0 = the per-tile kernel.
+// least two tiles, else 128-token tiles.  With fewer than half an SM's worth
+// of 128-token tiles the per-tile kernel's split-K keeps more SMs busy.
+// 0 = the per-tile kernel.
 int persistent_nt(const rfx_linear_desc& d, int nsm) {
   if (d.prologue != RFX_PRO_LOAD || d.splits != 0 || d.n_tile != 0 || d.T <= 128) return 0;
   const int m_tiles = d.O / kBM;
-  return m_tiles * ((d.T + 255) / 256) >= 2 * nsm ? 256 : 128;
+  if (m_tiles * ((d.T + 255) / 256) >= 2 * nsm) return 256;
+  return 2 * m_tiles * ((d.T + 127) / 128) >= nsm ? 128 : 0;
 }
 
 template <int NT, int EPI>

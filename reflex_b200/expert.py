@@ -222,10 +222,15 @@ class ActionExpertEngine:
                     w=self.w_qkv[l], x=self.xn, T=T, S=St, epilogue=L.RFX_EPI_QKV_ROPE,
                     rope_table=self.rope, positions=self.positions, q_out=self.q, k_out=self.k_new,
                     v_out=self.v_new, num_q_heads=H), ("qkv", tau, l)))
+                # several streams: each stream's query tiles share its keys, so the
+                # context is dequantized once per layer-step (RFX_KV_DENSE; PI0.5's
+                # suffix is one bidirectional block)
+                dense = cfg.variant == "pi05" and B > 1
                 ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l],
                                       n_ctx=self.n_ctx, out=self.attn_out, softmax_scale=D ** -0.5,
                                       new_block=self.new_block if cfg.variant == "pi0" else None,
-                                      kv_splits=self.kv_splits)
+                                      kv_splits=self.kv_splits,
+                                      kv_source=L.RFX_KV_DENSE if dense else L.RFX_KV_RING_TILES)
                 attn_descs.append(ad)
                 ops.append(("attn", ad, ("attn", tau, l)))
                 ops.append(("linear", K.linear_desc(
@@ -252,11 +257,11 @@ class ActionExpertEngine:
                         ("step", tau)))
         # one workspace serves every attention launch (they run in sequence)
         need = max(K.attention_workspace_bytes(d) for d in attn_descs) if attn_descs else 0
-        if need and (self.workspace is None or self.workspace.numel() < need):
-            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        if need and (self.workspace is None or self.workspace.numel() < need + 1024):
+            self.workspace = torch.empty(need + 1024, dtype=torch.uint8, device=self.dev)
         for d in attn_descs:
             if need:
-                d.workspace, d.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+                d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace, 1024), need
         self.ops = ops
         if self.plan is not None:
             self.plan.close()

@@ -107,7 +107,9 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     x = r(T, Kd).bfloat16().cuda()
     wide = epi.endswith("_wide")
     epi = epi.replace("_wide", "")
-    O = 16384 if wide else (640 if epi == "store" else 1024)  # output rows (2F for gate/up)
+    # output rows (2F for gate/up): enough 128-token tiles for the persistent kernel
+    O = 16384 if wide else 4096
+    Hq = 14  # QKV: (14 + 2) x 256 = 4096 rows
 
     def run(tiling):
         kw = dict(w=w, x=x, T=T, S=S, n_tile=tiling[0], splits=tiling[1])
@@ -146,6 +148,7 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
         pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
     nsm = torch.cuda.get_device_properties(0).multi_processor_count
     nt = 256 if (O // 128) * ((T + 255) // 256) >= 2 * nsm else 128
+    assert nt == 256 or 2 * (O // 128) * ((T + 127) // 128) >= nsm  # the persistent kernel serves these shapes
     got = run((0, 0))       # persistent tile kernel
     ref = run((nt, 1))      # per-tile kernel, same token tile
     torch.cuda.synchronize()
