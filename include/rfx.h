@@ -207,7 +207,7 @@ int rfx_pack_weight(int kind, const void* src, void* dst, int rows, int K, void*
  *     the workspace, then the attention streams those tiles by TMA with two
  *     key blocks in flight (right for many query tiles, e.g. a 768-token
  *     frame through the prefix layers, where every query tile visits every
- *     block).  Same results as the ring path; new_block must be NULL. */
+ *     block).  Same results as the ring path (new_block included). */
 #define RFX_KV_RING_TILES 0
 #define RFX_KV_DENSE 1
 typedef struct rfx_attn_desc {

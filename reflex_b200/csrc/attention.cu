@@ -74,6 +74,7 @@ struct AttnParams {
   float* key_ks;
   float* key_vs;
   float* key_add;
+  int* key_nb;  // block id of the key (-1 for context keys; new_block[k] for new key k)
   __nv_bfloat16* kd;
   __half* vd;
   int Lk;
@@ -531,6 +532,7 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
       bool valid = slot < p.n_ctx;
       if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
       p.key_add[row0 + t] = valid ? 0.f : -INFINITY;
+      p.key_nb[row0 + t] = -1;
       if (p.mode == kQuantI8Sym) {
         p.key_ks[row0 + t] = valid ? static_cast<const float*>(p.k_scale)[gi] * p.scale_log2 : 0.f;
         p.key_vs[row0 + t] = valid ? static_cast<const float*>(p.v_scale)[gi] : 0.f;
@@ -581,6 +583,7 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
       p.key_ks[row0 + threadIdx.x] = kk < p.S ? p.scale_log2 : 0.f;
       p.key_add[row0 + threadIdx.x] = kk < p.S ? 0.f : -INFINITY;
       p.key_vs[row0 + threadIdx.x] = 1.f;
+      p.key_nb[row0 + threadIdx.x] = (kk < p.S && p.new_block) ? p.new_block[kk] : 0;
     }
     // 64 keys x (K, V) x 32 chunks of 8 bf16 values
     for (int it = threadIdx.x; it < 2 * kKB * 32; it += blockDim.x) {
@@ -618,8 +621,8 @@ constexpr int kDOffQ = 0;
 constexpr int kDOffK = 65536;        // 2 stages x 4 x [64 x 64] bf16
 constexpr int kDOffV = 131072;       // 2 stages x 4 x [64 x 64] f16 (MN-major blocks)
 constexpr int kDOffP = 196608;       // [128 x 64] f16
-constexpr int kDOffScale = 212992;   // 2 stages x (ks, vs, kadd) x 64 floats
-constexpr int kDOffBar = 214528;
+constexpr int kDOffScale = 212992;   // 2 stages x (ks, vs, kadd, nb) x 64 words
+constexpr int kDOffBar = 215040;
 constexpr int kDSmemBytes = kDOffBar + 128 + 1024;
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -681,15 +684,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = jl & 1;
         if (jl >= 2 && !mbar_wait(&kv_empty[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
         const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + jl) * kKB;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * 32768 + 3 * 256);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * 32768 + 4 * 256);
         for (int a = 0; a < 4; ++a) {
           tma_load_2d(smem + kDOffK + st * 32768 + a * 8192, &tmK, &kv_full[st], a * 64, static_cast<int>(key0));
           tma_load_2d(smem + kDOffV + st * 32768 + a * 8192, &tmV, &kv_full[st], a * 64, static_cast<int>(key0));
         }
-        float* sc = sScale + st * 192;
+        float* sc = sScale + st * 256;
         bulk_load(sc, p.key_ks + key0, 256, &kv_full[st]);
         bulk_load(sc + 64, p.key_vs + key0, 256, &kv_full[st]);
         bulk_load(sc + 128, p.key_add + key0, 256, &kv_full[st]);
+        bulk_load(sc + 192, p.key_nb + key0, 256, &kv_full[st]);
         ++issued;
       }
       trace(p, kTrIssued);
@@ -739,11 +743,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool row_valid = R < p.Hq * p.S;
     const int s_row = row_valid ? R % p.S : 0;
     const int h_row = row_valid ? R / p.S : 0;
+    const int my_block = (row_valid && p.new_block) ? p.new_block[s_row] : 0;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int jl = 0; jl < nbl && ok; ++jl) {
       const int st = jl & 1;
+      const bool causal = p.new_block != nullptr && blk_begin + jl >= p.n_ctx_blocks;
       if (!(ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
       if (!(ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone))) break;
       tc_fence_after();
@@ -762,9 +768,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[st]);
-      const float* ks_s = sScale + st * 192;
+      const float* ks_s = sScale + st * 256;
       const float* vs_s = ks_s + 64;
       const float* kadd_s = ks_s + 128;
+      const int* nb_s = reinterpret_cast<const int*>(ks_s + 192);
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < kKB / 4; ++c) {
@@ -774,6 +781,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         z[4 * c + 1] = fmaf(z[4 * c + 1], km.y, ka.y);
         z[4 * c + 2] = fmaf(z[4 * c + 2], km.z, ka.z);
         z[4 * c + 3] = fmaf(z[4 * c + 3], km.w, ka.w);
+        if (causal) {  // new key j is visible to row i iff new_block[j] <= new_block[i]
+          const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
+          if (nb.x > my_block) z[4 * c + 0] = -INFINITY;
+          if (nb.y > my_block) z[4 * c + 1] = -INFINITY;
+          if (nb.z > my_block) z[4 * c + 2] = -INFINITY;
+          if (nb.w > my_block) z[4 * c + 3] = -INFINITY;
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
       }
@@ -961,8 +975,6 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
     return set_error(RFX_E_INVAL, "rfx_attention: quant_mode");
   if (d.kv_source != RFX_KV_RING_TILES && d.kv_source != RFX_KV_DENSE)
     return set_error(RFX_E_INVAL, "rfx_attention: kv_source");
-  if (d.kv_source == RFX_KV_DENSE && d.new_block)
-    return set_error(RFX_E_UNSUPPORTED, "rfx_attention: RFX_KV_DENSE serves a bidirectional new-key block (new_block NULL)");
   g->q_tiles = (d.num_q_heads * d.S + kQR - 1) / kQR;
   g->n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
   g->n_blocks = g->n_ctx_blocks + (d.S + kKB - 1) / kKB;
@@ -984,9 +996,9 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
 namespace {
 // Workspace: the split-KV partials (O, then (m, l)), then in dense mode the
 // dense keys at 1024-byte aligned offsets: bf16 K, f16 V [B][Lk][D] and the
-// per-key ks, vs, kadd [B][Lk] fp32.
+// per-key ks, vs, kadd [B][Lk] fp32 and block ids [B][Lk] int32.
 struct WsLayout {
-  size_t partials, kd, vd, ks, vs, kadd, total;
+  size_t partials, kd, vd, ks, vs, kadd, nb, total;
 };
 WsLayout ws_layout(const rfx_attn_desc& d, const Geometry& g) {
   WsLayout w{};
@@ -1005,6 +1017,7 @@ WsLayout ws_layout(const rfx_attn_desc& d, const Geometry& g) {
     w.ks = take(keys * 4);
     w.vs = take(keys * 4);
     w.kadd = take(keys * 4);
+    w.nb = take(keys * 4);
     w.total = off;
   } else {
     w.total = w.partials;
@@ -1107,6 +1120,7 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
     p.key_ks = reinterpret_cast<float*>(ws + wl.ks);
     p.key_vs = reinterpret_cast<float*>(ws + wl.vs);
     p.key_add = reinterpret_cast<float*>(ws + wl.kadd);
+    p.key_nb = reinterpret_cast<int*>(ws + wl.nb);
     p.Lk = g.n_blocks * kKB;
   }
   p.status = device_status_ptr();

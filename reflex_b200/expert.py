@@ -222,10 +222,10 @@ class ActionExpertEngine:
                     w=self.w_qkv[l], x=self.xn, T=T, S=St, epilogue=L.RFX_EPI_QKV_ROPE,
                     rope_table=self.rope, positions=self.positions, q_out=self.q, k_out=self.k_new,
                     v_out=self.v_new, num_q_heads=H), ("qkv", tau, l)))
-                # several streams: each stream's query tiles share its keys, so the
-                # context is dequantized once per layer-step (RFX_KV_DENSE; PI0.5's
-                # suffix is one bidirectional block)
-                dense = cfg.variant == "pi05" and B > 1
+                # several streams or a long context: every query tile of a stream
+                # visits the same key blocks, so the context is dequantized once
+                # per layer-step (RFX_KV_DENSE) instead of once per query tile
+                dense = B > 1 or self.n_ctx >= 32 * 64
                 ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l],
                                       n_ctx=self.n_ctx, out=self.attn_out, softmax_scale=D ** -0.5,
                                       new_block=self.new_block if cfg.variant == "pi0" else None,

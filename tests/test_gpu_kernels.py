@@ -324,12 +324,13 @@ def test_attention_partitioned(K, L, mode, n_ctx, S, splits):
 
 
 @pytest.mark.parametrize("mode", ["i8", "u8"])
-@pytest.mark.parametrize("n_ctx,S,splits", [(1584, 200, 0), (300, 100, 1), (0, 64, 0), (818, 50, 3)])
+@pytest.mark.parametrize("n_ctx,S,splits", [(1584, 200, 0), (300, 100, 1), (0, 64, 0), (818, 50, 3), (2100, 51, 0)])
 def test_attention_dense_source_matches_ring_tiles_and_oracle(K, L, mode, n_ctx, S, splits):
     """RFX_KV_DENSE (one dequantize pass, then TMA-fed bf16/f16 tiles with two key
     blocks in flight) against the in-kernel conversion path on the same inputs,
     and both against fp32 attention over the dequantized context (2e-2), with a
-    masked context range (an evicted frame) and a bidirectional new-key block."""
+    masked context range (an evicted frame); the new keys form one bidirectional
+    block, or (S = 51, PI0) a state token in its own block before the actions."""
     r = gen(9)
     B, Hq, D, cap = 1, 8, 256, max(64, n_ctx + 64)
     qm = L.RFX_QUANT_I8_SYM if mode == "i8" else L.RFX_QUANT_U8_REF
@@ -341,11 +342,16 @@ def test_attention_dense_source_matches_ring_tiles_and_oracle(K, L, mode, n_ctx,
     valid[:, n_ctx // 3: 2 * n_ctx // 3] = 0
     q = r(B, Hq, S, D).bfloat16()
     kn, vn = r(B, S, D).bfloat16(), r(B, S, D).bfloat16()
+    blk = None
+    if S == 51:
+        blk = torch.zeros(S, dtype=torch.int32)
+        blk[1:] = 1
     outs = []
     for src in (L.RFX_KV_RING_TILES, L.RFX_KV_DENSE):
         out = torch.empty(B * S, Hq * D, dtype=torch.bfloat16, device="cuda")
         K.attention(q=q.cuda(), k_new=kn.cuda(), v_new=vn.cuda(), ring=ring, n_ctx=n_ctx, out=out,
-                    softmax_scale=1 / 16, ctx_valid=valid.cuda(), kv_splits=splits, kv_source=src)
+                    softmax_scale=1 / 16, ctx_valid=valid.cuda(), kv_splits=splits, kv_source=src,
+                    new_block=None if blk is None else blk.cuda())
         torch.cuda.synchronize()
         outs.append(out.float().cpu())
     assert K.device_status() == 0
@@ -362,6 +368,8 @@ def test_attention_dense_source_matches_ring_tiles_and_oracle(K, L, mode, n_ctx,
     vd = torch.from_numpy(vd)[:, :, :n_ctx]
     att = torch.zeros(S, dtype=torch.int64)
     att[0] = 1
+    if S == 51:
+        att[1] = 1
     ref = partitioned_attention(q, kd, vd, kn[:, None], vn[:, None], valid[:, :n_ctx].bool(), att, 1 / 16)
     ref = ref.permute(0, 2, 1, 3).reshape(B * S, Hq * D)
     errs = [(o - ref).abs().max().item() for o in outs]
