@@ -410,6 +410,85 @@ def run_gpu(args):
         pg.destroy_process_group()
 
 
+def cpu_frame_ms(layers: int):
+    """The oracle port of one control tick with a frame update on the host CPU,
+    all host threads: the new 768-token frame through the prefix layers
+    (reflex/policies/pi05/modeling_pi05.py:1282-1333 with the full prefix
+    attention of :1379-1401) over the pinned prefix + the surviving frame, its
+    K/V quantized into the context, then one 10-step PI0.5 chunk over the
+    1584-token context."""
+    from oracle import quant as oq
+    from oracle.model import Context, prefix_frame, sample_chunk
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config, vlm_config
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    pinned, flen = 48, 768
+    vcfg = vlm_config(num_layers=layers)
+    cfg = pi05_config(num_layers=layers, adarms="ssg")
+    pw = synthetic.prefix_weights(vcfg, seed=10)
+    ew = synthetic.expert_weights(cfg, seed=0)
+    ks, vs = synthetic.context_kv(cfg, pinned + 2 * flen, seed=1)
+
+    def deq(x):
+        q, sc = oq.quant_i8_sym(x.numpy())
+        return torch.from_numpy(oq.dequant_i8_sym(q, sc))
+
+    old = [(deq(ks[l][:, :, :pinned + flen]), deq(vs[l][:, :, :pinned + flen])) for l in range(layers)]
+    emb = synthetic.frame_embeddings(vcfg, flen, seed=20).float()
+    x0 = synthetic.noise(cfg, seed=2)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        ctx = Context([k for k, _ in old], [v for _, v in old], torch.ones(1, pinned + flen, dtype=torch.bool))
+        pos = (pinned + flen + torch.arange(flen))[None]
+        _, kvs = prefix_frame(vcfg, pw, emb, ctx, pos)
+        full = Context([torch.cat([old[l][0], deq(kvs[l][0])], 2) for l in range(layers)],
+                       [torch.cat([old[l][1], deq(kvs[l][1])], 2) for l in range(layers)],
+                       torch.ones(1, pinned + 2 * flen, dtype=torch.bool))
+        sample_chunk(cfg, ew, full, x0)
+    return (time.perf_counter() - t0) * 1e3, torch.get_num_threads()
+
+
+def frame_gu_roofline(pre, bf16_peak, peak_kind):
+    """The frame update's dominant kernel: one prefix layer's gate/up projection
+    (768 tokens x 32768 rows x 2048), timed alone with CUDA events on the
+    launching stream; achieved TFLOP/s against the measured bf16 burst peak."""
+    from reflex_b200 import kernels as K
+
+    layer = [d for kind, d, _ in pre.ops(0) if kind != "barrier"]
+    gu = layer[5]  # norm, qkv, attn, o, norm2, gate/up, down, quant
+    for _ in range(2):
+        K.Plan.run_direct(gu)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    durs = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2_000_000)
+        e0.record(st)
+        K.Plan.run_direct(gu)
+        e1.record(st)
+        torch.cuda.synchronize()
+        durs.append(e0.elapsed_time(e1))
+    ms = statistics.median(durs)
+    flops = 2.0 * gu.T * gu.O * gu.K
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "linear_gate_up_frame768.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1])
+    except OSError:
+        pass
+    return {"kernel": "linear_tiles_kernel<256,GEGLU> (prefix gate/up projection, 768 tokens)", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
+            "traffic": traffic, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                                  "profiles/linear_gate_up_frame768.md",
+            "flops_per_launch": flops, "avg_launch_us": round(ms * 1e3, 2),
+            "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}
+
+
 def run_frame(args):
     """Streaming frame update + one chunk per control tick: a new frame of
     3 cameras x 256 patch embeddings through the 18 prefix layers (Gemma-2B
@@ -494,6 +573,9 @@ def run_frame(args):
             e2e.append(e0.elapsed_time(e1))
     prefix_bytes = args.layers * (2560 * 2048 + 2048 * 2048 + 32768 * 2048 + 2048 * 16384) * 2
     prefix_flops = 2.0 * flen * prefix_bytes / 2
+    _, bf16_peak, peak_kind = peaks()
+    roof = frame_gu_roofline(pre, bf16_peak, peak_kind)
+    cpu_ms, cores = cpu_frame_ms(args.layers)
     line = {
         "metric": "p50 streaming frame update + 10-step PI0.5 chunk latency (ms)", "value": round(p50, 4),
         "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -509,6 +591,10 @@ def run_frame(args):
         "e2e": {"value": round(statistics.median(e2e), 4), "unit": "ms",
                 "h2d_bytes_per_step": fh.numel() * 2 + xh.numel() * 4, "d2h_bytes_per_step": out.numel() * 4},
         "gpu_launches": sum(p.num_launches for p in plans) // win * args.steps,
+        "roofline": roof,
+        "cpu_baseline": {"value": round(cpu_ms, 3), "unit": "ms", "cores": cores, "kind": "port",
+                         "sample": "1 control tick of the same workload: frame through the prefix layers + "
+                                   "one chunk (fp32 torch oracle port)"},
         "clocks": clk.summary(), "device_status": status,
     }
     print(json.dumps(line), flush=True)
