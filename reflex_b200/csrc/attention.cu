@@ -623,9 +623,27 @@ constexpr int kDOffV = 131072;       // 2 stages x 4 x [64 x 64] f16 (MN-major b
 constexpr int kDOffP = 196608;       // [128 x 64] f16
 constexpr int kDOffScale = 212992;   // 2 stages x (ks, vs, kadd, nb) x 64 words
 constexpr int kDOffBar = 215040;
-constexpr int kDSmemBytes = kDOffBar + 128 + 1024;
+constexpr int kDOffXchg = 215168;    // 768 floats: row maxima and sums of the two column halves
+constexpr int kDSmemBytes = kDOffXchg + 3072 + 1024;
+// warps 0-1 as in attention_kernel; warps 2-9 run the softmax and the
+// epilogue, two per TMEM lane quadrant, each on half of a row's columns
+constexpr int kDWorkers = 256;
+constexpr int kDThreads = 64 + kDWorkers;
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Barrier over the two worker warps of a TMEM lane quadrant that also ANDs a
+// flag over them: both warps leave a loop together when either saw a failed
+// (bounded) wait, so neither waits at a named barrier for a warp that left.
+__device__ __forceinline__ bool pair_all(int quad, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(2 + quad)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(kDThreads, 1)
     attention_dense_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -653,9 +671,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&s_free[i], kDWorkers / 32);
     }
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, kDWorkers / 32);
     mbar_init(o_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -738,7 +756,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     pdl_wait();
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // query row inside the tile == TMEM lane
+    const int ch = (threadIdx.x - 64) >> 7;  // this warp's half of the row: 32 score / 128 output columns
+    const int r = quad * 32 + lane;          // query row inside the tile == TMEM lane
+    float* mx_x = reinterpret_cast<float*>(smem + kDOffXchg);  // [2 blocks][2 halves][128] row maxima
+    float* l_x = mx_x + 512;                                   // [2 halves][128] row sums
     const int R = qt * kQR + r;
     const bool row_valid = R < p.Hq * p.S;
     const int s_row = row_valid ? R % p.S : 0;
@@ -747,20 +768,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int jl = 0; jl < nbl && ok; ++jl) {
+    for (int jl = 0; jl < nbl; ++jl) {
       const int st = jl & 1;
       const bool causal = p.new_block != nullptr && blk_begin + jl >= p.n_ctx_blocks;
-      if (!(ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
-      if (!(ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone))) break;
+      if (ok) ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+      if (ok) ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone);
+      ok = __all_sync(0xffffffffu, ok);
+      constexpr int kHalf = kKB / 2;
+      float z[kHalf];
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      const float* ks_s = sScale + st * 256 + kHalf * ch;
+      const float* vs_s = ks_s + 64;
+      const float* kadd_s = ks_s + 128;
+      const int* nb_s = reinterpret_cast<const int*>(ks_s + 192);
+      if (ok) {
       tc_fence_after();
-      float z[kKB];
       {
-        uint32_t rr[kKB / 16][16];
+        uint32_t rr[2][16];
 #pragma unroll
-        for (int c = 0; c < kKB / 16; ++c) tmem_ld16(tmS + st * kKB + lane_base + c * 16, rr[c]);
+        for (int c = 0; c < 2; ++c) tmem_ld16(tmS + st * kKB + lane_base + (2 * ch + c) * 16, rr[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < kKB / 16; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[c][e]);
       }
@@ -768,13 +797,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[st]);
-      const float* ks_s = sScale + st * 256;
-      const float* vs_s = ks_s + 64;
-      const float* kadd_s = ks_s + 128;
-      const int* nb_s = reinterpret_cast<const int*>(ks_s + 192);
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kKB / 4; ++c) {
+      for (int c = 0; c < kHalf / 4; ++c) {
         const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
         const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
         z[4 * c + 0] = fmaf(z[4 * c + 0], km.x, ka.x);
@@ -791,7 +815,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
       }
-      const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      }
+      // the row's max over both column halves (the partner warp holds the other)
+      float* mxb = mx_x + (jl & 1) * 256;
+      mxb[ch * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      ok = pair_all(quad, ok);
+      if (!ok) break;  // both warps of the pair agree
+      const float bmax = fmaxf(mxb[r], mxb[128 + r]);
       const float m_new = fmaxf(m_run, bmax);
       bool need = false;
       float m_use;
@@ -806,9 +836,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float alpha = need ? exp2f(m_run - m_use) : 1.f;
       const float m_sub = m_use == -INFINITY ? 0.f : m_use;
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      float pv[kKB];
+      float pv[kHalf];
 #pragma unroll
-      for (int c = 0; c < kKB / 4; ++c) {
+      for (int c = 0; c < kHalf / 4; ++c) {
         const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
         const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
 #pragma unroll
@@ -821,12 +851,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
       m_run = m_use;
       // P_{jl-1} V_{jl-1} has finished: the P tile is free and O is final
-      // for the rescale
-      if (jl > 0 && !(ok = mbar_wait(o_done, (jl - 1) & 1, p.status, kDevTimeoutMmaDone))) break;
+      // for the rescale (a failed wait skips the rest of this block; the
+      // pair leaves the loop together at the next exchange)
+      if (jl > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (jl - 1) & 1, p.status, kDevTimeoutMmaDone));
+      if (!ok) continue;
       tc_fence_after();
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < kD / 16; c0 += 2) {
+        for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 2) {
           uint32_t rr[2][16];
 #pragma unroll
           for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
@@ -841,10 +873,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const uint4 v = make_uint4(pack_f16x2(pv[8 * c + 0], pv[8 * c + 1]), pack_f16x2(pv[8 * c + 2], pv[8 * c + 3]),
                                    pack_f16x2(pv[8 * c + 4], pv[8 * c + 5]), pack_f16x2(pv[8 * c + 6], pv[8 * c + 7]));
-        *reinterpret_cast<uint4*>(sP + sw128_offset(r, c)) = v;
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, 4 * ch + c)) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -852,17 +884,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(p_ready);
     }
     // ---- epilogue (the layout of attention_kernel's) ----
-    if (ok && nbl > 0) ok = mbar_wait(o_done, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone);
+    if (ok && nbl > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone));
     tc_fence_after();
+    // the row sum over both halves, in a fixed order (every pair takes this
+    // barrier once, whatever happened in the loop)
+    if (nbl > 0) {
+      l_x[ch * 128 + r] = l_run;
+      ok = pair_all(quad, ok);
+    }
     if (ok && nbl > 0) {
       const bool final_out = p.splits == 1;
+      l_run = l_x[r] + l_x[128 + r];
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const long tok = static_cast<long>(b) * p.S + s_row;
       __nv_bfloat16* orow = p.out + tok * (static_cast<long>(p.Hq) * kD) + h_row * kD;
       const long wcta = (static_cast<long>(b) * p.q_tiles + qt) * p.splits + sp;
       float* wrow_o = p.ws_o ? p.ws_o + (wcta * (kD / 16) * kQR + r) * 16 : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kD / 16; c0 += 4) {
+      for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 4) {
         uint32_t rr[4][16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
@@ -887,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!final_out && row_valid) p.ws_ml[wcta * kQR + r] = make_float2(m_run, l_run);
+      if (!final_out && row_valid && ch == 0) p.ws_ml[wcta * kQR + r] = make_float2(m_run, l_run);
     }
   }
   tc_fence_before();
@@ -1135,7 +1174,7 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
     if (rc) return rc;
   }
   dim3 grid(g.q_tiles, g.splits, d.B);
-  rc = launch_kernel(fn, grid, dim3(kThreads), smem_bytes, stream, pdl, 1, q, k, v, p);
+  rc = launch_kernel(fn, grid, dim3(dense ? kDThreads : kThreads), smem_bytes, stream, pdl, 1, q, k, v, p);
   if (rc || g.splits == 1) return rc;
   const long rows = static_cast<long>(d.B) * g.q_tiles * kQR;
   dim3 cgrid(static_cast<unsigned>((rows + 3) / 4));
