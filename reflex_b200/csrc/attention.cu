@@ -517,16 +517,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // reference uint8 dequantize ((q - zp) * scale, rounded per op to the scale
 // dtype) with unit scales; the new keys: bf16 K as is, V as f16 of its bf16
 // value; keys past n_ctx / S (or masked by ctx_valid) get scale 0 and -inf.
+// One CTA per 16 keys of a block (grid = 4 x blocks x streams).
 __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ AttnParams p, const uint8_t* k_ring,
                                                        const uint8_t* v_ring) {
+  constexpr int kKeys = 16;
   pdl_wait();
-  const int j = blockIdx.x, b = blockIdx.y;
+  const int j = blockIdx.x >> 2, q0 = (blockIdx.x & 3) * kKeys, b = blockIdx.y;
   const long row0 = static_cast<long>(b) * p.Lk + static_cast<long>(j) * kKB;
   const bool sbf16 = p.scale_bf16 != 0;
   __shared__ float dq[4][kKB];  // reference scheme: k scale, v scale, k zp, v zp
   if (j < p.n_ctx_blocks) {
-    if (threadIdx.x < kKB) {
-      const int t = threadIdx.x;
+    if (threadIdx.x < kKeys) {
+      const int t = q0 + threadIdx.x;
       const long slot = static_cast<long>(j) * kKB + t;
       const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
       bool valid = slot < p.n_ctx;
@@ -546,11 +548,11 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
       }
     }
     __syncthreads();
-    // 64 keys x (K, V) x 16 chunks of 16 quantized values
-    for (int it = threadIdx.x; it < 2 * kKB * 16; it += blockDim.x) {
-      const bool isv = it >= kKB * 16;
-      const int w = isv ? it - kKB * 16 : it;
-      const int key = w >> 4, g = w & 15;
+    // 16 keys x (K, V) x 16 chunks of 16 quantized values
+    for (int it = threadIdx.x; it < 2 * kKeys * 16; it += blockDim.x) {
+      const bool isv = it >= kKeys * 16;
+      const int w = isv ? it - kKeys * 16 : it;
+      const int key = q0 + (w >> 4), g = w & 15;
       long slot = static_cast<long>(j) * kKB + key;
       if (slot >= p.cap) slot = p.cap - 1;
       const uint4 raw = *reinterpret_cast<const uint4*>((isv ? v_ring : k_ring) +
@@ -578,18 +580,19 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
     }
   } else {
     const int nb0 = (j - p.n_ctx_blocks) * kKB;
-    if (threadIdx.x < kKB) {
-      const int kk = nb0 + threadIdx.x;
-      p.key_ks[row0 + threadIdx.x] = kk < p.S ? p.scale_log2 : 0.f;
-      p.key_add[row0 + threadIdx.x] = kk < p.S ? 0.f : -INFINITY;
-      p.key_vs[row0 + threadIdx.x] = 1.f;
-      p.key_nb[row0 + threadIdx.x] = (kk < p.S && p.new_block) ? p.new_block[kk] : 0;
+    if (threadIdx.x < kKeys) {
+      const int t = q0 + threadIdx.x;
+      const int kk = nb0 + t;
+      p.key_ks[row0 + t] = kk < p.S ? p.scale_log2 : 0.f;
+      p.key_add[row0 + t] = kk < p.S ? 0.f : -INFINITY;
+      p.key_vs[row0 + t] = 1.f;
+      p.key_nb[row0 + t] = (kk < p.S && p.new_block) ? p.new_block[kk] : 0;
     }
-    // 64 keys x (K, V) x 32 chunks of 8 bf16 values
-    for (int it = threadIdx.x; it < 2 * kKB * 32; it += blockDim.x) {
-      const bool isv = it >= kKB * 32;
-      const int w = isv ? it - kKB * 32 : it;
-      const int key = w >> 5, c = w & 31;
+    // 16 keys x (K, V) x 32 chunks of 8 bf16 values
+    for (int it = threadIdx.x; it < 2 * kKeys * 32; it += blockDim.x) {
+      const bool isv = it >= kKeys * 32;
+      const int w = isv ? it - kKeys * 32 : it;
+      const int key = q0 + (w >> 5), c = w & 31;
       const int kk = nb0 + key;
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);
       if (kk < p.S) raw = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) +
@@ -613,8 +616,9 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
 
 // Attention over the dense keys: the structure of attention_kernel with the
 // conversion gone and two key blocks in flight.  Producer: Q once, then per
-// block K (bf16) and V (f16) tiles by TMA plus the block's 3 x 64 per-key
-// floats by bulk copy into stage jl % 2.  MMA issuer: S_jl = Q K_jl^T into
+// block the K (bf16) tile with the block's 4 x 64 per-key words, and the V
+// (f16) tile, by TMA / bulk copy into stage jl % 2, K and V filled and freed
+// on their own barriers.  MMA issuer: S_jl = Q K_jl^T into
 // TMEM buffer jl % 2, then P_{jl-1} V_{jl-1} into O, so the scores of the next
 // block are computed while the workers run the softmax of this one.
 constexpr int kDOffQ = 0;
@@ -656,20 +660,28 @@ __global__ void __launch_bounds__(kDThreads, 1)
   uint8_t* sP = smem + kDOffP;
   float* sScale = reinterpret_cast<float*>(smem + kDOffScale);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDOffBar);
+  // K and V (with the block's per-key scales) of a stage are filled and
+  // released separately: a K stage is free once its scores are computed, long
+  // before the stage's V has been used; the scales, which the softmax reads
+  // after the scores, stay until the stage's P.V is done
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;   // [2]
+  uint64_t* s_free = bars + 7;   // [2]
   uint64_t* p_ready = bars + 9;
   uint64_t* o_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* v_full = bars + 11;   // [2]
+  uint64_t* v_empty = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   if (threadIdx.x == 0) trace(p, kTrStart);
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kDWorkers / 32);
     }
@@ -691,28 +703,48 @@ __global__ void __launch_bounds__(kDThreads, 1)
   const uint32_t tmO = tmem, tmS = tmem + 256;  // S buffers at columns 256 and 320
   pdl_launch_dependents();
   const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
-  int issued = 0;
+  int k_issued = 0, v_issued = 0;
 
   if (warp == 0) {
     pdl_wait();
     if (lane == 0 && nbl > 0) {
       mbar_arrive_expect_tx(q_full, 4 * 16384);
       for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
-      for (int jl = 0; jl < nbl; ++jl) {
-        const int st = jl & 1;
-        if (jl >= 2 && !mbar_wait(&kv_empty[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutStageEmpty)) break;
-        const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + jl) * kKB;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * 32768 + 4 * 256);
-        for (int a = 0; a < 4; ++a) {
-          tma_load_2d(smem + kDOffK + st * 32768 + a * 8192, &tmK, &kv_full[st], a * 64, static_cast<int>(key0));
-          tma_load_2d(smem + kDOffV + st * 32768 + a * 8192, &tmV, &kv_full[st], a * 64, static_cast<int>(key0));
+      // two queues from one thread: each block's K as soon as its stage's
+      // previous scores are done, its V (+ scales) once that stage's previous
+      // P.V is done (V never ahead of K); bounded in time
+      const unsigned long long t0 = globaltimer_ns();
+      while (k_issued < nbl || v_issued < nbl) {
+        bool moved = false;
+        if (k_issued < nbl &&
+            (k_issued < 2 || mbar_try_wait(&k_empty[k_issued & 1], ((k_issued - 2) >> 1) & 1))) {
+          const int st = k_issued & 1;
+          const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + k_issued) * kKB;
+          mbar_arrive_expect_tx(&k_full[st], 32768);
+          for (int a = 0; a < 4; ++a)
+            tma_load_2d(smem + kDOffK + st * 32768 + a * 8192, &tmK, &k_full[st], a * 64, static_cast<int>(key0));
+          ++k_issued;
+          moved = true;
         }
-        float* sc = sScale + st * 256;
-        bulk_load(sc, p.key_ks + key0, 256, &kv_full[st]);
-        bulk_load(sc + 64, p.key_vs + key0, 256, &kv_full[st]);
-        bulk_load(sc + 128, p.key_add + key0, 256, &kv_full[st]);
-        bulk_load(sc + 192, p.key_nb + key0, 256, &kv_full[st]);
-        ++issued;
+        if (v_issued < k_issued &&
+            (v_issued < 2 || mbar_try_wait(&v_empty[v_issued & 1], ((v_issued - 2) >> 1) & 1))) {
+          const int st = v_issued & 1;
+          const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + v_issued) * kKB;
+          mbar_arrive_expect_tx(&v_full[st], 32768 + 4 * 256);
+          for (int a = 0; a < 4; ++a)
+            tma_load_2d(smem + kDOffV + st * 32768 + a * 8192, &tmV, &v_full[st], a * 64, static_cast<int>(key0));
+          float* sc = sScale + st * 256;
+          bulk_load(sc, p.key_ks + key0, 256, &v_full[st]);
+          bulk_load(sc + 64, p.key_vs + key0, 256, &v_full[st]);
+          bulk_load(sc + 128, p.key_add + key0, 256, &v_full[st]);
+          bulk_load(sc + 192, p.key_nb + key0, 256, &v_full[st]);
+          ++v_issued;
+          moved = true;
+        }
+        if (!moved && globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_error(p.status, kDevTimeoutStageEmpty);
+          break;
+        }
       }
       trace(p, kTrIssued);
     }
@@ -723,6 +755,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
       constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
       bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutTmaFull);
       auto pv = [&](int jp) {  // O += P_jp V_jp
+        if (!(ok = mbar_wait(&v_full[jp & 1], (jp >> 1) & 1, p.status, kDevTimeoutTmaFull))) return;
         if (!(ok = mbar_wait(p_ready, jp & 1, p.status, kDevTimeoutConvert))) return;
         tc_fence_after();
         const uint32_t v_base = smem_u32(smem + kDOffV + (jp & 1) * 32768);
@@ -732,12 +765,12 @@ __global__ void __launch_bounds__(kDThreads, 1)
           const uint64_t bd = make_sdesc_sw128(v_base + ks * 2048, 8192, 1024);
           umma_f16_ss(tmO, ad, bd, idesc_o, (jp > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(&kv_empty[jp & 1]);
+        umma_commit(&v_empty[jp & 1]);
         umma_commit(o_done);
       };
       for (int jl = 0; jl < nbl && ok; ++jl) {
         const int st = jl & 1;
-        if (!(ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
+        if (!(ok = mbar_wait(&k_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
         if (jl >= 2 && !(ok = mbar_wait(&s_free[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutConvert))) break;
         tc_fence_after();
         const uint32_t k_base = smem_u32(smem + kDOffK + st * 32768);
@@ -748,6 +781,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
           const uint64_t bd = make_sdesc_sw128(k_base + a * 8192 + kk * 32, 16, 1024);
           umma_f16_ss(tmS + st * kKB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
         }
+        umma_commit(&k_empty[st]);  // the K stage is free once these scores are done
         umma_commit(&s_full[st]);
         if (jl >= 1) pv(jl - 1);
       }
@@ -771,7 +805,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
     for (int jl = 0; jl < nbl; ++jl) {
       const int st = jl & 1;
       const bool causal = p.new_block != nullptr && blk_begin + jl >= p.n_ctx_blocks;
-      if (ok) ok = mbar_wait(&kv_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+      if (ok) ok = mbar_wait(&v_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);  // scales
       if (ok) ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone);
       ok = __all_sync(0xffffffffu, ok);
       constexpr int kHalf = kKB / 2;
@@ -932,9 +966,12 @@ __global__ void __launch_bounds__(kDThreads, 1)
   tc_fence_before();
   __syncthreads();
   // drain a producer that stopped early: every issued stage completes
-  if (warp == 0 && lane == 0)
-    for (int jl = (issued > 2 ? issued - 2 : 0); jl < issued; ++jl)
-      mbar_wait(&kv_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+  if (warp == 0 && lane == 0) {
+    for (int jl = (k_issued > 2 ? k_issued - 2 : 0); jl < k_issued; ++jl)
+      mbar_wait(&k_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+    for (int jl = (v_issued > 2 ? v_issued - 2 : 0); jl < v_issued; ++jl)
+      mbar_wait(&v_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+  }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -943,7 +980,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
   if (threadIdx.x == 0) trace(p, kTrEnd);
 }
 
-// Merges the kv_splits partial results of every query row.
+// Merges the kv_splits partial results of every query row: one warp per row,
+// lane l holding 8 of the 256 columns.  Split s's (m, l) sits in lane s (at
+// most 32 splits), so the row max and the weights 2^(m_s - M) are a warp
+// reduction and broadcasts; the first 8 splits' partials are requested before
+// the (m, l) arrive, so the two loads overlap.
 __global__ void __launch_bounds__(128) attention_combine_kernel(const AttnParams p) {
   pdl_wait();
   const long g = static_cast<long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
@@ -956,37 +997,36 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const AttnParams
     const int R = qt * kQR + r;
     if (R < p.Hq * p.S) {
       const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.splits;
-      // all partials of this row are loaded before any is used (the loads overlap)
-      constexpr int kMaxSplits = 32;
-      float2 ml[kMaxSplits];
+      constexpr int kBatch = 8;
+      auto load = [&](int s, float4& a, float4& c) {
+        const float* o = p.ws_o + (((base + s) * (kD / 16) + (lane >> 1)) * kQR + r) * 16 + (lane & 1) * 8;
+        a = *reinterpret_cast<const float4*>(o);
+        c = *reinterpret_cast<const float4*>(o + 4);
+      };
+      float4 a[kBatch], c[kBatch];
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        if (s < p.splits) ml[s] = p.ws_ml[(base + s) * kQR + r];
-      float M = -INFINITY;
+      for (int q = 0; q < kBatch; ++q)
+        if (q < p.splits) load(q, a[q], c[q]);
+      const float2 ml = lane < p.splits ? p.ws_ml[(base + lane) * kQR + r] : make_float2(-INFINITY, 0.f);
+      const bool live = ml.x != -INFINITY && ml.y > 0.f;
+      const float M = warp_max(live ? ml.x : -INFINITY);
+      const float w = live ? exp2f(ml.x - M) : 0.f;
+      const float L = warp_sum(w * ml.y);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
+        if (s0 > 0) {
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        if (s < p.splits && ml[s].y > 0.f) M = fmaxf(M, ml[s].x);
-      float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s0 = 0; s0 < kMaxSplits; s0 += 8) {
-        if (s0 >= p.splits) break;
-        float4 a[8], c[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (s0 + q < p.splits) {
-            const float* o = p.ws_o + (((base + s0 + q) * (kD / 16) + (lane >> 1)) * kQR + r) * 16 + (lane & 1) * 8;
-            a[q] = *reinterpret_cast<const float4*>(o);
-            c[q] = *reinterpret_cast<const float4*>(o + 4);
-          }
+          for (int q = 0; q < kBatch; ++q)
+            if (s0 + q < p.splits) load(s0 + q, a[q], c[q]);
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int s = s0 + q;
-          if (s >= p.splits || ml[s].x == -INFINITY || ml[s].y <= 0.f) continue;
-          const float w = exp2f(ml[s].x - M);
-          L += w * ml[s].y;
-          acc[0] += w * a[q].x; acc[1] += w * a[q].y; acc[2] += w * a[q].z; acc[3] += w * a[q].w;
-          acc[4] += w * c[q].x; acc[5] += w * c[q].y; acc[6] += w * c[q].z; acc[7] += w * c[q].w;
+        for (int q = 0; q < kBatch; ++q) {
+          const float ws = __shfl_sync(0xffffffffu, w, (s0 + q) & 31);
+          if (s0 + q >= p.splits) continue;
+          acc[0] = fmaf(ws, a[q].x, acc[0]); acc[1] = fmaf(ws, a[q].y, acc[1]);
+          acc[2] = fmaf(ws, a[q].z, acc[2]); acc[3] = fmaf(ws, a[q].w, acc[3]);
+          acc[4] = fmaf(ws, c[q].x, acc[4]); acc[5] = fmaf(ws, c[q].y, acc[5]);
+          acc[6] = fmaf(ws, c[q].z, acc[6]); acc[7] = fmaf(ws, c[q].w, acc[7]);
         }
       }
       const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -1169,8 +1209,8 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
   if (dense) {
     const uint8_t* kr = static_cast<const uint8_t*>(d.k_ring);
     const uint8_t* vr = static_cast<const uint8_t*>(d.v_ring);
-    rc = launch_kernel(reinterpret_cast<const void*>(kv_dense_kernel), dim3(g.n_blocks, d.B), dim3(256), 0, stream, pdl,
-                       1, p, kr, vr);
+    rc = launch_kernel(reinterpret_cast<const void*>(kv_dense_kernel), dim3(4 * g.n_blocks, d.B), dim3(256), 0, stream,
+                       pdl, 1, p, kr, vr);
     if (rc) return rc;
   }
   dim3 grid(g.q_tiles, g.splits, d.B);
