@@ -160,8 +160,19 @@ typedef struct rfx_linear_desc {
    * (t / S) * y_rows_per_batch + y_row_offset + t % S; 0/0 means row t. */
   int y_rows_per_batch;
   int y_row_offset;
+  /* Optional split-K workspace (256-byte aligned, ZERO-FILLED once by the
+   * caller; every launch leaves its counters zero again).  With one of at
+   * least rfx_linear_workspace_size bytes, a many-token GEMM whose tiles
+   * leave SMs idle splits K over more CTAs and the last split of a tile sums
+   * the fp32 partials in split order (deterministic) before the epilogue.
+   * Launches sharing a workspace must not run concurrently (one stream, or
+   * ordered by events).  NULL / too small: no split. */
+  void* workspace;
+  size_t workspace_bytes;
 } rfx_linear_desc;
 int rfx_linear(const rfx_linear_desc* desc, void* stream);
+/* Bytes of split-K workspace rfx_linear would use for this descriptor (0: none). */
+int rfx_linear_workspace_size(const rfx_linear_desc* desc, size_t* bytes);
 
 /* (Ada)RMSNorm of token rows into a bf16 GEMM input:
  * y[t][k] = bf16(((x[t][k] * rstd[t]) * a1[k]) * a2[b][k] + b2[b][k]),

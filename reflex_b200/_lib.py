@@ -79,6 +79,7 @@ class LinearDesc(Structure):
         ("q_out", c_void_p), ("k_out", c_void_p), ("v_out", c_void_p), ("num_q_heads", c_int),
         ("n_tile", c_int), ("splits", c_int),
         ("y_rows_per_batch", c_int), ("y_row_offset", c_int),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -173,6 +174,7 @@ SIGNATURES = {
     "rfx_pack_weight": ([c_int, c_void_p, c_void_p, c_int, c_int, c_void_p], c_int),
     "rfx_attention": ([POINTER(AttnDesc), c_void_p], c_int),
     "rfx_attention_workspace_size": ([POINTER(AttnDesc), POINTER(c_size_t)], c_int),
+    "rfx_linear_workspace_size": ([POINTER(LinearDesc), POINTER(c_size_t)], c_int),
     "rfx_attention_noalloc": ([POINTER(AttnDesc), c_void_p], c_int),
     "rfx_time_cond": ([POINTER(TimeCondDesc), c_void_p], c_int),
     "rfx_modulation": ([POINTER(ModulationDesc), c_void_p], c_int),

@@ -101,6 +101,11 @@ struct LinParams {
   int recv_off;  // byte offset of the receive buffer [splits][2*pairs][NT] fp32
   int* status;
   unsigned long long* trace;
+  // persistent tiles with split-K (ksplit > 1): fp32 partial slots
+  // [tile][ksplit][NT][128] and per-tile arrival counters
+  int ksplit;
+  float* part;
+  int* ctr;
 };
 
 __device__ __forceinline__ void trace(const LinParams& p, int ev) {
@@ -658,7 +663,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + kPStages;  // [2]
   uint64_t* acc_free = acc_full + 2;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
-  const int n_tiles_total = (p.O / kBM) * p.n_tiles;
+  // work units: (tile, K split), the splits of a tile adjacent
+  const int n_units = (p.O / kBM) * p.n_tiles * p.ksplit;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPStages; ++i) {
       mbar_init(&full[i], 1);
@@ -689,9 +695,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol = l2_policy_evict_first();
       bool ok = true;
       bool waited = false;
-      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+      for (int un = blockIdx.x; un < n_units && ok; un += gridDim.x) {
+        const int tile = un / p.ksplit, ks = un % p.ksplit;
         const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
-        for (int kc = 0; kc < p.k_chunks; ++kc) {
+        const int kc0 = ks * p.k_chunks / p.ksplit, kc1 = (ks + 1) * p.k_chunks / p.ksplit;
+        for (int kc = kc0; kc < kc1; ++kc) {
           const int s = issued % kPStages;
           if (issued >= kPStages &&
               !(ok = mbar_wait(&empty[s], ((issued / kPStages) - 1) & 1, p.status, kDevTimeoutStageEmpty)))
@@ -717,19 +725,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t b0 = make_sdesc_sw128(smem_u32(smem + kWTileBytes), 16, 1024);
       bool ok = true;
       int it = 0, tl = 0;
-      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++tl) {
+      for (int un = blockIdx.x; un < n_units && ok; un += gridDim.x, ++tl) {
+        const int ks = un % p.ksplit;
+        const int kc0 = ks * p.k_chunks / p.ksplit, kc1 = (ks + 1) * p.k_chunks / p.ksplit;
         const int buf = tl & 1;
         if (tl >= 2 && !(ok = mbar_wait(&acc_free[buf], ((tl >> 1) - 1) & 1, p.status, kDevTimeoutMmaDone))) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * NT;
-        for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
+        for (int kc = kc0; kc < kc1; ++kc, ++it) {
           const int s = it % kPStages;
           if (!(ok = mbar_wait(&full[s], (it / kPStages) & 1, p.status, kDevTimeoutTmaFull))) break;
           tc_fence_after();
           const uint64_t off = static_cast<uint64_t>((s * kPStage) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16_ss(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ss(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[buf]);
@@ -741,7 +751,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     int tl = 0;
-    for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++tl) {
+    int* last_s = reinterpret_cast<int*>(acc_free + 2) + 1;  // the split counter outcome for all workers
+    for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++tl) {
+      const int tile = un / p.ksplit, ks = un % p.ksplit;
       const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
       const int buf = tl & 1;
       bool ok = true;
@@ -756,11 +768,75 @@ __global__ void __launch_bounds__(kThreads, 1)
           : "memory");
       if (!all) break;
       tc_fence_after();
+      bool split_last = false;
+      if (p.ksplit > 1) {
+        // this split's fp32 partial [t][row] to its slot, then the tile's arrival
+        // counter; the last split to arrive sums every slot in split order
+        float* slot = p.part + (static_cast<long>(tile) * p.ksplit + ks) * NT * 128;
+#pragma unroll 1
+        for (int c0 = 0; c0 < NT / 16; c0 += 4) {
+          uint32_t r[4][16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tmem_ld16(tmem + buf * NT + (static_cast<uint32_t>(quad * 32) << 16) + (c0 + c) * 16, r[c]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) __stcg(slot + ((c0 + c) * 16 + e) * 128 + row, __uint_as_float(r[c][e]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_free[buf]);
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (et == 0) {
+          const int old = atomicAdd(p.ctr + tile, 1);
+          if (old == p.ksplit - 1) {
+            __threadfence();
+            p.ctr[tile] = 0;  // ready for the next launch
+          }
+          *last_s = old == p.ksplit - 1 ? 1 : 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        split_last = *last_s != 0;
+        if (!split_last) continue;
+        __threadfence();
+      }
       // parts of 64 token columns: accumulator row `row` -> red[t][row], then
       // the fused epilogue of those tokens
 #pragma unroll 1
       for (int h = 0; h < NT / 64; ++h) {
-        {
+        if (split_last) {
+          // the sum of the splits' partials of tokens 64h .. 64h+63 in split
+          // order: per split 32 KB contiguous, float4 k * 128 + et holding
+          // token 4k + et / 32, rows 4 (et % 32) .. +3; 8 loads in flight per split
+          const float4* base =
+              reinterpret_cast<const float4*>(p.part + static_cast<long>(tile) * p.ksplit * NT * 128 + (64 * h) * 128);
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            float4 acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = __ldcg(base + (g * 8 + j) * 128 + et);
+#pragma unroll 1
+            for (int q = 1; q < p.ksplit; ++q) {
+              const float4* src = base + static_cast<long>(q) * (NT * 128 / 4);
+              float4 v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + (g * 8 + j) * 128 + et);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                acc[j].x += v[j].x;
+                acc[j].y += v[j].y;
+                acc[j].z += v[j].z;
+                acc[j].w += v[j].w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(red + (4 * (g * 8 + j) + (et >> 5)) * kRedLd + 4 * lane) = acc[j];
+          }
+        } else {
           uint32_t r[4][16];
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -771,7 +847,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kRedLd + row] = __uint_as_float(r[c][e]);
         }
-        if (h == NT / 64 - 1) {
+        if (h == NT / 64 - 1 && !split_last) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_free[buf]);
@@ -974,17 +1050,60 @@ int validate(const rfx_linear_desc& d) {
 }  // namespace
 
 namespace {
+// K splits of the persistent kernel's tiles: the count (1..4) that finishes
+// the units soonest, waves of units x their length (1 / ksplit) plus a tenth
+// of a unit for the partials' round trip; a split keeps at least 8 k-steps
+// and the partial slots stay within 64 MB.
+int pick_ksplit(int tiles, int k_chunks, int nt, int nsm) {
+  int best = 1;
+  double best_t = static_cast<double>((tiles + nsm - 1) / nsm);
+  for (int s = 2; s <= 4; ++s) {
+    if (k_chunks / s < 8 || static_cast<size_t>(tiles) * s * nt * 128 * 4 > (size_t(64) << 20)) break;
+    const double t = static_cast<double>((tiles * s + nsm - 1) / nsm) / s + 0.1;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+// Split-K workspace of the persistent kernel: per-tile arrival counters
+// (int, padded to 256 B) then fp32 partial slots [tile][ksplit][nt][128].
+size_t split_ctr_bytes(int tiles) { return (static_cast<size_t>(tiles) * 4 + 255) & ~size_t(255); }
+size_t split_workspace_bytes(int tiles, int ksplit, int nt) {
+  if (ksplit <= 1) return 0;
+  return split_ctr_bytes(tiles) + static_cast<size_t>(tiles) * ksplit * nt * 128 * 4;
+}
+
 // Many tokens (T > 128) with the load prologue and automatic tiling go to the
 // persistent tile kernel: 256-token tiles (more FLOPs per operand byte, the
 // per-SM operand stream being the bound) when that still gives every SM at
-// least two tiles, else 128-token tiles.  With fewer than half an SM's worth
-// of 128-token tiles the per-tile kernel's split-K keeps more SMs busy.
-// 0 = the per-tile kernel.
-int persistent_nt(const rfx_linear_desc& d, int nsm) {
-  if (d.prologue != RFX_PRO_LOAD || d.splits != 0 || d.n_tile != 0 || d.T <= 128) return 0;
+// least two tiles, else 128-token tiles, with K split over several CTAs when
+// the tiles alone leave SMs idle and the caller gave a workspace
+// (`assume_ws`: as if it had).  Without a split and with fewer than half an
+// SM's worth of 128-token tiles, the per-tile kernel's in-cluster split-K
+// keeps more SMs busy: nt = 0.
+struct TilesPlan {
+  int nt = 0, ksplit = 1;
+  size_t ws = 0;
+};
+TilesPlan plan_tiles(const rfx_linear_desc& d, int nsm, bool assume_ws) {
+  TilesPlan t;
+  if (d.prologue != RFX_PRO_LOAD || d.splits != 0 || d.n_tile != 0 || d.T <= 128) return t;
   const int m_tiles = d.O / kBM;
-  if (m_tiles * ((d.T + 255) / 256) >= 2 * nsm) return 256;
-  return 2 * m_tiles * ((d.T + 127) / 128) >= nsm ? 128 : 0;
+  t.nt = m_tiles * ((d.T + 255) / 256) >= 2 * nsm ? 256 : 128;
+  const int tiles = m_tiles * ((d.T + t.nt - 1) / t.nt);
+  t.ksplit = pick_ksplit(tiles, d.K / kBK, t.nt, nsm);
+  t.ws = split_workspace_bytes(tiles, t.ksplit, t.nt);
+  const bool have_ws =
+      assume_ws || (d.workspace && d.workspace_bytes >= t.ws && (reinterpret_cast<uintptr_t>(d.workspace) & 255) == 0);
+  if (t.ksplit > 1 && !have_ws) {
+    t.ksplit = 1;
+    t.ws = 0;
+  }
+  if (t.ksplit == 1 && 2 * tiles < nsm) t.nt = 0;
+  return t;
 }
 
 template <int NT, int EPI>
@@ -1036,8 +1155,9 @@ LinParams lin_params(const rfx_linear_desc& d) {
   return p;
 }
 
-int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, int nt, int nsm,
-                        cudaStream_t stream, bool pdl) {
+int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, const TilesPlan& tp,
+                        int nsm, cudaStream_t stream, bool pdl) {
+  const int nt = tp.nt;
   const void* fn = select_tiles(nt, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no tile kernel for this epilogue");
   const int smem = nt == 256 ? TilesLayout<256>::kSmem : TilesLayout<128>::kSmem;
@@ -1047,7 +1167,12 @@ int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const 
   p.splits = 1;
   p.n_tiles = (d.T + nt - 1) / nt;
   const int tiles = (d.O / kBM) * p.n_tiles;
-  const int grid = std::min(tiles, nsm);
+  p.ksplit = tp.ksplit;
+  if (p.ksplit > 1) {
+    p.ctr = static_cast<int*>(d.workspace);
+    p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + split_ctr_bytes(tiles));
+  }
+  const int grid = std::min(tiles * p.ksplit, nsm);
   p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(grid) * 16));
   CUtensorMap w = *tmW, x = *tmX;
   return launch_kernel(fn, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), stream, pdl, 1, w, x, p);
@@ -1064,7 +1189,7 @@ int build_linear_maps(const rfx_linear_desc& d, CUtensorMap* tmW, CUtensorMap* t
   if (rc) return rc;
   rc = make_tmap_2d(tmW, d.w, 2, d.K, d.O, static_cast<uint64_t>(d.K) * 2, kBK, kBM, true);
   if (rc) return rc;
-  const int pnt = persistent_nt(d, nsm);
+  const int pnt = plan_tiles(d, nsm, false).nt;
   return make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, pnt ? pnt : cfg.nt, true);
 }
 
@@ -1077,7 +1202,8 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   Config cfg;
   rc = pick_config(d, nsm, &cfg);
   if (rc) return rc;
-  if (const int pnt = persistent_nt(d, nsm)) return launch_linear_tiles(d, tmW, tmX, pnt, nsm, stream, pdl);
+  const TilesPlan tp = plan_tiles(d, nsm, false);
+  if (tp.nt) return launch_linear_tiles(d, tmW, tmX, tp, nsm, stream, pdl);
   const void* fn = select_kernel(cfg.nt, d.prologue, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no kernel for this configuration");
   rc = ensure_smem_attr(fn, cfg.smem, cfg.splits > 8);
@@ -1184,4 +1310,16 @@ extern "C" int rfx_linear(const rfx_linear_desc* desc, void* stream) {
   int rc = build_linear_maps(*desc, &w, &x);
   if (rc) return rc;
   return launch_linear(*desc, &w, &x, static_cast<cudaStream_t>(stream), pdl_enabled());
+}
+
+extern "C" int rfx_linear_workspace_size(const rfx_linear_desc* desc, size_t* bytes) {
+  using namespace rfx;
+  if (!desc || !bytes) return set_error(RFX_E_INVAL, "rfx_linear_workspace_size: null argument");
+  *bytes = 0;
+  int rc = validate(*desc);
+  if (rc) return rc;
+  int nsm = 148;
+  rfx_num_sms(&nsm);
+  *bytes = plan_tiles(*desc, nsm, true).ws;
+  return RFX_OK;
 }

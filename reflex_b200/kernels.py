@@ -108,7 +108,8 @@ def pack_weight(kind: int, w: torch.Tensor) -> torch.Tensor:
 def linear_desc(*, w, x, T, S, prologue=L.RFX_PRO_LOAD, epilogue=L.RFX_EPI_STORE, y=None, norm_a1=None,
                 norm_a2=None, norm_b2=None, norm_ab_stride=0, eps=1e-6, bias=None, gate=None, gate_stride=0,
                 rope_table=None, positions=None, q_out=None, k_out=None, v_out=None, num_q_heads=0,
-                n_tile=0, splits=0, y_rows_per_batch=0, y_row_offset=0) -> L.LinearDesc:
+                n_tile=0, splits=0, y_rows_per_batch=0, y_row_offset=0,
+                workspace=None) -> L.LinearDesc:
     _need_cuda(w, x, y)
     for t in (w, x, y, q_out, k_out, v_out):
         if t is not None and t.dtype != torch.bfloat16:
@@ -134,12 +135,27 @@ def linear_desc(*, w, x, T, S, prologue=L.RFX_PRO_LOAD, epilogue=L.RFX_EPI_STORE
     d.num_q_heads = num_q_heads
     d.n_tile, d.splits = n_tile, splits
     d.y_rows_per_batch, d.y_row_offset = y_rows_per_batch, y_row_offset
+    d.workspace = L.ptr(workspace)
+    d.workspace_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     return d
 
 
 def linear(**kw) -> None:
     d = linear_desc(**kw)
     L.call("rfx_linear", ctypes.byref(d), _stream())
+
+
+def linear_workspace_bytes(d: L.LinearDesc) -> int:
+    """Split-K workspace rfx_linear would use for `d` (0: none)."""
+    n = ctypes.c_size_t(0)
+    L.call("rfx_linear_workspace_size", ctypes.byref(d), ctypes.byref(n))
+    return n.value
+
+
+def linear_workspace(nbytes: int, device) -> torch.Tensor:
+    """A zero-filled split-K workspace (the counters start at zero); pass
+    aligned_ptr(ws, 256) or a 256-byte aligned slice of it."""
+    return torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=device)
 
 
 # ------------------------------------------------------------- attention ---

@@ -77,6 +77,7 @@ class PrefixEngine:
             self.valid.append(m.to(dev))
         self.kv_splits = kv_splits
         self.workspace = None
+        self.split_ws = None  # split-K workspace of the GEMMs (zero-filled; one stream)
         self.frames = 0  # frames appended so far
 
     def load_context(self, layer: int, k: torch.Tensor, v: torch.Tensor, slot_base: int = 0) -> None:
@@ -123,6 +124,13 @@ class PrefixEngine:
         for d in attn_descs:
             if need:
                 d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace, 1024), need
+        lin = [d for kind, d, _ in out if kind == "linear"]
+        need = max(K.linear_workspace_bytes(d) for d in lin)
+        if need and (self.split_ws is None or self.split_ws.numel() < need + 256):
+            self.split_ws = K.linear_workspace(need + 256, self.dev)
+        for d in lin:
+            if need:
+                d.workspace, d.workspace_bytes = K.aligned_ptr(self.split_ws, 256), need
         return out
 
     def run(self, emb: torch.Tensor | None = None) -> None:

@@ -77,3 +77,23 @@ def test_plan_calls_out_of_order():
         assert lib.rfx_plan_num_launches(plan, ctypes.byref(n)) == _lib.RFX_OK and n.value == 0
     finally:
         assert lib.rfx_plan_destroy(plan) == _lib.RFX_OK
+
+
+@pytest.mark.parametrize("T,O,K,want", [
+    (768, 2048, 16384, 512 + 96 * 3 * 128 * 128 * 4),  # down_proj of a 768-token frame: 96 tiles, K split 3
+    (768, 32768, 2048, 0),                              # gate/up: 768 tiles fill the SMs
+    (50, 2048, 16384, 0),                               # few tokens: the per-tile kernel
+])
+def test_linear_split_workspace_size(T, O, K, want):
+    """The split-K workspace query needs no device: counters padded to 256 B
+    plus fp32 partial slots [tile][split][128 tokens][128 rows] (148 SMs
+    assumed when no GPU answers)."""
+    lib = _lib.load()
+    d = _lib.LinearDesc()
+    d.T, d.O, d.K, d.tokens_per_batch = T, O, K, T
+    d.prologue, d.epilogue = _lib.RFX_PRO_LOAD, _lib.RFX_EPI_STORE
+    d.w, d.x, d.y = 1 << 20, 2 << 20, 3 << 20
+    d.ldx, d.ldy = K, O
+    n = ctypes.c_size_t(7)
+    assert lib.rfx_linear_workspace_size(ctypes.byref(d), ctypes.byref(n)) == _lib.RFX_OK
+    assert n.value == want

@@ -159,6 +159,82 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
         torch.testing.assert_close(got[0].float().cpu(), _mm(x, w).cpu() + bias.cpu(), atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv"])
+@pytest.mark.parametrize("B,S", [(1, 768), (2, 300)])
+def test_linear_split_k_workspace(K, L, epi, B, S):
+    """With a zero-filled workspace, a many-token GEMM whose tiles leave SMs
+    idle (a 2048-row weight at 600 or 768 tokens: 80 or 96 tiles of 128
+    tokens) splits K over three CTAs per tile (ragged: 32 k-steps as 10/11/11);
+    the last split to arrive sums the fp32 partials in split order and runs
+    the fused epilogue.  Checked against the fp32 product (store), against the
+    unsplit persistent kernel within bf16 rounding (every epilogue), for
+    run-to-run bit identity over back-to-back launches on one stream, and for
+    counters left at zero.  A workspace one byte short disables the split and
+    gives the unsplit result exactly."""
+    r = gen(7)
+    T, Kd, D = B * S, 2048, 256
+    Hq = 6  # QKV: (6 + 2) x 256 = 2048 rows
+    O = 2048
+    x = r(T, Kd).bfloat16().cuda()
+    if epi == "geglu":
+        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(O, Kd, std=0.03).bfloat16().cuda())
+    elif epi == "qkv":
+        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r(O, Kd, std=0.03).bfloat16().cuda())
+        tab = rope_table().cuda()
+        pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
+    else:
+        w = r(O, Kd, std=0.03).bfloat16().cuda()
+    bias = r(O, std=0.1).cuda()
+    gate = torch.from_numpy(bf16_round(r(B, O).numpy())).cuda()
+    y0 = r(T, O).bfloat16().cuda()
+
+    def run(ws):
+        kw = dict(w=w, x=x, T=T, S=S, workspace=ws)
+        if epi == "store":
+            outs = [torch.empty(T, O, dtype=torch.bfloat16, device="cuda")]
+            K.linear(y=outs[0], bias=bias, **kw)
+        elif epi == "residual":
+            outs = [y0.clone()]
+            K.linear(epilogue=L.RFX_EPI_RESIDUAL, y=outs[0], gate=gate, gate_stride=O, **kw)
+        elif epi == "geglu":
+            outs = [torch.empty(T, O // 2, dtype=torch.bfloat16, device="cuda")]
+            K.linear(epilogue=L.RFX_EPI_GEGLU, y=outs[0], **kw)
+        else:
+            outs = [torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device="cuda"),
+                    torch.empty(T, D, dtype=torch.bfloat16, device="cuda"),
+                    torch.empty(T, D, dtype=torch.bfloat16, device="cuda")]
+            K.linear(epilogue=L.RFX_EPI_QKV_ROPE, rope_table=tab, positions=pos, q_out=outs[0], k_out=outs[1],
+                     v_out=outs[2], num_q_heads=Hq, **kw)
+        return outs
+
+    tiles = (O // 128) * ((T + 127) // 128)
+    ctr_bytes = (tiles * 4 + 255) // 256 * 256
+    probe = K.linear_desc(w=w, x=x, T=T, S=S, y=torch.empty(T, O, dtype=torch.bfloat16, device="cuda"))
+    need = K.linear_workspace_bytes(probe)
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    if nsm == 148:
+        assert need == ctr_bytes + tiles * 3 * 128 * 128 * 4
+    assert need > 0
+    ws = K.linear_workspace(need, "cuda")
+    assert ws.data_ptr() % 256 == 0
+    plain = run(None)
+    split = [run(ws) for _ in range(3)]  # back-to-back on one stream (PDL overlap)
+    short = run(ws[:need - 1])
+    torch.cuda.synchronize()
+    assert K.device_status() == 0
+    assert int(ws[:ctr_bytes].count_nonzero()) == 0  # counters back at zero
+    for later in split[1:]:
+        for a, b in zip(split[0], later):
+            assert torch.equal(a, b)
+    for a, b in zip(short, plain):
+        assert torch.equal(a, b)
+    for a, b in zip(split[0], plain):
+        torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=1.6e-2)
+    if epi == "store":
+        torch.testing.assert_close(split[0][0].float().cpu(), _mm(x, w).cpu() + bias.cpu(), atol=ATOL, rtol=RTOL)
+
+
 def _norm_ref(x, a1, a2, b2, S, eps=1e-6):
     xf = x.float().cpu()
     rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
