@@ -246,6 +246,56 @@ __device__ __forceinline__ void epilogue_store(const LinParams& p, int m, int i,
   }
 }
 
+// Epilogue operands that do not depend on the accumulator, requested one
+// 64-token part ahead by the persistent tile kernel: the residual rows
+// (packed bf16) or the RoPE cos / sin of the token.  Gates and bias are
+// per-row vectors every item of a thread shares (cache hits), read at store time.
+struct EpiPre {
+  uint2 y0, y1;
+  float4 c, s;
+};
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_prefetch(const LinParams& p, int m, int i, int t, EpiPre& pre) {
+  if (EPI == kEpiResidual) {
+    const int b = t / p.S;
+    const long yrow = static_cast<long>(b) * p.y_rps + p.y_off + (t - b * p.S);
+    const __nv_bfloat16* y = p.y + yrow * p.ldy + m * kBM + i;
+    pre.y0 = *reinterpret_cast<const uint2*>(y);
+    pre.y1 = *reinterpret_cast<const uint2*>(y + 64);
+  } else if (EPI == kEpiQkvRope) {
+    if ((m >> 1) <= p.hq) {
+      int pos = p.pos[t];
+      pos = pos < 0 ? 0 : (pos >= p.rope_max_pos ? p.rope_max_pos - 1 : pos);
+      const float* cs = p.rope + static_cast<long>(pos) * 256 + (m & 1) * 64 + i;
+      pre.c = *reinterpret_cast<const float4*>(cs);
+      pre.s = *reinterpret_cast<const float4*>(cs + 128);
+    }
+  }
+}
+
+// The item's full operand set from its prefetched part (same values as epilogue_fetch).
+template <int EPI>
+__device__ __forceinline__ void epilogue_expand(const LinParams& p, int m, int i, int t, const EpiPre& pre,
+                                                EpiIn& in) {
+  if (EPI == kEpiResidual) {
+    unpack_bf16x4(pre.y0, in.r0);
+    unpack_bf16x4(pre.y1, in.r1);
+    if (p.gate) {
+      const float* g = p.gate + static_cast<long>(t / p.S) * p.gate_stride + m * kBM + i;
+      const float4 a = *reinterpret_cast<const float4*>(g);
+      const float4 c = *reinterpret_cast<const float4*>(g + 64);
+      in.g0[0] = a.x; in.g0[1] = a.y; in.g0[2] = a.z; in.g0[3] = a.w;
+      in.g1[0] = c.x; in.g1[1] = c.y; in.g1[2] = c.z; in.g1[3] = c.w;
+    }
+  } else if (EPI == kEpiStore || EPI == kEpiSilu) {
+    epilogue_fetch<EPI>(p, m, i, t, in);
+  } else if (EPI == kEpiQkvRope) {
+    in.c[0] = pre.c.x; in.c[1] = pre.c.y; in.c[2] = pre.c.z; in.c[3] = pre.c.w;
+    in.s[0] = pre.s.x; in.s[1] = pre.s.y; in.s[2] = pre.s.z; in.s[3] = pre.s.w;
+  }
+}
+
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 }
@@ -626,17 +676,20 @@ __global__ void __launch_bounds__(kThreads, NT == 128 ? 2 : 1)
 }
 
 // ----------------------------------------------------- persistent tiles ---
-// Many tokens (T > 128, load prologue): one CTA per SM walks tiles
-// t = blockIdx.x, blockIdx.x + gridDim.x, ... in weight-tile-major order (a
+// Many tokens (T > 128, load prologue): one CTA per SM walks work units
+// u = blockIdx.x, blockIdx.x + gridDim.x, ... in weight-tile-major order (a
 // weight tile's token tiles are adjacent, so they run at the same time and
-// the tile comes from HBM once).  The producer streams W / X k-steps through a
-// 4-stage ring without stopping at tile boundaries; the MMA issuer fills two
-// TMEM accumulators alternately; warps 2-5 drain the other one (TMEM ->
-// shared-memory transpose -> the fused epilogue), so a tile's epilogue runs
-// under the next tile's mainloop.
+// the tile comes from HBM once); a unit is a tile, or one of its K splits
+// when split-K is on.  The producer streams W / X k-steps through a 4-stage
+// ring without stopping at unit boundaries; the MMA issuer fills two TMEM
+// accumulators alternately; warps 2-9 drain the other one (TMEM ->
+// shared-memory transpose -> the fused epilogue, four items per thread with
+// their operands in flight together), so a tile's epilogue runs under the
+// next unit's mainloop.
 // Layout per token tile NT (128 or 256): a 4-stage ring of W [128 x 64] +
 // X [NT x 64] bf16, the epilogue's transpose buffer for 64 tokens at a time.
 constexpr int kPStages = 4;
+constexpr int kTThreads = 320;  // TMA producer warp, MMA warp, 8 epilogue warps
 template <int NT>
 struct TilesLayout {
   static constexpr int kStage = kWTileBytes + NT * 128;
@@ -647,7 +700,7 @@ struct TilesLayout {
 static_assert(TilesLayout<256>::kSmem <= kSmemLimit, "256-token tiles fit in shared memory");
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kTThreads, 1)
     linear_tiles_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                         const LinParams p) {
   using Lay = TilesLayout<NT>;
@@ -672,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_free[i], 4);
+      mbar_init(&acc_free[i], kTThreads / 32 - 2);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
@@ -747,49 +800,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     pdl_wait();
-    const int et = threadIdx.x - 64;  // 0..127
+    // 8 epilogue warps, two per TMEM lane quadrant: warps 2-5 take the first
+    // 32 token columns of each 64-token part, warps 6-9 the other 32
+    const int et = threadIdx.x - 64;  // 0..255
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
+    const int ch = et >> 7;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     int tl = 0;
     int* last_s = reinterpret_cast<int*>(acc_free + 2) + 1;  // the split counter outcome for all workers
     for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++tl) {
       const int tile = un / p.ksplit, ks = un % p.ksplit;
       const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
       const int buf = tl & 1;
+      // a thread's items: one row group, tokens 16 apart; the first part's
+      // operands are requested before the accumulator is waited for
+      const int irow = (et & 15) * 4;
+      EpiPre cur[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = n0 + (et >> 4) + 16 * u;
+        if (t < p.T) epilogue_prefetch<EPI>(p, m, irow, t, cur[u]);
+      }
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&acc_full[buf], (tl >> 1) & 1, p.status, kDevTimeoutMmaDone);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       // every epilogue warp agrees before anyone leaves the loop
       uint32_t all;
       asm volatile(
-          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
           : "=r"(all)
           : "r"(ok ? 1u : 0u)
           : "memory");
       if (!all) break;
       tc_fence_after();
+      const uint32_t acc = tmem + buf * NT + lane_base;
       bool split_last = false;
       if (p.ksplit > 1) {
         // this split's fp32 partial [t][row] to its slot, then the tile's arrival
         // counter; the last split to arrive sums every slot in split order
         float* slot = p.part + (static_cast<long>(tile) * p.ksplit + ks) * NT * 128;
 #pragma unroll 1
-        for (int c0 = 0; c0 < NT / 16; c0 += 4) {
-          uint32_t r[4][16];
+        for (int h = 0; h < NT / 64; ++h) {
+          uint32_t r[2][16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tmem_ld16(tmem + buf * NT + (static_cast<uint32_t>(quad * 32) << 16) + (c0 + c) * 16, r[c]);
+          for (int c = 0; c < 2; ++c) tmem_ld16(acc + 64 * h + 32 * ch + 16 * c, r[c]);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) __stcg(slot + ((c0 + c) * 16 + e) * 128 + row, __uint_as_float(r[c][e]));
+            for (int e = 0; e < 16; ++e)
+              __stcg(slot + (64 * h + 32 * ch + 16 * c + e) * 128 + row, __uint_as_float(r[c][e]));
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_free[buf]);
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (et == 0) {
           const int old = atomicAdd(p.ctr + tile, 1);
           if (old == p.ksplit - 1) {
@@ -798,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           *last_s = old == p.ksplit - 1 ? 1 : 0;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         split_last = *last_s != 0;
         if (!split_last) continue;
         __threadfence();
@@ -809,75 +876,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < NT / 64; ++h) {
         if (split_last) {
           // the sum of the splits' partials of tokens 64h .. 64h+63 in split
-          // order: per split 32 KB contiguous, float4 k * 128 + et holding
-          // token 4k + et / 32, rows 4 (et % 32) .. +3; 8 loads in flight per split
+          // order: per split 32 KB contiguous, float4 k * 256 + et holding
+          // token 8k + et / 32, rows 4 (et % 32) .. +3
           const float4* base =
               reinterpret_cast<const float4*>(p.part + static_cast<long>(tile) * p.ksplit * NT * 128 + (64 * h) * 128);
+          float4 sum[8];
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            float4 acc[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = __ldcg(base + (g * 8 + j) * 128 + et);
+          for (int j = 0; j < 8; ++j) sum[j] = __ldcg(base + j * 256 + et);
 #pragma unroll 1
-            for (int q = 1; q < p.ksplit; ++q) {
-              const float4* src = base + static_cast<long>(q) * (NT * 128 / 4);
-              float4 v[8];
+          for (int q = 1; q < p.ksplit; ++q) {
+            const float4* src = base + static_cast<long>(q) * (NT * 128 / 4);
+            float4 v[8];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + (g * 8 + j) * 128 + et);
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 256 + et);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                acc[j].x += v[j].x;
-                acc[j].y += v[j].y;
-                acc[j].z += v[j].z;
-                acc[j].w += v[j].w;
-              }
+            for (int j = 0; j < 8; ++j) {
+              sum[j].x += v[j].x;
+              sum[j].y += v[j].y;
+              sum[j].z += v[j].z;
+              sum[j].w += v[j].w;
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<float4*>(red + (4 * (g * 8 + j) + (et >> 5)) * kRedLd + 4 * lane) = acc[j];
           }
-        } else {
-          uint32_t r[4][16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tmem_ld16(tmem + buf * NT + (static_cast<uint32_t>(quad * 32) << 16) + (4 * h + c) * 16, r[c]);
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(red + (8 * j + (et >> 5)) * kRedLd + 4 * lane) = sum[j];
+        } else {
+          uint32_t r[2][16];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) tmem_ld16(acc + 64 * h + 32 * ch + 16 * c, r[c]);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) red[(c * 16 + e) * kRedLd + row] = __uint_as_float(r[c][e]);
+            for (int e = 0; e < 16; ++e) red[(32 * ch + 16 * c + e) * kRedLd + row] = __uint_as_float(r[c][e]);
+          if (h == NT / 64 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_free[buf]);
+          }
         }
-        if (h == NT / 64 - 1 && !split_last) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_free[buf]);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         // items: 16 groups of 4 row pairs x 64 tokens; 16 consecutive threads
-        // cover one token's 64 pairs (coalesced stores); operands of 4 items in flight
+        // cover one token's 64 pairs (coalesced stores); the next part's
+        // operands are requested before this part's stores
         const int t0 = n0 + 64 * h;
-#pragma unroll 1
-        for (int it0 = et; it0 < 16 * 64; it0 += 4 * 128) {
-          EpiIn in[4];
+        EpiPre nxt[4];
+        if (h + 1 < NT / 64) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int it = it0 + u * 128;
-            const int t = t0 + (it >> 4);
-            if (t < p.T) epilogue_fetch<EPI>(p, m, (it & 15) * 4, t, in[u]);
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int it = it0 + u * 128;
-            const int tt = it >> 4, i = (it & 15) * 4;
-            if (t0 + tt >= p.T) continue;
-            const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + i);
-            const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + i + 64);
-            const float v0[4] = {a.x, a.y, a.z, a.w};
-            const float v1[4] = {c.x, c.y, c.z, c.w};
-            epilogue_store<EPI>(p, m, i, t0 + tt, v0, v1, in[u]);
+            const int t = t0 + 64 + (et >> 4) + 16 * u;
+            if (t < p.T) epilogue_prefetch<EPI>(p, m, irow, t, nxt[u]);
           }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // red is free again
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int tt = (et >> 4) + 16 * u;
+          if (t0 + tt >= p.T) continue;
+          EpiIn in;
+          epilogue_expand<EPI>(p, m, irow, t0 + tt, cur[u], in);
+          const float4 a = *reinterpret_cast<const float4*>(red + tt * kRedLd + irow);
+          const float4 c = *reinterpret_cast<const float4*>(red + tt * kRedLd + irow + 64);
+          const float v0[4] = {a.x, a.y, a.z, a.w};
+          const float v1[4] = {c.x, c.y, c.z, c.w};
+          epilogue_store<EPI>(p, m, irow, t0 + tt, v0, v1, in);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) cur[u] = nxt[u];
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // red is free again
       }
     }
   }
@@ -1052,13 +1117,14 @@ int validate(const rfx_linear_desc& d) {
 namespace {
 // K splits of the persistent kernel's tiles: the count (1..4) that finishes
 // the units soonest, waves of units x their length (1 / ksplit) plus a tenth
-// of a unit for the partials' round trip; a split keeps at least 8 k-steps
-// and the partial slots stay within 64 MB.
+// of a unit for the partials' round trip.  A split keeps at least 32 k-steps
+// (shorter units do not cover the epilogue of the split that sums), and the
+// partial slots stay within 64 MB.
 int pick_ksplit(int tiles, int k_chunks, int nt, int nsm) {
   int best = 1;
   double best_t = static_cast<double>((tiles + nsm - 1) / nsm);
   for (int s = 2; s <= 4; ++s) {
-    if (k_chunks / s < 8 || static_cast<size_t>(tiles) * s * nt * 128 * 4 > (size_t(64) << 20)) break;
+    if (k_chunks / s < 32 || static_cast<size_t>(tiles) * s * nt * 128 * 4 > (size_t(64) << 20)) break;
     const double t = static_cast<double>((tiles * s + nsm - 1) / nsm) / s + 0.1;
     if (t < best_t - 1e-9) {
       best_t = t;
@@ -1175,7 +1241,7 @@ int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const 
   const int grid = std::min(tiles * p.ksplit, nsm);
   p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(grid) * 16));
   CUtensorMap w = *tmW, x = *tmX;
-  return launch_kernel(fn, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), stream, pdl, 1, w, x, p);
+  return launch_kernel(fn, dim3(grid), dim3(kTThreads), static_cast<size_t>(smem), stream, pdl, 1, w, x, p);
 }
 }  // namespace
 

@@ -165,7 +165,8 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
 def test_linear_split_k_workspace(K, L, epi, B, S):
     """With a zero-filled workspace, a many-token GEMM whose tiles leave SMs
     idle (a 2048-row weight at 600 or 768 tokens: 80 or 96 tiles of 128
-    tokens) splits K over three CTAs per tile (ragged: 32 k-steps as 10/11/11);
+    tokens, K = 8192) splits K over three CTAs per tile (ragged: 128 k-steps
+    as 42/43/43);
     the last split to arrive sums the fp32 partials in split order and runs
     the fused epilogue.  Checked against the fp32 product (store), against the
     unsplit persistent kernel within bf16 rounding (every epilogue), for
@@ -173,18 +174,18 @@ def test_linear_split_k_workspace(K, L, epi, B, S):
     counters left at zero.  A workspace one byte short disables the split and
     gives the unsplit result exactly."""
     r = gen(7)
-    T, Kd, D = B * S, 2048, 256
+    T, Kd, D = B * S, 8192, 256
     Hq = 6  # QKV: (6 + 2) x 256 = 2048 rows
     O = 2048
     x = r(T, Kd).bfloat16().cuda()
     if epi == "geglu":
-        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(O, Kd, std=0.03).bfloat16().cuda())
+        w = K.pack_weight(L.RFX_PACK_GATE_UP, r(O, Kd, std=0.011).bfloat16().cuda())
     elif epi == "qkv":
-        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r(O, Kd, std=0.03).bfloat16().cuda())
+        w = K.pack_weight(L.RFX_PACK_QKV_ROPE, r(O, Kd, std=0.011).bfloat16().cuda())
         tab = rope_table().cuda()
         pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
     else:
-        w = r(O, Kd, std=0.03).bfloat16().cuda()
+        w = r(O, Kd, std=0.011).bfloat16().cuda()
     bias = r(O, std=0.1).cuda()
     gate = torch.from_numpy(bf16_round(r(B, O).numpy())).cuda()
     y0 = r(T, O).bfloat16().cuda()
@@ -230,7 +231,9 @@ def test_linear_split_k_workspace(K, L, epi, B, S):
     for a, b in zip(short, plain):
         assert torch.equal(a, b)
     for a, b in zip(split[0], plain):
-        torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=1.6e-2)
+        # bf16 roundings of two fp32 sums: a one-ulp flip of a RoPE input
+        # (outputs of std ~1) moves a cancelling output by up to two ulps
+        torch.testing.assert_close(a.float(), b.float(), atol=3e-2, rtol=1.6e-2)
     if epi == "store":
         torch.testing.assert_close(split[0][0].float().cpu(), _mm(x, w).cpu() + bias.cpu(), atol=ATOL, rtol=RTOL)
 
