@@ -363,6 +363,9 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const NormParams p) {
   constexpr int kMaxChunks = 4;  // K <= 4096
   __shared__ float red[4];
   pdl_wait();
+  // the next kernel may start its set-up (barriers, TMEM, weight prefetch)
+  // now; its griddepcontrol.wait still waits for all of this grid
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   const int b = t / p.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -417,7 +420,6 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const NormParams p) {
     *reinterpret_cast<uint4*>(p.y + static_cast<long>(t) * p.ldy + k) =
         make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
   }
-  pdl_launch_dependents();
 }
 
 struct CopyRowsParams {

@@ -76,6 +76,9 @@ struct QuantArgs {
 template <typename Tin, int MODE>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) kv_quant_append_kernel(const QuantArgs a) {
   pdl_wait();
+  // the next kernel may start its set-up now; its griddepcontrol.wait still
+  // waits for all of this grid
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long row = static_cast<long>(blockIdx.x) * kWarpsPerBlock + warp;
   const long rows = static_cast<long>(a.B) * a.H * a.L;
@@ -140,7 +143,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) kv_quant_append_kernel(co
     }
     *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace

@@ -92,7 +92,8 @@ def test_linear_store(K, T, n_tile, splits):
     torch.testing.assert_close(y.float().cpu(), ref, atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv", "store_wide", "geglu_wide"])
+@pytest.mark.parametrize("epi", ["store", "residual", "geglu", "qkv",
+                                 "store_wide", "residual_wide", "geglu_wide", "qkv_wide"])
 @pytest.mark.parametrize("B,S", [(1, 300), (2, 384), (1, 768)])
 def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     """T > 128 tokens with the load prologue run the persistent tile kernel (two
@@ -101,7 +102,10 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     token tile and no split-K, so the outputs are bit-identical to it for every
     epilogue, with ragged last token tiles and several batches; the store
     epilogue is also checked against the fp32 product.  The *_wide cases have
-    16384 output rows: with enough tiles the kernel uses 256-token tiles."""
+    16384 output rows: enough pair tiles for CTA pairs (one cta_group::2 MMA
+    of 256 rows per pair, each CTA staging its own 128 weight rows and half of
+    the tokens; 192-token pair tiles at 300 tokens, 256 at 768), compared with
+    the per-tile kernel at 256-token tiles."""
     r = gen(6)
     T, Kd, Hq, D = B * S, 1024, 8, 256
     x = r(T, Kd).bfloat16().cuda()
@@ -109,7 +113,7 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     epi = epi.replace("_wide", "")
     # output rows (2F for gate/up): enough 128-token tiles for the persistent kernel
     O = 16384 if wide else 4096
-    Hq = 14  # QKV: (14 + 2) x 256 = 4096 rows
+    Hq = 62 if wide else 14  # QKV: (Hq + 2) x 256 = 16384 or 4096 rows
 
     def run(tiling):
         kw = dict(w=w, x=x, T=T, S=S, n_tile=tiling[0], splits=tiling[1])
@@ -147,7 +151,9 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
         tab = rope_table().cuda()
         pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
     nsm = torch.cuda.get_device_properties(0).multi_processor_count
-    nt = 256 if (O // 128) * ((T + 255) // 256) >= 2 * nsm else 128
+    pair = (O // 128) % 2 == 0 and any((O // 256) * ((T + w - 1) // w) >= nsm // 2 for w in (192, 256))
+    assert pair == wide
+    nt = 256 if pair or (O // 128) * ((T + 255) // 256) >= 2 * nsm else 128
     assert nt == 256 or 2 * (O // 128) * ((T + 127) // 128) >= nsm  # the persistent kernel serves these shapes
     got = run((0, 0))       # persistent tile kernel
     ref = run((nt, 1))      # per-tile kernel, same token tile
