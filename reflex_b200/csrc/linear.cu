@@ -690,32 +690,25 @@ __global__ void __launch_bounds__(kThreads, NT == 128 ? 2 : 1)
 // X [NT x 64] bf16, the epilogue's transpose buffer for 64 tokens at a time.
 constexpr int kPStages = 4;
 constexpr int kTThreads = 320;  // TMA producer warp, MMA warp, 8 epilogue warps
-// CTA pairs (PAIR): 256 weight rows x NT tokens per pair tile; each CTA
-// stages its own 128 weight rows and NT / 2 of the tokens (a 6-stage ring)
-// and receives its 128 rows x NT tokens in TMEM.
-template <int NT, bool PAIR = false>
+template <int NT>
 struct TilesLayout {
-  static constexpr int kStages = PAIR ? 6 : kPStages;
-  static constexpr int kXRows = PAIR ? NT / 2 : NT;
-  static constexpr int kStage = kWTileBytes + kXRows * 128;
-  static constexpr int kOffRed = kStages * kStage;              // [64 tokens][kRedLd] fp32
+  static constexpr int kStage = kWTileBytes + NT * 128;
+  static constexpr int kOffRed = kPStages * kStage;            // [64 tokens][kRedLd] fp32
   static constexpr int kOffSmall = kOffRed + 64 * kRedLd * 4;
   static constexpr int kSmem = kOffSmall + 128 + 1024;
 };
 static_assert(TilesLayout<256>::kSmem <= kSmemLimit, "256-token tiles fit in shared memory");
-static_assert(TilesLayout<256, true>::kSmem <= kSmemLimit, "pair tiles fit in shared memory");
 // TMEM columns of the two accumulators (allocations are powers of two)
 template <int NT>
 constexpr uint32_t tiles_tmem_cols() {
   return NT <= 128 ? 256u : 512u;
 }
 
-template <int NT, int EPI, bool PAIR = false>
+template <int NT, int EPI>
 __global__ void __launch_bounds__(kTThreads, 1)
     linear_tiles_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                         const LinParams p) {
-  using Lay = TilesLayout<NT, PAIR>;
-  constexpr int kPStages = Lay::kStages;
+  using Lay = TilesLayout<NT>;
   constexpr int kPStage = Lay::kStage;
   constexpr int kPOffRed = Lay::kOffRed;
   constexpr int kPOffSmall = Lay::kOffSmall;
@@ -728,13 +721,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
   uint64_t* acc_full = empty + kPStages;  // [2]
   uint64_t* acc_free = acc_full + 2;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
-  // work units: (tile, K split), the splits of a tile adjacent; with PAIR a
-  // unit is a pair tile (no split) and the cluster walks them
-  const uint32_t rank = PAIR ? cluster_ctarank() : 0;
-  const bool leader = rank == 0;
-  const int n_units = PAIR ? (p.O / (2 * kBM)) * p.n_tiles : (p.O / kBM) * p.n_tiles * p.ksplit;
-  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-  const int ustep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // work units: (tile, K split), the splits of a tile adjacent
+  const int n_units = (p.O / kBM) * p.n_tiles * p.ksplit;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPStages; ++i) {
       mbar_init(&full[i], 1);
@@ -742,27 +730,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      // with PAIR the even CTA's barrier collects both CTAs' epilogue warps
-      mbar_init(&acc_free[i], (PAIR ? 2 : 1) * (kTThreads / 32 - 2));
+      mbar_init(&acc_free[i], kTThreads / 32 - 2);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    if constexpr (PAIR) {
-      tmem_alloc_pair(tmem_slot, tiles_tmem_cols<NT>());
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(tmem_slot, tiles_tmem_cols<NT>());
-      tmem_relinquish();
-    }
+    tmem_alloc(tmem_slot, tiles_tmem_cols<NT>());
+    tmem_relinquish();
   }
   tc_fence_before();
-  if constexpr (PAIR)
-    cluster_sync();  // both CTAs' barriers initialised before any remote arrival
-  else
-    __syncthreads();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
@@ -774,10 +753,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
       const uint64_t pol = l2_policy_evict_first();
       bool ok = true;
       bool waited = false;
-      for (int un = unit0; un < n_units && ok; un += ustep) {
+      for (int un = blockIdx.x; un < n_units && ok; un += gridDim.x) {
         const int tile = un / p.ksplit, ks = un % p.ksplit;
-        const int m = PAIR ? 2 * (tile / p.n_tiles) + static_cast<int>(rank) : tile / p.n_tiles;
-        const int n0 = (tile % p.n_tiles) * NT;
+        const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
         const int kc0 = ks * p.k_chunks / p.ksplit, kc1 = (ks + 1) * p.k_chunks / p.ksplit;
         for (int kc = kc0; kc < kc1; ++kc) {
           const int s = issued % kPStages;
@@ -785,25 +763,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
               !(ok = mbar_wait(&empty[s], ((issued / kPStages) - 1) & 1, p.status, kDevTimeoutStageEmpty)))
             break;
           uint8_t* st = smem + s * kPStage;
-          if constexpr (PAIR) {
-            // both CTAs' bytes count on the even CTA's full barrier
-            const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
-            if (leader) mbar_arrive_expect_tx(&full[s], 2 * kPStage);
-            tma_load_2d_pair(st, &tmW, fb, kc * kBK, m * kBM, pol);
-            if (!waited) {
-              pdl_wait();
-              waited = true;
-            }
-            tma_load_2d_pair(st + kWTileBytes, &tmX, fb, kc * kBK, n0 + static_cast<int>(rank) * Lay::kXRows);
-          } else {
-            mbar_arrive_expect_tx(&full[s], kPStage);
-            tma_load_2d_hint(st, &tmW, &full[s], kc * kBK, m * kBM, pol);
-            if (!waited) {  // the activations come from the previous kernel
-              pdl_wait();
-              waited = true;
-            }
-            tma_load_2d(st + kWTileBytes, &tmX, &full[s], kc * kBK, n0);
+          mbar_arrive_expect_tx(&full[s], kPStage);
+          tma_load_2d_hint(st, &tmW, &full[s], kc * kBK, m * kBM, pol);
+          if (!waited) {  // the activations come from the previous kernel
+            pdl_wait();
+            waited = true;
           }
+          tma_load_2d(st + kWTileBytes, &tmX, &full[s], kc * kBK, n0);
           ++issued;
         }
       }
@@ -811,13 +777,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
   } else if (warp == 1) {
     pdl_wait();
-    if (lane == 0 && (!PAIR || leader)) {
-      constexpr uint32_t idesc = make_idesc_f16(PAIR ? 2 * kBM : kBM, NT, true);
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(kBM, NT, true);
       const uint64_t a0 = make_sdesc_sw128(smem_u32(smem), 16, 1024);
       const uint64_t b0 = make_sdesc_sw128(smem_u32(smem + kWTileBytes), 16, 1024);
       bool ok = true;
       int it = 0, tl = 0;
-      for (int un = unit0; un < n_units && ok; un += ustep, ++tl) {
+      for (int un = blockIdx.x; un < n_units && ok; un += gridDim.x, ++tl) {
         const int ks = un % p.ksplit;
         const int kc0 = ks * p.k_chunks / p.ksplit, kc1 = (ks + 1) * p.k_chunks / p.ksplit;
         const int buf = tl & 1;
@@ -829,27 +795,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
           if (!(ok = mbar_wait(&full[s], (it / kPStages) & 1, p.status, kDevTimeoutTmaFull))) break;
           tc_fence_after();
           const uint64_t off = static_cast<uint64_t>((s * kPStage) >> 4);
-          if constexpr (PAIR) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16_ss_pair(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
-            umma_commit_pair(smem_u32(&empty[s]));
-            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
-          } else {
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16_ss(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
-            umma_commit(&empty[s]);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_ss(acc, a0 + off + kk * 2, b0 + off + kk * 2, idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
         }
-        if (ok) {
-          if constexpr (PAIR) {
-            umma_commit_pair(smem_u32(&acc_full[buf]));
-            umma_commit_pair(mapa_shared(smem_u32(&acc_full[buf]), 1));
-          } else {
-            umma_commit(&acc_full[buf]);
-          }
-        }
+        if (ok) umma_commit(&acc_full[buf]);
       }
     }
   } else {
@@ -863,12 +814,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     int tl = 0;
     int* last_s = reinterpret_cast<int*>(acc_free + 2) + 1;  // the split counter outcome for all workers
-    // the accumulator buffer is released on the even CTA's barrier
-    const uint32_t free_bar0 = PAIR ? mapa_shared(smem_u32(&acc_free[0]), 0) : 0;
-    for (int un = unit0; un < n_units; un += ustep, ++tl) {
+    for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++tl) {
       const int tile = un / p.ksplit, ks = un % p.ksplit;
-      const int m = PAIR ? 2 * (tile / p.n_tiles) + static_cast<int>(rank) : tile / p.n_tiles;
-      const int n0 = (tile % p.n_tiles) * NT;
+      const int m = tile / p.n_tiles, n0 = (tile % p.n_tiles) * NT;
       const int buf = tl & 1;
       // a thread's items: one row group, tokens 16 apart; the first part's
       // operands are requested before the accumulator is waited for
@@ -969,12 +917,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
           if (h == NT / 64 - 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-              if constexpr (PAIR)
-                mbar_arrive_cluster(free_bar0 + 8u * buf);
-              else
-                mbar_arrive(&acc_free[buf]);
-            }
+            if (lane == 0) mbar_arrive(&acc_free[buf]);
           }
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -1011,20 +954,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
   tc_fence_before();
   __syncthreads();
   // drain: a producer that stopped early waits (bounded) for its TMA writes
-  // (with PAIR the even CTA's full barriers count both CTAs' bytes)
-  if (warp == 0 && lane == 0 && (!PAIR || leader))
+  if (warp == 0 && lane == 0)
     for (int i = (issued > kPStages ? issued - kPStages : 0); i < issued; ++i)
       mbar_wait(&full[i % kPStages], (i / kPStages) & 1, p.status, kDevTimeoutTmaFull);
-  if constexpr (PAIR)
-    cluster_sync();  // neither CTA leaves while the pair's copies or MMAs may touch it
-  else
-    __syncthreads();
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    if constexpr (PAIR)
-      tmem_dealloc_pair(tmem, tiles_tmem_cols<NT>());
-    else
-      tmem_dealloc(tmem, tiles_tmem_cols<NT>());
+    tmem_dealloc(tmem, tiles_tmem_cols<NT>());
   }
   if (threadIdx.x == 0) trace(p, kTrEnd);
 }
@@ -1212,54 +1148,33 @@ size_t split_workspace_bytes(int tiles, int ksplit, int nt) {
 }
 
 // Many tokens (T > 128) with the load prologue and automatic tiling go to the
-// persistent tile kernel.  With an even number of 128-row weight tiles and at
-// least one pair tile per CTA pair, CTA pairs (cta_group::2) on 256 x NT pair
-// tiles: each CTA streams 16 KB of weights + NT / 2 x 128 B of tokens per
-// k-step for 128 x NT outputs.  Else 192- or 256-token tiles (more FLOPs per
-// operand byte) when that still gives every SM at least two tiles, else
-// 128-token tiles, with K split over several CTAs when
+// persistent tile kernel with 128-, 192- or 256-token tiles: the width with
+// the least (rounds of tiles over the SMs) x (width + 300), a round's time
+// growing with the width on top of a fixed part of about 300 tokens' worth
+// (set-up, pipeline fill, the last epilogue; fitted to measured times of the
+// frame and 64-stream shapes).  With 128-token tiles, K is split over several CTAs when
 // the tiles alone leave SMs idle and the caller gave a workspace
 // (`assume_ws`: as if it had).  Without a split and with fewer than half an
 // SM's worth of 128-token tiles, the per-tile kernel's in-cluster split-K
-// keeps more SMs busy: nt = 0.  Between token widths, the one with the least
-// (rounds of tiles over the SMs or pairs) x (width + 32): tiles of one round
-// run side by side, and a round's time grows with the width plus a fixed part.
+// keeps more SMs busy: nt = 0.
 struct TilesPlan {
   int nt = 0, ksplit = 1;
   size_t ws = 0;
-  bool pair = false;
 };
 TilesPlan plan_tiles(const rfx_linear_desc& d, int nsm, bool assume_ws) {
   TilesPlan t;
   if (d.prologue != RFX_PRO_LOAD || d.splits != 0 || d.n_tile != 0 || d.T <= 128) return t;
   const int m_tiles = d.O / kBM;
-  auto cost = [&](int units, int slots, int nt) { return static_cast<long>((units + slots - 1) / slots) * (nt + 32); };
-  const int pairs = nsm / 2;
-  if (m_tiles % 2 == 0) {
-    long best = 0;
-    for (int nt : {192, 256}) {
-      const int pt = (m_tiles / 2) * ((d.T + nt - 1) / nt);
-      if (pt < pairs) continue;
-      const long c = cost(pt, pairs, nt);
-      if (!t.pair || c < best) {
-        t.pair = true;
-        t.nt = nt;
-        best = c;
-      }
-    }
-    if (t.pair) return t;
-  }
-  t.nt = 128;
-  long best = 0;
-  for (int nt : {192, 256}) {
+  long best = -1;
+  for (int nt : {128, 192, 256}) {
     const int tiles = m_tiles * ((d.T + nt - 1) / nt);
-    if (tiles < 2 * nsm) continue;
-    const long c = cost(tiles, nsm, nt);
-    if (t.nt == 128 || c < best) {
+    const long c = static_cast<long>((tiles + nsm - 1) / nsm) * (nt + 300);
+    if (best < 0 || c < best) {
       t.nt = nt;
       best = c;
     }
   }
+  if (t.nt != 128) return t;
   const int tiles = m_tiles * ((d.T + t.nt - 1) / t.nt);
   t.ksplit = pick_ksplit(tiles, d.K / kBK, t.nt, nsm);
   t.ws = split_workspace_bytes(tiles, t.ksplit, t.nt);
@@ -1273,22 +1188,10 @@ TilesPlan plan_tiles(const rfx_linear_desc& d, int nsm, bool assume_ws) {
   return t;
 }
 
-template <int NT, int EPI, bool PAIR = false>
+template <int NT, int EPI>
 const void* tiles_ptr() {
-  return reinterpret_cast<const void*>(linear_tiles_kernel<NT, EPI, PAIR>);
+  return reinterpret_cast<const void*>(linear_tiles_kernel<NT, EPI>);
 }
-template <int NT>
-const void* select_pair_nt(int epi) {
-  switch (epi) {
-    case kEpiStore: return tiles_ptr<NT, kEpiStore, true>();
-    case kEpiSilu: return tiles_ptr<NT, kEpiSilu, true>();
-    case kEpiQkvRope: return tiles_ptr<NT, kEpiQkvRope, true>();
-    case kEpiResidual: return tiles_ptr<NT, kEpiResidual, true>();
-    case kEpiGeglu: return tiles_ptr<NT, kEpiGeglu, true>();
-    default: return nullptr;
-  }
-}
-const void* select_pair(int nt, int epi) { return nt == 256 ? select_pair_nt<256>(epi) : select_pair_nt<192>(epi); }
 template <int NT>
 const void* select_tiles_nt(int epi) {
   switch (epi) {
@@ -1303,8 +1206,7 @@ const void* select_tiles_nt(int epi) {
 const void* select_tiles(int nt, int epi) {
   return nt == 256 ? select_tiles_nt<256>(epi) : nt == 192 ? select_tiles_nt<192>(epi) : select_tiles_nt<128>(epi);
 }
-int tiles_smem(int nt, bool pair) {
-  if (pair) return nt == 256 ? TilesLayout<256, true>::kSmem : TilesLayout<192, true>::kSmem;
+int tiles_smem(int nt) {
   return nt == 256 ? TilesLayout<256>::kSmem : nt == 192 ? TilesLayout<192>::kSmem : TilesLayout<128>::kSmem;
 }
 
@@ -1343,28 +1245,9 @@ LinParams lin_params(const rfx_linear_desc& d) {
 int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, const TilesPlan& tp,
                         int nsm, cudaStream_t stream, bool pdl) {
   const int nt = tp.nt;
-  if (tp.pair) {
-    const void* fn = select_pair(nt, d.epilogue);
-    if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no pair tile kernel for this epilogue");
-    const int smem = tiles_smem(nt, true);
-    int rc = ensure_smem_attr(fn, smem);
-    if (rc) return rc;
-    LinParams p = lin_params(d);
-    p.splits = 1;
-    p.ksplit = 1;
-    p.n_tiles = (d.T + nt - 1) / nt;
-    const int pair_tiles = (d.O / (2 * kBM)) * p.n_tiles;
-    // one cluster per resident CTA pair (a GPC with an odd SM count leaves one out)
-    int pairs = max_active_clusters(fn, kTThreads, smem, 2);
-    if (pairs <= 0) pairs = nsm / 2;
-    const int grid = 2 * std::min(pair_tiles, pairs);
-    p.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(grid) * 16));
-    CUtensorMap w = *tmW, x = *tmX;
-    return launch_kernel(fn, dim3(grid), dim3(kTThreads), static_cast<size_t>(smem), stream, pdl, 2, w, x, p);
-  }
   const void* fn = select_tiles(nt, d.epilogue);
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no tile kernel for this epilogue");
-  const int smem = tiles_smem(nt, false);
+  const int smem = tiles_smem(nt);
   int rc = ensure_smem_attr(fn, smem);
   if (rc) return rc;
   LinParams p = lin_params(d);
@@ -1393,8 +1276,7 @@ int build_linear_maps(const rfx_linear_desc& d, CUtensorMap* tmW, CUtensorMap* t
   if (rc) return rc;
   rc = make_tmap_2d(tmW, d.w, 2, d.K, d.O, static_cast<uint64_t>(d.K) * 2, kBK, kBM, true);
   if (rc) return rc;
-  const TilesPlan tp = plan_tiles(d, nsm, false);
-  const int pnt = tp.pair ? tp.nt / 2 : tp.nt;
+  const int pnt = plan_tiles(d, nsm, false).nt;
   return make_tmap_2d(tmX, d.x, 2, d.K, d.T, static_cast<uint64_t>(d.ldx) * 2, kBK, pnt ? pnt : cfg.nt, true);
 }
 

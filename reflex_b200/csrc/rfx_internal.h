@@ -49,8 +49,6 @@ int launch_kernel_cluster(const void* func, dim3 grid, dim3 block, size_t smem, 
 
 // Whether a cluster of cluster_x CTAs of this kernel can be resident at once.
 bool cluster_fits(const void* func, dim3 grid, int threads, int smem, int cluster_x);
-// Clusters of `cluster_x` CTAs of `func` that can be resident at once (0 if none; memoised).
-int max_active_clusters(const void* func, int threads, int smem, int cluster_x);
 
 // Raises the dynamic shared-memory limit of a kernel once per process.
 int ensure_smem_attr(const void* func, int bytes, bool nonportable_cluster = false);

@@ -117,37 +117,6 @@ int ensure_smem_attr(const void* func, int bytes, bool nonportable_cluster) {
   return RFX_OK;
 }
 
-int max_active_clusters(const void* func, int threads, int smem, int cluster_x) {
-  static std::mutex mu;
-  static std::unordered_map<uint64_t, int> memo;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t key = (reinterpret_cast<uintptr_t>(func) * 1315423911ull) ^ (static_cast<uint64_t>(smem) << 20) ^
-                       (static_cast<uint64_t>(cluster_x) << 8) ^ static_cast<uint64_t>(dev);
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    auto it = memo.find(key);
-    if (it != memo.end()) return it->second;
-  }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(cluster_x);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = cluster_x;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, func, &cfg) != cudaSuccess) n = 0;
-  cudaGetLastError();
-  std::lock_guard<std::mutex> lk(mu);
-  memo[key] = n;
-  return n;
-}
-
 bool cluster_fits(const void* func, dim3 grid, int threads, int smem, int cluster_x) {
   static std::mutex mu;
   static std::unordered_map<uint64_t, bool> memo;

@@ -97,15 +97,15 @@ def test_linear_store(K, T, n_tile, splits):
 @pytest.mark.parametrize("B,S", [(1, 300), (2, 384), (1, 768)])
 def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
     """T > 128 tokens with the load prologue run the persistent tile kernel (two
-    TMEM accumulators, a tile's epilogue under the next tile's mainloop).  It
-    issues the same MMA sequence per tile as the per-tile kernel with the same
-    token tile and no split-K, so the outputs are bit-identical to it for every
+    TMEM accumulators, a tile's epilogue under the next tile's mainloop).  Each
+    output sums the same k-steps in the same order as in the per-tile kernel
+    without split-K, so the outputs are bit-identical to it for every
     epilogue, with ragged last token tiles and several batches; the store
-    epilogue is also checked against the fp32 product.  The *_wide cases have
-    16384 output rows: enough pair tiles for CTA pairs (one cta_group::2 MMA
-    of 256 rows per pair, each CTA staging its own 128 weight rows and half of
-    the tokens; 192-token pair tiles at 300 tokens, 256 at 768), compared with
-    the per-tile kernel at 256-token tiles."""
+    epilogue is also checked against the fp32 product.  The token tile width
+    (the MMA's N) does not change a result bit, so the reference is the
+    per-tile kernel at 128-token tiles for all of them; the persistent kernel
+    picks 128-token tiles at 4096 rows x 300 tokens, 192 at 4096 x 768 and
+    16384 x 300, 256 at 16384 x 768 (the *_wide cases have 16384 rows)."""
     r = gen(6)
     T, Kd, Hq, D = B * S, 1024, 8, 256
     x = r(T, Kd).bfloat16().cuda()
@@ -151,12 +151,9 @@ def test_linear_many_tokens_persistent_tiles(K, L, epi, B, S):
         tab = rope_table().cuda()
         pos = (100 + torch.arange(S, dtype=torch.int32)).repeat(B).cuda()
     nsm = torch.cuda.get_device_properties(0).multi_processor_count
-    pair = (O // 128) % 2 == 0 and any((O // 256) * ((T + w - 1) // w) >= nsm // 2 for w in (192, 256))
-    assert pair == wide
-    nt = 256 if pair or (O // 128) * ((T + 255) // 256) >= 2 * nsm else 128
-    assert nt == 256 or 2 * (O // 128) * ((T + 127) // 128) >= nsm  # the persistent kernel serves these shapes
+    assert 2 * (O // 128) * ((T + 127) // 128) >= nsm  # the persistent kernel serves these shapes
     got = run((0, 0))       # persistent tile kernel
-    ref = run((nt, 1))      # per-tile kernel, same token tile
+    ref = run((128, 1))     # per-tile kernel
     torch.cuda.synchronize()
     assert K.device_status() == 0
     for a, b in zip(got, ref):
