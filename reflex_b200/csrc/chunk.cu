@@ -9,9 +9,10 @@
 // current phase.
 //
 // Work decomposition (T = B*S <= 64 tokens; per layer, in phase order):
-//   QKV   20 row tiles x 2 K-splits: tcgen05 GEMM of the packed [Wq;Wk;Wv]
-//         against the normed input; the second split to finish sums the two
-//         fp32 partials and applies RoPE (rows r / r+64 of a tile are the
+//   QKV   20 row tiles x 2 K-splits on the two CTAs of a cluster: tcgen05
+//         GEMM of the packed [Wq;Wk;Wv] against the normed input; each CTA
+//         pushes the peer's rows of its fp32 partial through DSMEM, sums the
+//         rows it finishes and applies RoPE (rows r / r+64 of a tile are the
 //         rotary pair) -> q (head-major), k_new, v_new (bf16).
 //   ATTN  (stream, 128-row query tile, key-block split): the partitioned
 //         attention of the new tokens over the int8 context ring + the new
@@ -22,7 +23,7 @@
 //   O     8 row tiles x 8 K-splits -> fp32 partials.
 //   FIN_O per token: h += gate * bf16(sum of O partials); post-attention
 //         (Ada)RMSNorm -> GEMM input.
-//   GU    64 row tiles x 2 K-splits, last split: GELU-tanh(gate) * up.
+//   GU    64 row tiles x 2 K-splits on a cluster, as QKV: GELU-tanh(gate) * up.
 //   DOWN  8 row tiles x 8 K-splits -> fp32 partials.
 //   FIN_D per token: h += gate * bf16(sum of down partials); next layer's
 //         input norm, or after the last layer the Euler tail (final norm,
@@ -33,10 +34,10 @@
 // Counters only grow within a chunk and are cleared before each chunk.
 // Partials are summed in a fixed order, so results do not depend on timing.
 //
-// Roles (192 threads, as in the standalone kernels): warp 0 lane 0 streams
-// weight / activation tiles through a 7-stage TMA ring (weights are issued
-// before the tile's input is ready), warp 1 lane 0 issues tcgen05.mma, warps
-// 2-5 do everything else.  The attention tiles reuse the ring's shared memory;
+// Roles (320 threads): warp 0 lane 0 streams weight / activation tiles
+// through an 8-stage TMA ring (weights are issued before the tile's input is
+// ready), warp 1 lane 0 issues tcgen05.mma, warps 2-9 (two per TMEM lane
+// quadrant) do everything else.  The attention tiles reuse the ring's shared memory;
 // the producer drains the ring before an attention item and resumes after it.
 //
 // Every wait is bounded (about one second); a wait that runs out records a

@@ -176,6 +176,9 @@ def trace_chunk(eng, per_cta: int = 256) -> None:
         print(f"{name:5s} producer saw input -> first stage {seg(name, 3, 10):.2f}, first -> last stage "
               f"{seg(name, 10, 11):.2f}, last stage -> accumulator ready {seg(name, 11, 1):.2f}, "
               f"accumulator -> stored {seg(name, 1, 6):.2f}, stored -> end {seg(name, 6, 2):.2f} us")
+        print(f"{'':5s} read out -> own rows stored {seg(name, 6, 8):.2f}, -> peer partial arrived "
+              f"{seg(name, 8, 9):.2f}, -> epilogue done {seg(name, 9, 12):.2f}, -> end {seg(name, 12, 2):.2f}, "
+              f"task start -> producer saw input {seg(name, 0, 3):.2f} us")
 
 
 if __name__ == "__main__":
