@@ -86,7 +86,7 @@ int rfx_num_sms(int* out);
  * of q[b][h][slot][0..D) (byte strides qs_*), scale/zp[b][h][slot] (element
  * strides ss_*). Eviction of the oldest frame is overwriting its slots.
  * With v, v_q, v_scale and v_zp all NULL only K is quantized (one tensor, as
- * fused_quantize_store does). */
+ * fused_quantize_store does). B * H is at most 65535 (RFX_E_INVAL beyond). */
 typedef struct rfx_kv_quant_desc {
   int mode;     /* RFX_QUANT_* */
   int in_dtype; /* RFX_DTYPE_BF16 or RFX_DTYPE_F32 */

@@ -8,13 +8,13 @@
 // and adds the int8 symmetric per-token/per-head scheme (scale = absmax/127 in
 // fp32, q = clamp(rne(x/scale), -127, 127)).
 //
-// Layout: one warp per (b, h, token) row of D = 256 elements; each lane owns 8
-// contiguous elements (one 16-byte bf16 vector or two fp32 vectors) and
-// reductions are warp shuffles.  The destination slot of token l is
+// Layout: one warp per four (b, h, token) rows of D = 256 elements; each lane
+// owns 8 contiguous elements of a row (one 16-byte bf16 vector or two fp32
+// vectors) and reductions are warp shuffles.  The destination slot of token l is
 //   region_base + (region_off + l) % region_len
 // so an append that wraps around the ring window is one launch, and eviction
 // of the oldest frame is simply overwriting its slots (no data movement).
-// Grid: x = row blocks, y = {K, V}.
+// Grid: x = blocks of 32 tokens, y = (b, h), z = {K, V}.
 #include "rfx_internal.h"
 
 namespace rfx {
@@ -73,53 +73,138 @@ struct QuantArgs {
   int region_base, region_off, region_len;
 };
 
+// int8 symmetric quantization of one lane's 8 values of a row, packed little
+// endian into two words: q = clamp(rne(x / scale), -127, 127), exactly as with
+// rintf(__fdiv_rn(x, scale)), but from a product with rcp = __frcp_rn(scale),
+// the correctly rounded 1 / scale.
+//
+// Error bound: |x| <= absmax and scale = fl(absmax / 127) is a normal float,
+// so the exact quotient q has |q| <= 127 (1 + 2^-23); then y = fl(x * rcp)
+// and fl(q) both lie within |q| * (3 * 2^-24 + 2^-48) + 2^-149, under 2.3e-5,
+// of q.  Hence |y| < 127.5 (rne(y) needs no clamp), and whenever y is at least
+// 2^-14 (6.1e-5) away from every half-integer, fl(q) is on the same side of
+// all of them and on none, so both round to the same integer.  Values closer
+// than that (bf16 inputs put about 0.2 % of the quotients there, most on a
+// tie) are divided in a second pass; a denormal scale divides all 8.
+//
+// Rounding: t = y + 1.5 * 2^23 holds rne(y) in its low mantissa bits, so the
+// low byte of t's bit pattern is the two's-complement int8 and t - 1.5 * 2^23
+// is rne(y) as a float; y - rne(y) is exact (Sterbenz).  A NaN input fails
+// the distance test and takes the divide, as before.
+__device__ __forceinline__ void quant8_i8(const float (&v)[8], float scale, float rcp, uint32_t (&packed)[2]) {
+  constexpr float kMagic = 12582912.0f;     // 1.5 * 2^23
+  constexpr float kFar = 0.5f - 0x1p-14f;   // |y - rne(y)| <= kFar: 2^-14 or more from a half-integer
+  uint32_t tb[8];
+  if (scale >= 0x1p-126f) {
+    bool near = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = __fmul_rn(v[i], rcp);
+      const float t = __fadd_rn(y, kMagic);
+      near |= !(fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) <= kFar);
+      tb[i] = __float_as_uint(t);
+    }
+    if (near) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float y = __fmul_rn(v[i], rcp);
+        const float t = __uint_as_float(tb[i]);
+        if (!(fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) <= kFar))
+          tb[i] = __float_as_uint(__fadd_rn(fminf(fmaxf(rintf(__fdiv_rn(v[i], scale)), -127.f), 127.f), kMagic));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float r = fminf(fmaxf(rintf(__fdiv_rn(v[i], scale)), -127.f), 127.f);
+      tb[i] = __float_as_uint(__fadd_rn(r, kMagic));
+    }
+  }
+  packed[0] = __byte_perm(__byte_perm(tb[0], tb[1], 0x0040), __byte_perm(tb[2], tb[3], 0x0040), 0x5410);
+  packed[1] = __byte_perm(__byte_perm(tb[4], tb[5], 0x0040), __byte_perm(tb[6], tb[7], 0x0040), 0x5410);
+}
+
+// One warp quantizes kRowsPerWarp consecutive tokens of one (b, h): every
+// row's 16-byte loads are issued first, and in the int8 scheme lane j computes
+// row j's scale and reciprocal (one exact divide per row instead of one per
+// lane), broadcast by shuffles.
+constexpr int kRowsPerWarp = 4;
+
 template <typename Tin, int MODE>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) kv_quant_append_kernel(const QuantArgs a) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) kv_quant_append_kernel(const QuantArgs a) {
   pdl_wait();
   // the next kernel may start its set-up now; its griddepcontrol.wait still
   // waits for all of this grid
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long row = static_cast<long>(blockIdx.x) * kWarpsPerBlock + warp;
-  const long rows = static_cast<long>(a.B) * a.H * a.L;
-  const int which = blockIdx.y;  // 0 = K, 1 = V
-  if (row < rows) {
-    const int l = static_cast<int>(row % a.L);
-    const int h = static_cast<int>((row / a.L) % a.H);
-    const int b = static_cast<int>(row / (static_cast<long>(a.L) * a.H));
-    const Tin* src = static_cast<const Tin*>(a.x[which]) + b * a.xs_b + h * a.xs_h + l * a.xs_l + lane * 8;
-    float v[8];
-    load8(src, v);
-    const long slot = a.region_base + (static_cast<long>(a.region_off) + l) % a.region_len;
-    uint8_t* dst = static_cast<uint8_t*>(a.q[which]) + b * a.qs_b + h * a.qs_h + slot * a.qs_c + lane * 8;
-    const long sidx = b * a.ss_b + h * a.ss_h + slot * a.ss_c;
-    uint32_t packed[2] = {0u, 0u};
-    if (MODE == kQuantI8Sym) {
-      float amax = 0.f;
+  // grid: x = token blocks, y = b * H + h, z = {K, V}; each thread divides
+  // twice (b, and the ring offset), never per row
+  const int which = blockIdx.z;
+  const int b = static_cast<int>(blockIdx.y) / a.H;
+  const int h = static_cast<int>(blockIdx.y) - b * a.H;
+  const int l0 = (static_cast<int>(blockIdx.x) * kWarpsPerBlock + warp) * kRowsPerWarp;
+  if (l0 >= a.L) return;
+  const int off = a.region_off % a.region_len;
+  const Tin* src = static_cast<const Tin*>(a.x[which]) + b * a.xs_b + h * a.xs_h + lane * 8;
+  uint8_t* qbase = static_cast<uint8_t*>(a.q[which]) + b * a.qs_b + h * a.qs_h + lane * 8;
+  const long sbase = b * a.ss_b + h * a.ss_h;
+  float v[kRowsPerWarp][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-      amax = warp_max(amax);
-      const float scale = __fdiv_rn(amax, 127.0f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        int qi = 0;
-        if (amax > 0.f) {
-          float r = rintf(__fdiv_rn(v[i], scale));
-          r = fminf(fmaxf(r, -127.f), 127.f);
-          qi = static_cast<int>(r);
-        }
-        packed[i >> 2] |= (static_cast<uint32_t>(qi) & 0xFFu) << (8 * (i & 3));
-      }
-      if (lane == 0) static_cast<float*>(a.scale[which])[sidx] = scale;
+  for (int j = 0; j < kRowsPerWarp; ++j) {
+    if (l0 + j < a.L) {
+      load8(src + static_cast<long>(l0 + j) * a.xs_l, v[j]);
     } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j][i] = 0.f;
+    }
+  }
+  // ring slot of token l: region_base + (off + l) mod region_len, with
+  // l < L <= region_len and off < region_len, so one conditional subtract wraps
+  auto slot_of = [&](int l) {
+    const long ol = static_cast<long>(off) + l;
+    return a.region_base + (ol >= a.region_len ? ol - a.region_len : ol);
+  };
+  if (MODE == kQuantI8Sym) {
+    float amax[kRowsPerWarp];
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      float m = 0.f;  // fmaxf skips NaN, so every lane's value is a non-negative number
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[j][i]));
+      // non-negative floats order like their bit patterns: one warp-wide integer max
+      amax[j] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+    }
+    float mine = amax[0];
+#pragma unroll
+    for (int j = 1; j < kRowsPerWarp; ++j)
+      if (lane == j) mine = amax[j];
+    const float my_scale = __fdiv_rn(mine, 127.0f);
+    const float my_rcp = __frcp_rn(my_scale);
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int l = l0 + j;
+      if (l >= a.L) break;
+      const float scale = __shfl_sync(0xffffffffu, my_scale, j);
+      const float rcp = __shfl_sync(0xffffffffu, my_rcp, j);
+      uint32_t packed[2] = {0u, 0u};
+      if (amax[j] > 0.f) quant8_i8(v[j], scale, rcp, packed);
+      const long slot = slot_of(l);
+      *reinterpret_cast<uint2*>(qbase + slot * a.qs_c) = make_uint2(packed[0], packed[1]);
+      if (lane == 0) static_cast<float*>(a.scale[which])[sbase + slot * a.ss_c] = scale;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int l = l0 + j;
+      if (l >= a.L) break;
       // Reference scheme, each op rounded to the activation dtype:
       //   range = clamp(max - min, min=1e-5); scale = range / 255;
       //   zp = -min / scale; q = clamp(round(x / scale + zp), 0, 255)
-      float mn = v[0], mx = v[0];
+      float mn = v[j][0], mx = v[j][0];
 #pragma unroll
       for (int i = 1; i < 8; ++i) {
-        mn = fminf(mn, v[i]);
-        mx = fmaxf(mx, v[i]);
+        mn = fminf(mn, v[j][i]);
+        mx = fmaxf(mx, v[j][i]);
       }
       mn = warp_min(mn);
       mx = warp_max(mx);
@@ -128,20 +213,23 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) kv_quant_append_kernel(co
       if (range < 1e-5f) range = kMinRange;
       const float scale = to_act<Tin>(__fdiv_rn(range, 255.0f));
       const float zp = to_act<Tin>(__fdiv_rn(-mn, scale));
+      uint32_t packed[2] = {0u, 0u};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float t1 = to_act<Tin>(__fdiv_rn(v[i], scale));
+        const float t1 = to_act<Tin>(__fdiv_rn(v[j][i], scale));
         const float t2 = to_act<Tin>(__fadd_rn(t1, zp));
         float r = rintf(t2);
         r = fminf(fmaxf(r, 0.f), 255.f);
         packed[i >> 2] |= (static_cast<uint32_t>(r) & 0xFFu) << (8 * (i & 3));
       }
+      const long slot = slot_of(l);
+      *reinterpret_cast<uint2*>(qbase + slot * a.qs_c) = make_uint2(packed[0], packed[1]);
       if (lane == 0) {
+        const long sidx = sbase + slot * a.ss_c;
         store_act<Tin>(static_cast<Tin*>(a.scale[which]) + sidx, scale);
         store_act<Tin>(static_cast<Tin*>(a.zp[which]) + sidx, zp);
       }
     }
-    *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
   }
 }
 
@@ -184,8 +272,10 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   a.B = d.B; a.H = d.H; a.L = d.L;
   a.region_base = d.region_base; a.region_off = d.region_off; a.region_len = d.region_len;
 
-  const long rows = static_cast<long>(d.B) * d.H * d.L;
-  dim3 grid(static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock), nw);
+  if (static_cast<long>(d.B) * d.H > 65535)
+    return set_error(RFX_E_INVAL, "kv_quant_append: B * H must be at most 65535");
+  constexpr int kRowsPerBlock = kWarpsPerBlock * kRowsPerWarp;
+  dim3 grid(static_cast<unsigned>((d.L + kRowsPerBlock - 1) / kRowsPerBlock), static_cast<unsigned>(d.B * d.H), nw);
   dim3 block(kWarpsPerBlock * 32);
   void (*kern)(QuantArgs) = nullptr;
   if (d.in_dtype == kDtypeBF16)

@@ -5,6 +5,7 @@
     python -m reflex_b200.profile --layers 2 --chunk --fused   # the same through the chunk executor
     python -m reflex_b200.profile --layers 18 --chunk --fused --trace   # per-phase timeline of the executor
     python -m reflex_b200.profile --frame --ops qkv,attn,gu,down   # frame-update ops (768 tokens, Gemma-2B layer)
+    python -m reflex_b200.profile --quant-bulk --reps 20   # int8 quantize-append of 64 streams x 2048 tokens
 
 Builds the PI0.5 engine at the benchmark's shapes (width 1024, 8x256 heads,
 818-token int8 context, 50 action tokens) with a few layers, runs one chunk to
@@ -40,7 +41,12 @@ def main():
     ap.add_argument("--frame", action="store_true",
                     help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
                          "pinned prefix and a 2-frame window)")
+    ap.add_argument("--quant-bulk", action="store_true",
+                    help="time the int8 quantize-append of a 64-stream x 2048-token prefill (larger than L2)")
     args = ap.parse_args()
+    if args.quant_bulk:
+        quant_bulk(args.reps)
+        return
     if args.frame:
         frame_ops(args.ops, args.reps)
         return
@@ -84,6 +90,41 @@ def main():
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     print("ok", K.device_status())
+
+
+def quant_bulk(reps: int, streams: int = 64, tokens: int = 2048, sets: int = 3) -> None:
+    """Times a bulk int8 quantize-append: K and V of `streams` rings x `tokens`
+    bf16 tokens (one head of 256) into rings of the same capacity, the prefill of
+    a multi-stream batch.  `sets` input sets are cycled so that no launch finds
+    its input in L2 (each set is 2 x streams x tokens x 512 B, 134 MB at the
+    defaults).  Prints the CUDA-event time per launch and the achieved bandwidth
+    over the algorithmic bytes: per (token, head) row 512 B read, 256 B + a
+    4-byte fp32 scale written."""
+    from . import _lib as L
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ring = K.KVRing.allocate(streams, 1, tokens, 256, L.RFX_QUANT_I8_SYM, scale_dtype=torch.float32)
+    xs = [(torch.randn(streams, 1, tokens, 256, generator=g, device="cuda").bfloat16(),
+           torch.randn(streams, 1, tokens, 256, generator=g, device="cuda").bfloat16()) for _ in range(sets)]
+    for k, v in xs:
+        K.kv_quant_append(k, v, ring)
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    torch.cuda.profiler.start()
+    evs[0].record()
+    for i in range(reps):
+        k, v = xs[i % sets]
+        K.kv_quant_append(k, v, ring)
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    per = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(reps))
+    med = per[len(per) // 2]
+    rows = 2 * streams * tokens
+    nbytes = rows * (512 + 256 + 4)
+    print(f"quant bulk {streams}x{tokens} tokens, K+V: {med * 1e3:.1f} us per launch (median of {reps}), "
+          f"{nbytes / 1e6:.1f} MB algorithmic, {nbytes / (med * 1e-3) / 1e9:.0f} GB/s")
+    print("status", K.device_status())
 
 
 def frame_ops(ops: str, reps: int) -> None:

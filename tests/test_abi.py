@@ -97,3 +97,18 @@ def test_linear_split_workspace_size(T, O, K, want):
     n = ctypes.c_size_t(7)
     assert lib.rfx_linear_workspace_size(ctypes.byref(d), ctypes.byref(n)) == _lib.RFX_OK
     assert n.value == want
+
+
+def test_kv_quant_rejects_too_many_rings():
+    """B * H above 65535 (one grid row per (b, h)) is refused before any launch."""
+    lib = _lib.load()
+    d = _lib.KvQuantDesc()
+    d.mode, d.in_dtype = _lib.RFX_QUANT_I8_SYM, _lib.RFX_DTYPE_BF16
+    d.k = d.v = d.k_q = d.v_q = d.k_scale = d.v_scale = 1 << 20  # aligned, never dereferenced
+    d.B, d.H, d.L, d.D, d.capacity = 65536, 1, 1, 256, 1
+    d.xs_b = d.xs_h = d.xs_l = 256
+    d.qs_b = d.qs_h = d.qs_c = 256
+    d.ss_b = d.ss_h = d.ss_c = 1
+    d.region_base, d.region_off, d.region_len = 0, 0, 1
+    assert lib.rfx_kv_quant_append(ctypes.byref(d), None) == _lib.RFX_E_INVAL
+    assert b"65535" in lib.rfx_last_error()

@@ -73,6 +73,43 @@ def test_kv_quant_bit_exact(K, L, mode, dtype):
         np.testing.assert_array_equal(s.float().cpu().numpy()[:, :, slots], es[..., 0])
 
 
+def _near_tie_rows(D=256, n=96, seed=3):
+    """Rows whose quotients x / scale sit on or within a few ulps of
+    half-integers (the int8 quantizer rounds them from a product with the
+    reciprocal and must fall back to the exact divide there), over scales from
+    normal down to denormal (where the reciprocal overflows)."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    rows = []
+    for i in range(n):
+        amax = f32(10.0 ** rng.uniform(-41, 30)) if i % 4 else f32(127.0) * f32(rng.uniform(0.05, 2.0))
+        s = f32(amax / f32(127))
+        k = rng.integers(-127, 127, D).astype(f32) + f32(0.5)
+        x = (k * s).astype(f32)
+        x = (x.view(np.int32) + rng.integers(-3, 4, D).astype(np.int32)).view(f32)
+        x = np.clip(x, -amax, amax)
+        x[0] = amax
+        rows.append(x)
+    return np.stack(rows).astype(np.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_kv_quant_i8_near_ties(K, L, dtype):
+    """int8 scheme, bit-exact against the oracle on quotients at and next to
+    rounding boundaries, denormal scales included."""
+    x = torch.from_numpy(_near_tie_rows()).to(dtype)
+    B, Lnew = 2, x.shape[0] // 2
+    k = x.reshape(B, 1, Lnew, 256).contiguous()
+    v = torch.flip(k, dims=[2]).contiguous()
+    ring = K.KVRing.allocate(B, 1, Lnew, 256, L.RFX_QUANT_I8_SYM, scale_dtype=torch.float32)
+    K.kv_quant_append(k.cuda(), v.cuda(), ring)
+    torch.cuda.synchronize()
+    for src, q, s in ((k, ring.k_q, ring.k_scale), (v, ring.v_q, ring.v_scale)):
+        eq, es = oq.quant_i8_sym(src.float().numpy())
+        np.testing.assert_array_equal(q.cpu().numpy(), eq)
+        np.testing.assert_array_equal(s.cpu().numpy(), es[..., 0])
+
+
 # ------------------------------------------------------------------ linear ---
 def _mm(x, w):
     return x.float() @ w.float().t()
