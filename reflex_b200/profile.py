@@ -37,7 +37,7 @@ def main():
     ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
     ap.add_argument("--trace", action="store_true",
-                    help="with --chunk --fused: %globaltimer stamps of every task of the first Euler step")
+                    help="with --chunk --fused: %%globaltimer stamps of every task of the first Euler step")
     ap.add_argument("--frame", action="store_true",
                     help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
                          "pinned prefix and a 2-frame window)")
