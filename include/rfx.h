@@ -248,21 +248,29 @@ typedef struct rfx_attn_desc {
 int rfx_attention(const rfx_attn_desc* desc, void* stream);
 /* Workspace needed by rfx_attention for this descriptor (0 if none). */
 int rfx_attention_workspace_size(const rfx_attn_desc* desc, size_t* bytes);
-/* rfx_attention without a caller workspace and without any allocation: the
- * split-KV partials go to an 8 MiB scratch array in the library's device
- * code (desc->workspace / workspace_bytes are ignored).  No counterpart in
- * the reference; it serves callers that may not allocate device memory at
- * call time (code under CUDA stream capture, hosts whose allocator owns all
- * device memory).
- *   - Make the first call on each device before any stream capture: it looks
- *     up the scratch address (and may load the module's device code).
- *   - Shapes whose partials need more than 8 MiB (B * q_tiles * kv_splits
- *     above 63, at 132,096 bytes per CTA) return RFX_E_INVAL with the size
- *     in rfx_last_error(); lower kv_splits or use rfx_attention.
- *   - The scratch needs no zeroing; every partial read is written by the
- *     same call.
- *   - The scratch is shared per device: calls whose launches may overlap
- *     (other streams, racing host threads) corrupt each other; order them. */
+/* rfx_attention without a caller workspace and without any allocation: its
+ * scratch (split-KV partials; for RFX_KV_DENSE also the dense key copy) lives
+ * in an 8 MiB array in the library's device code, of which 8 MiB - 1 KiB
+ * from its first 1024-byte boundary is used (desc->workspace and
+ * workspace_bytes are ignored).  No counterpart in the reference.  It is for
+ * hosts that may not allocate device memory while they run: a controller
+ * whose memory pool reserves every device byte at start-up, or a real-time
+ * loop that forbids cudaMalloc after start-up because it can synchronize the
+ * device and has no bounded latency.  Every GPU that loads the library holds
+ * the array until the process exits.
+ *   - The first call on each device (with that device current) looks up the
+ *     array's device address and may load the module's device code; make it
+ *     before any stream capture.
+ *   - kv_splits = 0 picks the largest automatic split count whose scratch
+ *     fits.  Shapes that still need more than 8 MiB - 1 KiB (ring source:
+ *     B * q_tiles * kv_splits above 63, at 132,096 bytes per CTA; dense
+ *     source: also 1,040 bytes per key and stream) return RFX_E_INVAL with
+ *     the size in rfx_last_error(); lower kv_splits or use rfx_attention.
+ *   - Nothing in the scratch needs zeroing; every byte a call reads was
+ *     written earlier in the same call.
+ *   - The scratch is shared per device and keeps the last call's contents:
+ *     calls whose launches may overlap (other streams, racing host threads)
+ *     race on it and corrupt each other; order them. */
 int rfx_attention_noalloc(const rfx_attn_desc* desc, void* stream);
 
 /* ----------------------------------------- timestep conditioning + heads ---- */

@@ -1223,28 +1223,32 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
 }
 
 // ------------------------------------------------- no-allocation variant ---
-// Split-KV scratch for rfx_attention_noalloc: a file-scope device array, so
-// the call never allocates.  It is for callers that may not allocate device
-// memory at call time: code running while a CUDA stream is being captured
-// (an allocation there breaks or invalidates the capture) and hosts whose
-// allocator owns every device byte and hands the kernel library none.
-// 8 MiB holds the partials of B * q_tiles * kv_splits <= 63 CTAs (each CTA
-// needs 128 rows * (256 + 2) fp32 = 132,096 bytes), e.g. 4 streams of
-// 10 actions x 8 heads at up to 15 splits.  Nothing in it has to start at
-// zero: the attention launch writes every partial (O, m, l) that the combine
-// launch of the same call reads.  The array is shared by all calls on a
-// device, so two calls whose launches can overlap (different streams, or
-// host threads racing on one device) corrupt each other's partials; the
-// caller orders them.
+// Scratch for rfx_attention_noalloc: a file-scope device array, so the call
+// never allocates.  It is for hosts that may not allocate device memory once
+// they run: a controller whose memory pool reserves every device byte at
+// start-up, or a real-time loop that treats any later cudaMalloc (which can
+// synchronize the device and has no bounded latency) as a fault.
+// The usable part starts at the first 1024-byte boundary inside the array
+// (the dense key tiles need that alignment) and is kNoAllocUsableBytes long
+// wherever the linker places the array.  The ring-tile source keeps only the
+// split-KV partials there: B * q_tiles * kv_splits <= 63 CTAs at 132,096
+// bytes each.  The dense source also keeps its bf16 K / f16 V copy of the
+// keys there (1,040 bytes per key and stream).  Nothing in it has to start at
+// zero: every byte a call reads was written earlier in the same call.  The
+// array is shared by all calls on a device, so two calls whose launches can
+// overlap (different streams, or host threads racing on one device) corrupt
+// each other's data; the caller orders them.
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+constexpr size_t kNoAllocUsableBytes = kNoAllocScratchBytes - 1024;
 static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
 std::mutex g_scratch_mu;
 std::unordered_map<int, void*> g_scratch_ptrs;
 
-// Device address of the scratch array on the current device, looked up once
-// per device.  The first call on a device can load the module's device code
-// (lazy loading), so it belongs before any stream capture.
+// 1024-byte aligned start of the scratch array on the current device, looked
+// up once per device (cudaGetSymbolAddress with that device current).  The
+// first call on a device can load the module's device code (lazy loading),
+// so it belongs before any stream capture.
 int noalloc_scratch(void** out) {
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "rfx_attention_noalloc: cudaGetDevice");
@@ -1258,8 +1262,10 @@ int noalloc_scratch(void** out) {
   void* p = nullptr;
   rc = check_cuda(cudaGetSymbolAddress(&p, g_attn_scratch), "rfx_attention_noalloc: cudaGetSymbolAddress(scratch)");
   if (rc) return rc;
-  g_scratch_ptrs[dev] = p;
-  *out = p;
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023);
+  void* aligned = reinterpret_cast<void*>(a);
+  g_scratch_ptrs[dev] = aligned;
+  *out = aligned;
   return RFX_OK;
 }
 }  // namespace
@@ -1273,18 +1279,28 @@ extern "C" int rfx_attention_noalloc(const rfx_attn_desc* desc, void* stream) {
   int rc = geometry(*desc, &g);
   if (rc) return rc;
   rfx_attn_desc d = *desc;
-  const size_t need = attention_workspace_bytes(d);
-  if (need > kNoAllocScratchBytes)
+  size_t need = attention_workspace_bytes(d);
+  if (desc->kv_splits <= 0) {
+    // automatic split count: the largest one (up to the automatic choice)
+    // whose scratch fits
+    int splits = g.splits;
+    while (need > kNoAllocUsableBytes && splits > 1) {
+      d.kv_splits = --splits;
+      need = attention_workspace_bytes(d);
+    }
+    d.kv_splits = splits;
+  }
+  if (need > kNoAllocUsableBytes)
     return set_error(RFX_E_INVAL,
-                     "rfx_attention_noalloc: this shape needs %zu bytes of split-KV scratch, the static scratch "
-                     "holds %zu; lower kv_splits or call rfx_attention with a workspace",
-                     need, kNoAllocScratchBytes);
+                     "rfx_attention_noalloc: this shape needs %zu bytes of scratch, the static scratch holds %zu; "
+                     "lower kv_splits or call rfx_attention with a workspace",
+                     need, kNoAllocUsableBytes);
   d.workspace = nullptr;
   d.workspace_bytes = 0;
   if (need > 0) {
     rc = noalloc_scratch(&d.workspace);
     if (rc) return rc;
-    d.workspace_bytes = kNoAllocScratchBytes;
+    d.workspace_bytes = kNoAllocUsableBytes;
   }
   CUtensorMap q, k, v;
   rc = build_attention_maps(d, &q, &k, &v);
