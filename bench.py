@@ -14,7 +14,9 @@ rank 0 with NCCL after the timed region.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 --impl reference times the reference's PyTorch path for the same workload on
-the host CPU (the oracle port of reflex/policies/pi05/modeling_pi05.py).
+the host CPU: Reflex's own modules from its `pip install --target baseline/_ref`
+copy when present, else the oracle port of
+reflex/policies/pi05/modeling_pi05.py.
 """
 from __future__ import annotations
 
@@ -53,6 +55,10 @@ def parse():
                     help="fused: the persistent chunk executor (one launch per chunk); per-op: one launch per op")
     ap.add_argument("--streams-per-gpu", type=int, default=1,
                     help="independent robot streams served per GPU, batched along B (multi-stream sweep)")
+    ap.add_argument("--multistream", type=int, default=64,
+                    help="after the headline: serve this many independent streams sharded over the ranks "
+                         "(streams.shard_range) and report chunks/s and the timed NCCL gather in a 'multistream' "
+                         "sub-record (0: skip)")
     return ap.parse_args()
 
 
@@ -126,6 +132,14 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def sustained_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        return 1400.0
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -167,18 +181,67 @@ def cpu_chunk_ms(layers: int, chunks: int):
     return statistics.median(times), torch.get_num_threads(), times
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_chunks_ms(layers: int, chunks: int, warmup: int):
+    """Reflex's own PyTorch modules on the host CPU: the action expert built
+    from its PI05ModelLayer / AdaRMSNorm (in-tree, gate form) / suffix embedder
+    / QKVLinear / MergedColumnLinear / StreamingAttention with the uint8
+    quantized 818-token context in its caches, driven through the Euler loop
+    of sample_actions (reflex/policies/pi05/modeling_pi05.py:1181-1241,
+    1403-1419), fp32, all host threads.  The package is the `pip install
+    --target baseline/_ref` copy of the reference, imported through the
+    oracle's harness (stub modules for the absent lerobot)."""
+    import contextlib
+
+    from oracle import reference_harness as H
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    with contextlib.redirect_stdout(sys.stderr):  # the reference prints banners; stdout carries one JSON line
+        R = H.import_reference(REF_DIR)
+        cfg = pi05_config(num_layers=layers, adarms="gate")
+        wts = synthetic.expert_weights(cfg, seed=0)
+        ks, vs = synthetic.context_kv(cfg, N_CTX, seed=1)
+        ctx = [H.quantized_context(R, ks[l], vs[l]) for l in range(layers)]
+        model = H.build_reference_model(R, cfg, wts, "pi05")
+        H.install_context(R, model, "pi05", ctx)
+        x0, st = synthetic.noise(cfg, seed=2), synthetic.state(cfg, seed=3)
+        times = []
+        with torch.no_grad():
+            for i in range(warmup + chunks):
+                t0 = time.perf_counter()
+                H.run_reference_chunk(R, model, cfg, x0, st, N_CTX)
+                if i >= warmup:
+                    times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times), torch.get_num_threads(), times
+
+
 def run_reference(args):
+    """The reference arm: rank 0 alone times the reference's CPU path of the
+    workload (its own modules from baseline/_ref when that install exists,
+    else the oracle port); the other ranks exit without work."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    med, cores, times = cpu_chunk_ms(args.layers, max(1, args.steps))
+    steps = max(1, args.steps)
+    if os.path.isdir(os.path.join(REF_DIR, "reflex")):
+        med, cores, times = reference_chunks_ms(args.layers, steps, min(max(args.warmup, 0), 2))
+        kind, dtype = "reference", "f32"
+        sample = (f"{len(times)} full 10-step chunks of the workload through Reflex's own PyTorch modules "
+                  "(baseline/_ref install; in-tree gate AdaRMSNorm, its uint8 KV cache; fp32 on the host CPU)")
+    else:
+        med, cores, times = cpu_chunk_ms(args.layers, steps)
+        kind, dtype = "port", "f32"
+        sample = f"{len(times)} full chunks of the workload on the host CPU (fp32 torch oracle port)"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(med, 3), "unit": "ms", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": round(statistics.mean(times), 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
         "config": workload_config(args, world),
-        "cpu_baseline": {"value": round(med, 3), "unit": "ms", "cores": cores, "kind": "port",
-                         "sample": f"{len(times)} full chunks of the workload on the host CPU (fp32 torch)"},
+        "cpu_baseline": {"value": round(med, 3), "unit": "ms", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(med, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -287,6 +350,98 @@ def kernel_roofline(eng, hbm_peak, reps=3):
             "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
 
 
+def multistream_record(args, rank, world, device, pg, hbm_peak, tflops_peak):
+    """The multi-stream configuration: `args.multistream` independent robot
+    streams (each with its own 818-token int8 KV ring, 50-token suffix and
+    x0) sharded data-parallel over the ranks with streams.shard_range and
+    batched along B on each GPU (one CUDA graph per chunk), no collective on
+    the hot path.  Device-timed per chunk with CUDA events, max over ranks;
+    then the final NCCL gather of the [streams, 50, 32] action chunks, timed
+    on its own.  The per-GPU roofline is the slower of the chunk's GEMM +
+    attention FLOPs at the measured sustained bf16 rate and its algorithmic
+    bytes at the measured HBM bandwidth."""
+    from reflex_b200 import synthetic
+    from reflex_b200.config import pi05_config
+    from reflex_b200.expert import ActionExpertEngine
+    from reflex_b200.streams import gather_chunks, shard_range
+
+    total = args.multistream
+    first, n = shard_range(total, rank, world)
+    cfg = pi05_config(num_layers=args.layers, adarms="ssg", quant_mode="i8_sym")
+    wts = synthetic.expert_weights(cfg, seed=0, device=device)
+    eng = ActionExpertEngine(cfg, wts, batch=n, capacity=CAPACITY, n_ctx=N_CTX, device=device,
+                             scale_dtype=torch.float32, fused=n * cfg.suffix_len <= 64)
+    del wts
+    ks, vs = synthetic.context_kv(cfg, N_CTX, B=n, seed=100 + first, device=device)
+    for l in range(cfg.num_layers):
+        eng.load_context(l, ks[l], vs[l])
+    del ks, vs
+    x0 = synthetic.noise(cfg, B=n, seed=200 + first, device=device)
+    eng.set_inputs(x0)
+    eng.capture()
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        eng.set_inputs(x0)
+        eng.launch_chunk()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    evs[0].record(st)
+    for i in range(reps):
+        eng.set_inputs(x0)
+        eng.launch_chunk()
+        evs[i + 1].record(st)
+    torch.cuda.synchronize()
+    per = statistics.median([evs[i].elapsed_time(evs[i + 1]) for i in range(reps)])
+    gather_ms = None
+    if pg:
+        t = torch.tensor([per], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        per = t.item()
+        gt = []
+        for i in range(6):
+            pg.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            out = gather_chunks(eng.x, total, pg)
+            e1.record(st)
+            torch.cuda.synchronize()
+            if i > 0:
+                gt.append(e0.elapsed_time(e1))
+        assert out.shape[0] == total
+        t = torch.tensor([statistics.median(gt)], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        gather_ms = round(t.item(), 4)
+    launches = eng.num_launches
+    eng.plan = None
+    del eng
+    torch.cuda.empty_cache()
+    # per GPU and chunk: GEMM FLOPs of n*50 tokens through 18 layers, attention of n*8*50 query rows over
+    # 868 keys, 10 steps; bytes: weights once per step, each stream's int8 K+V + fp32 scales per step,
+    # and the fp32 modulation weights once per chunk
+    flops = 10 * n * (2 * 50 * 17301504 * args.layers + args.layers * 2 * 2 * 400 * (N_CTX + 50) * 256)
+    nbytes = 10 * (args.layers * 17301504 * 2 + n * args.layers * N_CTX * (256 + 4) * 2) + \
+        (2 * args.layers + 1) * 3 * 1024 * 1024 * 4
+    t_flops = flops / (tflops_peak * 1e12) * 1e3
+    t_bytes = nbytes / (hbm_peak * 1e9) * 1e3
+    return {
+        "workload": f"{total} independent PI0.5 streams (818-token int8 KV ring, 50-token suffix each), "
+                    f"{n} per GPU on {world} GPU(s), batched along B, one CUDA graph per chunk",
+        "streams_total": total, "streams_per_gpu": n, "chunk_ms_p50": round(per, 4),
+        "chunks_per_s": round(total * 1e3 / per, 2), "gather_ms": gather_ms,
+        "gather_bytes": total * 50 * 32 * 4,
+        "engine": "persistent chunk executor" if n * 50 <= 64 else "one launch per op",
+        "gpu_launches_per_chunk": launches,
+        "roofline": {"bound": "tensor" if t_flops >= t_bytes else "hbm", "flops_per_gpu_chunk": flops,
+                     "bytes_per_gpu_chunk": nbytes, "floor_ms": round(max(t_flops, t_bytes), 4),
+                     "frac": round(max(t_flops, t_bytes) / per, 4),
+                     "peaks": f"{tflops_peak} TFLOP/s bf16 sustained, {hbm_peak} GB/s (MEASURED_PEAKS.json)"},
+    }
+
+
 def run_gpu(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -371,6 +526,13 @@ def run_gpu(args):
     roof = chunk_kernel_roofline(eng, hbm_peak) if eng.fused else kernel_roofline(eng, hbm_peak)
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
     status = K.device_status()
+    multi = None
+    if args.multistream > 0:
+        eng.plan = None
+        del eng
+        torch.cuda.empty_cache()
+        multi = multistream_record(args, rank, world, device, pg, hbm_peak, sustained_tflops())
+        status = status or K.device_status()
 
     cpu = None
     if rank == 0 and world == 1:
@@ -381,8 +543,8 @@ def run_gpu(args):
     if rank == 0:
         # weights once per step, each stream's int8 K+V context and fp32 scales per step, and the fp32
         # scale/shift/gate modulation weights once per chunk
-        bytes_chunk = 10 * (eng.cfg.num_layers * 17301504 * 2 + B * eng.cfg.num_layers * N_CTX * (256 + 4) * 2) + \
-            (2 * eng.cfg.num_layers + 1) * 3 * 1024 * 1024 * 4
+        bytes_chunk = 10 * (cfg.num_layers * 17301504 * 2 + B * cfg.num_layers * N_CTX * (256 + 4) * 2) + \
+            (2 * cfg.num_layers + 1) * 3 * 1024 * 1024 * 4
         line = {
             "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": False,
@@ -398,6 +560,7 @@ def run_gpu(args):
             "e2e": {"value": round(e2e_p50, 4), "unit": "ms", "h2d_bytes_per_step": x_host.numel() * 4,
                     "d2h_bytes_per_step": out_host.numel() * 4},
             "gpu_launches": launches * args.steps,
+            "multistream": multi,
             "clocks": clk.summary(),
             "graph": not args.no_graph,
             "device_status": status,
@@ -406,7 +569,6 @@ def run_gpu(args):
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
-        eng.plan = None
         pg.destroy_process_group()
 
 

@@ -1248,6 +1248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d_hint(smem + s * kWBytes, wmap(maps, op), &full[s], (kb0 + j) * kBK, wrow, pol);
               ++armed;
             }
+            if (p.trace && tau == 0 && i < p.trace_tasks)
+              p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 7] = globaltimer_ns();
             int line;
             unsigned target;
             gemm_input(p, op, use, &line, &target);
@@ -1262,6 +1264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(smem + kOffX + s * kXBytes, xmap(maps, op), &full[s], (kb0 + j) * kBK, 0);
             }
             issued += armed;
+            if (p.trace && tau == 0 && i < p.trace_tasks && nw == nkb)
+              p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 13] = globaltimer_ns();
             for (int j = nw; j < nkb && ok; ++j) {
               const uint32_t ii = issued;
               const int s = ii % kStages;
@@ -1336,11 +1340,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned long long* mts =
                 (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                            : nullptr;
+            unsigned long long waited = 0;
             for (int j = 0; j < nkb && ok; ++j) {
               const uint32_t ii = consumed + j;
               const int s = ii % kStages;
-              if (!mbar_try_wait(&full[s], (ii / kStages) & 1))
+              if (!mbar_try_wait(&full[s], (ii / kStages) & 1)) {
+                const unsigned long long w0 = mts ? globaltimer_ns() : 0ull;
                 ok = bar_wait(p, &full[s], (ii / kStages) & 1, kDevTimeoutTmaFull);
+                if (mts && j > 0) waited += globaltimer_ns() - w0;
+              }
               if (!ok) break;
               if (j == 0) stamp(mts, 10);
               if (j == nkb - 1) stamp(mts, 11);
@@ -1356,6 +1364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_commit(&empty[s]);
             }
             consumed += nkb;
+            if (mts) mts[14] = waited;
             if (ok) umma_commit(acc_full);
           } else if (ty == kTAttn) {
             const int sp = tk.w;

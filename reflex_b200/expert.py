@@ -29,9 +29,40 @@ from .synthetic import rope_table
 _QUANT = {"i8_sym": L.RFX_QUANT_I8_SYM, "u8_ref": L.RFX_QUANT_U8_REF}
 
 
+def fused_qkv_weight(weights: dict, prefix: str) -> torch.Tensor:
+    """[Wq; Wk; Wv] of one layer: the fused QKVLinear weight when the state
+    dict holds one (after the reference's init_qkv_fusion_from_existing,
+    modeling_pi05.py:843-866), else the three projections concatenated in
+    that order."""
+    if prefix + "qkv_proj.weight" in weights:
+        return weights[prefix + "qkv_proj.weight"]
+    return torch.cat([weights[prefix + "q_proj.weight"], weights[prefix + "k_proj.weight"],
+                      weights[prefix + "v_proj.weight"]])
+
+
+def fused_gate_up_weight(weights: dict, prefix: str) -> torch.Tensor:
+    """[Wgate; Wup] of one layer (MergedColumnLinear of the reference's
+    init_mlp_fusion_from_existing, modeling_pi05.py:883-917, or the two
+    projections concatenated)."""
+    if prefix + "gate_up_proj.weight" in weights:
+        return weights[prefix + "gate_up_proj.weight"]
+    return torch.cat([weights[prefix + "gate_proj.weight"], weights[prefix + "up_proj.weight"]])
+
+
 class ActionExpertEngine:
+    """Weights, KV rings, activations and launch plan of one action chunk.
+
+    Layer weights come either as separate q/k/v and gate/up projections or
+    as the fused ``qkv_proj`` / ``gate_up_proj`` weights the reference's
+    fusion init leaves.  ``timesteps`` / ``dt`` override the Euler schedule
+    (1.0, 1 - 1/T, ..., 1/T and -1/T by default); the timestep buffer ``t``
+    can be rewritten between chunks.  ``ctx_valid`` [B, capacity] (uint8)
+    masks context slots (all of [0, n_ctx) are visible when every entry is
+    1, the initial state)."""
+
     def __init__(self, cfg: ExpertConfig, weights: dict, *, batch: int = 1, capacity: int = 1024, n_ctx: int = 0,
-                 device="cuda", kv_splits: int = 0, scale_dtype=torch.bfloat16, fused: bool = False):
+                 device="cuda", kv_splits: int = 0, scale_dtype=torch.bfloat16, fused: bool = False,
+                 timesteps=None, dt: float | None = None):
         if not torch.cuda.is_available():
             raise RuntimeError("ActionExpertEngine needs a CUDA device (there is no CPU path)")
         if cfg.num_kv_heads != 1 or cfg.head_dim != 256:
@@ -47,12 +78,44 @@ class ActionExpertEngine:
             raise ValueError("the fused chunk executor keeps fp32 scales for the int8 scheme")
         self.kv_splits = kv_splits
         dev = self.dev
+        Lh, D = cfg.num_layers, cfg.head_dim
+        self.S, self.St = cfg.chunk_size, cfg.suffix_len
+
+        shared = weights if isinstance(weights, ActionExpertEngine) else None
+        if shared is not None:
+            self._share(shared, capacity)
+        else:
+            self._load_weights(weights)
+            # ---- KV rings (one per layer)
+            self.quant_mode = _QUANT[cfg.quant_mode]
+            self.rings = [K.KVRing.allocate(batch, 1, capacity, D, self.quant_mode, scale_dtype=scale_dtype,
+                                            device=dev) for _ in range(Lh)]
+        self.capacity = capacity
+        self._alloc_activations(timesteps, dt)
+        self.workspace = None
+        self.chunk = None
+        self.chunk_ws = None
+        self.plan = None
+        self.set_context_length(n_ctx)
+
+    def _share(self, src: "ActionExpertEngine", capacity: int) -> None:
+        """Weights and KV rings of another engine of the same model and batch
+        (e.g. a one-step engine next to the chunk engine)."""
+        if src.cfg.num_layers != self.cfg.num_layers or src.cfg.variant != self.cfg.variant or src.B != self.B:
+            raise ValueError("a shared engine needs the same model and batch")
+        if src.capacity != capacity:
+            raise ValueError("a shared engine reads the same rings: pass their capacity")
+        for name in ("w_qkv_all", "w_o_all", "w_gu_all", "w_down_all", "w_qkv", "w_o", "w_gu", "w_down", "norm_names",
+                     "norm_a1", "mod_w", "mod_b", "ain_w", "ain_b", "aout_w", "aout_b", "tin_w", "tin_b", "tout_w",
+                     "tout_b", "st_w", "st_b", "atin_w", "atin_b", "atout_w", "atout_b", "quant_mode", "rings"):
+            if hasattr(src, name):
+                setattr(self, name, getattr(src, name))
+
+    def _load_weights(self, weights: dict) -> None:
+        cfg, dev = self.cfg, self.dev
         bf = lambda t: t.to(dev, torch.bfloat16).contiguous()  # noqa: E731
         f32 = lambda t: t.to(dev, torch.float32).contiguous()  # noqa: E731
-        Lh, W, H, D, F, A = cfg.num_layers, cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim, cfg.action_dim
-        S, St = cfg.chunk_size, cfg.suffix_len
-        self.S, self.St = S, St
-
+        Lh, W, H, D, F = cfg.num_layers, cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim
         # ---- weights (fused packs, QKV / gate-up rows permuted for the epilogues),
         # stacked over layers; self.w_*[l] are views of one layer
         self.w_qkv_all = torch.empty(Lh, (H + 2) * D, W, dtype=torch.bfloat16, device=dev)
@@ -61,11 +124,9 @@ class ActionExpertEngine:
         self.w_down_all = torch.empty(Lh, W, F, dtype=torch.bfloat16, device=dev)
         for l in range(Lh):
             p = f"layers.{l}."
-            qkv = torch.cat([weights[p + "q_proj.weight"], weights[p + "k_proj.weight"], weights[p + "v_proj.weight"]])
-            self.w_qkv_all[l].copy_(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
+            self.w_qkv_all[l].copy_(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(fused_qkv_weight(weights, p))))
             self.w_o_all[l].copy_(bf(weights[p + "o_proj.weight"]))
-            gu = torch.cat([weights[p + "gate_proj.weight"], weights[p + "up_proj.weight"]])
-            self.w_gu_all[l].copy_(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
+            self.w_gu_all[l].copy_(K.pack_weight(L.RFX_PACK_GATE_UP, bf(fused_gate_up_weight(weights, p))))
             self.w_down_all[l].copy_(bf(weights[p + "down_proj.weight"]))
         self.w_qkv = list(self.w_qkv_all.unbind(0))
         self.w_o = list(self.w_o_all.unbind(0))
@@ -94,12 +155,11 @@ class ActionExpertEngine:
             self.atout_w = bf(weights["action_time_mlp_out.weight"])
             self.atout_b = f32(weights["action_time_mlp_out.bias"])
 
-        # ---- KV rings (one per layer)
-        self.quant_mode = _QUANT[cfg.quant_mode]
-        self.rings = [K.KVRing.allocate(batch, 1, capacity, D, self.quant_mode, scale_dtype=scale_dtype, device=dev)
-                      for _ in range(Lh)]
-        self.capacity = capacity
-
+    def _alloc_activations(self, timesteps, dt) -> None:
+        cfg, dev, batch = self.cfg, self.dev, self.B
+        W, H, D, F, A = cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim, cfg.action_dim
+        S, St = self.S, self.St
+        norm_names = self.norm_names
         # ---- activations
         T = batch * St
         self.T = T
@@ -112,8 +172,13 @@ class ActionExpertEngine:
         self.act = z(T, F)
         self.x = z(batch, S, A, dt=torch.float32)
         nt = cfg.num_steps
-        self.t = torch.tensor(timestep_schedule(nt), dtype=torch.float32, device=dev)
-        self.dt = float(np.float32(-1.0 / nt))
+        sched = timestep_schedule(nt) if timesteps is None else [float(x) for x in timesteps]
+        if len(sched) != nt:
+            raise ValueError(f"{len(sched)} timesteps for {nt} Euler steps")
+        self.t = torch.tensor(sched, dtype=torch.float32, device=dev)
+        self.dt = float(np.float32(-1.0 / nt if dt is None else dt))
+        self.ctx_valid = torch.ones(batch, self.capacity, dtype=torch.uint8, device=dev)
+        self.use_ctx_valid = False
         self.cond = z(nt, W)
         self.tc_hidden = z(nt, W)
         nn_ = len(norm_names)
@@ -132,11 +197,6 @@ class ActionExpertEngine:
             self.temb = z(nt, W)
             self.at_x = z(batch * S, 2 * W)
             self.at_hid = z(batch * S, W)
-        self.workspace = None
-        self.chunk = None
-        self.chunk_ws = None
-        self.plan = None
-        self.set_context_length(n_ctx)
 
     # ------------------------------------------------------------ context ---
     def set_context_length(self, n_ctx: int) -> None:
@@ -149,6 +209,24 @@ class ActionExpertEngine:
         pos = n_ctx + torch.arange(self.St, dtype=torch.int32)
         self.positions.copy_(pos.repeat(self.B))
         self._build_ops()
+
+    def set_context_mask(self, valid: torch.Tensor | None) -> None:
+        """Per-slot visibility of the context [B, n_ctx] (bool / 0-1) for the
+        following chunks (a padded prefix token is invisible to the suffix,
+        as build_attention_mask_and_position_ids makes it, reflex/policies/
+        pi05/utils.py:210-215); None makes every slot of [0, n_ctx) visible."""
+        if valid is None:
+            if self.use_ctx_valid:
+                self.ctx_valid.fill_(1)
+                self.use_ctx_valid = False
+                self._build_ops()
+            return
+        if valid.shape != (self.B, self.n_ctx):
+            raise ValueError(f"context mask must be [{self.B}, {self.n_ctx}], got {tuple(valid.shape)}")
+        self.ctx_valid[:, :self.n_ctx].copy_(valid.to(self.dev, torch.uint8), non_blocking=True)
+        if not self.use_ctx_valid:
+            self.use_ctx_valid = True
+            self._build_ops()
 
     def load_context(self, layer: int, k: torch.Tensor, v: torch.Tensor, region_base: int = 0,
                      region_off: int = 0, region_len: int | None = None) -> None:
@@ -228,6 +306,7 @@ class ActionExpertEngine:
                 dense = B > 1 or self.n_ctx >= 32 * 64
                 ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l],
                                       n_ctx=self.n_ctx, out=self.attn_out, softmax_scale=D ** -0.5,
+                                      ctx_valid=self.ctx_valid if self.use_ctx_valid else None,
                                       new_block=self.new_block if cfg.variant == "pi0" else None,
                                       kv_splits=self.kv_splits,
                                       kv_source=L.RFX_KV_DENSE if dense else L.RFX_KV_RING_TILES)
@@ -295,7 +374,7 @@ class ActionExpertEngine:
                             arr([r.k_zp for r in self.rings]), arr([r.v_zp for r in self.rings])]
         cast = lambda a: ctypes.cast(a, ctypes.POINTER(ctypes.c_void_p))  # noqa: E731
         d.k_ring, d.v_ring, d.k_scale, d.v_scale, d.k_zp, d.v_zp = [cast(a) for a in self._chunk_ptrs]
-        d.ctx_valid = None
+        d.ctx_valid = self.ctx_valid.data_ptr() if self.use_ctx_valid else None
         d.x = self.x.data_ptr()
         n = ctypes.c_size_t(0)
         L.call("rfx_chunk_workspace_size", ctypes.byref(d), ctypes.byref(n))

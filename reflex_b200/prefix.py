@@ -25,11 +25,19 @@ import torch
 from . import _lib as L
 from . import kernels as K
 from .config import ExpertConfig
+from .expert import fused_gate_up_weight, fused_qkv_weight
 from .synthetic import rope_table
 
 
 class PrefixEngine:
-    def __init__(self, cfg: ExpertConfig, weights: dict, rings: list, *, pinned: int, frame_len: int,
+    """``weights`` is a state dict of the prefix layers (separate or fused
+    projections) or another PrefixEngine whose packed weights are shared
+    (e.g. one engine for the pinned instruction, pinned=0 and
+    window_frames=1, and one for the observation frames over the same rings).
+    ``ops(slot, prior)`` also serves the window while it fills: ``prior``
+    frames (slots 0 .. prior-1) are in the window before the new one."""
+
+    def __init__(self, cfg: ExpertConfig, weights, rings: list, *, pinned: int, frame_len: int,
                  window_frames: int = 2, batch: int = 1, device="cuda", kv_splits: int = 0):
         if cfg.num_kv_heads != 1 or cfg.head_dim != 256:
             raise ValueError("the kernels serve one 256-wide KV head (MQA)")
@@ -45,17 +53,20 @@ class PrefixEngine:
         dev = self.dev
         bf = lambda t: t.to(dev, torch.bfloat16).contiguous()  # noqa: E731
         Lh, W, H, D, F = cfg.num_layers, cfg.width, cfg.num_heads, cfg.head_dim, cfg.mlp_dim
-        self.w_qkv, self.w_o, self.w_gu, self.w_down, self.a_in, self.a_post = [], [], [], [], [], []
-        for l in range(Lh):
-            p = f"layers.{l}."
-            qkv = torch.cat([weights[p + "q_proj.weight"], weights[p + "k_proj.weight"], weights[p + "v_proj.weight"]])
-            self.w_qkv.append(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(qkv)))
-            self.w_o.append(bf(weights[p + "o_proj.weight"]))
-            gu = torch.cat([weights[p + "gate_proj.weight"], weights[p + "up_proj.weight"]])
-            self.w_gu.append(K.pack_weight(L.RFX_PACK_GATE_UP, bf(gu)))
-            self.w_down.append(bf(weights[p + "down_proj.weight"]))
-            self.a_in.append(weights[p + "input_layernorm.weight"].to(dev, torch.float32).contiguous())
-            self.a_post.append(weights[p + "post_attention_layernorm.weight"].to(dev, torch.float32).contiguous())
+        if isinstance(weights, PrefixEngine):
+            src = weights
+            self.w_qkv, self.w_o, self.w_gu, self.w_down = src.w_qkv, src.w_o, src.w_gu, src.w_down
+            self.a_in, self.a_post = src.a_in, src.a_post
+        else:
+            self.w_qkv, self.w_o, self.w_gu, self.w_down, self.a_in, self.a_post = [], [], [], [], [], []
+            for l in range(Lh):
+                p = f"layers.{l}."
+                self.w_qkv.append(K.pack_weight(L.RFX_PACK_QKV_ROPE, bf(fused_qkv_weight(weights, p))))
+                self.w_o.append(bf(weights[p + "o_proj.weight"]))
+                self.w_gu.append(K.pack_weight(L.RFX_PACK_GATE_UP, bf(fused_gate_up_weight(weights, p))))
+                self.w_down.append(bf(weights[p + "down_proj.weight"]))
+                self.a_in.append(weights[p + "input_layernorm.weight"].to(dev, torch.float32).contiguous())
+                self.a_post.append(weights[p + "post_attention_layernorm.weight"].to(dev, torch.float32).contiguous())
         T = batch * frame_len
         self.T = T
         z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
@@ -66,15 +77,7 @@ class PrefixEngine:
         self.attn_out = z(T, H * D)
         self.act = z(T, F)
         self.rope = rope_table(cfg.max_position_embeddings, D, cfg.rope_theta).to(dev)
-        pos = pinned + (window_frames - 1) * frame_len + torch.arange(frame_len, dtype=torch.int32)
-        self.positions = pos.repeat(batch).to(dev)
-        # context validity while frame slot s is being replaced: everything but slot s
-        self.valid = []
-        for s in range(window_frames):
-            m = torch.ones(batch, rings[0].capacity, dtype=torch.uint8)
-            m[:, cap:] = 0
-            m[:, pinned + s * frame_len: pinned + (s + 1) * frame_len] = 0
-            self.valid.append(m.to(dev))
+        self._state = {}  # (slot, prior) -> (positions, context validity)
         self.kv_splits = kv_splits
         self.workspace = None
         self.split_ws = None  # split-K workspace of the GEMMs (zero-filled; one stream)
@@ -89,22 +92,49 @@ class PrefixEngine:
         """The new frame's embeddings [B, frame_len, width]."""
         self.h.copy_(emb.reshape(self.T, -1), non_blocking=True)
 
-    def ops(self, slot: int) -> list:
-        """Launch list of one frame update that replaces frame slot `slot`."""
+    def _positions_and_valid(self, slot: int, prior: int):
+        """Positions of the new frame's tokens and the context it sees when it
+        replaces frame slot `slot` with `prior` frames in the window: the
+        pinned prefix plus the window's other filled slots (slots 0 .. prior-1
+        while the window fills, every slot but `slot` once it is full).  The
+        positions continue after that context, as the reference's streaming
+        prefill counts them (modeling_pi05.py:1301-1316)."""
+        key = (slot, prior)
+        if key not in self._state:
+            W, F, P = self.window_frames, self.frame_len, self.pinned
+            if not 0 <= prior <= W - 1 or not 0 <= slot < W or (prior < W - 1 and slot != prior):
+                raise ValueError(f"frame slot {slot} with {prior} prior frames in a window of {W}")
+            pos = P + prior * F + torch.arange(F, dtype=torch.int32)
+            m = torch.zeros(self.B, self.rings[0].capacity, dtype=torch.uint8)
+            m[:, :P] = 1
+            for s in range(W):
+                if s != slot and (s < prior or prior == W - 1):
+                    m[:, P + s * F: P + (s + 1) * F] = 1
+            self._state[key] = (pos.repeat(self.B).to(self.dev), m.to(self.dev))
+        return self._state[key]
+
+    @property
+    def positions(self):
+        return self._positions_and_valid(0, self.window_frames - 1)[0]
+
+    def ops(self, slot: int, prior: int | None = None) -> list:
+        """Launch list of one frame update that replaces frame slot `slot`
+        (`prior` frames already in the window; default: a full window)."""
         cfg, B, S, T = self.cfg, self.B, self.frame_len, self.T
         H, D = cfg.num_heads, cfg.head_dim
         base = self.pinned + slot * self.frame_len
+        positions, valid = self._positions_and_valid(slot, self.window_frames - 1 if prior is None else prior)
         out = [("barrier", None, None)]
         attn_descs = []
         for l in range(cfg.num_layers):
             out.append(("norm", K.norm_desc(x=self.h, y=self.xn, S=S, norm_a1=self.a_in[l], eps=cfg.eps), None))
             out.append(("linear", K.linear_desc(
                 w=self.w_qkv[l], x=self.xn, T=T, S=S, epilogue=L.RFX_EPI_QKV_ROPE, rope_table=self.rope,
-                positions=self.positions, q_out=self.q, k_out=self.k_new, v_out=self.v_new, num_q_heads=H), None))
+                positions=positions, q_out=self.q, k_out=self.k_new, v_out=self.v_new, num_q_heads=H), None))
             # every one of the frame's query tiles visits every key block:
             # dequantize the context once per layer (RFX_KV_DENSE)
             ad = K.attention_desc(q=self.q, k_new=self.k_new, v_new=self.v_new, ring=self.rings[l], n_ctx=self.n_ctx,
-                                  out=self.attn_out, softmax_scale=D ** -0.5, ctx_valid=self.valid[slot],
+                                  out=self.attn_out, softmax_scale=D ** -0.5, ctx_valid=valid,
                                   kv_splits=self.kv_splits, kv_source=L.RFX_KV_DENSE)
             attn_descs.append(ad)
             out.append(("attn", ad, None))
@@ -134,10 +164,12 @@ class PrefixEngine:
         return out
 
     def run(self, emb: torch.Tensor | None = None) -> None:
-        """One frame update through the direct entry points (eager)."""
+        """One frame update through the direct entry points (eager); the
+        window fills first (frame f goes to slot f % window_frames)."""
         if emb is not None:
             self.set_frame(emb)
-        for kind, desc, _ in self.ops(self.frames % self.window_frames):
+        W = self.window_frames
+        for kind, desc, _ in self.ops(self.frames % W, min(self.frames, W - 1)):
             if kind != "barrier":
                 K.Plan.run_direct(desc)
         self.frames += 1

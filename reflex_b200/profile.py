@@ -38,6 +38,7 @@ def main():
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
     ap.add_argument("--trace", action="store_true",
                     help="with --chunk --fused: %%globaltimer stamps of every task of the first Euler step")
+    ap.add_argument("--trace-out", default=None, help="with --trace: also save the raw stamps (.npy)")
     ap.add_argument("--frame", action="store_true",
                     help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
                          "pinned prefix and a 2-frame window)")
@@ -61,7 +62,7 @@ def main():
     eng.run_eager()
     torch.cuda.synchronize()
     if args.chunk and args.fused and args.trace:
-        trace_chunk(eng)
+        trace_chunk(eng, out=args.trace_out)
         return
     if args.chunk:
         print("launches per chunk", eng.num_launches)
@@ -166,7 +167,7 @@ _TASKS = {1: "qkv", 2: "o", 3: "gu", 4: "down", 5: "attn", 6: "comb", 7: "fin_o"
 _ORDER = ["qkv", "attn", "comb", "o", "fin_o", "gu", "down", "fin_d"]
 
 
-def trace_chunk(eng, per_cta: int = 256) -> None:
+def trace_chunk(eng, per_cta: int = 256, out: str | None = None) -> None:
     """Runs one chunk with task tracing on and prints, for the first Euler step,
     the per-layer phase timeline and the median segments of the GEMM tasks."""
     import numpy as np
@@ -184,6 +185,8 @@ def trace_chunk(eng, per_cta: int = 256) -> None:
     L.call("rfx_set_trace", None, 0)
     print("status", K.device_status())
     tr = buf.view(nsm, per_cta, 16).cpu().numpy().astype(np.int64)
+    if out:
+        np.save(out, tr)
     rows = []
     for c in range(nsm):
         for i in range(per_cta):
@@ -217,6 +220,9 @@ def trace_chunk(eng, per_cta: int = 256) -> None:
         print(f"{name:5s} producer saw input -> first stage {seg(name, 3, 10):.2f}, first -> last stage "
               f"{seg(name, 10, 11):.2f}, last stage -> accumulator ready {seg(name, 11, 1):.2f}, "
               f"accumulator -> stored {seg(name, 1, 6):.2f}, stored -> end {seg(name, 6, 2):.2f} us")
+        print(f"{'':5s} weights issued (last) -> producer saw input {seg(name, 13, 3):.2f}, armed weights issued -> "
+              f"saw input {seg(name, 7, 3):.2f}, MMA waited on stages 2..n: "
+              f"{float(np.median([r[2][14] / 1e3 for r in rows if r[0] == name])):.2f} us")
         print(f"{'':5s} read out -> own rows stored {seg(name, 6, 8):.2f}, -> peer partial arrived "
               f"{seg(name, 8, 9):.2f}, -> epilogue done {seg(name, 9, 12):.2f}, -> end {seg(name, 12, 2):.2f}, "
               f"task start -> producer saw input {seg(name, 0, 3):.2f} us")

@@ -23,12 +23,18 @@ def gen(seed):
 
 
 def _dequant(a):
+    """The source tokens [0, source_length) in logical order, dequantized (fp32)."""
     r = a.ring
-    n = a.source_length
-    kd = oq.dequant_u8_ref(r.k_q[:, :, :n].cpu().numpy(), r.k_scale[:, :, :n, None].float().cpu().numpy(),
-                           r.k_zp[:, :, :n, None].float().cpu().numpy(), True)
-    vd = oq.dequant_u8_ref(r.v_q[:, :, :n].cpu().numpy(), r.v_scale[:, :, :n, None].float().cpu().numpy(),
-                           r.v_zp[:, :, :n, None].float().cpu().numpy(), True)
+    sl = a.source_slots(0, a.source_length).to(r.k_q.device)
+    g = lambda t: t[:, :, sl]  # noqa: E731
+    if r.k_zp is None:  # int8 symmetric
+        kd = oq.dequant_i8_sym(g(r.k_q).cpu().numpy(), g(r.k_scale)[..., None].cpu().numpy())
+        vd = oq.dequant_i8_sym(g(r.v_q).cpu().numpy(), g(r.v_scale)[..., None].cpu().numpy())
+        return torch.from_numpy(kd), torch.from_numpy(vd)
+    kd = oq.dequant_u8_ref(g(r.k_q).cpu().numpy(), g(r.k_scale)[..., None].float().cpu().numpy(),
+                           g(r.k_zp)[..., None].float().cpu().numpy(), True)
+    vd = oq.dequant_u8_ref(g(r.v_q).cpu().numpy(), g(r.v_scale)[..., None].float().cpu().numpy(),
+                           g(r.v_zp)[..., None].float().cpu().numpy(), True)
     return torch.from_numpy(kd), torch.from_numpy(vd)
 
 
@@ -49,12 +55,14 @@ def test_fused_quantize_store_bit_exact():
     assert int(cache[:, :, :11].abs().sum()) == 0
 
 
-@pytest.mark.parametrize("masked", [False, True])
-def test_streaming_attention_lifecycle(masked):
+@pytest.mark.parametrize("masked,quantize", [(False, True), (True, True), (True, False)])
+def test_streaming_attention_lifecycle(masked, quantize):
+    """quantize=True: the reference's uint8 source cache; quantize=False (the
+    reference's default): the source kept as int8 with per-token scales."""
     from reflex_b200.layers import StreamingAttention
     r = gen(2)
     B, Hq, D, S = 2, 8, 256, 51
-    a = StreamingAttention(D ** -0.5, max_cache_size=1024, quantize_kv_cache=True)
+    a = StreamingAttention(D ** -0.5, max_cache_size=1024, quantize_kv_cache=quantize)
     k1, v1 = r(B, 1, 300, D).bfloat16(), r(B, 1, 300, D).bfloat16()
     k2, v2 = r(B, 1, 200, D).bfloat16(), r(B, 1, 200, D).bfloat16()
     a.prefill_source(k1.cuda(), v1.cuda())
@@ -91,10 +99,57 @@ def test_streaming_attention_lifecycle(masked):
     ref = partitioned_attention(q.float(), kd, vd, ks.float(), vs.float(), pad, att, D ** -0.5)
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 2e-2, err
-    # the evicted source kept its values: the slots after the shift hold the old ones
+    # the surviving source tokens keep their quantized values after the eviction
     kd_all, _ = _dequant(a)
-    k_ref = oq.dequant_u8_ref(*oq.quant_u8_ref(torch.cat([k1, k2], 2).float().numpy(), True), True)
+    both = torch.cat([k1, k2], 2).float().numpy()
+    if quantize:
+        k_ref = oq.dequant_u8_ref(*oq.quant_u8_ref(both, True), True)
+    else:
+        k_ref = oq.dequant_i8_sym(*oq.quant_i8_sym(both))
+        # against the unquantized source: int8 keys / values cost at most absmax / 254 per value
+        ref_exact = partitioned_attention(q.float(), torch.cat([k1, k2], 2)[:, :, 120 + start:500].float(),
+                                          torch.cat([v1, v2], 2)[:, :, 120 + start:500].float(), ks.float(),
+                                          vs.float(), pad, att, D ** -0.5)
+        assert (out.float().cpu() - ref_exact).abs().max().item() <= 5e-2
     assert np.array_equal(kd_all.numpy(), k_ref[:, :, 120:500])
+    # the same mask object again: its structure comes from the cache
+    if masked:
+        hits = a.cache_stats["mask_cache_hits"]
+        out2 = a.forward(q.cuda(), ks.cuda(), vs.cuda(), attention_mask=mask)
+        assert a.cache_stats["mask_cache_hits"] == hits + 1
+        assert torch.equal(out2, out)
+
+
+def test_streaming_attention_wrapping_ring():
+    """Appends after evictions wrap around the ring; decode over the wrapped
+    source matches attention over the logical source order."""
+    from reflex_b200.layers import StreamingAttention
+    r = gen(4)
+    B, Hq, D, S, cap = 1, 8, 256, 50, 512
+    a = StreamingAttention(D ** -0.5, max_cache_size=cap)
+    ks_all, vs_all = [], []
+    for _ in range(4):  # four frames of 200 tokens, keeping the last two
+        k, v = r(B, 1, 200, D).bfloat16(), r(B, 1, 200, D).bfloat16()
+        if a.source_length + 200 > cap:
+            a.evict_source_prefix(200)
+            ks_all, vs_all = ks_all[1:], vs_all[1:]
+        a.prefill_source(k.cuda(), v.cuda())
+        ks_all.append(k)
+        vs_all.append(v)
+    assert a.source_length == 400 and a._head == 400  # slots 400..511 then 0..287
+    a.merge_caches()
+    q = r(B, Hq, S, D).bfloat16()
+    kn, vn = r(B, 1, S, D).bfloat16(), r(B, 1, S, D).bfloat16()
+    out = a.forward(q.cuda(), kn.cuda(), vn.cuda())
+    torch.cuda.synchronize()
+    kd, vd = _dequant(a)
+    src = torch.cat(ks_all, 2).float().numpy()
+    assert np.array_equal(kd.numpy(), oq.dequant_i8_sym(*oq.quant_i8_sym(src)))
+    att = torch.zeros(S, dtype=torch.int64)
+    att[0] = 1
+    ref = partitioned_attention(q.float(), kd, vd, kn.float(), vn.float(), torch.ones(B, 400, dtype=torch.bool),
+                                att, D ** -0.5)
+    assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
 
 
 def test_qkv_and_merged_linear():
@@ -102,8 +157,9 @@ def test_qkv_and_merged_linear():
     r = gen(3)
     B, Lx, Hd = 2, 50, 1024
     x = (r(B, Lx, Hd)).bfloat16()
-    qkv = QKVLinear(Hd, 256, 8, 1)
-    qkv.weight.copy_((r(*qkv.weight.shape) * 0.03).bfloat16())
+    qkv = QKVLinear(Hd, 256, 8, 1).to(device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        qkv.weight.copy_((r(*qkv.weight.shape) * 0.03).bfloat16())
     q, k, v = qkv.forward(x.cuda())
     y = x.float().reshape(-1, Hd) @ qkv.weight.float().cpu().t()
     ref_q = y[:, :2048].view(B, Lx, 8, 256).transpose(1, 2)
@@ -112,11 +168,12 @@ def test_qkv_and_merged_linear():
     for got, ref in ((q, ref_q), (k, ref_k), (v, ref_v)):
         assert got.shape == ref.shape
         assert torch.allclose(got.float().cpu(), ref, atol=1e-2, rtol=1e-2)
-    mc = MergedColumnLinear(Hd, [4096, 4096], bias=True)
-    mc.weight.copy_((r(*mc.weight.shape) * 0.03).bfloat16())
-    mc.bias.copy_(r(8192) * 0.1)
+    mc = MergedColumnLinear(Hd, [4096, 4096], bias=True).to(device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        mc.weight.copy_((r(*mc.weight.shape) * 0.03).bfloat16())
+        mc.bias.copy_(r(8192) * 0.1)
     g, u = mc.forward(x.cuda())
-    y = x.float().reshape(-1, Hd) @ mc.weight.float().cpu().t() + mc.bias.cpu()
+    y = x.float().reshape(-1, Hd) @ mc.weight.float().cpu().t() + mc.bias.float().cpu()
     assert g.shape == (B, Lx, 4096) and u.shape == (B, Lx, 4096)
     assert torch.allclose(g.float().cpu().reshape(-1, 4096), y[:, :4096], atol=1e-2, rtol=1e-2)
     assert torch.allclose(u.float().cpu().reshape(-1, 4096), y[:, 4096:], atol=1e-2, rtol=1e-2)
