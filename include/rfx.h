@@ -64,6 +64,16 @@ const char* rfx_last_error(void);
  * synchronizing `stream`. *out receives 0 or a non-zero device error code. */
 int rfx_device_status(void* stream, int* out);
 
+/* Bound, in nanoseconds, of the device waits on other CTAs' work in the
+ * persistent chunk executor (phase counters), for launches made afterwards
+ * by this process; 0 restores the default of one second.  A wait that runs
+ * out records a device status code (rfx_device_status), every role of the
+ * launch leaves its loop, drains its copies and MMAs in flight and frees its
+ * TMEM, and the next launch runs normally.  Waits on a CTA's own copies and
+ * MMAs keep the one-second bound.  No counterpart in the reference (its
+ * kernels do not wait on one another). */
+int rfx_set_wait_limit_ns(unsigned long long ns);
+
 /* Enables (1) or disables (0) programmatic dependent launch for kernels
  * launched afterwards by this process. Default: enabled. */
 int rfx_set_pdl(int enable);
@@ -399,6 +409,11 @@ typedef struct rfx_chunk_desc {
   const void* const* v_zp;
   const unsigned char* ctx_valid; /* [B][capacity] or NULL */
   float* x;                   /* fp32 [B][S][action_dim]: x0 in, denoised actions out */
+  /* Parity checks only (NULL in production): the first Euler step's residual
+   * stream after each layer, bf16 [num_layers][B*S][width], and attention
+   * output of each layer, bf16 [num_layers][B*S][num_q_heads*256]. */
+  void* debug_hidden;
+  void* debug_attn;
 } rfx_chunk_desc;
 /* Device workspace the executor needs (activations, partial sums, counters,
  * task tables); 256-byte aligned, owned by the caller. */

@@ -157,7 +157,7 @@ class ChunkDesc(Structure):
         ("k_ring", POINTER(c_void_p)), ("v_ring", POINTER(c_void_p)),
         ("k_scale", POINTER(c_void_p)), ("v_scale", POINTER(c_void_p)),
         ("k_zp", POINTER(c_void_p)), ("v_zp", POINTER(c_void_p)),
-        ("ctx_valid", c_void_p), ("x", c_void_p),
+        ("ctx_valid", c_void_p), ("x", c_void_p), ("debug_hidden", c_void_p), ("debug_attn", c_void_p),
     ]
 
 
@@ -167,6 +167,7 @@ SIGNATURES = {
     "rfx_last_error": ([], ctypes.c_char_p),
     "rfx_device_status": ([c_void_p, POINTER(c_int)], c_int),
     "rfx_set_pdl": ([c_int], c_int),
+    "rfx_set_wait_limit_ns": ([ctypes.c_ulonglong], c_int),
     "rfx_set_trace": ([c_void_p, c_size_t], c_int),
     "rfx_num_sms": ([POINTER(c_int)], c_int),
     "rfx_kv_quant_append": ([POINTER(KvQuantDesc), c_void_p], c_int),

@@ -92,6 +92,7 @@ constexpr int kSmTmem = 192;
 constexpr int kSmKvnFull = 200;    // mbarrier: the new keys' K / V tiles (TMA) have landed
 constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA has pushed its partial into this CTA's tile buffer
 constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has read its tile buffer (this CTA may push again)
+constexpr int kSmMmaDrain = 224;   // mbarrier: every MMA this CTA issued has completed (teardown)
 constexpr int kSmRed8 = 320;       // 8 floats
 constexpr int kSmXs = 512;         // 64 floats
 static_assert(kSmXs + 256 <= kSmallBytes, "small region");
@@ -157,6 +158,9 @@ struct ChunkParams {
   int* status;
   unsigned long long* trace;  // [grid][trace_tasks][16] stamps + task of the first step, or null
   int trace_tasks;
+  unsigned long long dep_limit_ns;  // bound of a wait on another CTA's phase counter (rfx_set_wait_limit_ns)
+  __nv_bfloat16* dbg_h;     // [NL][T][W] step-0 residual stream after each layer, or null
+  __nv_bfloat16* dbg_attn;  // [NL][T][Hq*256] step-0 attention output of each layer, or null
 };
 
 struct Maps {
@@ -220,7 +224,7 @@ __device__ bool ctr_wait(const ChunkParams& p, int line, unsigned target) {
       __nanosleep(32);
     }
     if (aborted(p)) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > p.dep_limit_ns) {
       raise_abort(p, kDevTimeoutDependency);
       return false;
     }
@@ -934,6 +938,11 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
             w8[e] = pack_bf16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
           *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
           *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          if (p.dbg_attn && use < static_cast<unsigned>(p.NL)) {
+            __nv_bfloat16* drow = p.dbg_attn + static_cast<long>(use) * p.T * p.Hq * kD + (orow - p.attn_out);
+            *reinterpret_cast<uint4*>(drow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+            *reinterpret_cast<uint4*>(drow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          }
         } else {
           uint32_t w8[8];
 #pragma unroll
@@ -1008,10 +1017,11 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
     const int s_row = R % p.S, h_row = R / p.S;
     __nv_bfloat16* orow =
         p.attn_out + (static_cast<long>(b) * p.S + s_row) * (static_cast<long>(p.Hq) * kD) + h_row * kD + lane * 8;
-    *reinterpret_cast<uint4*>(orow) = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv),
-                                                 pack_bf16x2(acc[2] * inv, acc[3] * inv),
-                                                 pack_bf16x2(acc[4] * inv, acc[5] * inv),
-                                                 pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    const uint4 packed = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                                    pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    *reinterpret_cast<uint4*>(orow) = packed;
+    if (p.dbg_attn && use < static_cast<unsigned>(p.NL))
+      *reinterpret_cast<uint4*>(p.dbg_attn + static_cast<long>(use) * p.T * p.Hq * kD + (orow - p.attn_out)) = packed;
   }
   workers_publish(p, et, kCComb);
   return true;
@@ -1081,6 +1091,8 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
       hv[e] = bf16_round(__fadd_rn(hres[e], ga));
     }
   }
+  if (kind == kTFinD && tau == 0 && p.dbg_h)
+    *reinterpret_cast<uint2*>(p.dbg_h + (static_cast<long>(layer) * p.T + t) * p.W + f0) = pack4_bf16(hv);
   if (tail) {
     // final norm -> action_out_proj -> x += bf16(dt * v) -> next step's action_in_proj
     float y[4];
@@ -1195,6 +1207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmKvnFull), 1);
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), kWorkers / 64);  // the peer's pushing warps
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), kWorkers / 32);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmMmaDrain), 1);
     fence_mbar_init();
     for (int i = 0; i < 4; ++i) {
       tma_prefetch_desc(&maps.w[i]);
@@ -1220,6 +1233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int4* stasks = p.step_tasks + p.step_off[cta];
   const int n_step = p.step_off[cta + 1] - p.step_off[cta];
   uint32_t issued = 0;  // ring stages issued by the producer
+  uint32_t q_issued = 0, kvn_issued = 0;  // attention Q / new-key tile loads issued by the producer
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1293,6 +1307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int b = tk.y, qt = tk.z;
             const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
             mbar_arrive_expect_tx(q_full, 4 * 16384);
+            ++q_issued;
             for (int a = 0; a < 4; ++a)
               tma_load_2d(smem + kOffAQ + a * 16384, &maps.q, q_full, a * 64, static_cast<int>(q_row0));
             const int sp = tk.w;
@@ -1304,6 +1319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int row0 = b * p.S + (blk0 - p.n_ctx_blocks) * kKB;
               uint64_t* kvn_full = reinterpret_cast<uint64_t*>(small + kSmKvnFull);
               mbar_arrive_expect_tx(kvn_full, 8 * 8192);
+              ++kvn_issued;
               for (int a = 0; a < 4; ++a) {
                 tma_load_2d(smem + kOffAK + a * 8192, &maps.kn, kvn_full, a * 64, row0);
                 tma_load_2d(smem + kOffAV + a * 8192, &maps.vn, kvn_full, a * 64, row0);
@@ -1446,11 +1462,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---- teardown: bounded drain of copies in flight, then free TMEM ----
+  // ---- teardown: bounded drain of copies and MMAs in flight (after an
+  // abort some were never waited for), then free TMEM ----
   __syncthreads();
   if (warp == 0 && lane == 0) {
     for (uint32_t ii = (issued > kStages ? issued - kStages : 0); ii < issued; ++ii)
       mbar_wait(&full[ii % kStages], (ii / kStages) & 1, p.status, kDevTimeoutTmaFull);
+    if (q_issued > 0) mbar_wait(q_full, (q_issued - 1) & 1, p.status, kDevTimeoutTmaFull);
+    if (kvn_issued > 0)
+      mbar_wait(reinterpret_cast<uint64_t*>(small + kSmKvnFull), (kvn_issued - 1) & 1, p.status, kDevTimeoutTmaFull);
+  }
+  if (warp == 1 && lane == 0) {
+    uint64_t* drain = reinterpret_cast<uint64_t*>(small + kSmMmaDrain);
+    umma_commit(drain);  // arrives once every MMA issued before it has completed
+    mbar_wait(drain, 0, p.status, kDevTimeoutMmaDone);
   }
   // the peer CTA writes into this CTA's shared memory until its last paired item
   tc_fence_before();
@@ -1766,6 +1791,8 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
   p.ws_ml = reinterpret_cast<float2*>(ws + L.off_ws_ml);
   p.ctr = reinterpret_cast<unsigned*>(ws + L.off_ctr);
   p.status = device_status_ptr();
+  p.dbg_h = static_cast<__nv_bfloat16*>(d.debug_hidden);
+  p.dbg_attn = static_cast<__nv_bfloat16*>(d.debug_attn);
 
   // per-layer context pointer tables
   const int NL = d.num_layers;
@@ -1857,6 +1884,7 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   // resident at once (one per SM), which the cooperative attribute guarantees
   // trace layout: [grid][256 tasks][16] (tasks past 256 of a CTA are not recorded)
   c->params.trace_tasks = 256;
+  c->params.dep_limit_ns = dependency_wait_limit_ns();
   c->params.trace = static_cast<unsigned long long*>(trace_buffer(static_cast<size_t>(c->grid) * 256 * 16));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->grid);

@@ -25,6 +25,9 @@ void* trace_buffer(size_t n_events);
 // Whether kernels are launched with programmatic dependent launch.
 bool pdl_enabled();
 
+// Bound (ns) of device waits on work of other CTAs (rfx_set_wait_limit_ns).
+unsigned long long dependency_wait_limit_ns();
+
 // ------------------------------------------------------------------ enums ---
 enum QuantMode : int { kQuantI8Sym = RFX_QUANT_I8_SYM, kQuantU8Ref = RFX_QUANT_U8_REF };
 enum Dtype : int { kDtypeF32 = RFX_DTYPE_F32, kDtypeBF16 = RFX_DTYPE_BF16 };

@@ -34,6 +34,11 @@ int check_cuda(cudaError_t e, const char* what) {
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 
+namespace {
+std::atomic<unsigned long long> g_dep_wait_ns{kWaitLimitNs};
+}  // namespace
+unsigned long long dependency_wait_limit_ns() { return g_dep_wait_ns.load(std::memory_order_relaxed); }
+
 // ------------------------------------------------------------ tracing ---
 namespace {
 std::atomic<void*> g_trace_buf{nullptr};
@@ -204,6 +209,11 @@ extern "C" int rfx_set_trace(void* buf, size_t bytes) {
   if (buf && (reinterpret_cast<uintptr_t>(buf) & 7u)) return set_error(RFX_E_INVAL, "rfx_set_trace: 8-byte alignment");
   g_trace_bytes.store(buf ? bytes : 0);
   g_trace_buf.store(buf);
+  return RFX_OK;
+}
+
+extern "C" int rfx_set_wait_limit_ns(unsigned long long ns) {
+  g_dep_wait_ns.store(ns == 0 ? kWaitLimitNs : ns);
   return RFX_OK;
 }
 

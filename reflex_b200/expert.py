@@ -210,6 +210,16 @@ class ActionExpertEngine:
         self.positions.copy_(pos.repeat(self.B))
         self._build_ops()
 
+    def enable_chunk_debug(self) -> None:
+        """Parity checks of the fused executor: it records the first Euler
+        step's residual stream after each layer (dbg_h [L, T, W]) and each
+        layer's attention output (dbg_attn [L, T, H*D]), bf16."""
+        cfg = self.cfg
+        self.dbg_h = torch.zeros(cfg.num_layers, self.T, cfg.width, dtype=torch.bfloat16, device=self.dev)
+        self.dbg_attn = torch.zeros(cfg.num_layers, self.T, cfg.num_heads * cfg.head_dim, dtype=torch.bfloat16,
+                                    device=self.dev)
+        self._build_ops()
+
     def set_context_mask(self, valid: torch.Tensor | None) -> None:
         """Per-slot visibility of the context [B, n_ctx] (bool / 0-1) for the
         following chunks (a padded prefix token is invisible to the suffix,
@@ -376,6 +386,8 @@ class ActionExpertEngine:
         d.k_ring, d.v_ring, d.k_scale, d.v_scale, d.k_zp, d.v_zp = [cast(a) for a in self._chunk_ptrs]
         d.ctx_valid = self.ctx_valid.data_ptr() if self.use_ctx_valid else None
         d.x = self.x.data_ptr()
+        d.debug_hidden = L.ptr(getattr(self, "dbg_h", None))
+        d.debug_attn = L.ptr(getattr(self, "dbg_attn", None))
         n = ctypes.c_size_t(0)
         L.call("rfx_chunk_workspace_size", ctypes.byref(d), ctypes.byref(n))
         if self.chunk_ws is None or self.chunk_ws.numel() < n.value:

@@ -59,6 +59,34 @@ def test_fused_c2_full_size():
     assert err <= TOL
 
 
+@pytest.mark.parametrize("adarms,quant", [("gate", "u8_ref"), ("ssg", "i8_sym")])
+def test_fused_c2_full_size_per_layer(adarms, quant):
+    """18 layers, 818-token context through the persistent executor, with the
+    first step's hidden states and attention outputs of every layer checked
+    against the fp32 oracle (gate / u8_ref is the variant the reference's
+    own goldens pin; ssg / i8_sym is the benchmark's)."""
+    from test_gpu_model import hidden_tol, report
+    cfg = pi05_config(adarms=adarms, quant_mode=quant)
+    n_ctx = 818
+    wts, ctx, parts, x0, st = make_case(cfg, n_ctx)
+    eng = make_engine(cfg, wts, parts, n_ctx, capacity=1024, fused=True)
+    eng.enable_chunk_debug()
+    xf = run_chunk(eng, x0)
+    torch.set_num_threads(os.cpu_count() or 1)
+    h32, trace = [], {}
+    with torch.no_grad():
+        x32 = sample_chunk(cfg, wts, ctx, x0, st, hidden_step0=h32, trace_step0=trace)
+    hid = [eng.dbg_h[l].view(1, eng.St, -1).float().cpu() for l in range(cfg.num_layers)]
+    att = [eng.dbg_attn[l].view(1, eng.St, -1).float().cpu() for l in range(cfg.num_layers)]
+    report(f"fused-c2-{adarms}-{quant}", h32, hid, trace["attn"], att)
+    for l in range(cfg.num_layers):
+        assert (hid[l] - h32[l]).abs().max().item() <= hidden_tol(h32[l]), f"layer {l}"
+        assert (att[l] - trace["attn"][l]).abs().max().item() <= TOL, f"layer {l}"
+    err = (xf - x32).abs().max().item()
+    print(f"fused c2 {adarms}/{quant}: actions maxerr vs fp32 oracle {err:.5f}")
+    assert err <= TOL
+
+
 def test_fused_graph_replay_is_deterministic():
     cfg = pi05_config(num_layers=4)
     wts, ctx, parts, x0, st = make_case(cfg, 300)
@@ -71,3 +99,31 @@ def test_fused_graph_replay_is_deterministic():
         torch.cuda.synchronize()
         assert torch.equal(eng.x.float().cpu(), ref)
     assert kernels.device_status() == 0
+
+
+def test_dependency_wait_timeout_aborts_cleanly_and_next_chunk_runs():
+    """A wait on another CTA's phase counter that runs out: with the bound
+    cut to 2 us (every chunk has waits far longer than that), the executor
+    records the timeout in the device status word, every role leaves, drains
+    its copies and MMAs and frees TMEM, and the launch returns; with the
+    default bound back, the next chunk is bit-identical to one before."""
+    import ctypes
+
+    from reflex_b200 import _lib as L
+    cfg = pi05_config(num_layers=2)
+    wts, ctx, parts, x0, st = make_case(cfg, 200)
+    eng = make_engine(cfg, wts, parts, 200, fused=True)
+    ref = run_chunk(eng, x0)
+    try:
+        L.call("rfx_set_wait_limit_ns", ctypes.c_ulonglong(2000))  # taken at each launch
+        eng.set_inputs(x0.cuda())
+        eng.run_eager()
+        torch.cuda.synchronize()
+        assert kernels.device_status() == 8  # the executor's dependency-timeout code
+    finally:
+        L.call("rfx_set_wait_limit_ns", ctypes.c_ulonglong(0))
+    eng.set_inputs(x0.cuda())
+    eng.run_eager()
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    assert torch.equal(eng.x.float().cpu(), ref)

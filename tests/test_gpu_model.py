@@ -165,18 +165,53 @@ def test_graph_replay_matches_eager_and_is_repeatable():
     assert eng.num_launches > 0
 
 
-def test_multistream_batch_matches_single_streams():
-    """B streams batched along the token dimension give each stream's own chunk."""
+@pytest.mark.parametrize("B,check", [(4, (0, 1, 2, 3)), (16, (0, 5, 11, 15))])
+def test_multistream_batch_matches_single_streams(B, check):
+    """B streams batched along the token dimension give each stream's own chunk
+    (B=16: 800 tokens, the many-token GEMM tiles and the dense key source)."""
     cfg = pi05_config(num_layers=3)
-    B = 4
     wts, ctx, parts, x0, st = make_case(cfg, 200, B=B)
     eng = make_engine(cfg, wts, parts, 200, B=B)
     eng.set_inputs(x0.cuda())
     eng.run_eager()
     xb = eng.x.float().cpu()
-    for b in range(B):
+    for b in check:
         pb = [tuple(None if a is None else a[b:b + 1] for a in p) for p in parts]
         e1 = make_engine(cfg, wts, pb, 200, B=1)
         e1.set_inputs(x0[b:b + 1].cuda())
         e1.run_eager()
         assert (e1.x.float().cpu() - xb[b:b + 1]).abs().max().item() <= 5e-3
+
+
+def test_pi0_long_context_full_size():
+    """PI0 (state token + 50 actions, plain RMSNorm, [action, time] MLP) over
+    the long-context configuration: 200-token prefix + 8 frames x 3 cameras x
+    256 tokens = 6344 int8 context tokens, 18 layers, 10 steps, per layer
+    against the fp32 oracle (reflex/policies/pi0/modeling_pi0.py:740-845)."""
+    cfg = pi0_config(quant_mode="i8_sym")
+    n_ctx = 200 + 8 * 3 * 256
+    wts, ctx, parts, x0, st = make_case(cfg, n_ctx)
+    eng = make_engine(cfg, wts, parts, n_ctx, capacity=(n_ctx + 63) // 64 * 64)
+    x, hid, att = run_traced(eng, x0, st)
+    torch.set_num_threads(os.cpu_count() or 1)
+    h32, hbf, trace = [], [], {}
+    with torch.no_grad():
+        x32 = sample_chunk(cfg, wts, ctx, x0, st, hidden_step0=h32, trace_step0=trace)
+        xbf = sample_chunk(cfg, wts, ctx, x0, st, bf16=True, hidden_step0=hbf)
+    report("pi0-6344", h32, hid, trace["attn"], att)
+    # PI0's residual stream is not gated and grows to |h| ~ 6 over 18 layers:
+    # bf16 storage alone (the oracle with every op rounded to bf16, as the
+    # reference's bf16 PyTorch path rounds) drifts from fp32 by more than
+    # 2e-2 * |h|max in the deep layers, so a layer's hidden state may be as
+    # far off as 1.5x that drift; attention keeps 2e-2 absolute, and so do the
+    # actions unless the bf16 oracle's own actions drift further (then 1.5x).
+    for l in range(cfg.num_layers):
+        drift = (hbf[l] - h32[l]).abs().max().item()
+        err = (hid[l] - h32[l]).abs().max().item()
+        print(f"pi0-6344 layer {l:2d}: engine {err:.4f}, bf16 oracle {drift:.4f}")
+        assert err <= max(hidden_tol(h32[l]), 1.5 * drift), f"layer {l}"
+        assert (att[l] - trace["attn"][l]).abs().max().item() <= TOL, f"layer {l}"
+    err = (x - x32).abs().max().item()
+    drift = (xbf - x32).abs().max().item()
+    print(f"pi0-6344 actions maxerr vs fp32 oracle: {err:.5f} (bf16 oracle: {drift:.5f})")
+    assert err <= max(TOL, 1.5 * drift)

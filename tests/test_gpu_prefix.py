@@ -26,10 +26,14 @@ def _deq(ring, a, b):
     return torch.from_numpy(k), torch.from_numpy(v)
 
 
-def test_frame_update_matches_oracle():
+@pytest.mark.parametrize("layers,flen", [(2, 128), (4, 768)])
+def test_frame_update_matches_oracle(layers, flen):
+    """(4, 768): the streaming configuration's frame of 3 cameras x 256
+    tokens, through four Gemma-2B-shape prefix layers."""
     from reflex_b200.prefix import PrefixEngine
-    cfg = vlm_config(num_layers=2)
-    B, pinned, flen, cap = 1, 48, 128, 320
+    cfg = vlm_config(num_layers=layers)
+    B, pinned = 1, 48
+    cap = pinned + 2 * flen
     wts = synthetic.prefix_weights(cfg, seed=10)
     rings = [K.KVRing.allocate(B, 1, cap, 256, L.RFX_QUANT_I8_SYM, scale_dtype=torch.float32)
              for _ in range(cfg.num_layers)]
