@@ -367,6 +367,41 @@ typedef struct rfx_copy_rows_desc {
 } rfx_copy_rows_desc;
 int rfx_copy_rows(const rfx_copy_rows_desc* desc, void* stream);
 
+/* --------------------------------------- observation-embedding cache gate ---- */
+/* Decides on the device whether each camera image is close enough to the one
+ * whose embedding was computed last for that embedding to be reused (the
+ * vision tower is skipped on a hit).  Two checks, as in the reference:
+ *   RFX_EMBED_CACHE_POOL_MSE: PI05PrefixEmbedder.forward's cache
+ *     (reflex/policies/pi05/modeling_pi05.py:173-247): adaptive average
+ *     pooling of every channel to pool x pool (32), mean squared difference
+ *     per image against the stored features; hit iff every image's
+ *     mse < threshold (the reference's 1 - embedding_cache_threshold).
+ *   RFX_EMBED_CACHE_BILINEAR_COS: LastFrameCache.get_or_compute
+ *     (reflex/optimizations/dynamic_embedding_cache.py:284-392): bilinear
+ *     resampling to pool x pool (16, align_corners=False), cosine similarity
+ *     per image, hit iff the batch mean >= threshold.
+ * state[0] (0 = nothing stored yet) and state[1] (the decision: 1 = hit) are
+ * int32 on the device; on a miss the new features replace the stored ones and
+ * state[0] becomes 1.  metric[b] receives each image's mse or similarity.
+ * image is [B][C][H][W] contiguous; feat_prev / feat_new are fp32
+ * [B][C][pool][pool]; sums is fp32 scratch [B][3]. */
+#define RFX_EMBED_CACHE_POOL_MSE 0
+#define RFX_EMBED_CACHE_BILINEAR_COS 1
+typedef struct rfx_embed_cache_desc {
+  int mode;
+  int B, C, H, W;
+  int in_dtype; /* RFX_DTYPE_F32 or RFX_DTYPE_BF16 */
+  int pool;
+  float threshold;
+  const void* image;
+  float* feat_prev;
+  float* feat_new;
+  float* sums;
+  int* state;
+  float* metric;
+} rfx_embed_cache_desc;
+int rfx_embed_cache_check(const rfx_embed_cache_desc* desc, void* stream);
+
 /* ------------------------------------------------ fused chunk executor ---- */
 /* The whole PI0.5 denoising loop of one chunk (all Euler steps x layers:
  * input norm, QKV+RoPE, partitioned attention over the context ring,

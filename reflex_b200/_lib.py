@@ -24,6 +24,8 @@ RFX_DTYPE_F32 = 0
 RFX_DTYPE_BF16 = 1
 RFX_QUANT_I8_SYM = 0
 RFX_QUANT_U8_REF = 1
+RFX_EMBED_CACHE_POOL_MSE = 0
+RFX_EMBED_CACHE_BILINEAR_COS = 1
 RFX_KV_RING_TILES = 0
 RFX_KV_DENSE = 1
 
@@ -161,12 +163,21 @@ class ChunkDesc(Structure):
     ]
 
 
+class EmbedCacheDesc(ctypes.Structure):
+    _fields_ = [
+        ("mode", c_int), ("B", c_int), ("C", c_int), ("H", c_int), ("W", c_int), ("in_dtype", c_int),
+        ("pool", c_int), ("threshold", c_float), ("image", c_void_p), ("feat_prev", c_void_p),
+        ("feat_new", c_void_p), ("sums", c_void_p), ("state", c_void_p), ("metric", c_void_p),
+    ]
+
+
 # Every entry point declared in include/rfx.h: name -> (argtypes, restype).
 SIGNATURES = {
     "rfx_version": ([], c_int),
     "rfx_last_error": ([], ctypes.c_char_p),
     "rfx_device_status": ([c_void_p, POINTER(c_int)], c_int),
     "rfx_set_pdl": ([c_int], c_int),
+    "rfx_embed_cache_check": ([POINTER(EmbedCacheDesc), c_void_p], c_int),
     "rfx_set_wait_limit_ns": ([ctypes.c_ulonglong], c_int),
     "rfx_set_trace": ([c_void_p, c_size_t], c_int),
     "rfx_num_sms": ([POINTER(c_int)], c_int),

@@ -19,6 +19,7 @@ STRUCTS = {
     "rfx_kv_quant_desc": "KvQuantDesc", "rfx_linear_desc": "LinearDesc", "rfx_norm_desc": "NormDesc",
     "rfx_attn_desc": "AttnDesc", "rfx_time_cond_desc": "TimeCondDesc", "rfx_modulation_desc": "ModulationDesc",
     "rfx_action_io_desc": "ActionIoDesc", "rfx_copy_rows_desc": "CopyRowsDesc", "rfx_chunk_desc": "ChunkDesc",
+    "rfx_embed_cache_desc": "EmbedCacheDesc",
 }
 
 
