@@ -33,6 +33,8 @@ def main():
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--ops", default="qkv,attn,o,gu,down,tail")
     ap.add_argument("--n-ctx", type=int, default=818)
+    ap.add_argument("--variant", default="pi05", choices=["pi05", "pi0"],
+                    help="pi0: 1 state + 50 action tokens, plain RMSNorm (the long-context configuration)")
     ap.add_argument("--streams", type=int, default=1)
     ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
@@ -51,14 +53,20 @@ def main():
     if args.frame:
         frame_ops(args.ops, args.reps)
         return
-    cfg = pi05_config(num_layers=args.layers, adarms="ssg")
+    if args.variant == "pi0":
+        from .config import pi0_config
+        cfg = pi0_config(num_layers=args.layers)
+    else:
+        cfg = pi05_config(num_layers=args.layers, adarms="ssg")
     wts = synthetic.expert_weights(cfg, seed=0, device="cuda")
-    eng = ActionExpertEngine(cfg, wts, batch=args.streams, capacity=1024, n_ctx=args.n_ctx,
+    eng = ActionExpertEngine(cfg, wts, batch=args.streams, capacity=max(1024, (args.n_ctx + 63) // 64 * 64),
+                             n_ctx=args.n_ctx,
                              scale_dtype=torch.float32, fused=args.chunk and args.fused)
     ks, vs = synthetic.context_kv(cfg, args.n_ctx, B=args.streams, seed=1, device="cuda")
     for l in range(cfg.num_layers):
         eng.load_context(l, ks[l], vs[l])
-    eng.set_inputs(synthetic.noise(cfg, B=args.streams, seed=2, device="cuda"))
+    eng.set_inputs(synthetic.noise(cfg, B=args.streams, seed=2, device="cuda"),
+                   synthetic.state(cfg, B=args.streams, seed=3, device="cuda") if cfg.variant == "pi0" else None)
     eng.run_eager()
     torch.cuda.synchronize()
     if args.chunk and args.fused and args.trace:
