@@ -279,7 +279,10 @@ def chunk_kernel_roofline(eng, hbm_peak, reps=3):
 
     cfg = eng.cfg
     # per Euler step: every layer's bf16 weights once, each stream's int8 K+V context and fp32 scales
-    per_step = cfg.num_layers * 17301504 * 2 + eng.B * cfg.num_layers * N_CTX * (256 + 4) * 2
+    # (PI0 adds its action-time MLP: [W, 2W] + [W, W] bf16)
+    per_step = cfg.num_layers * 17301504 * 2 + eng.B * cfg.num_layers * eng.n_ctx * (256 + 4) * 2
+    if cfg.variant == "pi0":
+        per_step += 3 * cfg.width * cfg.width * 2
     bytes_per = cfg.num_steps * per_step
     st = torch.cuda.current_stream()
     L.call("rfx_chunk_run", eng.chunk, K._stream())
@@ -295,6 +298,8 @@ def chunk_kernel_roofline(eng, hbm_peak, reps=3):
     achieved = bytes_per / (avg_ms * 1e-3) / 1e9
     traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and workload
     try:
+        if cfg.variant != "pi05" or eng.n_ctx != N_CTX:
+            raise OSError("no capture of this workload")
         with open(os.path.join(ROOT, "profiles", "chunk_kernel_pi05_818ctx.md")) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
@@ -798,7 +803,9 @@ def cpu_pi0_long_ms(layers: int, chunks: int):
 def run_pi0_long(args):
     """One PI0 chunk (1 state token + 50 action tokens, [action, time] MLP, plain
     RMSNorm, 18 layers, 10 Euler steps) over a 200-token prefix + 8 frames x 3
-    cameras x 256 tokens of int8 KV, one CUDA graph per chunk (per-op engine)."""
+    cameras x 256 tokens of int8 KV: one chunk is one CUDA graph of the time
+    embedding and the persistent chunk executor (--engine per-op: one launch
+    per op)."""
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -811,8 +818,9 @@ def run_pi0_long(args):
     cfg = pi0_config(num_layers=args.layers)
     wts = synthetic.expert_weights(cfg, seed=0, device=device)
     cap = (PI0_LONG_CTX + 63) // 64 * 64
+    fused = args.engine == "fused"
     eng = ActionExpertEngine(cfg, wts, batch=1, capacity=cap, n_ctx=PI0_LONG_CTX, device=device,
-                             scale_dtype=torch.float32)
+                             scale_dtype=torch.float32, fused=fused)
     del wts
     ks, vs = synthetic.context_kv(cfg, PI0_LONG_CTX, B=1, seed=1, device=device)
     for l in range(cfg.num_layers):
@@ -854,7 +862,7 @@ def run_pi0_long(args):
         e1.synchronize()
         if i >= 2:
             e2e.append(e0.elapsed_time(e1))
-    roof = kernel_roofline(eng, hbm_peak)
+    roof = chunk_kernel_roofline(eng, hbm_peak) if fused else kernel_roofline(eng, hbm_peak)
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)"
     cpu = None
     if rank == 0:
@@ -862,7 +870,8 @@ def run_pi0_long(args):
         cpu = {"value": round(med, 3), "unit": "ms", "cores": cores, "kind": "port",
                "sample": f"{len(times)} full PI0 chunk of the same workload (fp32 torch oracle port)"}
     # per step: the expert's bf16 weights, the int8 K+V context with fp32 scales
-    bytes_chunk = 10 * (cfg.num_layers * 17301504 * 2 + cfg.num_layers * PI0_LONG_CTX * (256 + 4) * 2)
+    bytes_chunk = 10 * (cfg.num_layers * 17301504 * 2 + cfg.num_layers * PI0_LONG_CTX * (256 + 4) * 2
+                        + 3 * cfg.width * cfg.width * 2)
     if rank == 0:
         line = {
             "metric": "p50 10-step PI0 action-chunk latency over a 6344-token context (ms)", "value": round(p50, 4),
@@ -873,7 +882,8 @@ def run_pi0_long(args):
             "config": {"workload": "PI0 10-step action chunk: 1 state + 50 action tokens, 18x(1024, 8x256 MQA, GeGLU "
                                    "4096), plain RMSNorm, 200-token prefix + 8 frames x 3 cameras x 256 int8 KV "
                                    "(6344 tokens); one CUDA graph", "layers": cfg.num_layers,
-                       "context_tokens": PI0_LONG_CTX, "suffix_tokens": cfg.suffix_len, "engine": "one launch per op",
+                       "context_tokens": PI0_LONG_CTX, "suffix_tokens": cfg.suffix_len,
+                       "engine": "persistent chunk executor" if fused else "one launch per op",
                        "l2": "no flush: each chunk streams 6.2 GB of weights + 0.6 GB of KV per step (>> 126 MB L2)"},
             "chunk_roofline": {"algorithmic_bytes": bytes_chunk,
                                "achieved_GBps": round(bytes_chunk / (p50 * 1e-3) / 1e9, 1), "peak_GBps": hbm_peak,

@@ -412,8 +412,12 @@ int rfx_embed_cache_check(const rfx_embed_cache_desc* desc, void* stream);
  * (modeling_pi05.py:1181-1241 per step, 1403-1419 the Euler loop); partial
  * sums of split GEMMs are added in a fixed order. The timestep embedding and
  * the modulation vectors (rfx_time_cond, rfx_modulation) are computed before.
- * Limits: B*S <= 64 tokens, width 1024, head_dim 256 with one KV head. */
+ * PI0 runs on the same executor (variant RFX_CHUNK_PI0, fields below).
+ * Limits: B*S (PI0: B*(S+1)) <= 64 tokens, width 1024, head_dim 256 with one
+ * KV head. */
 typedef struct rfx_chunk rfx_chunk;
+#define RFX_CHUNK_PI05 0
+#define RFX_CHUNK_PI0 1
 typedef struct rfx_chunk_desc {
   int B, S;                   /* streams, action tokens per stream */
   int num_layers, num_steps;
@@ -435,7 +439,8 @@ typedef struct rfx_chunk_desc {
   int rope_max_pos;
   const int* positions;       /* [B*S] */
   int capacity, n_ctx, quant_mode, scale_dtype;
-  int kv_splits;              /* key-block splits of the attention, 0 = one per 64-key block */
+  int kv_splits;              /* key-range splits of the attention (at most 64); 0 = one per 64-key block,
+                                 at most as many as give each SM one attention item */
   const void* const* k_ring;  /* HOST array of num_layers device pointers: int8/uint8 [B][capacity][256] */
   const void* const* v_ring;
   const void* const* k_scale; /* HOST arrays of device pointers: [B][capacity] */
@@ -444,6 +449,23 @@ typedef struct rfx_chunk_desc {
   const void* const* v_zp;
   const unsigned char* ctx_valid; /* [B][capacity] or NULL */
   float* x;                   /* fp32 [B][S][action_dim]: x0 in, denoised actions out */
+  /* PI0 (variant = RFX_CHUNK_PI0, modeling_pi0.py:144-206,740-845): every
+   * stream's tokens are its state token then its S action tokens; the state
+   * token is state_proj(state), the action tokens come from the action-time
+   * MLP over [action_in_proj(x), sinusoid(t)] each step; plain RMSNorm
+   * (mod_* NULL); new_block gives the block-causal attention among the new
+   * tokens (the state token does not see the actions). */
+  int variant;                /* RFX_CHUNK_PI05 (0) or RFX_CHUNK_PI0 */
+  int state_dim;
+  const float* state;         /* fp32 [B][state_dim] */
+  const void* w_state;        /* bf16 [width][state_dim], state_proj */
+  const void* b_state;        /* bf16 [width] */
+  const void* w_atin;         /* bf16 [width][2*width], action_time_mlp_in */
+  const float* b_atin;        /* fp32 [width] */
+  const void* w_atout;        /* bf16 [width][width], action_time_mlp_out */
+  const float* b_atout;       /* fp32 [width] */
+  const void* time_emb;       /* bf16 [num_steps][width]: sinusoid of each step's t (rfx_time_cond, w_in NULL) */
+  const int* new_block;       /* [S + 1] block ids of a stream's new tokens */
   /* Parity checks only (NULL in production): the first Euler step's residual
    * stream after each layer, bf16 [num_layers][B*S][width], and attention
    * output of each layer, bf16 [num_layers][B*S][num_q_heads*256]. */

@@ -24,6 +24,8 @@ RFX_DTYPE_F32 = 0
 RFX_DTYPE_BF16 = 1
 RFX_QUANT_I8_SYM = 0
 RFX_QUANT_U8_REF = 1
+RFX_CHUNK_PI05 = 0
+RFX_CHUNK_PI0 = 1
 RFX_EMBED_CACHE_POOL_MSE = 0
 RFX_EMBED_CACHE_BILINEAR_COS = 1
 RFX_KV_RING_TILES = 0
@@ -159,7 +161,11 @@ class ChunkDesc(Structure):
         ("k_ring", POINTER(c_void_p)), ("v_ring", POINTER(c_void_p)),
         ("k_scale", POINTER(c_void_p)), ("v_scale", POINTER(c_void_p)),
         ("k_zp", POINTER(c_void_p)), ("v_zp", POINTER(c_void_p)),
-        ("ctx_valid", c_void_p), ("x", c_void_p), ("debug_hidden", c_void_p), ("debug_attn", c_void_p),
+        ("ctx_valid", c_void_p), ("x", c_void_p),
+        ("variant", c_int), ("state_dim", c_int), ("state", c_void_p), ("w_state", c_void_p), ("b_state", c_void_p),
+        ("w_atin", c_void_p), ("b_atin", c_void_p), ("w_atout", c_void_p), ("b_atout", c_void_p),
+        ("time_emb", c_void_p), ("new_block", c_void_p),
+        ("debug_hidden", c_void_p), ("debug_attn", c_void_p),
     ]
 
 

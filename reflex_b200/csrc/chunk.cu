@@ -72,10 +72,14 @@ constexpr int kOffAQ = 0;        // 4 x [128 x 64] bf16
 constexpr int kOffAK = 65536;    // 4 x [64 x 64] bf16
 constexpr int kOffAV = 98304;    // 4 x [64 x 64] f16, MN-major blocks
 constexpr int kOffAP = 131072;   // [128 x 64] f16
-constexpr int kOffAScales = 147456;  // 8 x 64 floats (2 KB): per-key scales, zero points, block ids
+constexpr int kOffAScales = 147456;  // 8 x 64 floats (2 KB): per-key scales, zero points, block ids (first set)
 constexpr int kOffAXchg = 149504;    // 768 floats: row maxima and sums of the two column halves
+constexpr int kOffAStg = 155648;     // int8 rows of one context block, K [64][256] then V [64][256]
+constexpr int kStgBytes = kKB * kD;  // 16 KB per tensor
+constexpr int kOffAScales1 = kOffAStg + 2 * kStgBytes;  // the second set of per-key values
 // the attention tiles overlay the ring (idle while an attention item runs)
-static_assert(kOffAXchg + 3072 <= kOffRed, "attention tiles must fit in the ring");
+static_assert(kOffAXchg + 3072 <= kOffAStg && kOffAScales1 + 2048 <= kOffRed,
+              "attention tiles must fit in the ring");
 
 // small region (byte offsets)
 constexpr int kSmFull = 0;         // 8 mbarriers
@@ -93,15 +97,27 @@ constexpr int kSmKvnFull = 200;    // mbarrier: the new keys' K / V tiles (TMA) 
 constexpr int kSmPairReady = 208;  // mbarrier: the peer CTA has pushed its partial into this CTA's tile buffer
 constexpr int kSmPairDone = 216;   // mbarrier: the peer CTA has read its tile buffer (this CTA may push again)
 constexpr int kSmMmaDrain = 224;   // mbarrier: every MMA this CTA issued has completed (teardown)
+constexpr int kSmStgFull = 232;    // mbarrier: a context block's int8 rows have landed in the staging buffer
+constexpr int kSmStgEmpty = 240;   // mbarrier: the workers have converted the staged block out of it
+constexpr int kSmVReady = 248;     // mbarrier: the block's V tile is in sV (P.V may run)
 constexpr int kSmRed8 = 320;       // 8 floats
 constexpr int kSmXs = 512;         // 64 floats
 static_assert(kSmXs + 256 <= kSmallBytes, "small region");
 
-enum TaskType : int { kTInit = 0, kTQkv = 1, kTO = 2, kTGu = 3, kTDown = 4, kTAttn = 5, kTComb = 6, kTFinO = 7, kTFinD = 8 };
-enum Op : int { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3 };
+// kTAtIn / kTAtOut and kTFinAt1 / kTFinAt2: PI0's action-time MLP at the start
+// of every step (modeling_pi0.py:163-200), as GEMM phases with per-token
+// reductions.
+enum TaskType : int { kTInit = 0, kTQkv = 1, kTO = 2, kTGu = 3, kTDown = 4, kTAttn = 5, kTComb = 6, kTFinO = 7, kTFinD = 8,
+                      kTAtIn = 9, kTAtOut = 10, kTFinAt1 = 11, kTFinAt2 = 12 };
+enum Op : int { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3, kOpAtIn = 4, kOpAtOut = 5, kNumOps = 6 };
+enum Variant : int { kPi05 = 0, kPi0 = 1 };
+// GEMM op of a task type, or -1
+__host__ __device__ constexpr int gemm_op(int ty) {
+  return (ty >= kTQkv && ty <= kTDown) ? ty - kTQkv : ty == kTAtIn ? kOpAtIn : ty == kTAtOut ? kOpAtOut : -1;
+}
 // counter lines (32 u32 = 128 B apart)
 enum CtrLine : int { kCXn = 0, kCQkv = 1, kCAttn = 2, kCComb = 3, kCPo = 4, kCXn2 = 5, kCAct = 6, kCPd = 7, kCAbort = 8,
-                     kNumCtrLines = 16 };
+                     kCAtX = 9, kCPat1 = 10, kCAtH = 11, kCPat2 = 12, kNumCtrLines = 16 };
 
 
 enum ChunkError : int { kDevTimeoutDependency = 8 };
@@ -117,11 +133,13 @@ struct OpCfg {
 
 struct ChunkParams {
   int T, S, B, NL, steps, W, Hq, F, A, NN;
+  int variant;  // kPi05 / kPi0
+  int SA, TA;   // action tokens per stream / in all (PI0: S = SA + 1, the state token first)
   int n_ctx, cap, mode, scale_bf16;
   int q_tiles, attn_splits, n_ctx_blocks, n_blocks;
   int n_attn, n_comb, n_fin;
   float eps, dt, scale_log2;
-  OpCfg op[4];
+  OpCfg op[kNumOps];
   const float* a1;    // [NN][W]
   const float* a2;    // [steps][NN][W] or null
   const float* b2;
@@ -143,9 +161,9 @@ struct ChunkParams {
   float* x;                    // [B][S][A]
   __nv_bfloat16* h;            // [T][W]
   __nv_bfloat16* xn;           // [T][W]
-  __nv_bfloat16* q;            // [B][Hq][S][256]
-  __nv_bfloat16* kn;           // [T][256]
-  __nv_bfloat16* vn;
+  __nv_bfloat16* q;            // [B][Hq][S][256], f16 bits (values rounded to bf16 first)
+  __nv_bfloat16* kn;           // [T][256], f16 bits as q
+  __nv_bfloat16* vn;           // [T][256], f16 bits as q
   __nv_bfloat16* attn_out;     // [T][Hq*256]
   __nv_bfloat16* act;          // [T][F]
   float* ws_o;
@@ -159,15 +177,27 @@ struct ChunkParams {
   unsigned long long* trace;  // [grid][trace_tasks][16] stamps + task of the first step, or null
   int trace_tasks;
   unsigned long long dep_limit_ns;  // bound of a wait on another CTA's phase counter (rfx_set_wait_limit_ns)
+  // PI0 only
+  const float* state;            // [B][SD]
+  int SD;
+  const __nv_bfloat16* w_st;     // [W][SD] state_proj
+  const __nv_bfloat16* b_st;     // [W]
+  const float* b_atin;           // [W] action_time_mlp_in bias
+  const float* b_atout;          // [W] action_time_mlp_out bias
+  const __nv_bfloat16* temb;     // [steps][W] bf16 sinusoidal time embedding
+  __nv_bfloat16* at_x;           // [TA][2W]: [action_in(x), time embedding]
+  __nv_bfloat16* at_hid;         // [TA][W]
+  __nv_bfloat16* st_emb;         // [B][W]
+  const int* new_block;          // [S] block ids of the new tokens, or null (all see all)
   __nv_bfloat16* dbg_h;     // [NL][T][W] step-0 residual stream after each layer, or null
   __nv_bfloat16* dbg_attn;  // [NL][T][Hq*256] step-0 attention output of each layer, or null
 };
 
 struct Maps {
-  CUtensorMap w[4];
-  CUtensorMap x[4];
+  CUtensorMap w[kNumOps];
+  CUtensorMap x[kNumOps];
   CUtensorMap q;
-  CUtensorMap kn;  // the new tokens' keys, bf16 [B*S][256]
+  CUtensorMap kn;  // the new tokens' keys, f16 [B*S][256]
   CUtensorMap vn;  // the new tokens' values, f16 [B*S][256]
 };
 
@@ -332,7 +362,9 @@ __device__ __forceinline__ OpCfg op_cfg(const ChunkParams& p, int op) {
     case kOpQkv: return p.op[kOpQkv];
     case kOpO: return p.op[kOpO];
     case kOpGu: return p.op[kOpGu];
-    default: return p.op[kOpDown];
+    case kOpDown: return p.op[kOpDown];
+    case kOpAtIn: return p.op[kOpAtIn];
+    default: return p.op[kOpAtOut];
   }
 }
 
@@ -382,14 +414,16 @@ __device__ void norm_row(const ChunkParams& p, int et, const float (&hv)[4], con
   workers_sync();  // red8 is reused by the next row
 }
 
-// h_row[o] = bf16(sum_a xs[a] * W_in[o][a] + b_in[o]) for the worker's 4 features.
-__device__ __forceinline__ void action_in4(const ChunkParams& p, int et, const float* xs, float (&hv)[4]) {
+// h_row[o] = bf16(sum_a xs[a] * W[o][a] + b[o]) for the worker's 4 features
+// (action_in_proj, or PI0's state_proj).
+__device__ __forceinline__ void proj_in4(const ChunkParams& p, int et, const float* xs, float (&hv)[4],
+                                         const __nv_bfloat16* w, const __nv_bfloat16* bias, int n_in) {
 #pragma unroll 1
   for (int e = 0; e < 4; ++e) {
     const int o = et * 4 + e;
-    const __nv_bfloat16* wr = p.w_in + static_cast<long>(o) * p.A;
+    const __nv_bfloat16* wr = w + static_cast<long>(o) * n_in;
     float acc = 0.f;
-    for (int a = 0; a < p.A; a += 8) {
+    for (int a = 0; a < n_in; a += 8) {
       const uint4 raw = *reinterpret_cast<const uint4*>(wr + a);
       const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -399,7 +433,43 @@ __device__ __forceinline__ void action_in4(const ChunkParams& p, int et, const f
         acc = fmaf(f.y, xs[a + 2 * q + 1], acc);
       }
     }
-    hv[e] = bf16_round(acc + (p.b_in ? __bfloat162float(p.b_in[o]) : 0.f));
+    hv[e] = bf16_round(acc + (bias ? __bfloat162float(bias[o]) : 0.f));
+  }
+}
+__device__ __forceinline__ void action_in4(const ChunkParams& p, int et, const float* xs, float (&hv)[4]) {
+  proj_in4(p, et, xs, hv, p.w_in, p.b_in, p.A);
+}
+
+// PI0: the action rows of the next action-time MLP input, [action_in(x), t_emb(tau)].
+__device__ __forceinline__ void write_at_x(const ChunkParams& p, int et, int at, int tau, const float (&hv)[4]) {
+  const int f0 = et * 4;
+  __nv_bfloat16* row = p.at_x + static_cast<long>(at) * 2 * p.W;
+  *reinterpret_cast<uint2*>(row + f0) = pack4_bf16(hv);
+  *reinterpret_cast<uint2*>(row + p.W + f0) =
+      *reinterpret_cast<const uint2*>(p.temb + static_cast<long>(tau) * p.W + f0);
+}
+
+// Sum of the split-K partials [m][split][t][128] of op for token row t, the
+// worker's 4 features, in split order.
+__device__ __forceinline__ void sum_partials4(const ChunkParams& p, int op, int t, int f0, float (&acc)[4]) {
+  const OpCfg oc = op_cfg(p, op);
+  const int m = f0 / kBM, r0 = f0 % kBM;
+  acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  for (int s0 = 0; s0 < oc.splits; s0 += 4) {
+    float4 a[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (s0 + q < oc.splits) {
+        const float* ps = oc.part + ((static_cast<long>(m) * oc.splits + s0 + q) * kNT + t) * kBM + r0;
+        a[q] = __ldcg(reinterpret_cast<const float4*>(ps));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (s0 + q < oc.splits) {
+        acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
+      }
+    }
   }
 }
 
@@ -504,7 +574,7 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
   }
   if (et == 0) stamp(ts, 6);
   if (!paired) {
-    workers_publish(p, et, op == kOpO ? kCPo : kCPd);
+    workers_publish(p, et, op == kOpO ? kCPo : op == kOpDown ? kCPd : op == kOpAtIn ? kCPat1 : kCPat2);
     return true;
   }
   // this CTA's own rows are in its buffer (the barrier orders them for every
@@ -571,17 +641,14 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
         dst = p.kn + static_cast<long>(t) * 256;
       else
         dst = p.vn + static_cast<long>(t) * 256;
-      if (head <= p.Hq) {
-        *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_bf16x2(r0[0], r0[1]), pack_bf16x2(r0[2], r0[3]));
-        *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_bf16x2(r1[0], r1[1]), pack_bf16x2(r1[2], r1[3]));
-      } else {
-        // values are kept as f16 of their bf16 rounding (exact), the operand
-        // type of the P.V product, so attention loads them by TMA unchanged
-        *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_f16x2(bf16_round(r0[0]), bf16_round(r0[1])),
-                                                         pack_f16x2(bf16_round(r0[2]), bf16_round(r0[3])));
-        *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_f16x2(bf16_round(r1[0]), bf16_round(r1[1])),
-                                                               pack_f16x2(bf16_round(r1[2]), bf16_round(r1[3])));
-      }
+      // q, k and v are rounded to bf16 (the reference's dtype) and kept as
+      // f16 of that value (exact for |x| in [2^-14, 65504]; smaller values
+      // keep 2^-24 absolute precision): the operand type of both attention
+      // products, whose int8 keys and values convert to f16 by integer ops
+      *reinterpret_cast<uint2*>(dst + d0) = make_uint2(pack_f16x2(bf16_round(r0[0]), bf16_round(r0[1])),
+                                                       pack_f16x2(bf16_round(r0[2]), bf16_round(r0[3])));
+      *reinterpret_cast<uint2*>(dst + d0 + 128) = make_uint2(pack_f16x2(bf16_round(r1[0]), bf16_round(r1[1])),
+                                                             pack_f16x2(bf16_round(r1[2]), bf16_round(r1[3])));
     }
   }
   if (et == 0) stamp(ts, 12);
@@ -596,47 +663,60 @@ __device__ __forceinline__ bool worker_gemm(const ChunkParams& p, uint8_t* smem,
 // ----------------------------------------------------- worker: attention ---
 // Converts 16 quantized values (one 16-byte chunk of a key row) into bf16 (K)
 // or f16 (V) and stores them into a 128-byte-swizzled tile.
-template <bool IS_K>
+// int8 -> f16 of 4 bytes by integer ops (exact): the bytes, offset to
+// unsigned, become the low mantissa bytes of 1024 + u (f16 0x6400 | u), and
+// one packed subtraction of 1152 leaves u - 128, the signed value.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  x ^= 0x80808080u;
+  const uint32_t a = __byte_perm(x, 0x64646464u, 0x4140);
+  const uint32_t b = __byte_perm(x, 0x64646464u, 0x4342);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  const __half2 ra = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+  const __half2 rb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+  lo = *reinterpret_cast<const uint32_t*>(&ra);
+  hi = *reinterpret_cast<const uint32_t*>(&rb);
+}
+
+// 16 quantized values of one key (dims 16 g .. 16 g + 15) -> f16 into the
+// K-major (K) or MN-major (V) swizzled tile: int8 values exactly (the key's
+// scale is applied to its score / probability), uint8 values dequantized as
+// the reference does, (u - zp) then * scale, each rounded to the scale dtype,
+// then held as f16 (exact in f16's range).
 __device__ __forceinline__ void convert16r(uint4 raw, uint8_t* tile_base, int key, int g, int mode, bool sbf16,
                                            float sc, float zp) {
-  const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&raw);
-  float f[16];
+  uint32_t w[8];
   if (mode == kQuantI8Sym) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) f[e] = static_cast<float>(static_cast<int8_t>(b8[e]));
+    i8x4_to_f16x4(raw.x, w[0], w[1]);
+    i8x4_to_f16x4(raw.y, w[2], w[3]);
+    i8x4_to_f16x4(raw.z, w[4], w[5]);
+    i8x4_to_f16x4(raw.w, w[6], w[7]);
   } else {
+    const uint8_t* b8 = reinterpret_cast<const uint8_t*>(&raw);
+    float f[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const float t = round_to(__fsub_rn(static_cast<float>(b8[e]), zp), sbf16);
       f[e] = round_to(__fmul_rn(t, sc), sbf16);
     }
-  }
-  uint32_t w[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) w[e] = IS_K ? pack_bf16x2(f[2 * e], f[2 * e + 1]) : pack_f16x2(f[2 * e], f[2 * e + 1]);
+    for (int e = 0; e < 8; ++e) w[e] = pack_f16x2(f[2 * e], f[2 * e + 1]);
+  }
   uint8_t* atom = tile_base + (g >> 2) * 8192;
   const int c0 = (g & 3) * 2;
   *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0)) = make_uint4(w[0], w[1], w[2], w[3]);
   *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
+template <int V>
 __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int layer,
                             unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, uint32_t& kvn_cnt,
-                            unsigned long long* ts) {
+                            uint32_t& stg_cnt, unsigned long long* ts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int ch = et >> 7;  // this warp's half of the columns of its rows (S: 32 keys, O: 128 dims)
   uint8_t* sK = smem + kOffAK;
   uint8_t* sV = smem + kOffAV;
   uint8_t* sP = smem + kOffAP;
-  float* ks_s = reinterpret_cast<float*>(smem + kOffAScales);
-  float* vs_s = ks_s + 64;
-  float* kdq_s = vs_s + 64;
-  float* vdq_s = kdq_s + 64;
-  float* kzp_s = vdq_s + 64;
-  float* vzp_s = kzp_s + 64;
-  int* nb_s = reinterpret_cast<int*>(vzp_s + 64);
-  float* kadd_s = reinterpret_cast<float*>(nb_s + 64);
   // row maxima of the two column halves (two buffers, alternating by block)
   // and the final row sums, exchanged between the warps of a lane quadrant
   float* mx_x = reinterpret_cast<float*>(smem + kOffAXchg);  // [2][2][128]
@@ -648,6 +728,10 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   uint64_t* acc_free = reinterpret_cast<uint64_t*>(small + kSmAccFree);
   uint64_t* attn_done = reinterpret_cast<uint64_t*>(small + kSmAttnDone);
   uint64_t* kvn_full = reinterpret_cast<uint64_t*>(small + kSmKvnFull);
+  uint64_t* stg_full = reinterpret_cast<uint64_t*>(small + kSmStgFull);
+  uint64_t* stg_empty = reinterpret_cast<uint64_t*>(small + kSmStgEmpty);
+  uint64_t* v_ready = reinterpret_cast<uint64_t*>(small + kSmVReady);
+  const uint8_t* stg = smem + kOffAStg;
   const uint32_t tmO = tmem, tmS = tmem + 256;
   const int blk_begin = sp * p.n_blocks / p.attn_splits;
   const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk_begin;
@@ -656,249 +740,300 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   const bool row_valid = R < p.Hq * p.S;
   const int s_row = row_valid ? R % p.S : 0;
   const int h_row = row_valid ? R / p.S : 0;
+  // block of this query row among the new tokens: new key j is visible iff
+  // new_block[j] <= it (PI0's state token does not see the action tokens)
+  const int my_block = (V == kPi0 && row_valid && p.new_block) ? p.new_block[s_row] : 0;
   const bool sbf16 = p.scale_bf16 != 0;
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-  const uint8_t* kring = p.k_ring[layer];
-  const uint8_t* vring = p.v_ring[layer];
-  const void* kscale = p.k_scale[layer];
-  const void* vscale = p.v_scale[layer];
-  const void* kzp = p.k_zp[layer];
-  const void* vzp = p.v_zp[layer];
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
   bool new_ready = false;
-
-  for (int jl = 0; jl < nbl && ok; ++jl) {
-    const int j = blk_begin + jl;
-    const bool is_ctx = j < p.n_ctx_blocks;
-    if (jl > 0) {
-      bool w = true;
-      if (lane == 0) w = bar_wait(p, o_full, (blk_cnt - 1) & 1, kDevTimeoutMmaDone);
-      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
-      if (!ok) break;
-    }
-    if (is_ctx) {
-      // int8 rows straight from the ring (no dependency on this chunk's work);
-      // the first half of this thread's 16-byte chunks is requested here, the
-      // second half while the first is converted
-      auto ctx_chunk = [&](int q) {
-        const int it = et + q * kWorkers;  // 0..2047: K chunks then V chunks
-        const bool isv = it >= kKB * 16;
-        const int w = isv ? it - kKB * 16 : it;
-        const int key = w >> 4, g = w & 15;
-        long slot = static_cast<long>(j) * kKB + key;
-        if (slot >= p.cap) slot = p.cap - 1;
-        return *reinterpret_cast<const uint4*>((isv ? vring : kring) + (static_cast<long>(b) * p.cap + slot) * kD +
-                                               g * 16);
-      };
-      uint4 raw[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) raw[q] = ctx_chunk(q);
-      if (et < 64) {
-        const long slot = static_cast<long>(j) * kKB + et;
-        const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
-        bool valid = slot < p.n_ctx;
-        if (valid && p.ctx_valid) valid = p.ctx_valid[gi] != 0;
-        kadd_s[et] = valid ? 0.f : -INFINITY;
-        if (p.mode == kQuantI8Sym) {
-          ks_s[et] = valid ? static_cast<const float*>(kscale)[gi] * p.scale_log2 : 0.f;
-          vs_s[et] = valid ? static_cast<const float*>(vscale)[gi] : 0.f;
-        } else {
-          ks_s[et] = valid ? p.scale_log2 : 0.f;
-          vs_s[et] = 1.f;
-          kdq_s[et] = load_scalar(kscale, gi, sbf16);
-          vdq_s[et] = load_scalar(vscale, gi, sbf16);
-          kzp_s[et] = load_scalar(kzp, gi, sbf16);
-          vzp_s[et] = load_scalar(vzp, gi, sbf16);
-        }
-      }
-      workers_sync();
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint4 nxt[4];
-        if (half == 0) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) nxt[q] = ctx_chunk(4 + q);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int it = et + (half * 4 + q) * kWorkers;
-          const bool isv = it >= kKB * 16;
-          const int w = isv ? it - kKB * 16 : it;
-          const int key = w >> 4, g = w & 15;
-          float sc = 0.f, zp = 0.f;
-          if (p.mode != kQuantI8Sym) {
-            sc = isv ? vdq_s[key] : kdq_s[key];
-            zp = isv ? vzp_s[key] : kzp_s[key];
-          }
-          if (isv)
-            convert16r<false>(raw[q], sV, key, g, p.mode, sbf16, sc, zp);
-          else
-            convert16r<true>(raw[q], sK, key, g, p.mode, sbf16, sc, zp);
-        }
-        if (half == 0) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) raw[q] = nxt[q];
-        }
-      }
-    } else if (nbl == 1) {
-      // the split's only block holds the new keys: the producer loads its K
-      // (bf16) and V (f16) tiles by TMA once the QKV tiles are published
-      const int nb0 = (j - p.n_ctx_blocks) * kKB;
-      if (et < 64) {
-        const int kk = nb0 + et;
-        ks_s[et] = kk < p.S ? p.scale_log2 : 0.f;
-        kadd_s[et] = kk < p.S ? 0.f : -INFINITY;
-        vs_s[et] = 1.f;
-        nb_s[et] = 0;
-      }
-      bool w = true;
-      if (lane == 0) w = bar_wait(p, kvn_full, kvn_cnt & 1, kDevTimeoutTmaFull);
-      ++kvn_cnt;
-      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
-      if (!ok) break;
+  // per-key values of a block, in two sets alternating by block: [0, 64)
+  // score scale (log2 units, 0 for a masked key), [64, 128) value scale,
+  // [128, 192) additive mask, [192, 256) block ids of new keys (int), then
+  // (uint8 scheme) K / V dequantization scales and K / V zero points
+  auto scale_set = [&](int jl) { return reinterpret_cast<float*>(smem + ((jl & 1) ? kOffAScales1 : kOffAScales)); };
+  // Block j's per-key values into set sc, in two halves: request() starts
+  // the asynchronous copies of the per-key scales (fp32) and zero points of a
+  // context block, finish() (after the copies of this thread completed)
+  // turns them into the softmax's values; bf16 scales are loaded in finish().
+  const bool async_sc = !sbf16;
+  auto request = [&](int j, float* sc) {
+    if (et >= 64 || j >= p.n_ctx_blocks || !async_sc) return;
+    const long slot = static_cast<long>(j) * kKB + et;
+    const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
+    if (p.mode == kQuantI8Sym) {
+      cp_async4(sc + et, static_cast<const float*>(p.k_scale[layer]) + gi);
+      cp_async4(sc + 64 + et, static_cast<const float*>(p.v_scale[layer]) + gi);
     } else {
-      if (!new_ready) {
-        ok = workers_ctr_wait(p, et, kCQkv,
-                              static_cast<unsigned>(p.op[kOpQkv].m_tiles * p.op[kOpQkv].splits) * (use + 1));
-        if (!ok) break;
-        new_ready = true;
+      cp_async4(sc + 256 + et, static_cast<const float*>(p.k_scale[layer]) + gi);
+      cp_async4(sc + 320 + et, static_cast<const float*>(p.v_scale[layer]) + gi);
+      cp_async4(sc + 384 + et, static_cast<const float*>(p.k_zp[layer]) + gi);
+      cp_async4(sc + 448 + et, static_cast<const float*>(p.v_zp[layer]) + gi);
+    }
+    cp_async_commit();
+  };
+  auto finish = [&](int j, float* sc) {
+    if (et >= 64) return;
+    int* nb = reinterpret_cast<int*>(sc + 192);
+    if (j < p.n_ctx_blocks) {
+      const long slot = static_cast<long>(j) * kKB + et;
+      const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
+      const bool valid = slot < p.n_ctx && (!p.ctx_valid || p.ctx_valid[gi] != 0);
+      if (async_sc) {
+        cp_async_wait_all();
+      } else {
+        sc[256 + et] = load_scalar(p.k_scale[layer], gi, true);
+        sc[320 + et] = load_scalar(p.v_scale[layer], gi, true);
+        sc[384 + et] = load_scalar(p.k_zp[layer], gi, true);
+        sc[448 + et] = load_scalar(p.v_zp[layer], gi, true);
       }
+      if (p.mode == kQuantI8Sym) {
+        sc[et] = valid ? sc[et] * p.scale_log2 : 0.f;
+        sc[64 + et] = valid ? sc[64 + et] : 0.f;
+      } else {
+        sc[et] = valid ? p.scale_log2 : 0.f;
+        sc[64 + et] = 1.f;
+      }
+      sc[128 + et] = valid ? 0.f : -INFINITY;
+      nb[et] = 0;
+    } else {
+      const int kk = (j - p.n_ctx_blocks) * kKB + et;
+      sc[et] = kk < p.S ? p.scale_log2 : 0.f;
+      sc[64 + et] = 1.f;
+      sc[128 + et] = kk < p.S ? 0.f : -INFINITY;
+      nb[et] = (V == kPi0 && kk < p.S && p.new_block) ? p.new_block[kk] : 0;
+    }
+  };
+
+  // ---- block pipeline.  Block jl: QK (MMA) -> softmax -> P; then the next
+  // block's K is converted into sK (free once QK(jl) is done), so the MMA
+  // issues QK(jl + 1) right after P.V(jl), and its V follows into sV once
+  // P.V(jl) is done.  Iteration -1 prepares the first block. ----
+  auto wait_all = [&](uint64_t* bar, uint32_t parity, int code) {
+    bool w = true;
+    if (lane == 0) w = bar_wait(p, bar, parity, code);
+    return workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
+  };
+  // K (half 0) or V (half 1) of block j into sK / sV: the staged int8 rows
+  // of a context block, or the new tokens' f16 rows
+  auto fill = [&](int j, int half, const float* sc) {
+    uint8_t* tile = half ? sV : sK;
+    if (j < p.n_ctx_blocks) {
+      const float* dq = sc + 256 + half * 64;
+      const float* zq = sc + 384 + half * 64;
+      const bool u8 = p.mode != kQuantI8Sym;
+#pragma unroll 4
+      for (int q = 0; q < 4; ++q) {
+        const int it = et + q * kWorkers;  // 0..1023: 16 chunks of 16 bytes per key
+        const int key = it >> 4, g = it & 15;
+        const uint4 raw = *reinterpret_cast<const uint4*>(stg + half * kStgBytes + key * kD + g * 16);
+        convert16r(raw, tile, key, g, p.mode, sbf16, u8 ? dq[key] : 0.f, u8 ? zq[key] : 0.f);
+      }
+    } else {
       const int nb0 = (j - p.n_ctx_blocks) * kKB;
-      if (et < 64) {
-        const int kk = nb0 + et;
-        ks_s[et] = kk < p.S ? p.scale_log2 : 0.f;
-        kadd_s[et] = kk < p.S ? 0.f : -INFINITY;
-        vs_s[et] = 1.f;
-        nb_s[et] = 0;
-      }
+      const __nv_bfloat16* rows = half ? p.vn : p.kn;
 #pragma unroll 2
-      for (int it = et; it < 2 * kKB * 32; it += kWorkers) {
-        const bool isv = it >= kKB * 32;
-        const int w = isv ? it - kKB * 32 : it;
-        const int key = w >> 5, c = w & 31;
+      for (int it = et; it < kKB * 32; it += kWorkers) {
+        const int key = it >> 5, c = it & 31;
         const int kk = nb0 + key;
         uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-        if (kk < p.S) {
-          const __nv_bfloat16* src = (isv ? p.vn : p.kn) + (static_cast<long>(b) * p.S + kk) * kD + c * 8;
-          raw = __ldcg(reinterpret_cast<const uint4*>(src));
-        }
-        uint8_t* atom = (isv ? sV : sK) + (c >> 3) * 8192;  // values are stored as f16 already
-        *reinterpret_cast<uint4*>(atom + sw128_offset(key, c & 7)) = raw;
+        if (kk < p.S) raw = __ldcg(reinterpret_cast<const uint4*>(rows + (static_cast<long>(b) * p.S + kk) * kD + c * 8));
+        *reinterpret_cast<uint4*>(tile + (c >> 3) * 8192 + sw128_offset(key, c & 7)) = raw;
       }
     }
     fence_proxy_async_smem();
     workers_sync();
-    if (lane == 0) mbar_arrive(conv_done);
-    if (et == 0 && jl == 0) stamp(ts, 6);
+  };
 
-    // ---- softmax on S ----
-    {
-      bool w = true;
-      if (lane == 0) w = bar_wait(p, s_full, blk_cnt & 1, kDevTimeoutMmaDone);
-      ok = workers_all(__shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0);
-      if (!ok) break;
-    }
-    ++blk_cnt;
-    if (et == 0 && jl == 0) stamp(ts, 1);
-    tc_fence_after();
-    // two passes over this warp's 32 score columns in TMEM (16 at a time): the
-    // block max (combined with the other column half through shared memory),
-    // then p = 2^(z - m) -> P tile; scores in log2 units, one FMA per key
-    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      const int q = 2 * ch + qq;
-      uint32_t rr[16];
-      tmem_ld16(tmS + lane_base + q * 16, rr);
-      tmem_wait_ld();
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int c = 4 * q + cc;
-        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
-        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
-        mx[0] = fmaxf(mx[0], fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x));
-        mx[1] = fmaxf(mx[1], fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y));
-        mx[2] = fmaxf(mx[2], fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z));
-        mx[3] = fmaxf(mx[3], fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w));
+  for (int jl = -1; jl < nbl && ok; ++jl) {
+    const bool more = jl + 1 < nbl;
+    if (jl >= 0) {
+      const int j = blk_begin + jl;
+      const bool causal = V == kPi0 && j >= p.n_ctx_blocks && p.new_block != nullptr;
+      const float* sc = scale_set(jl);
+      const float* ks_s = sc;
+      const float* vs_s = sc + 64;
+      const float* kadd_s = sc + 128;
+      const int* nb_s = reinterpret_cast<const int*>(sc + 192);
+      if (more) request(j + 1, scale_set(jl + 1));  // in flight during this block's softmax
+
+      // ---- softmax on S ----
+      if (!wait_all(s_full, blk_cnt & 1, kDevTimeoutMmaDone)) {
+        ok = false;
+        break;
       }
-    }
-    float* mxb = mx_x + (jl & 1) * 256;
-    mxb[ch * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-    quad_pair_sync(quad);
-    const float bmax = fmaxf(mxb[r], mxb[128 + r]);
-    const float m_new = fmaxf(m_run, bmax);
-    bool need = false;
-    float m_use;
-    if (m_run == -INFINITY) {
-      m_use = m_new;
-    } else if (m_new > m_run + 8.f) {
-      need = true;
-      m_use = m_new;
-    } else {
-      m_use = m_run;
-    }
-    const float alpha = need ? exp2f(m_run - m_use) : 1.f;
-    const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      ++blk_cnt;
+      if (et == 0 && jl == 0) stamp(ts, 1);
+      if (et == 0 && jl == 1) stamp(ts, 8);
+      tc_fence_after();
+      // two passes over this warp's 32 score columns in TMEM (16 at a time): the
+      // block max (combined with the other column half through shared memory),
+      // then p = 2^(z - m) -> P tile; scores in log2 units, one FMA per key
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      const int q = 2 * ch + qq;
-      uint32_t rr[16];
-      tmem_ld16(tmS + lane_base + q * 16, rr);
-      tmem_wait_ld();
-      float pvq[16];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int c = 4 * q + cc;
-        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
-        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
-        const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
-        const float zz[4] = {fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x),
-                             fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y),
-                             fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z),
-                             fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w)};
-        const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float pe = ex2_approx(zz[e] - m_sub);
-          ps[e] += pe;
-          pvq[4 * cc + e] = pe * vv[e];
-        }
-      }
-      // keys 16q .. 16q+15 of row r: two 16-byte chunks of the P tile
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const uint4 v = make_uint4(pack_f16x2(pvq[8 * h2 + 0], pvq[8 * h2 + 1]),
-                                   pack_f16x2(pvq[8 * h2 + 2], pvq[8 * h2 + 3]),
-                                   pack_f16x2(pvq[8 * h2 + 4], pvq[8 * h2 + 5]),
-                                   pack_f16x2(pvq[8 * h2 + 6], pvq[8 * h2 + 7]));
-        *reinterpret_cast<uint4*>(sP + sw128_offset(r, 2 * q + h2)) = v;
-      }
-    }
-    const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-    l_run = l_run * alpha + psum;
-    m_run = m_use;
-    if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-      for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 2) {
-        uint32_t rr[2][16];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+      for (int qq = 0; qq < 2; ++qq) {
+        const int q = 2 * ch + qq;
+        uint32_t rr[16];
+        tmem_ld16(tmS + lane_base + q * 16, rr);
         tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) rr[q][e] = __float_as_uint(__uint_as_float(rr[q][e]) * alpha);
-          tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * q + cc;
+          const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+          float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+          if (causal) {
+            const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
+            if (nb.x > my_block) ka.x = -INFINITY;
+            if (nb.y > my_block) ka.y = -INFINITY;
+            if (nb.z > my_block) ka.z = -INFINITY;
+            if (nb.w > my_block) ka.w = -INFINITY;
+          }
+          mx[0] = fmaxf(mx[0], fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x));
+          mx[1] = fmaxf(mx[1], fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y));
+          mx[2] = fmaxf(mx[2], fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z));
+          mx[3] = fmaxf(mx[3], fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w));
         }
       }
-      tmem_wait_st();
+      float* mxb = mx_x + (jl & 1) * 256;
+      mxb[ch * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      quad_pair_sync(quad);
+      const float bmax = fmaxf(mxb[r], mxb[128 + r]);
+      const float m_new = fmaxf(m_run, bmax);
+      bool need = false;
+      float m_use;
+      if (m_run == -INFINITY) {
+        m_use = m_new;
+      } else if (m_new > m_run + 8.f) {
+        need = true;
+        m_use = m_new;
+      } else {
+        m_use = m_run;
+      }
+      const float alpha = need ? exp2f(m_run - m_use) : 1.f;
+      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq) {
+        const int q = 2 * ch + qq;
+        uint32_t rr[16];
+        tmem_ld16(tmS + lane_base + q * 16, rr);
+        tmem_wait_ld();
+        float pvq[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * q + cc;
+          const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+          float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+          if (causal) {
+            const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
+            if (nb.x > my_block) ka.x = -INFINITY;
+            if (nb.y > my_block) ka.y = -INFINITY;
+            if (nb.z > my_block) ka.z = -INFINITY;
+            if (nb.w > my_block) ka.w = -INFINITY;
+          }
+          const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
+          const float zz[4] = {fmaf(__uint_as_float(rr[4 * cc + 0]), km.x, ka.x),
+                               fmaf(__uint_as_float(rr[4 * cc + 1]), km.y, ka.y),
+                               fmaf(__uint_as_float(rr[4 * cc + 2]), km.z, ka.z),
+                               fmaf(__uint_as_float(rr[4 * cc + 3]), km.w, ka.w)};
+          const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float pe = ex2_approx(zz[e] - m_sub);
+            ps[e] += pe;
+            pvq[4 * cc + e] = pe * vv[e];
+          }
+        }
+        // keys 16q .. 16q+15 of row r: two 16-byte chunks of the P tile
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint4 v = make_uint4(pack_f16x2(pvq[8 * h2 + 0], pvq[8 * h2 + 1]),
+                                     pack_f16x2(pvq[8 * h2 + 2], pvq[8 * h2 + 3]),
+                                     pack_f16x2(pvq[8 * h2 + 4], pvq[8 * h2 + 5]),
+                                     pack_f16x2(pvq[8 * h2 + 6], pvq[8 * h2 + 7]));
+          *reinterpret_cast<uint4*>(sP + sw128_offset(r, 2 * q + h2)) = v;
+        }
+      }
+      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      l_run = l_run * alpha + psum;
+      m_run = m_use;
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 2) {
+          uint32_t rr[2][16];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) tmem_ld16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[q][e] = __float_as_uint(__uint_as_float(rr[q][e]) * alpha);
+            tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
+          }
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      if (et == 0 && jl == 1) stamp(ts, 9);
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(p_ready);
+    if (!more) break;
+
+    // ---- block jl + 1: per-key values, K, then (after P.V(jl)) V ----
+    const int jn = blk_begin + jl + 1;
+    float* scn = scale_set(jl + 1);
+    if (jl < 0) request(jn, scn);
+    finish(jn, scn);
+    if (jn >= p.n_ctx_blocks && nbl == 1) {
+      // the item's only block holds the new keys: the producer loads its K
+      // and V tiles by TMA once the QKV tiles are published
+      ok = wait_all(kvn_full, kvn_cnt & 1, kDevTimeoutTmaFull);  // also orders the values above
+      ++kvn_cnt;
+      if (ok && lane == 0) {
+        mbar_arrive(conv_done);
+        mbar_arrive(v_ready);
+      }
+      continue;
+    }
+    if (jn < p.n_ctx_blocks) {
+      // the int8 rows, staged by the producer
+      bool w = true;
+      if (lane == 0) w = bar_wait(p, stg_full, stg_cnt & 1, kDevTimeoutTmaFull);
+      w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+      // every reader observes the completed phase itself (it completed for
+      // lane 0, so this returns at once)
+      for (int n = 0; w && lane != 0 && n < (1 << 16) && !mbar_try_wait(stg_full, stg_cnt & 1); ++n) {
+      }
+      ++stg_cnt;
+      ok = workers_all(w);  // also orders the values above
+    } else {
+      // the new tokens' rows, written by this layer's QKV tiles
+      if (!new_ready)
+        ok = workers_ctr_wait(p, et, kCQkv,
+                              static_cast<unsigned>(p.op[kOpQkv].m_tiles * p.op[kOpQkv].splits) * (use + 1));
+      new_ready = true;
+      if (ok) workers_sync();
+    }
+    if (!ok) break;
+    fill(jn, 0, scn);
+    if (lane == 0) mbar_arrive(conv_done);
+    if (et == 0 && jl == 1) stamp(ts, 10);
+    if (jl >= 0 && !wait_all(o_full, (blk_cnt - 1) & 1, kDevTimeoutMmaDone)) {
+      ok = false;
+      break;
+    }
+    if (et == 0 && jl == 1) stamp(ts, 11);
+    fill(jn, 1, scn);
+    if (lane == 0) mbar_arrive(v_ready);
+    if (jn < p.n_ctx_blocks) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stg_empty);  // this warp's share of the staging buffer is read
+    }
+    if (et == 0 && jl == -1) stamp(ts, 6);
+    if (et == 0 && jl == 1) stamp(ts, 15);
   }
 
   // ---- epilogue: partial (O, m, l) of this split ----
@@ -981,17 +1116,22 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
     const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
     // lane: 8 of the row's 256 columns (chunk lane / 2, half lane % 2)
     const __half* ob = reinterpret_cast<const __half*>(p.ws_o) + ((lane >> 1) * kQR + r) * 16 + (lane & 1) * 8;
-    // split s's (m, l) sits in lane s (at most 32 splits): the row max M and
-    // the weights w_s = l_s * 2^(m_s - M) are warp reductions and broadcasts
+    // split s's (m, l) sits in lane s % 32, as the first (s < 32) or second
+    // of its pair: the row max M and the weights w_s = l_s * 2^(m_s - M) are
+    // warp reductions and broadcasts
     const float2 ml = lane < p.attn_splits ? __ldcg(p.ws_ml + (base + lane) * kQR + r) : make_float2(-INFINITY, 0.f);
+    const float2 ml2 =
+        lane + 32 < p.attn_splits ? __ldcg(p.ws_ml + (base + lane + 32) * kQR + r) : make_float2(-INFINITY, 0.f);
     uint4 o[kBatch];
 #pragma unroll
     for (int q = 0; q < kBatch; ++q)
       if (q < p.attn_splits) o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + q) * (kD / 16) * kQR * 16));
     const bool live = ml.x != -INFINITY && ml.y > 0.f;
-    const float M = warp_max(live ? ml.x : -INFINITY);
+    const bool live2 = ml2.x != -INFINITY && ml2.y > 0.f;
+    const float M = warp_max(fmaxf(live ? ml.x : -INFINITY, live2 ? ml2.x : -INFINITY));
     const float w = live ? exp2f(ml.x - M) * ml.y : 0.f;
-    const float L = warp_sum(w);
+    const float w2 = live2 ? exp2f(ml2.x - M) * ml2.y : 0.f;
+    const float L = warp_sum(w + w2);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int s0 = 0; s0 < p.attn_splits; s0 += kBatch) {
       if (s0 > 0) {
@@ -1002,7 +1142,7 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
       }
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
-        const float ws = __shfl_sync(0xffffffffu, w, (s0 + q) & 31);
+        const float ws = __shfl_sync(0xffffffffu, s0 + q < 32 ? w : w2, (s0 + q) & 31);
         if (s0 + q >= p.attn_splits) continue;
         const __half2* h2 = reinterpret_cast<const __half2*>(&o[q]);
 #pragma unroll
@@ -1027,10 +1167,82 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
   return true;
 }
 
+// PI0's per-step prefix of the token rows: the state token's projection and
+// the action-time MLP (action_in_proj -> concat with the time embedding ->
+// action_time_mlp_in -> SiLU -> action_time_mlp_out), reflex/policies/pi0/
+// modeling_pi0.py embed_suffix.  Kept out of line so that its registers do not
+// add to the PI0.5 finalize path.
+__device__ __noinline__ bool worker_fin_at(const ChunkParams& p, uint8_t* small, int et, int kind, int tau, int t,
+                                           unsigned long long* ts) {
+  float* red8 = reinterpret_cast<float*>(small + kSmRed8);
+  float* xs = reinterpret_cast<float*>(small + kSmXs);
+  const int f0 = et * 4;
+  const int b = t / p.S, s = t - b * p.S;
+  const int sa = s - 1;         // action row of the token (-1: the state token)
+  const int at = b * p.SA + sa;  // its row in the action-major buffers
+  if (kind == kTInit) {
+    float hv[4];
+    if (sa < 0) {
+      if (et < p.SD) xs[et] = bf16_round(p.state[static_cast<long>(b) * p.SD + et]);
+      workers_sync();
+      proj_in4(p, et, xs, hv, p.w_st, p.b_st, p.SD);
+      *reinterpret_cast<uint2*>(p.st_emb + static_cast<long>(b) * p.W + f0) = pack4_bf16(hv);
+    } else {
+      if (et < p.A) xs[et] = bf16_round(p.x[static_cast<long>(at) * p.A + et]);
+      workers_sync();
+      action_in4(p, et, xs, hv);
+      write_at_x(p, et, at, 0, hv);
+    }
+    workers_publish(p, et, kCAtX);
+    return true;
+  }
+  if (kind == kTFinAt1 || kind == kTFinAt2) {
+    const bool first = kind == kTFinAt1;
+    const int op = first ? kOpAtIn : kOpAtOut;
+    const OpCfg oc = op_cfg(p, op);
+    NormVec nv1;
+    if (!first) load_norm_vec(p, et, tau, 0, nv1);  // the first layer's input norm
+    if (!workers_ctr_wait(p, et, first ? kCPat1 : kCPat2, static_cast<unsigned>(oc.m_tiles * oc.splits) * (tau + 1)))
+      return false;
+    if (et == 0) stamp(ts, 1);
+    float hv[4];
+    if (sa >= 0) {
+      float acc[4];
+      sum_partials4(p, op, at, f0, acc);
+      const float4 bias = *reinterpret_cast<const float4*>((first ? p.b_atin : p.b_atout) + f0);
+      const float bb[4] = {bias.x, bias.y, bias.z, bias.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = bf16_round(acc[e] + bb[e]);
+        hv[e] = first ? bf16_round(v / (1.f + expf(-v))) : v;
+      }
+      if (first) *reinterpret_cast<uint2*>(p.at_hid + static_cast<long>(at) * p.W + f0) = pack4_bf16(hv);
+    } else if (!first) {
+      unpack4_bf16(__ldcg(reinterpret_cast<const uint2*>(p.st_emb + static_cast<long>(b) * p.W + f0)), hv);
+    }
+    if (first) {
+      workers_publish(p, et, kCAtH);
+      return true;
+    }
+    *reinterpret_cast<uint2*>(p.h + static_cast<long>(t) * p.W + f0) = pack4_bf16(hv);
+    float y[4];
+    norm_row(p, et, hv, nv1, red8, y);
+    *reinterpret_cast<uint2*>(p.xn + static_cast<long>(t) * p.W + f0) = pack4_bf16(y);
+    workers_publish(p, et, kCXn);
+    return true;
+  }
+  return false;
+}
+
 // ------------------------------------------ worker: per-token finalization ---
-// kind kTInit: h = action_in_proj(x) at the first step; kTFinO / kTFinD: the
-// gated residual of o_proj / down_proj.  Then the next norm (or the Euler tail
-// after the last layer).
+// kind kTInit: the first step's input (PI0.5: h = action_in_proj(x) and its
+// norm; PI0: state_proj(state) for the state token, [action_in(x), t_emb]
+// for the action tokens); kTFinO / kTFinD: the gated residual of o_proj /
+// down_proj, then the next norm (or the Euler tail after the last layer);
+// PI0's kTFinAt1 (action_time_mlp_in: bias + SiLU) and kTFinAt2
+// (action_time_mlp_out: bias, or the state token's embedding, then the first
+// layer's input norm).
+template <int V>
 __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small, int et, int kind, int tau, int layer, int t,
                            unsigned long long* ts) {
   const int lane = et & 31, wq = et >> 5;
@@ -1043,6 +1255,9 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
   const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
   const int f0 = et * 4;
   const int b = t / p.S, s = t - b * p.S;
+  constexpr bool pi0 = V == kPi0;
+  const int sa = pi0 ? s - 1 : s;  // action row of the token (-1: PI0's state token)
+  const int at = b * p.SA + sa;    // its row in the action-major buffers
   const bool tail = kind == kTFinD && layer == p.NL - 1;
   const bool next_step = tail && tau + 1 < p.steps;
   // everything that does not depend on the phase input is requested first
@@ -1053,7 +1268,7 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
   if (kind != kTInit && p.gate) load4(p.gate + mod_off(p, tau, kind == kTFinO ? 2 * layer : 2 * layer + 1) + f0, g);
   float hv[4];
   if (kind == kTInit) {
-    if (et < p.A) xs[et] = bf16_round(p.x[(static_cast<long>(b) * p.S + s) * p.A + et]);
+    if (et < p.A) xs[et] = bf16_round(p.x[static_cast<long>(at) * p.A + et]);
     workers_sync();
     action_in4(p, et, xs, hv);
   } else {
@@ -1063,25 +1278,9 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
                           static_cast<unsigned>(oc.m_tiles * oc.splits) * (use + 1)))
       return false;
     if (et == 0) stamp(ts, 1);
-    const int m = f0 / kBM, r0 = f0 % kBM;
     uint2 hraw = __ldcg(reinterpret_cast<const uint2*>(p.h + static_cast<long>(t) * p.W + f0));
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < oc.splits; s0 += 4) {
-      float4 a[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (s0 + q < oc.splits) {
-          const float* ps = oc.part + ((static_cast<long>(m) * oc.splits + s0 + q) * kNT + t) * kBM + r0;
-          a[q] = __ldcg(reinterpret_cast<const float4*>(ps));
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (s0 + q < oc.splits) {
-          acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
-        }
-      }
-    }
+    float acc[4];
+    sum_partials4(p, op, t, f0, acc);
     float hres[4];
     unpack4_bf16(hraw, hres);
 #pragma unroll
@@ -1094,6 +1293,11 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
   if (kind == kTFinD && tau == 0 && p.dbg_h)
     *reinterpret_cast<uint2*>(p.dbg_h + (static_cast<long>(layer) * p.T + t) * p.W + f0) = pack4_bf16(hv);
   if (tail) {
+    if (sa < 0) {
+      // PI0's state token: its next input row is rebuilt by kTFinAt2
+      workers_publish(p, et, kCAtX);
+      return true;
+    }
     // final norm -> action_out_proj -> x += bf16(dt * v) -> next step's action_in_proj
     float y[4];
     norm_row(p, et, hv, nv1, red8, y);
@@ -1117,7 +1321,7 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
       acc = warp_sum(acc);
       if (lane == 0) {
         const float v = bf16_round(acc + (p.b_out ? __bfloat162float(p.b_out[a]) : 0.f));
-        float* xp = p.x + (static_cast<long>(b) * p.S + s) * p.A + a;
+        float* xp = p.x + static_cast<long>(at) * p.A + a;
         const float xn = __fadd_rn(*xp, bf16_round(__fmul_rn(p.dt, v)));
         *xp = xn;
         xs[a] = bf16_round(xn);
@@ -1125,11 +1329,16 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
     }
     workers_sync();
     if (!next_step) {
-      workers_publish(p, et, kCXn);
+      workers_publish(p, et, pi0 ? kCAtX : kCXn);
+      return true;
+    }
+    action_in4(p, et, xs, hv);
+    if (pi0) {
+      write_at_x(p, et, at, tau + 1, hv);
+      workers_publish(p, et, kCAtX);
       return true;
     }
     load_norm_vec(p, et, tau + 1, 0, nv1);  // the next step's first input norm
-    action_in4(p, et, xs, hv);
   }
   *reinterpret_cast<uint2*>(p.h + static_cast<long>(t) * p.W + f0) = pack4_bf16(hv);
   float y[4];
@@ -1143,10 +1352,12 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
 // Tensor maps of a GEMM op, selected with constant indices (a runtime index
 // into the kernel parameters would copy them to local memory).
 __device__ __forceinline__ const CUtensorMap* wmap(const Maps& maps, int op) {
-  return op == kOpQkv ? &maps.w[kOpQkv] : op == kOpO ? &maps.w[kOpO] : op == kOpGu ? &maps.w[kOpGu] : &maps.w[kOpDown];
+  return op == kOpQkv ? &maps.w[kOpQkv] : op == kOpO ? &maps.w[kOpO] : op == kOpGu ? &maps.w[kOpGu]
+         : op == kOpDown ? &maps.w[kOpDown] : op == kOpAtIn ? &maps.w[kOpAtIn] : &maps.w[kOpAtOut];
 }
 __device__ __forceinline__ const CUtensorMap* xmap(const Maps& maps, int op) {
-  return op == kOpQkv ? &maps.x[kOpQkv] : op == kOpO ? &maps.x[kOpO] : op == kOpGu ? &maps.x[kOpGu] : &maps.x[kOpDown];
+  return op == kOpQkv ? &maps.x[kOpQkv] : op == kOpO ? &maps.x[kOpO] : op == kOpGu ? &maps.x[kOpGu]
+         : op == kOpDown ? &maps.x[kOpDown] : op == kOpAtIn ? &maps.x[kOpAtIn] : &maps.x[kOpAtOut];
 }
 
 __device__ __forceinline__ int task_type(int4 t) { return t.x & 0xff; }
@@ -1166,6 +1377,8 @@ __device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigne
       }
       break;
     case kOpGu: *line = kCXn2; *target = static_cast<unsigned>(p.n_fin) * (use + 1); break;
+    case kOpAtIn: *line = kCAtX; *target = static_cast<unsigned>(p.n_fin) * (use / p.NL + 1); break;
+    case kOpAtOut: *line = kCAtH; *target = static_cast<unsigned>(p.n_fin) * (use / p.NL + 1); break;
     default:
       *line = kCAct;
       *target = static_cast<unsigned>(p.op[kOpGu].m_tiles * p.op[kOpGu].splits) * (use + 1);
@@ -1173,6 +1386,8 @@ __device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigne
   }
 }
 
+// V: kPi05 or kPi0 (PI0's code paths are compiled only into its instantiation)
+template <int V>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_kernel(const __grid_constant__ Maps maps, const __grid_constant__ ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -1208,8 +1423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairReady), kWorkers / 64);  // the peer's pushing warps
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmPairDone), kWorkers / 32);
     mbar_init(reinterpret_cast<uint64_t*>(small + kSmMmaDrain), 1);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmStgFull), 1);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmStgEmpty), kWorkers / 32);
+    mbar_init(reinterpret_cast<uint64_t*>(small + kSmVReady), kWorkers / 32);
     fence_mbar_init();
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < (V == kPi0 ? kNumOps : kOpDown + 1); ++i) {
       tma_prefetch_desc(&maps.w[i]);
       tma_prefetch_desc(&maps.x[i]);
     }
@@ -1234,6 +1452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_step = p.step_off[cta + 1] - p.step_off[cta];
   uint32_t issued = 0;  // ring stages issued by the producer
   uint32_t q_issued = 0, kvn_issued = 0;  // attention Q / new-key tile loads issued by the producer
+  uint32_t stg_issued = 0;                // context blocks staged by the producer
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1245,8 +1464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int4 tk = stasks[i];
           const int ty = task_type(tk), layer = task_layer(tk);
           const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
-          if (ty >= kTQkv && ty <= kTDown) {
-            const int op = ty - kTQkv;
+          if (gemm_op(ty) >= 0) {
+            const int op = gemm_op(ty);
             const OpCfg oc = op_cfg(p, op);
             const int m = tk.y, kb0 = tk.w >> 16, kb1 = tk.w & 0xffff;
             const int nkb = kb1 - kb0;
@@ -1300,19 +1519,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                            : nullptr;
             stamp(pts, 12);
+            const int b = tk.y, qt = tk.z;
+            const int sp = tk.w;
+            const int blk0 = sp * p.n_blocks / p.attn_splits;
+            const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk0;
+            const int n_stage = max(0, min(nbl, p.n_ctx_blocks - blk0));  // context blocks of the item
+            // context block j's int8 K / V rows (slots past the capacity are
+            // not copied: those keys are masked and the stale bytes convert to
+            // finite values) -> staging buffer, after the workers have
+            // converted the block before it out of the buffer
+            auto stage = [&](int j) {
+              if (stg_issued > 0)
+                ok = ok && bar_wait(p, reinterpret_cast<uint64_t*>(small + kSmStgEmpty), (stg_issued - 1) & 1,
+                                    kDevTimeoutConvert);
+              if (!ok) return;
+              const int rows = min(kKB, p.cap - j * kKB);
+              const uint32_t bytes = static_cast<uint32_t>(rows) * kD;
+              const long off = (static_cast<long>(b) * p.cap + static_cast<long>(j) * kKB) * kD;
+              uint64_t* stg_full = reinterpret_cast<uint64_t*>(small + kSmStgFull);
+              mbar_arrive_expect_tx(stg_full, 2 * bytes);
+              ++stg_issued;
+              bulk_load(smem + kOffAStg, p.k_ring[layer] + off, bytes, stg_full);
+              bulk_load(smem + kOffAStg + kStgBytes, p.v_ring[layer] + off, bytes, stg_full);
+            };
+            if (n_stage > 0) stage(blk0);
+            if (!ok) break;
             ok = ctr_wait(p, kCQkv, static_cast<unsigned>(p.op[kOpQkv].m_tiles * p.op[kOpQkv].splits) * (use + 1));
             stamp(pts, 13);
             if (!ok) break;
             fence_proxy_async_global();
-            const int b = tk.y, qt = tk.z;
             const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
             mbar_arrive_expect_tx(q_full, 4 * 16384);
             ++q_issued;
             for (int a = 0; a < 4; ++a)
               tma_load_2d(smem + kOffAQ + a * 16384, &maps.q, q_full, a * 64, static_cast<int>(q_row0));
-            const int sp = tk.w;
-            const int blk0 = sp * p.n_blocks / p.attn_splits;
-            const int nbl = (sp + 1) * p.n_blocks / p.attn_splits - blk0;
             if (nbl == 1 && blk0 >= p.n_ctx_blocks) {
               // the new keys' K / V tiles (rows of the next stream, or zero
               // fill, beyond S are masked in the softmax)
@@ -1325,6 +1565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(smem + kOffAV + a * 8192, &maps.vn, kvn_full, a * 64, row0);
               }
             }
+            for (int jl = 1; jl < n_stage && ok; ++jl) stage(blk0 + jl);
+            if (!ok) break;
             ok = bar_wait(p, attn_done, attn_cnt & 1, kDevTimeoutConvert);
             ++attn_cnt;
           }
@@ -1335,7 +1577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_g = make_idesc_f16(kBM, kNT, true);
-      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
+      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, false);  // f16 Q and K
       constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
       uint32_t consumed = 0, tmem_uses = 0, q_cnt = 0, conv_cnt = 0, p_cnt = 0;
       // ring stage 0's operand descriptors (shared-memory addresses stay below
@@ -1347,7 +1589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < n_step && ok; ++i) {
           const int4 tk = stasks[i];
           const int ty = task_type(tk);
-          if (ty >= kTQkv && ty <= kTDown) {
+          if (gemm_op(ty) >= 0) {
             const int nkb = (tk.w & 0xffff) - (tk.w >> 16);
             if (tmem_uses > 0) ok = bar_wait(p, acc_free, (tmem_uses - 1) & 1, kDevTimeoutMmaDone);
             if (!ok) break;
@@ -1408,7 +1650,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_f16_ss(tmem + 256, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
               }
               umma_commit(s_full);
-              ok = bar_wait(p, p_ready, p_cnt & 1, kDevTimeoutConvert);
+              ok = bar_wait(p, p_ready, p_cnt & 1, kDevTimeoutConvert) &&
+                   bar_wait(p, reinterpret_cast<uint64_t*>(small + kSmVReady), p_cnt & 1, kDevTimeoutConvert);
               ++p_cnt;
               if (!ok) break;
               tc_fence_after();
@@ -1426,9 +1669,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int et = threadIdx.x - 64;
-    uint32_t acc_cnt = 0, blk_cnt = 0, kvn_cnt = 0, pair_cnt = 0;
+    uint32_t acc_cnt = 0, blk_cnt = 0, kvn_cnt = 0, pair_cnt = 0, stg_cnt = 0;
     bool ok = true;
-    for (int i = 0; i < n_init && ok; ++i) ok = worker_fin(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
+    for (int i = 0; i < n_init && ok; ++i)
+      ok = V == kPi0 ? worker_fin_at(p, small, et, kTInit, 0, itasks[i].y, nullptr)
+                     : worker_fin<V>(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
     for (int tau = 0; tau < p.steps && ok; ++tau) {
       for (int i = 0; i < n_step && ok; ++i) {
         const int4 tk = stasks[i];
@@ -1447,14 +1692,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         switch (ty) {
-          case kTQkv: case kTO: case kTGu: case kTDown:
-            ok = worker_gemm(p, smem, small, tmem, et, ty - kTQkv, layer, tk.y, tk.z, acc_cnt, pair_cnt, ts);
+          case kTQkv: case kTO: case kTGu: case kTDown: case kTAtIn: case kTAtOut:
+            ok = worker_gemm(p, smem, small, tmem, et, gemm_op(ty), layer, tk.y, tk.z, acc_cnt, pair_cnt, ts);
             break;
           case kTAttn:
-            ok = worker_attn(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, ts);
+            ok = worker_attn<V>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
             break;
           case kTComb: ok = worker_comb(p, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
-          case kTFinO: case kTFinD: ok = worker_fin(p, small, et, ty, tau, layer, tk.y, ts); break;
+          case kTFinO: case kTFinD: ok = worker_fin<V>(p, small, et, ty, tau, layer, tk.y, ts); break;
+          case kTFinAt1: case kTFinAt2:
+            if (V == kPi0) ok = worker_fin_at(p, small, et, ty, tau, tk.y, ts);
+            break;
           default: break;
         }
         if (et == 0) stamp(ts, 2);
@@ -1471,6 +1719,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (q_issued > 0) mbar_wait(q_full, (q_issued - 1) & 1, p.status, kDevTimeoutTmaFull);
     if (kvn_issued > 0)
       mbar_wait(reinterpret_cast<uint64_t*>(small + kSmKvnFull), (kvn_issued - 1) & 1, p.status, kDevTimeoutTmaFull);
+    if (stg_issued > 0)
+      mbar_wait(reinterpret_cast<uint64_t*>(small + kSmStgFull), (stg_issued - 1) & 1, p.status, kDevTimeoutTmaFull);
   }
   if (warp == 1 && lane == 0) {
     uint64_t* drain = reinterpret_cast<uint64_t*>(small + kSmMmaDrain);
@@ -1497,24 +1747,34 @@ namespace {
 // cluster (summed through DSMEM); o_proj / down_proj tiles are split eight
 // ways and summed per token by the next phase
 constexpr int kSplitsQkv = 2, kSplitsO = 8, kSplitsGu = 2, kSplitsDown = 8;
+constexpr int kMaxSplits = 64;  // attention key-range splits (the combine holds two per lane)
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct Layout {
-  int T, q_tiles, n_ctx_blocks, n_blocks, splits, n_attn, n_comb;
-  OpCfg op[4];
-  size_t off_ctr, off_part[4], off_ws_o, off_ws_ml, off_h, off_xn, off_q, off_kn, off_vn, off_attn, off_act,
-      off_ptrs, off_tasks, total;
+  int T, S, q_tiles, n_ctx_blocks, n_blocks, splits, n_attn, n_comb;
+  OpCfg op[kNumOps];
+  size_t off_ctr, off_part[kNumOps], off_ws_o, off_ws_ml, off_h, off_xn, off_q, off_kn, off_vn, off_attn, off_act,
+      off_at_x, off_at_hid, off_st, off_ptrs, off_tasks, total;
 };
 
+// tokens per stream inside the layers: PI0 puts its state token first
+int layer_tokens(const rfx_chunk_desc& d) { return d.S + (d.variant == RFX_CHUNK_PI0 ? 1 : 0); }
+
 int validate(const rfx_chunk_desc& d) {
-  const int T = d.B * d.S;
+  if (d.variant != RFX_CHUNK_PI05 && d.variant != RFX_CHUNK_PI0) return set_error(RFX_E_INVAL, "rfx_chunk: variant");
+  const int T = d.B * layer_tokens(d);
   if (d.B < 1 || d.S < 1 || T > kNT || d.num_layers < 1 || d.num_layers > 255 || d.num_steps < 1 ||
       d.width != 1024 || d.num_q_heads < 1 || (d.num_q_heads + 2) * 256 % kBM || d.mlp_dim < kBM ||
       d.mlp_dim % 64 || d.action_dim < 8 || d.action_dim > 64 || d.action_dim % 8)
     return set_error(RFX_E_UNSUPPORTED,
-                     "rfx_chunk: needs B*S <= 64 tokens, width 1024, head_dim 256, mlp_dim %% 64 == 0, action_dim "
-                     "8..64 (multiple of 8)");
+                     "rfx_chunk: needs B*S <= 64 tokens (PI0: B*(S+1)), width 1024, head_dim 256, mlp_dim %% 64 == 0, "
+                     "action_dim 8..64 (multiple of 8)");
+  if (d.variant == RFX_CHUNK_PI0 &&
+      (!d.state || !d.w_state || !d.w_atin || !d.b_atin || !d.w_atout || !d.b_atout || !d.time_emb || !d.new_block ||
+       d.state_dim < 8 || d.state_dim > 64 || d.state_dim % 8))
+    return set_error(RFX_E_INVAL, "rfx_chunk: PI0 needs state, state_proj, action-time MLP, time embedding and "
+                                  "new_block, state_dim 8..64 (multiple of 8)");
   if (!d.w_qkv || !d.w_o || !d.w_gu || !d.w_down || !d.norm_a1 || !d.w_in || !d.w_out || !d.rope_table ||
       !d.positions || !d.x || !d.k_ring || !d.v_ring || !d.k_scale || !d.v_scale)
     return set_error(RFX_E_INVAL, "rfx_chunk: null pointer in the descriptor");
@@ -1529,24 +1789,34 @@ int validate(const rfx_chunk_desc& d) {
     if (!d.k_ring[l] || !d.v_ring[l] || !d.k_scale[l] || !d.v_scale[l] ||
         (d.quant_mode == RFX_QUANT_U8_REF && (!d.k_zp[l] || !d.v_zp[l])))
       return set_error(RFX_E_INVAL, "rfx_chunk: null ring pointer of layer %d", l);
+  for (int l = 0; l < d.num_layers; ++l)  // context blocks are staged by bulk copies
+    if ((reinterpret_cast<uintptr_t>(d.k_ring[l]) | reinterpret_cast<uintptr_t>(d.v_ring[l])) & 15)
+      return set_error(RFX_E_INVAL, "rfx_chunk: the rings of layer %d must be 16-byte aligned", l);
   return RFX_OK;
 }
 
 Layout layout(const rfx_chunk_desc& d, int nct) {
   Layout L{};
-  L.T = d.B * d.S;
+  L.S = layer_tokens(d);
+  L.T = d.B * L.S;
   const int hq = d.num_q_heads;
-  L.q_tiles = (hq * d.S + kQR - 1) / kQR;
+  const bool pi0 = d.variant == RFX_CHUNK_PI0;
+  L.q_tiles = (hq * L.S + kQR - 1) / kQR;
   L.n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
-  L.n_blocks = L.n_ctx_blocks + (d.S + kKB - 1) / kKB;
-  int splits = d.kv_splits > 0 ? d.kv_splits : L.n_blocks;
-  splits = std::max(1, std::min({splits, L.n_blocks, 32}));
+  L.n_blocks = L.n_ctx_blocks + (L.S + kKB - 1) / kKB;
+  // by default one key block per split, or, for long contexts, as many
+  // splits as put one attention item on each CTA (those without a QKV tile
+  // take theirs first: they stage and convert their first block while the
+  // QKV tiles run)
+  int splits = d.kv_splits;
+  if (splits <= 0) splits = std::max(1, nct / (d.B * L.q_tiles));
+  splits = std::max(1, std::min({splits, L.n_blocks, kMaxSplits}));
   L.splits = splits;
   L.n_attn = d.B * L.q_tiles * splits;
   L.n_comb = splits > 1 ? d.B * L.q_tiles * (kQR / 4) : 0;  // 4 query rows (one per worker warp) per item
-  const int rows[4] = {(hq + 2) * 256, d.width, 2 * d.mlp_dim, d.width};
-  const int Ks[4] = {d.width, hq * 256, d.width, d.mlp_dim};
-  const int sp[4] = {kSplitsQkv, kSplitsO, kSplitsGu, kSplitsDown};
+  const int rows[kNumOps] = {(hq + 2) * 256, d.width, 2 * d.mlp_dim, d.width, d.width, d.width};
+  const int Ks[kNumOps] = {d.width, hq * 256, d.width, d.mlp_dim, 2 * d.width, d.width};
+  const int sp[kNumOps] = {kSplitsQkv, kSplitsO, kSplitsGu, kSplitsDown, kSplitsO, kSplitsO};
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1554,7 +1824,7 @@ Layout layout(const rfx_chunk_desc& d, int nct) {
     return o;
   };
   L.off_ctr = take(static_cast<size_t>(kNumCtrLines) * 128);
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < kNumOps; ++i) {
     OpCfg& oc = L.op[i];
     oc.rows = rows[i];
     oc.K = Ks[i];
@@ -1563,18 +1833,23 @@ Layout layout(const rfx_chunk_desc& d, int nct) {
     oc.splits = std::min(sp[i], kb_total);
     while (kb_total % oc.splits) --oc.splits;
     oc.kb = kb_total / oc.splits;
-    L.off_part[i] = take(static_cast<size_t>(oc.m_tiles) * oc.splits * kNT * kBM * 4);
+    const bool used = i <= kOpDown || pi0;  // PI0's action-time MLP
+    L.off_part[i] = take(used ? static_cast<size_t>(oc.m_tiles) * oc.splits * kNT * kBM * 4 : 0);
   }
   const size_t wrows = static_cast<size_t>(d.B) * L.q_tiles * splits * kQR;
   L.off_ws_o = take(wrows * kD * 4);
   L.off_ws_ml = take(wrows * 8);
   L.off_h = take(static_cast<size_t>(L.T) * d.width * 2);
   L.off_xn = take(static_cast<size_t>(L.T) * d.width * 2);
-  L.off_q = take(static_cast<size_t>(d.B) * hq * d.S * 256 * 2);
+  L.off_q = take(static_cast<size_t>(d.B) * hq * L.S * 256 * 2);
   L.off_kn = take(static_cast<size_t>(L.T) * 256 * 2);
   L.off_vn = take(static_cast<size_t>(L.T) * 256 * 2);
   L.off_attn = take(static_cast<size_t>(L.T) * hq * 256 * 2);
   L.off_act = take(static_cast<size_t>(L.T) * d.mlp_dim * 2);
+  const size_t TA = static_cast<size_t>(d.B) * d.S;
+  L.off_at_x = take(pi0 ? TA * 2 * d.width * 2 : 0);
+  L.off_at_hid = take(pi0 ? TA * d.width * 2 : 0);
+  L.off_st = take(pi0 ? static_cast<size_t>(d.B) * d.width * 2 : 0);
   L.off_ptrs = take(static_cast<size_t>(6) * d.num_layers * sizeof(void*));
   L.off_tasks = off;  // the task tables follow (size known after scheduling)
   L.total = off;
@@ -1595,6 +1870,7 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
   std::vector<long> load(nct, 0);
   int rr = 0;  // rotating start for the light tasks
   auto enc = [](int type, int layer) { return type | (layer << 8); };
+  auto task_of = [](int op) { return op <= kOpDown ? kTQkv + op : op == kOpAtIn ? kTAtIn : kTAtOut; };
   auto gemm_phase = [&](int layer, int op, const std::vector<char>& excl) {
     const OpCfg& oc = L.op[op];
     std::vector<int> cnt(nct, 0);
@@ -1611,7 +1887,7 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
         }
         for (int s = 0; s < 2; ++s) {
           const int kb0 = s * oc.kb, kb1 = kb0 + oc.kb;
-          lst[best + s].push_back(make_int4(enc(kTQkv + op, layer), m, s, (kb0 << 16) | kb1));
+          lst[best + s].push_back(make_int4(enc(task_of(op), layer), m, s, (kb0 << 16) | kb1));
           cnt[best + s]++;
           used[best + s] = 1;
           load[best + s] += static_cast<long>(oc.kb) * kWBytes;
@@ -1627,7 +1903,7 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
           if (best < 0 || cnt[c] < cnt[best] || (cnt[c] == cnt[best] && load[c] < load[best])) best = c;
         }
         const int kb0 = s * oc.kb, kb1 = kb0 + oc.kb;
-        lst[best].push_back(make_int4(enc(kTQkv + op, layer), m, s, (kb0 << 16) | kb1));
+        lst[best].push_back(make_int4(enc(task_of(op), layer), m, s, (kb0 << 16) | kb1));
         cnt[best]++;
         used[best] = 1;
         load[best] += static_cast<long>(oc.kb) * kWBytes;
@@ -1640,31 +1916,45 @@ Schedule build_schedule(const rfx_chunk_desc& d, const Layout& L, int nct) {
   };
   for (int t = 0; t < L.T; ++t) ini[t % nct].push_back(make_int4(kTInit, t, 0, 0));
   const std::vector<char> none(nct, 0);
+  if (d.variant == RFX_CHUNK_PI0) {
+    // every step starts with the action-time MLP: [action_in(x), t_emb] ->
+    // Linear + SiLU -> Linear -> the action rows of h (the state row is its
+    // embedding), then the first layer's input norm
+    gemm_phase(0, kOpAtIn, none);
+    for (int t = 0; t < L.T; ++t) light(make_int4(enc(kTFinAt1, 0), t, 0, 0));
+    gemm_phase(0, kOpAtOut, none);
+    for (int t = 0; t < L.T; ++t) light(make_int4(enc(kTFinAt2, 0), t, 0, 0));
+  }
   for (int l = 0; l < d.num_layers; ++l) {
     const std::vector<char> qkv_cta = gemm_phase(l, kOpQkv, none);
-    // attention items go to CTAs without a QKV tile in this layer, so they
-    // convert their context blocks while the QKV tiles run
+    // attention items go to CTAs without a QKV tile in this layer first, so
+    // they stage and convert their first context block while the QKV tiles run
     std::vector<char> attn_cta(nct, 0);
-    int n_free = 0;
-    for (char c : qkv_cta) n_free += c ? 0 : 1;
-    int c = rr % nct;
+    std::vector<int> order;  // CTAs without a QKV tile first, then the others
+    for (int pass = 0; pass < 2; ++pass)
+      for (int k = 0; k < nct; ++k) {
+        const int c = (rr + k) % nct;
+        if ((qkv_cta[c] != 0) == (pass == 1)) order.push_back(c);
+      }
+    int n_items = 0;
     for (int b = 0; b < d.B; ++b)
       for (int qt = 0; qt < L.q_tiles; ++qt)
         for (int s = 0; s < L.splits; ++s) {
-          if (n_free > 0)
-            while (qkv_cta[c]) c = (c + 1) % nct;
+          const int c = order[n_items++ % nct];
           attn_cta[c] = 1;
           lst[c].push_back(make_int4(enc(kTAttn, l), b, qt, s));
-          c = (c + 1) % nct;
         }
-    rr = c;
+    rr = order[n_items % nct];
     if (L.splits > 1)
       for (int b = 0; b < d.B; ++b)
         for (int qt = 0; qt < L.q_tiles; ++qt)
           for (int g = 0; g < kQR / 4; ++g) light(make_int4(enc(kTComb, l), b, qt, ((g * 4) << 16) | (g * 4 + 4)));
+    // o_proj tiles avoid the attention CTAs (whose shared memory holds the
+    // attention tiles until their item ends) when the others can take one
+    // tile each
     int n_attn_cta = 0;
     for (char c : attn_cta) n_attn_cta += c;
-    gemm_phase(l, kOpO, n_attn_cta < nct ? attn_cta : none);
+    gemm_phase(l, kOpO, nct - n_attn_cta >= L.op[kOpO].m_tiles * L.op[kOpO].splits ? attn_cta : none);
     for (int t = 0; t < L.T; ++t) light(make_int4(enc(kTFinO, l), t, 0, 0));
     gemm_phase(l, kOpGu, none);
     gemm_phase(l, kOpDown, none);
@@ -1740,7 +2030,10 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
   c->ctr_bytes = static_cast<size_t>(kNumCtrLines) * 128;
   ChunkParams& p = c->params;
   p.T = L.T;
-  p.S = d.S;
+  p.S = L.S;
+  p.variant = d.variant;
+  p.SA = d.S;
+  p.TA = d.B * d.S;
   p.B = d.B;
   p.NL = d.num_layers;
   p.steps = d.num_steps;
@@ -1763,9 +2056,22 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
   p.eps = d.eps;
   p.dt = d.dt;
   p.scale_log2 = d.softmax_scale * 1.4426950408889634f;
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < kNumOps; ++i) {
     p.op[i] = L.op[i];
     p.op[i].part = reinterpret_cast<float*>(ws + L.off_part[i]);
+  }
+  if (d.variant == RFX_CHUNK_PI0) {
+    p.state = d.state;
+    p.SD = d.state_dim;
+    p.w_st = static_cast<const __nv_bfloat16*>(d.w_state);
+    p.b_st = static_cast<const __nv_bfloat16*>(d.b_state);
+    p.b_atin = d.b_atin;
+    p.b_atout = d.b_atout;
+    p.temb = static_cast<const __nv_bfloat16*>(d.time_emb);
+    p.at_x = reinterpret_cast<__nv_bfloat16*>(ws + L.off_at_x);
+    p.at_hid = reinterpret_cast<__nv_bfloat16*>(ws + L.off_at_hid);
+    p.st_emb = reinterpret_cast<__nv_bfloat16*>(ws + L.off_st);
+    p.new_block = d.new_block;
   }
   p.a1 = d.norm_a1;
   p.a2 = d.mod_a2;
@@ -1838,31 +2144,38 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
 
   // tensor maps: weights stacked over layers, activations [T][K], q rows
   const int T = L.T;
-  const uint64_t wrows[4] = {static_cast<uint64_t>(NL) * L.op[0].rows, static_cast<uint64_t>(NL) * L.op[1].rows,
-                             static_cast<uint64_t>(NL) * L.op[2].rows, static_cast<uint64_t>(NL) * L.op[3].rows};
-  const void* wptr[4] = {d.w_qkv, d.w_o, d.w_gu, d.w_down};
-  const void* xptr[4] = {p.xn, p.attn_out, p.xn, p.act};
-  for (int i = 0; i < 4 && !rc; ++i) {
+  // the action-time MLP's weights are not per layer; its inputs are action-token rows
+  const uint64_t wrows[kNumOps] = {static_cast<uint64_t>(NL) * L.op[0].rows, static_cast<uint64_t>(NL) * L.op[1].rows,
+                                   static_cast<uint64_t>(NL) * L.op[2].rows, static_cast<uint64_t>(NL) * L.op[3].rows,
+                                   static_cast<uint64_t>(L.op[4].rows), static_cast<uint64_t>(L.op[5].rows)};
+  const void* wptr[kNumOps] = {d.w_qkv, d.w_o, d.w_gu, d.w_down, d.w_atin, d.w_atout};
+  const void* xptr[kNumOps] = {p.xn, p.attn_out, p.xn, p.act, p.at_x, p.at_hid};
+  const uint64_t xrows[kNumOps] = {static_cast<uint64_t>(T), static_cast<uint64_t>(T), static_cast<uint64_t>(T),
+                                   static_cast<uint64_t>(T), static_cast<uint64_t>(p.TA), static_cast<uint64_t>(p.TA)};
+  const int n_ops = d.variant == RFX_CHUNK_PI0 ? kNumOps : kOpDown + 1;
+  for (int i = 0; i < n_ops && !rc; ++i) {
     rc = make_tmap_2d(&c->maps.w[i], wptr[i], 2, L.op[i].K, wrows[i], static_cast<uint64_t>(L.op[i].K) * 2, kBK, kBM,
                       true);
     if (!rc)
-      rc = make_tmap_2d(&c->maps.x[i], xptr[i], 2, L.op[i].K, T, static_cast<uint64_t>(L.op[i].K) * 2, kBK, kNT, true);
+      rc = make_tmap_2d(&c->maps.x[i], xptr[i], 2, L.op[i].K, xrows[i], static_cast<uint64_t>(L.op[i].K) * 2, kBK,
+                        kNT, true);
   }
   if (!rc)
-    rc = make_tmap_2d(&c->maps.q, p.q, 2, kD, static_cast<uint64_t>(d.B) * d.num_q_heads * d.S, kD * 2, 64, kQR, true);
+    rc = make_tmap_2d(&c->maps.q, p.q, 2, kD, static_cast<uint64_t>(d.B) * d.num_q_heads * L.S, kD * 2, 64, kQR, true);
   if (!rc) rc = make_tmap_2d(&c->maps.kn, p.kn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
   if (!rc) rc = make_tmap_2d(&c->maps.vn, p.vn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
-  if (!rc) rc = ensure_smem_attr(reinterpret_cast<const void*>(chunk_kernel), kSmemBytes);
+  const void* kfn = d.variant == RFX_CHUNK_PI0 ? reinterpret_cast<const void*>(chunk_kernel<kPi0>)
+                                                : reinterpret_cast<const void*>(chunk_kernel<kPi05>);
+  if (!rc) rc = ensure_smem_attr(kfn, kSmemBytes);
   // the smallest shared-memory carveout that holds the kernel (164 of 228 KB),
   // so the rest of the unified L1 caches local memory and global loads
   if (!rc)
-    rc = check_cuda(cudaFuncSetAttribute(reinterpret_cast<const void*>(chunk_kernel),
-                                         cudaFuncAttributePreferredSharedMemoryCarveout,
+    rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (kSmemBytes * 100 + 228 * 1024 - 1) / (228 * 1024)),
                     "rfx_chunk: carveout");
   if (!rc) {
     int occ = 0;
-    rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, chunk_kernel, kThreads, kSmemBytes),
+    rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn, kThreads, kSmemBytes),
                     "rfx_chunk: occupancy");
     if (!rc && occ < 1) rc = set_error(RFX_E_UNSUPPORTED, "rfx_chunk: the kernel does not fit on an SM");
   }
@@ -1900,7 +2213,9 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel, c->maps, c->params), "rfx_chunk_run: launch");
+  if (c->params.variant == kPi0)
+    return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel<kPi0>, c->maps, c->params), "rfx_chunk_run: launch");
+  return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel<kPi05>, c->maps, c->params), "rfx_chunk_run: launch");
 }
 
 extern "C" int rfx_chunk_destroy(rfx_chunk* c) {

@@ -72,8 +72,9 @@ class ActionExpertEngine:
         # fused: the whole chunk runs in the persistent executor (rfx_chunk);
         # otherwise one launch per op
         self.fused = fused
-        if fused and (cfg.variant != "pi05" or batch * cfg.suffix_len > 64):
-            raise ValueError("the fused chunk executor serves PI0.5 with at most 64 tokens (batch * chunk_size)")
+        if fused and batch * cfg.suffix_len > 64:
+            raise ValueError("the fused chunk executor serves at most 64 tokens (batch * chunk_size; PI0: "
+                             "batch * (chunk_size + 1))")
         if fused and cfg.quant_mode == "i8_sym" and scale_dtype != torch.float32:
             raise ValueError("the fused chunk executor keeps fp32 scales for the int8 scheme")
         self.kv_splits = kv_splits
@@ -386,6 +387,12 @@ class ActionExpertEngine:
         d.k_ring, d.v_ring, d.k_scale, d.v_scale, d.k_zp, d.v_zp = [cast(a) for a in self._chunk_ptrs]
         d.ctx_valid = self.ctx_valid.data_ptr() if self.use_ctx_valid else None
         d.x = self.x.data_ptr()
+        if cfg.variant == "pi0":
+            d.variant, d.state_dim = L.RFX_CHUNK_PI0, cfg.state_dim
+            d.state, d.w_state, d.b_state = self.state.data_ptr(), self.st_w.data_ptr(), self.st_b.data_ptr()
+            d.w_atin, d.b_atin = self.atin_w.data_ptr(), self.atin_b.data_ptr()
+            d.w_atout, d.b_atout = self.atout_w.data_ptr(), self.atout_b.data_ptr()
+            d.time_emb, d.new_block = self.temb.data_ptr(), self.new_block.data_ptr()
         d.debug_hidden = L.ptr(getattr(self, "dbg_h", None))
         d.debug_attn = L.ptr(getattr(self, "dbg_attn", None))
         n = ctypes.c_size_t(0)
