@@ -310,7 +310,10 @@ def chunk_kernel_roofline(eng, hbm_peak, reps=3):
     return {"kernel": "chunk_kernel (persistent executor of the whole 10-step chunk, 1 CTA per SM)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/chunk_kernel_pi05_818ctx.md",
+            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/chunk_kernel_pi05_818ctx.md"
+                               if traffic is not None else
+                               "not captured: ncu reports LaunchFailed for this clustered cooperative launch "
+                               "(profiles/chunk_kernel_pi05_818ctx.md)"),
             "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
 
 

@@ -43,7 +43,8 @@ class PI05Model:
     Ring layout per layer: slots [0, n_lang) hold the instruction, then
     ``window_frames`` frame slots of ``frame_len`` (frame f in slot
     f % window_frames).  ``fused`` selects the persistent chunk executor
-    (PI0.5, at most 64 suffix tokens per GPU) over one launch per op."""
+    (at most 64 suffix tokens per GPU; the default where they fit) over one
+    launch per op."""
 
     variant = "pi05"
 
@@ -56,7 +57,7 @@ class PI05Model:
         if cap < n_lang + window_frames * frame_len:
             raise ValueError(f"capacity {cap} < instruction {n_lang} + {window_frames} frames of {frame_len}")
         if fused is None:
-            fused = cfg.variant == "pi05" and batch * cfg.suffix_len <= 64
+            fused = batch * cfg.suffix_len <= 64
         self.cfg, self.B, self.dev = cfg, batch, torch.device(device)
         self.n_lang, self.frame_len, self.window_frames = n_lang, frame_len, window_frames
         self.num_inference_steps = cfg.num_steps
@@ -184,13 +185,9 @@ class PI05Model:
 
 
 class PI0Model(PI05Model):
-    """PI0: state token + action/time MLP suffix, plain RMSNorm (per-op engine)."""
+    """PI0: state token + action/time MLP suffix, plain RMSNorm."""
 
     variant = "pi0"
-
-    def __init__(self, cfg: ExpertConfig, weights: dict, **kw):
-        kw.setdefault("fused", False)
-        super().__init__(cfg, weights, **kw)
 
     @torch.no_grad()
     def sample_actions(self, images, img_masks, tokens, masks, state, noise=None, num_steps=None) -> torch.Tensor:

@@ -122,6 +122,13 @@ class ChunkScheduler:
             self._incremental = True
         return pending
 
+    def wait(self) -> None:
+        """Blocks until the pending inference (if any) has completed.  The
+        policy's engine belongs to that inference until then: call this before
+        using the policy outside the scheduler."""
+        if self.next_chunk is not None and self.next_chunk.event is not None:
+            self.next_chunk.event.synchronize()
+
     def get_action(self, observation: dict) -> np.ndarray:
         """The action to execute now (the control loop calls this once per step)."""
         if not self.is_running():  # bootstrap: the first chunk, synchronously

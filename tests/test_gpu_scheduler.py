@@ -32,6 +32,7 @@ def test_async_schedule_matches_synchronous_chunks():
     sch = ChunkScheduler(FixedNoise(pol, noise), 6, 2)
     obs = {"observation.state": st.cuda()}
     acts = [sch.get_action(obs) for _ in range(12)]
+    sch.wait()  # the third chunk, launched at step 10, still owns the engine
     # the same two chunks synchronously: the first from the observed state,
     # the second from the first chunk's last executed action as the state
     c1 = pol.predict_action_chunk(obs, noise=noise)[0].cpu().numpy()

@@ -59,3 +59,14 @@ def test_argument_checks():
     assert sch.should_fetch_observation() and not sch.is_running()
     with pytest.raises(RuntimeError):
         sch.get_current_action()
+
+
+def test_wait_returns_with_or_without_a_pending_inference():
+    pol = FakePolicy(4, 3)
+    sch = ChunkScheduler(pol, 4, 2)
+    sch.wait()  # nothing pending
+    obs = {"observation.state": np.zeros(3, dtype=np.float32)}
+    for _ in range(3):  # the second inference is launched at index 2 (host policy: completed at once)
+        sch.get_action(obs)
+    assert sch.next_chunk is not None
+    sch.wait()
