@@ -254,6 +254,12 @@ typedef struct rfx_attn_desc {
   size_t workspace_bytes;
   int kv_splits; /* 0 = auto */
   int kv_source;  /* RFX_KV_RING_TILES (0) or RFX_KV_DENSE */
+  /* RFX_KV_DENSE only: nonzero when this workspace already holds the
+   * context's dense rows, written by an earlier call with the same ring
+   * contents, n_ctx, ctx_valid, capacity and geometry (e.g. the first Euler
+   * step of a chunk): only the new keys are converted.  Ignored by
+   * rfx_attention_noalloc (its scratch is shared). */
+  int dense_ctx_ready;
 } rfx_attn_desc;
 int rfx_attention(const rfx_attn_desc* desc, void* stream);
 /* Workspace needed by rfx_attention for this descriptor (0 if none). */

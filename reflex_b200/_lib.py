@@ -97,6 +97,7 @@ class AttnDesc(Structure):
         ("ctx_valid", c_void_p), ("new_block", c_void_p),
         ("softmax_scale", c_float), ("out", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("kv_splits", c_int), ("kv_source", c_int),
+        ("dense_ctx_ready", c_int),
     ]
 
 

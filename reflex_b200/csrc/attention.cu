@@ -517,12 +517,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // reference uint8 dequantize ((q - zp) * scale, rounded per op to the scale
 // dtype) with unit scales; the new keys: bf16 K as is, V as f16 of its bf16
 // value; keys past n_ctx / S (or masked by ctx_valid) get scale 0 and -inf.
-// One CTA per 16 keys of a block (grid = 4 x blocks x streams).
+// One CTA per 16 keys of a block (grid = 4 x blocks x streams), blocks from
+// j0 on (j0 = n_ctx_blocks: only the new keys, the context rows are kept).
 __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ AttnParams p, const uint8_t* k_ring,
-                                                       const uint8_t* v_ring) {
+                                                       const uint8_t* v_ring, int j0) {
   constexpr int kKeys = 16;
   pdl_wait();
-  const int j = blockIdx.x >> 2, q0 = (blockIdx.x & 3) * kKeys, b = blockIdx.y;
+  const int j = j0 + (blockIdx.x >> 2), q0 = (blockIdx.x & 3) * kKeys, b = blockIdx.y;
   const long row0 = static_cast<long>(b) * p.Lk + static_cast<long>(j) * kKB;
   const bool sbf16 = p.scale_bf16 != 0;
   __shared__ float dq[4][kKB];  // reference scheme: k scale, v scale, k zp, v zp
@@ -1209,8 +1210,9 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
   if (dense) {
     const uint8_t* kr = static_cast<const uint8_t*>(d.k_ring);
     const uint8_t* vr = static_cast<const uint8_t*>(d.v_ring);
-    rc = launch_kernel(reinterpret_cast<const void*>(kv_dense_kernel), dim3(4 * g.n_blocks, d.B), dim3(256), 0, stream,
-                       pdl, 1, p, kr, vr);
+    int j0 = d.dense_ctx_ready ? g.n_ctx_blocks : 0;
+    rc = launch_kernel(reinterpret_cast<const void*>(kv_dense_kernel), dim3(4 * (g.n_blocks - j0), d.B), dim3(256), 0,
+                       stream, pdl, 1, p, kr, vr, j0);
     if (rc) return rc;
   }
   dim3 grid(g.q_tiles, g.splits, d.B);
@@ -1279,6 +1281,7 @@ extern "C" int rfx_attention_noalloc(const rfx_attn_desc* desc, void* stream) {
   int rc = geometry(*desc, &g);
   if (rc) return rc;
   rfx_attn_desc d = *desc;
+  d.dense_ctx_ready = 0;  // the scratch is shared by every call: always convert the whole context
   size_t need = attention_workspace_bytes(d);
   if (desc->kv_splits <= 0) {
     // automatic split count: the largest one (up to the automatic choice)

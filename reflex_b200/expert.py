@@ -321,7 +321,10 @@ class ActionExpertEngine:
                                       new_block=self.new_block if cfg.variant == "pi0" else None,
                                       kv_splits=self.kv_splits,
                                       kv_source=L.RFX_KV_DENSE if dense else L.RFX_KV_RING_TILES)
-                attn_descs.append(ad)
+                # the dense source keeps each layer's converted context for
+                # the whole chunk: later steps convert only the new keys
+                ad.dense_ctx_ready = 1 if dense and tau > 0 else 0
+                attn_descs.append((l, ad))
                 ops.append(("attn", ad, ("attn", tau, l)))
                 ops.append(("linear", K.linear_desc(
                     w=self.w_o[l], x=self.attn_out, T=T, S=St, epilogue=L.RFX_EPI_RESIDUAL, y=self.h,
@@ -345,13 +348,18 @@ class ActionExpertEngine:
                                                  norm_a2=a2(tau, nf), norm_b2=b2(tau, nf), eps=cfg.eps,
                                                  w_out=self.aout_w, b_out=self.aout_b, dt=self.dt, **nxt),
                         ("step", tau)))
-        # one workspace serves every attention launch (they run in sequence)
-        need = max(K.attention_workspace_bytes(d) for d in attn_descs) if attn_descs else 0
-        if need and (self.workspace is None or self.workspace.numel() < need + 1024):
-            self.workspace = torch.empty(need + 1024, dtype=torch.uint8, device=self.dev)
-        for d in attn_descs:
+        # attention workspaces: one per layer with the dense source (it holds
+        # the layer's converted context through the chunk), else one shared by
+        # every launch (they run in sequence)
+        need = max(K.attention_workspace_bytes(d) for _, d in attn_descs) if attn_descs else 0
+        per_layer = any(d.kv_source == L.RFX_KV_DENSE for _, d in attn_descs)
+        n_ws = cfg.num_layers if per_layer else 1
+        if need and (not isinstance(self.workspace, list) or len(self.workspace) != n_ws
+                     or self.workspace[0].numel() < need + 1024):
+            self.workspace = [torch.empty(need + 1024, dtype=torch.uint8, device=self.dev) for _ in range(n_ws)]
+        for l, d in attn_descs:
             if need:
-                d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace, 1024), need
+                d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace[l if per_layer else 0], 1024), need
         self.ops = ops
         if self.plan is not None:
             self.plan.close()

@@ -4,6 +4,7 @@ Bit-exact for the KV quantizers; the bf16 GEMMs and attention against an
 fp32 torch computation on the same bf16 inputs with the tolerance stated in
 each test.
 """
+import ctypes
 import math
 
 import numpy as np
@@ -496,6 +497,43 @@ def test_attention_dense_source_matches_ring_tiles_and_oracle(K, L, mode, n_ctx,
     assert d_paths <= 2e-3
     assert max(errs) <= 2e-2
 
+
+
+@pytest.mark.parametrize("mode", ["i8", "u8"])
+def test_attention_dense_context_kept_across_calls(K, L, mode):
+    """dense_ctx_ready: a second call on the same workspace with new queries
+    and new keys converts only the new keys and gives bit-identical output to
+    a call that converts everything (the engine's steps 1.. of a chunk); B = 3
+    streams, a masked context range."""
+    r = gen(12)
+    B, Hq, D, S, n_ctx = 3, 8, 256, 50, 700
+    cap = n_ctx + 64
+    qm = L.RFX_QUANT_I8_SYM if mode == "i8" else L.RFX_QUANT_U8_REF
+    ring = K.KVRing.allocate(B, 1, cap, D, qm, scale_dtype=torch.float32 if mode == "i8" else torch.bfloat16)
+    K.kv_quant_append(r(B, 1, n_ctx, D).bfloat16().cuda(), r(B, 1, n_ctx, D).bfloat16().cuda(), ring, 0, 0, cap)
+    valid = torch.ones(B, cap, dtype=torch.uint8)
+    valid[1, 100:300] = 0
+    step_inputs = [(r(B, Hq, S, D).bfloat16().cuda(), r(B * S, D).bfloat16().cuda(), r(B * S, D).bfloat16().cuda())
+                   for _ in range(2)]
+    kw = dict(ring=ring, n_ctx=n_ctx, softmax_scale=1 / 16, ctx_valid=valid.cuda(), kv_source=L.RFX_KV_DENSE)
+    d0 = K.attention_desc(q=step_inputs[0][0], k_new=step_inputs[0][1], v_new=step_inputs[0][2],
+                          out=torch.empty(B * S, Hq * D, dtype=torch.bfloat16, device="cuda"), **kw)
+    need = K.attention_workspace_bytes(d0)
+    ws_keep = torch.empty(need + 1024, dtype=torch.uint8, device="cuda")
+    outs = {}
+    for name, ready in (("kept", (0, 1)), ("full", (0, 0))):
+        ws = ws_keep if name == "kept" else torch.empty(need + 1024, dtype=torch.uint8, device="cuda")
+        for i, (q, kn, vn) in enumerate(step_inputs):
+            out = torch.empty(B * S, Hq * D, dtype=torch.bfloat16, device="cuda")
+            d = K.attention_desc(q=q, k_new=kn, v_new=vn, out=out, **kw)
+            d.workspace, d.workspace_bytes = K.aligned_ptr(ws, 1024), need
+            d.dense_ctx_ready = ready[i]
+            L.call("rfx_attention", ctypes.byref(d), K._stream())
+            outs[(name, i)] = out
+    torch.cuda.synchronize()
+    assert K.device_status() == 0
+    assert torch.equal(outs[("kept", 1)], outs[("full", 1)])
+    assert not torch.equal(outs[("kept", 0)], outs[("kept", 1)])
 
 # ------------------------------------------------------ conditioning heads ---
 def test_time_cond_matches_fp64_embedding_and_mlp(K):
