@@ -1104,46 +1104,54 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
 }
 
 // ------------------------------------------------------ worker: combine ---
-__device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsigned use, int b, int qt, int r0, int r1,
-                            unsigned long long* ts) {
+__device__ __forceinline__ bool worker_comb(const ChunkParams& p, uint8_t* smem, int et, unsigned use, int b, int qt,
+                                            int r0, int r1, unsigned long long* ts) {
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
   if (et == 0) stamp(ts, 1);
   const int wq = et >> 5, lane = et & 31;
+  // two warps per row (r1 - r0 <= 4 rows), each summing half of the splits;
+  // the second half's sums meet the first's in the accumulator-tile buffer
+  // (idle here: the paired tiles that fill it need this layer's combine)
+  const int r = r0 + (wq & 3), half = wq >> 2;
+  const int R = qt * kQR + r;
+  const bool active = r < r1 && R < p.Hq * p.S;
+  float* xchg = reinterpret_cast<float*>(smem + kOffRed) + ((wq & 3) * 32 + lane) * 8;
   constexpr int kBatch = 8;  // splits whose partials are in flight together
-  for (int r = r0 + wq; r < r1; r += kWorkers / 32) {
-    const int R = qt * kQR + r;
-    if (R >= p.Hq * p.S) continue;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float L = 0.f;
+  if (active) {
     const long base = (static_cast<long>(b) * p.q_tiles + qt) * p.attn_splits;
     // lane: 8 of the row's 256 columns (chunk lane / 2, half lane % 2)
     const __half* ob = reinterpret_cast<const __half*>(p.ws_o) + ((lane >> 1) * kQR + r) * 16 + (lane & 1) * 8;
+    const int s_mid = (p.attn_splits + 1) >> 1;
+    const int s_begin = half ? s_mid : 0, s_end = half ? p.attn_splits : s_mid;
     // split s's (m, l) sits in lane s % 32, as the first (s < 32) or second
     // of its pair: the row max M and the weights w_s = l_s * 2^(m_s - M) are
     // warp reductions and broadcasts
-    const float2 ml = lane < p.attn_splits ? __ldcg(p.ws_ml + (base + lane) * kQR + r) : make_float2(-INFINITY, 0.f);
-    const float2 ml2 =
-        lane + 32 < p.attn_splits ? __ldcg(p.ws_ml + (base + lane + 32) * kQR + r) : make_float2(-INFINITY, 0.f);
     uint4 o[kBatch];
 #pragma unroll
     for (int q = 0; q < kBatch; ++q)
-      if (q < p.attn_splits) o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + q) * (kD / 16) * kQR * 16));
+      if (s_begin + q < s_end)
+        o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s_begin + q) * (kD / 16) * kQR * 16));
+    const float2 ml = lane < p.attn_splits ? __ldcg(p.ws_ml + (base + lane) * kQR + r) : make_float2(-INFINITY, 0.f);
+    const float2 ml2 =
+        lane + 32 < p.attn_splits ? __ldcg(p.ws_ml + (base + lane + 32) * kQR + r) : make_float2(-INFINITY, 0.f);
     const bool live = ml.x != -INFINITY && ml.y > 0.f;
     const bool live2 = ml2.x != -INFINITY && ml2.y > 0.f;
     const float M = warp_max(fmaxf(live ? ml.x : -INFINITY, live2 ? ml2.x : -INFINITY));
     const float w = live ? exp2f(ml.x - M) * ml.y : 0.f;
     const float w2 = live2 ? exp2f(ml2.x - M) * ml2.y : 0.f;
-    const float L = warp_sum(w + w2);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < p.attn_splits; s0 += kBatch) {
-      if (s0 > 0) {
+    L = warp_sum(w + w2);
+    for (int s0 = s_begin; s0 < s_end; s0 += kBatch) {
+      if (s0 > s_begin) {
 #pragma unroll
         for (int q = 0; q < kBatch; ++q)
-          if (s0 + q < p.attn_splits)
-            o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s0 + q) * (kD / 16) * kQR * 16));
+          if (s0 + q < s_end) o[q] = __ldcg(reinterpret_cast<const uint4*>(ob + (base + s0 + q) * (kD / 16) * kQR * 16));
       }
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
         const float ws = __shfl_sync(0xffffffffu, s0 + q < 32 ? w : w2, (s0 + q) & 31);
-        if (s0 + q >= p.attn_splits) continue;
+        if (s0 + q >= s_end) continue;
         const __half2* h2 = reinterpret_cast<const __half2*>(&o[q]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1153,16 +1161,30 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, int et, unsign
         }
       }
     }
+    if (half) {
+      *reinterpret_cast<float4*>(xchg) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(xchg + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+  workers_sync();
+  if (active && !half) {
+    const float4 u = *reinterpret_cast<const float4*>(xchg);
+    const float4 v = *reinterpret_cast<const float4*>(xchg + 4);
+    const float hsum[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
     const float inv = L > 0.f ? 1.f / L : 0.f;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = (acc[e] + hsum[e]) * inv;
     const int s_row = R % p.S, h_row = R / p.S;
     __nv_bfloat16* orow =
         p.attn_out + (static_cast<long>(b) * p.S + s_row) * (static_cast<long>(p.Hq) * kD) + h_row * kD + lane * 8;
-    const uint4 packed = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
-                                    pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    const uint4 packed = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                                    pack_bf16x2(y[6], y[7]));
     *reinterpret_cast<uint4*>(orow) = packed;
     if (p.dbg_attn && use < static_cast<unsigned>(p.NL))
       *reinterpret_cast<uint4*>(p.dbg_attn + static_cast<long>(use) * p.T * p.Hq * kD + (orow - p.attn_out)) = packed;
   }
+  workers_sync();  // the buffer is read before any later use of it
   workers_publish(p, et, kCComb);
   return true;
 }
@@ -1698,7 +1720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           case kTAttn:
             ok = worker_attn<V>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
             break;
-          case kTComb: ok = worker_comb(p, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
+          case kTComb: ok = worker_comb(p, smem, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
           case kTFinO: case kTFinD: ok = worker_fin<V>(p, small, et, ty, tau, layer, tk.y, ts); break;
           case kTFinAt1: case kTFinAt2:
             if (V == kPi0) ok = worker_fin_at(p, small, et, ty, tau, tk.y, ts);
