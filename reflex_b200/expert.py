@@ -224,17 +224,25 @@ class ActionExpertEngine:
     def set_context_mask(self, valid: torch.Tensor | None) -> None:
         """Per-slot visibility of the context [B, n_ctx] (bool / 0-1) for the
         following chunks (a padded prefix token is invisible to the suffix,
-        as build_attention_mask_and_position_ids makes it, reflex/policies/
-        pi05/utils.py:210-215); None makes every slot of [0, n_ctx) visible."""
+        and the suffix positions start after each stream's visible tokens,
+        as build_attention_mask_and_position_ids makes them, reflex/policies/
+        pi05/utils.py:210-215,234); None makes every slot of [0, n_ctx)
+        visible again."""
         if valid is None:
             if self.use_ctx_valid:
                 self.ctx_valid.fill_(1)
+                self.positions.copy_((self.n_ctx + torch.arange(self.St, dtype=torch.int32)).repeat(self.B))
                 self.use_ctx_valid = False
                 self._build_ops()
             return
         if valid.shape != (self.B, self.n_ctx):
             raise ValueError(f"context mask must be [{self.B}, {self.n_ctx}], got {tuple(valid.shape)}")
-        self.ctx_valid[:, :self.n_ctx].copy_(valid.to(self.dev, torch.uint8), non_blocking=True)
+        valid = valid.to(self.dev)
+        self.ctx_valid[:, :self.n_ctx].copy_(valid.to(torch.uint8), non_blocking=True)
+        # suffix positions continue after each stream's visible tokens
+        # (position = cumsum(pad) - 1, reflex/policies/pi05/utils.py:234)
+        n_valid = valid.bool().sum(dim=1, dtype=torch.int32)
+        self.positions.copy_((n_valid[:, None] + torch.arange(self.St, device=self.dev, dtype=torch.int32)).flatten())
         if not self.use_ctx_valid:
             self.use_ctx_valid = True
             self._build_ops()

@@ -155,11 +155,9 @@ class PI05Model:
             self.engine.set_context_length(Lc)
         step = self._step()
         pad = prefix_pad_masks.to(self.dev).bool()
+        # padded slots are invisible and the suffix positions continue after
+        # each stream's unpadded prefix tokens (set_context_mask)
         step.set_context_mask(None if bool(pad.all()) else pad)
-        # suffix positions continue after each stream's unpadded prefix tokens
-        # (position = cumsum(pad) - 1, reflex/policies/pi05/utils.py:234)
-        n_valid = pad.sum(dim=1, dtype=torch.int32)
-        step.positions.copy_((n_valid[:, None] + torch.arange(step.St, device=self.dev, dtype=torch.int32)).flatten())
         step.t.fill_(float(ts[0]))
         x_t = x_t.to(self.dev, torch.float32)
         step.set_inputs(x_t, state if self.cfg.variant == "pi0" else None)

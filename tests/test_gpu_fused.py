@@ -217,3 +217,51 @@ def test_fused_pi0_graph_replay_is_deterministic():
         torch.cuda.synchronize()
         assert torch.equal(eng.x.float().cpu(), ref)
     assert kernels.device_status() == 0
+
+
+# ------------------------------------------------- several streams, masks ---
+@pytest.mark.parametrize("variant,B,chunk", [("pi05", 4, 12), ("pi0", 3, 16)])
+def test_fused_several_streams_match_per_op_engine(variant, B, chunk):
+    """B streams in one executor launch (B * tokens <= 64): every stream's own
+    context ring, query tiles and new-key block; against the per-op engine and
+    the fp32 oracle on the same inputs."""
+    cfg = (pi05_config(num_layers=2, quant_mode="i8_sym", chunk_size=chunk) if variant == "pi05"
+           else pi0_config(num_layers=2, quant_mode="i8_sym", chunk_size=chunk))
+    n_ctx = 150
+    wts, ctx, parts, x0, st = make_case(cfg, n_ctx, B=B)
+    xf = run_chunk(make_engine(cfg, wts, parts, n_ctx, B=B, fused=True), x0, st)
+    xp = run_chunk(make_engine(cfg, wts, parts, n_ctx, B=B), x0, st)
+    with torch.no_grad():
+        x32 = sample_chunk(cfg, wts, ctx, x0, st)
+    e_oracle = (xf - x32).abs().max().item()
+    e_per_op = (xf - xp).abs().max().item()
+    print(f"fused {variant} B={B}: vs fp32 oracle {e_oracle:.5f}, vs per-op engine {e_per_op:.5f}")
+    assert e_oracle <= TOL
+    assert e_per_op <= TOL
+
+
+@pytest.mark.parametrize("variant", ["pi05", "pi0"])
+def test_fused_context_mask_matches_per_op_engine(variant):
+    """A per-slot context mask (padded prefix tokens, an evicted range) on the
+    executor against the per-op engine with the same mask."""
+    cfg = (pi05_config(num_layers=2, quant_mode="u8_ref", adarms="gate", chunk_size=16) if variant == "pi05"
+           else pi0_config(num_layers=2, quant_mode="u8_ref", chunk_size=16))
+    B, n_ctx = 2, 260
+    wts, ctx, parts, x0, st = make_case(cfg, n_ctx, B=B)
+    valid = torch.ones(B, n_ctx, dtype=torch.bool)
+    valid[0, 40:100] = False
+    valid[1, 250:] = False
+    outs = []
+    for fused in (True, False):
+        eng = make_engine(cfg, wts, parts, n_ctx, B=B, fused=fused)
+        eng.set_context_mask(valid.cuda())
+        outs.append(run_chunk(eng, x0, st))
+    from oracle.model import Context
+    with torch.no_grad():
+        x32 = sample_chunk(cfg, wts, Context(ctx.k, ctx.v, valid), x0, st)
+    err = (outs[0] - outs[1]).abs().max().item()
+    e_oracle = (outs[0] - x32).abs().max().item()
+    print(f"fused {variant} with a context mask: vs per-op engine {err:.5f}, vs fp32 oracle {e_oracle:.5f}")
+    assert err <= TOL
+    assert e_oracle <= TOL
+    assert kernels.device_status() == 0
