@@ -73,6 +73,45 @@ struct QuantArgs {
   int region_base, region_off, region_len;
 };
 
+// Packed fp32x2 arithmetic (sm_100): two round-to-nearest fp32 operations per
+// instruction, each lane exactly as the scalar one.
+__device__ __forceinline__ unsigned long long pack_f32x2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo_f32(unsigned long long v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo;
+}
+__device__ __forceinline__ float hi_f32(unsigned long long v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return hi;
+}
+// max that returns NaN when either operand is NaN
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long sub_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // int8 symmetric quantization of one lane's 8 values of a row, packed little
 // endian into two words: q = clamp(rne(x / scale), -127, 127), exactly as with
 // rintf(__fdiv_rn(x, scale)), but from a product with rcp = __frcp_rn(scale),
@@ -96,14 +135,21 @@ __device__ __forceinline__ void quant8_i8(const float (&v)[8], float scale, floa
   constexpr float kFar = 0.5f - 0x1p-14f;   // |y - rne(y)| <= kFar: 2^-14 or more from a half-integer
   uint32_t tb[8];
   if (scale >= 0x1p-126f) {
-    bool near = false;
+    // two values per instruction (packed fp32x2, each lane rounded as the
+    // scalar op); the largest distance to a rounded value decides the pass
+    const unsigned long long r2 = pack_f32x2(rcp, rcp), m2 = pack_f32x2(kMagic, kMagic);
+    float dmax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = __fmul_rn(v[i], rcp);
-      const float t = __fadd_rn(y, kMagic);
-      near |= !(fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) <= kFar);
-      tb[i] = __float_as_uint(t);
+    for (int i = 0; i < 8; i += 2) {
+      const unsigned long long y = mul_f32x2(pack_f32x2(v[i], v[i + 1]), r2);
+      const unsigned long long t = add_f32x2(y, m2);
+      const unsigned long long d = sub_f32x2(y, sub_f32x2(t, m2));
+      dmax = max_nan(dmax, max_nan(fabsf(lo_f32(d)), fabsf(hi_f32(d))));
+      tb[i] = __float_as_uint(lo_f32(t));
+      tb[i + 1] = __float_as_uint(hi_f32(t));
     }
+    // a NaN distance (NaN input) fails the test and takes the divide
+    const bool near = !(dmax <= kFar);
     if (near) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
