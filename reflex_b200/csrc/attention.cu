@@ -615,21 +615,28 @@ __global__ void __launch_bounds__(256) kv_dense_kernel(const __grid_constant__ A
   pdl_launch_dependents();
 }
 
-// Attention over the dense keys: the structure of attention_kernel with the
-// conversion gone and two key blocks in flight.  Producer: Q once, then per
-// block the K (bf16) tile with the block's 4 x 64 per-key words, and the V
-// (f16) tile, by TMA / bulk copy into stage jl % 2, K and V filled and freed
-// on their own barriers.  MMA issuer: S_jl = Q K_jl^T into
-// TMEM buffer jl % 2, then P_{jl-1} V_{jl-1} into O, so the scores of the next
-// block are computed while the workers run the softmax of this one.
-constexpr int kDOffQ = 0;
-constexpr int kDOffK = 65536;        // 2 stages x 4 x [64 x 64] bf16
-constexpr int kDOffV = 131072;       // 2 stages x 4 x [64 x 64] f16 (MN-major blocks)
-constexpr int kDOffP = 196608;       // [128 x 64] f16
-constexpr int kDOffScale = 212992;   // 2 stages x (ks, vs, kadd, nb) x 64 words
-constexpr int kDOffBar = 215040;
-constexpr int kDOffXchg = 215168;    // 768 floats: row maxima and sums of the two column halves
+// Attention over the dense keys in 128-key blocks.  One QK^T instruction then
+// covers 128 keys (N = 128), so a 128-key block costs 16 score and 8 P.V
+// instructions instead of 2 x (16 + 4) at 64 keys, and P stays in TMEM (the
+// A operand of P.V), which leaves shared memory for whole 128-key K tiles.
+//   Producer: Q once; per block the K tile by dim block (each of the four
+//   64-dim blocks reloads as soon as the previous block's scores over it are
+//   done), the block's per-key words (three stages), and V in two 64-key
+//   halves (each reloads once the previous block's P.V over it is done).
+//   MMA issuer: S_jl = Q K_jl^T into TMEM buffer jl % 2, then P_{jl-1} V_{jl-1}
+//   into O, so the next block's scores are computed during the softmax.
+//   Workers: the softmax of S_jl into P_jl (f16, written over S_jl's own
+//   columns), O rescaled when the running maximum moves.
+constexpr int kDKB = 128;               // keys per block
+constexpr int kDOffQ = 0;               // 4 x [128 rows x 64 dims] bf16
+constexpr int kDOffK = 65536;           // 4 x [128 keys x 64 dims] bf16, K-major
+constexpr int kDOffV = 131072;          // 2 halves x 4 x [64 keys x 64 dims] f16, MN-major
+constexpr int kDScaleWords = 4 * kDKB;  // ks, vs, kadd, nb of one block
+constexpr int kDOffScale = 196608;      // 3 stages x kDScaleWords words
+constexpr int kDOffBar = kDOffScale + 3 * kDScaleWords * 4;
+constexpr int kDOffXchg = kDOffBar + 256;  // 768 floats: row maxima and sums of the two column halves
 constexpr int kDSmemBytes = kDOffXchg + 3072 + 1024;
+static_assert(kDSmemBytes <= 227 * 1024, "dense attention shared memory");
 // warps 0-1 as in attention_kernel; warps 2-9 run the softmax and the
 // epilogue, two per TMEM lane quadrant, each on half of a row's columns
 constexpr int kDWorkers = 256;
@@ -655,38 +662,36 @@ __global__ void __launch_bounds__(kDThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  // p.n_blocks counts 128-key blocks here
   const int blk_begin = sp * p.n_blocks / p.splits;
   const int nbl = (sp + 1) * p.n_blocks / p.splits - blk_begin;
   uint8_t* sQ = smem + kDOffQ;
-  uint8_t* sP = smem + kDOffP;
   float* sScale = reinterpret_cast<float*>(smem + kDOffScale);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDOffBar);
-  // K and V (with the block's per-key scales) of a stage are filled and
-  // released separately: a K stage is free once its scores are computed, long
-  // before the stage's V has been used; the scales, which the softmax reads
-  // after the scores, stay until the stage's P.V is done
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;   // [2]
-  uint64_t* s_free = bars + 7;   // [2]
-  uint64_t* p_ready = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* v_full = bars + 11;   // [2]
-  uint64_t* v_empty = bars + 13;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* k_full = bars + 1;    // [4] per dim block
+  uint64_t* k_empty = bars + 5;   // [4]
+  uint64_t* v_full = bars + 9;    // [2] per 64-key half
+  uint64_t* v_empty = bars + 11;  // [2]
+  uint64_t* s_full = bars + 13;   // [2] per S buffer
+  uint64_t* sc_full = bars + 15;  // [3] per scale stage
+  uint64_t* p_ready = bars + 18;  // [2] per S buffer: P_jl written (blocks jl, jl + 2, ... on one barrier)
+  uint64_t* o_done = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   if (threadIdx.x == 0) trace(p, kTrStart);
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kDWorkers / 32);
     }
-    mbar_init(p_ready, kDWorkers / 32);
+    for (int i = 0; i < 3; ++i) mbar_init(&sc_full[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&p_ready[i], kDWorkers / 32);
     mbar_init(o_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -701,46 +706,52 @@ __global__ void __launch_bounds__(kDThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmO = tmem, tmS = tmem + 256;  // S buffers at columns 256 and 320
+  const uint32_t tmO = tmem;  // S buffers at columns 256 and 384, P over each S's own columns
+  auto tmS = [&](int jl) { return tmem + 256 + static_cast<uint32_t>(jl & 1) * kDKB; };
   pdl_launch_dependents();
   const long q_row0 = static_cast<long>(b) * p.Hq * p.S + static_cast<long>(qt) * kQR;
-  int k_issued = 0, v_issued = 0;
+  int k_iss = 0, v_iss = 0;  // dim-block / half loads issued (4 / 2 per block)
 
   if (warp == 0) {
     pdl_wait();
     if (lane == 0 && nbl > 0) {
       mbar_arrive_expect_tx(q_full, 4 * 16384);
       for (int a = 0; a < 4; ++a) tma_load_2d(sQ + a * 16384, &tmQ, q_full, a * 64, static_cast<int>(q_row0));
-      // two queues from one thread: each block's K as soon as its stage's
-      // previous scores are done, its V (+ scales) once that stage's previous
-      // P.V is done (V never ahead of K); bounded in time
+      // two queues from one thread, bounded in time: K dim block a of block
+      // kb once the scores of block kb-1 over it are done (with dim block 0,
+      // the block's per-key words into stage kb % 3), V half h of block vb
+      // once P.V of block vb-1 over it is done; V never ahead of K
       const unsigned long long t0 = globaltimer_ns();
-      while (k_issued < nbl || v_issued < nbl) {
+      while (v_iss < 2 * nbl) {
         bool moved = false;
-        if (k_issued < nbl &&
-            (k_issued < 2 || mbar_try_wait(&k_empty[k_issued & 1], ((k_issued - 2) >> 1) & 1))) {
-          const int st = k_issued & 1;
-          const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + k_issued) * kKB;
-          mbar_arrive_expect_tx(&k_full[st], 32768);
-          for (int a = 0; a < 4; ++a)
-            tma_load_2d(smem + kDOffK + st * 32768 + a * 8192, &tmK, &k_full[st], a * 64, static_cast<int>(key0));
-          ++k_issued;
-          moved = true;
+        if (k_iss < 4 * nbl) {
+          const int kb = k_iss >> 2, a = k_iss & 3;
+          if (kb == 0 || mbar_try_wait(&k_empty[a], (kb - 1) & 1)) {
+            const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + kb) * kDKB;
+            if (a == 0) {
+              float* sc = sScale + (kb % 3) * kDScaleWords;
+              mbar_arrive_expect_tx(&sc_full[kb % 3], kDScaleWords * 4);
+              bulk_load(sc, p.key_ks + key0, kDKB * 4, &sc_full[kb % 3]);
+              bulk_load(sc + kDKB, p.key_vs + key0, kDKB * 4, &sc_full[kb % 3]);
+              bulk_load(sc + 2 * kDKB, p.key_add + key0, kDKB * 4, &sc_full[kb % 3]);
+              bulk_load(sc + 3 * kDKB, p.key_nb + key0, kDKB * 4, &sc_full[kb % 3]);
+            }
+            mbar_arrive_expect_tx(&k_full[a], kDKB * 128);
+            tma_load_2d(smem + kDOffK + a * 16384, &tmK, &k_full[a], a * 64, static_cast<int>(key0));
+            ++k_iss;
+            moved = true;
+          }
         }
-        if (v_issued < k_issued &&
-            (v_issued < 2 || mbar_try_wait(&v_empty[v_issued & 1], ((v_issued - 2) >> 1) & 1))) {
-          const int st = v_issued & 1;
-          const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + v_issued) * kKB;
-          mbar_arrive_expect_tx(&v_full[st], 32768 + 4 * 256);
-          for (int a = 0; a < 4; ++a)
-            tma_load_2d(smem + kDOffV + st * 32768 + a * 8192, &tmV, &v_full[st], a * 64, static_cast<int>(key0));
-          float* sc = sScale + st * 256;
-          bulk_load(sc, p.key_ks + key0, 256, &v_full[st]);
-          bulk_load(sc + 64, p.key_vs + key0, 256, &v_full[st]);
-          bulk_load(sc + 128, p.key_add + key0, 256, &v_full[st]);
-          bulk_load(sc + 192, p.key_nb + key0, 256, &v_full[st]);
-          ++v_issued;
-          moved = true;
+        if (v_iss < 2 * (k_iss >> 2)) {
+          const int vb = v_iss >> 1, h = v_iss & 1;
+          if (vb == 0 || mbar_try_wait(&v_empty[h], (vb - 1) & 1)) {
+            const long key0 = static_cast<long>(b) * p.Lk + static_cast<long>(blk_begin + vb) * kDKB + h * 64;
+            mbar_arrive_expect_tx(&v_full[h], 32768);
+            for (int a = 0; a < 4; ++a)
+              tma_load_2d(smem + kDOffV + h * 32768 + a * 8192, &tmV, &v_full[h], a * 64, static_cast<int>(key0));
+            ++v_iss;
+            moved = true;
+          }
         }
         if (!moved && globaltimer_ns() - t0 > kWaitLimitNs) {
           record_error(p.status, kDevTimeoutStageEmpty);
@@ -752,38 +763,42 @@ __global__ void __launch_bounds__(kDThreads, 1)
   } else if (warp == 1) {
     pdl_wait();
     if (lane == 0 && nbl > 0) {
-      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kKB, true);
+      constexpr uint32_t idesc_s = make_idesc_f16(kQR, kDKB, true);
       constexpr uint32_t idesc_o = make_idesc_f16(kQR, kD, false, true);
       bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutTmaFull);
-      auto pv = [&](int jp) {  // O += P_jp V_jp
-        if (!(ok = mbar_wait(&v_full[jp & 1], (jp >> 1) & 1, p.status, kDevTimeoutTmaFull))) return;
-        if (!(ok = mbar_wait(p_ready, jp & 1, p.status, kDevTimeoutConvert))) return;
+      auto pv = [&](int jp) {  // O += P_jp V_jp, P from TMEM
+        if (!(ok = mbar_wait(&p_ready[jp & 1], (jp >> 1) & 1, p.status, kDevTimeoutConvert))) return;
         tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + kDOffV + (jp & 1) * 32768);
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!(ok = mbar_wait(&v_full[h], jp & 1, p.status, kDevTimeoutTmaFull))) return;
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(smem + kDOffV + h * 32768);
 #pragma unroll
-        for (int ks = 0; ks < kKB / 16; ++ks) {
-          const uint64_t ad = make_sdesc_sw128(smem_u32(sP) + ks * 32, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(v_base + ks * 2048, 8192, 1024);
-          umma_f16_ss(tmO, ad, bd, idesc_o, (jp > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t bd = make_sdesc_sw128(v_base + ks * 2048, 8192, 1024);
+            umma_f16_ts(tmO, tmS(jp) + static_cast<uint32_t>(h * 64 + ks * 8), bd, idesc_o,
+                        (jp > 0 || h > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(&v_empty[h]);
         }
-        umma_commit(&v_empty[jp & 1]);
         umma_commit(o_done);
       };
       for (int jl = 0; jl < nbl && ok; ++jl) {
-        const int st = jl & 1;
-        if (!(ok = mbar_wait(&k_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull))) break;
-        if (jl >= 2 && !(ok = mbar_wait(&s_free[st], ((jl - 2) >> 1) & 1, p.status, kDevTimeoutConvert))) break;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + kDOffK + st * 32768);
+        // S buffer jl % 2 last held P_{jl-2}, read by the P.V issued before
+        // this point (tcgen05.mma of one thread run in order)
+        for (int a = 0; a < 4 && ok; ++a) {
+          if (!(ok = mbar_wait(&k_full[a], jl & 1, p.status, kDevTimeoutTmaFull))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const int a = ks >> 2, kk = ks & 3;
-          const uint64_t ad = make_sdesc_sw128(smem_u32(sQ + a * 16384) + kk * 32, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(k_base + a * 8192 + kk * 32, 16, 1024);
-          umma_f16_ss(tmS + st * kKB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = make_sdesc_sw128(smem_u32(sQ + a * 16384) + kk * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(smem_u32(smem + kDOffK + a * 16384) + kk * 32, 16, 1024);
+            umma_f16_ss(tmS(jl), ad, bd, idesc_s, (a > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&k_empty[a]);  // this dim block may be reloaded
         }
-        umma_commit(&k_empty[st]);  // the K stage is free once these scores are done
-        umma_commit(&s_full[st]);
+        if (!ok) break;
+        umma_commit(&s_full[jl & 1]);
         if (jl >= 1) pv(jl - 1);
       }
       if (ok) pv(nbl - 1);
@@ -791,7 +806,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
   } else {
     pdl_wait();
     const int quad = warp & 3;
-    const int ch = (threadIdx.x - 64) >> 7;  // this warp's half of the row: 32 score / 128 output columns
+    const int ch = (threadIdx.x - 64) >> 7;  // this warp's half of the row: 64 score / 128 output columns
     const int r = quad * 32 + lane;          // query row inside the tile == TMEM lane
     float* mx_x = reinterpret_cast<float*>(smem + kDOffXchg);  // [2 blocks][2 halves][128] row maxima
     float* l_x = mx_x + 512;                                   // [2 halves][128] row sums
@@ -801,55 +816,52 @@ __global__ void __launch_bounds__(kDThreads, 1)
     const int h_row = row_valid ? R / p.S : 0;
     const int my_block = (row_valid && p.new_block) ? p.new_block[s_row] : 0;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    constexpr int kHalf = kDKB / 2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int jl = 0; jl < nbl; ++jl) {
-      const int st = jl & 1;
-      const bool causal = p.new_block != nullptr && blk_begin + jl >= p.n_ctx_blocks;
-      if (ok) ok = mbar_wait(&v_full[st], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);  // scales
-      if (ok) ok = mbar_wait(&s_full[st], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone);
+      if (ok) ok = mbar_wait(&sc_full[jl % 3], (jl / 3) & 1, p.status, kDevTimeoutTmaFull);
+      if (ok) ok = mbar_wait(&s_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutMmaDone);
       ok = __all_sync(0xffffffffu, ok);
-      constexpr int kHalf = kKB / 2;
+      // this half's keys: score scale (log2 units), value scale, additive
+      // mask and block id (context keys -1: always visible)
+      const float* sc = sScale + (jl % 3) * kDScaleWords + kHalf * ch;
+      const float* ks_s = sc;
+      const float* vs_s = sc + kDKB;
+      const float* kadd_s = sc + 2 * kDKB;
+      const int* nb_s = reinterpret_cast<const int*>(sc + 3 * kDKB);
       float z[kHalf];
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      const float* ks_s = sScale + st * 256 + kHalf * ch;
-      const float* vs_s = ks_s + 64;
-      const float* kadd_s = ks_s + 128;
-      const int* nb_s = reinterpret_cast<const int*>(ks_s + 192);
       if (ok) {
-      tc_fence_after();
-      {
-        uint32_t rr[2][16];
+        tc_fence_after();
+        {
+          uint32_t rr[4][16];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_ld16(tmS + st * kKB + lane_base + (2 * ch + c) * 16, rr[c]);
-        tmem_wait_ld();
+          for (int c = 0; c < 4; ++c) tmem_ld16(tmS(jl) + lane_base + kHalf * ch + 16 * c, rr[c]);
+          tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[c][e]);
-      }
-      // the scores are in registers: the MMA may overwrite this S buffer
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[st]);
-#pragma unroll
-      for (int c = 0; c < kHalf / 4; ++c) {
-        const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
-        const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
-        z[4 * c + 0] = fmaf(z[4 * c + 0], km.x, ka.x);
-        z[4 * c + 1] = fmaf(z[4 * c + 1], km.y, ka.y);
-        z[4 * c + 2] = fmaf(z[4 * c + 2], km.z, ka.z);
-        z[4 * c + 3] = fmaf(z[4 * c + 3], km.w, ka.w);
-        if (causal) {  // new key j is visible to row i iff new_block[j] <= new_block[i]
-          const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
-          if (nb.x > my_block) z[4 * c + 0] = -INFINITY;
-          if (nb.y > my_block) z[4 * c + 1] = -INFINITY;
-          if (nb.z > my_block) z[4 * c + 2] = -INFINITY;
-          if (nb.w > my_block) z[4 * c + 3] = -INFINITY;
+            for (int e = 0; e < 16; ++e) z[c * 16 + e] = __uint_as_float(rr[c][e]);
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
-      }
+        for (int c = 0; c < kHalf / 4; ++c) {
+          const float4 km = reinterpret_cast<const float4*>(ks_s)[c];
+          const float4 ka = reinterpret_cast<const float4*>(kadd_s)[c];
+          z[4 * c + 0] = fmaf(z[4 * c + 0], km.x, ka.x);
+          z[4 * c + 1] = fmaf(z[4 * c + 1], km.y, ka.y);
+          z[4 * c + 2] = fmaf(z[4 * c + 2], km.z, ka.z);
+          z[4 * c + 3] = fmaf(z[4 * c + 3], km.w, ka.w);
+          if (p.new_block) {  // new key j is visible to row i iff new_block[j] <= new_block[i]
+            const int4 nb = reinterpret_cast<const int4*>(nb_s)[c];
+            if (nb.x > my_block) z[4 * c + 0] = -INFINITY;
+            if (nb.y > my_block) z[4 * c + 1] = -INFINITY;
+            if (nb.z > my_block) z[4 * c + 2] = -INFINITY;
+            if (nb.w > my_block) z[4 * c + 3] = -INFINITY;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], z[4 * c + e]);
+        }
       }
       // the row's max over both column halves (the partner warp holds the other)
       float* mxb = mx_x + (jl & 1) * 256;
@@ -870,28 +882,13 @@ __global__ void __launch_bounds__(kDThreads, 1)
       }
       const float alpha = need ? exp2f(m_run - m_use) : 1.f;
       const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      float pv[kHalf];
-#pragma unroll
-      for (int c = 0; c < kHalf / 4; ++c) {
-        const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
-        const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float pe = ex2_approx(z[4 * c + e] - m_sub);
-          ps[e] += pe;
-          pv[4 * c + e] = pe * vv[e];
-        }
-      }
-      l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
-      m_run = m_use;
-      // P_{jl-1} V_{jl-1} has finished: the P tile is free and O is final
-      // for the rescale (a failed wait skips the rest of this block; the
-      // pair leaves the loop together at the next exchange)
-      if (jl > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (jl - 1) & 1, p.status, kDevTimeoutMmaDone));
-      if (!ok) continue;
-      tc_fence_after();
       if (__any_sync(0xffffffffu, need)) {
+        // O is final for the rescale once P_{jl-1} V_{jl-1} is done (need
+        // implies jl >= 1; a failed wait skips the rest of this block and the
+        // pair leaves the loop together at the next exchange)
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (jl - 1) & 1, p.status, kDevTimeoutMmaDone));
+        if (!ok) continue;
+        tc_fence_after();
 #pragma unroll 1
         for (int c0 = 8 * ch; c0 < 8 * ch + 8; c0 += 2) {
           uint32_t rr[2][16];
@@ -905,18 +902,35 @@ __global__ void __launch_bounds__(kDThreads, 1)
             tmem_st16(tmO + lane_base + (c0 + q) * 16, rr[q]);
           }
         }
-        tmem_wait_st();
       }
+      // P (times the value scales) as f16 pairs over the first 32 of this
+      // half's 64 score columns, which are already read
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = make_uint4(pack_f16x2(pv[8 * c + 0], pv[8 * c + 1]), pack_f16x2(pv[8 * c + 2], pv[8 * c + 3]),
-                                   pack_f16x2(pv[8 * c + 4], pv[8 * c + 5]), pack_f16x2(pv[8 * c + 6], pv[8 * c + 7]));
-        *reinterpret_cast<uint4*>(sP + sw128_offset(r, 4 * ch + c)) = v;
+      for (int hq = 0; hq < 2; ++hq) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 8 * hq; c < 8 * hq + 8; ++c) {
+          const float4 vsc = reinterpret_cast<const float4*>(vs_s)[c];
+          const float vv[4] = {vsc.x, vsc.y, vsc.z, vsc.w};
+          float pe[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            pe[e] = ex2_approx(z[4 * c + e] - m_sub);
+            ps[e] += pe[e];
+            pe[e] *= vv[e];
+          }
+          pk[(2 * c) & 15] = pack_f16x2(pe[0], pe[1]);
+          pk[(2 * c + 1) & 15] = pack_f16x2(pe[2], pe[3]);
+        }
+        tmem_st16(tmS(jl) + lane_base + kHalf * ch + 16 * hq, pk);
       }
-      fence_proxy_async_smem();
+      l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      m_run = m_use;
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
+      if (lane == 0) mbar_arrive(&p_ready[jl & 1]);
     }
     // ---- epilogue (the layout of attention_kernel's) ----
     if (ok && nbl > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nbl - 1) & 1, p.status, kDevTimeoutMmaDone));
@@ -966,12 +980,22 @@ __global__ void __launch_bounds__(kDThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  // drain a producer that stopped early: every issued stage completes
+  // every issued load completes before the block leaves (a producer or MMA
+  // issuer that stopped early)
   if (warp == 0 && lane == 0) {
-    for (int jl = (k_issued > 2 ? k_issued - 2 : 0); jl < k_issued; ++jl)
-      mbar_wait(&k_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
-    for (int jl = (v_issued > 2 ? v_issued - 2 : 0); jl < v_issued; ++jl)
-      mbar_wait(&v_full[jl & 1], (jl >> 1) & 1, p.status, kDevTimeoutTmaFull);
+    for (int a = 0; a < 4; ++a) {
+      const int n = (k_iss - a + 3) / 4;
+      if (n > 0) mbar_wait(&k_full[a], (n - 1) & 1, p.status, kDevTimeoutTmaFull);
+    }
+    for (int h = 0; h < 2; ++h) {
+      const int n = (v_iss - h + 1) / 2;
+      if (n > 0) mbar_wait(&v_full[h], (n - 1) & 1, p.status, kDevTimeoutTmaFull);
+    }
+    const int n_sc = (k_iss + 3) / 4;
+    for (int s = 0; s < 3; ++s) {
+      const int n = (n_sc - s + 2) / 3;
+      if (n > 0) mbar_wait(&sc_full[s], (n - 1) & 1, p.status, kDevTimeoutTmaFull);
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -1058,14 +1082,19 @@ int geometry(const rfx_attn_desc& d, Geometry* g) {
   g->q_tiles = (d.num_q_heads * d.S + kQR - 1) / kQR;
   g->n_ctx_blocks = (d.n_ctx + kKB - 1) / kKB;
   g->n_blocks = g->n_ctx_blocks + (d.S + kKB - 1) / kKB;
+  // the dense attention walks 128-key blocks: the conversion pads the keys to
+  // an even number of 64-key blocks (the padding keys are masked)
+  const bool dense = d.kv_source == RFX_KV_DENSE;
+  if (dense) g->n_blocks += g->n_blocks & 1;
+  const int att_blocks = dense ? g->n_blocks / 2 : g->n_blocks;
   int nsm = 148;
   rfx_num_sms(&nsm);
   int splits = d.kv_splits;
   if (splits <= 0) {
     const int ctas = d.B * g->q_tiles;
-    splits = std::max(1, std::min(g->n_blocks, nsm / std::max(1, ctas)));
+    splits = std::max(1, std::min(att_blocks, nsm / std::max(1, ctas)));
   }
-  if (splits > g->n_blocks) splits = g->n_blocks;
+  if (splits > att_blocks) splits = att_blocks;
   if (splits > 32) splits = 32;  // the combine kernel merges at most 32 partials per row
   g->splits = splits;
   return RFX_OK;
@@ -1131,9 +1160,9 @@ int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* 
                        w.total);
     const uint64_t keys = static_cast<uint64_t>(d.B) * g.n_blocks * kKB;
     char* ws = static_cast<char*>(d.workspace);
-    rc = make_tmap_2d(tmK, ws + w.kd, 2, kD, keys, kD * 2, 64, kKB, true);
+    rc = make_tmap_2d(tmK, ws + w.kd, 2, kD, keys, kD * 2, 64, kDKB, true);  // 128-key K tiles
     if (rc) return rc;
-    return make_tmap_2d(tmV, ws + w.vd, 2, kD, keys, kD * 2, 64, kKB, true);
+    return make_tmap_2d(tmV, ws + w.vd, 2, kD, keys, kD * 2, 64, kKB, true);   // 64-key V halves
   }
   if (d.n_ctx > 0) {
     const uint64_t krows = static_cast<uint64_t>(d.B) * d.capacity;
@@ -1177,7 +1206,7 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
   p.q_tiles = g.q_tiles;
   p.splits = g.splits;
   p.n_ctx_blocks = g.n_ctx_blocks;
-  p.n_blocks = g.n_blocks;
+  p.n_blocks = dense ? g.n_blocks / 2 : g.n_blocks;  // attention blocks: 128 keys (dense) or 64
   p.k_new = static_cast<const __nv_bfloat16*>(d.k_new);
   p.v_new = static_cast<const __nv_bfloat16*>(d.v_new);
   p.k_scale = d.k_scale;

@@ -80,15 +80,9 @@ __device__ __forceinline__ unsigned long long pack_f32x2(float lo, float hi) {
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
   return r;
 }
-__device__ __forceinline__ float lo_f32(unsigned long long v) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return lo;
-}
+__device__ __forceinline__ float lo_f32(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
 __device__ __forceinline__ float hi_f32(unsigned long long v) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return hi;
+  return __uint_as_float(static_cast<uint32_t>(v >> 32));
 }
 // max that returns NaN when either operand is NaN
 __device__ __forceinline__ float max_nan(float a, float b) {

@@ -168,7 +168,11 @@ def test_graph_replay_matches_eager_and_is_repeatable():
 @pytest.mark.parametrize("B,check", [(4, (0, 1, 2, 3)), (16, (0, 5, 11, 15))])
 def test_multistream_batch_matches_single_streams(B, check):
     """B streams batched along the token dimension give each stream's own chunk
-    (B=16: 800 tokens, the many-token GEMM tiles and the dense key source)."""
+    (B=16: 800 tokens, the many-token GEMM tiles and the dense key source).
+    The batch's attention takes the dense key source (128-key blocks) and the
+    single stream's the ring tiles (64-key blocks): the online softmax groups
+    keys differently, so the chunks agree to 1e-2, half the 2e-2 bar each
+    meets against the fp32 path."""
     cfg = pi05_config(num_layers=3)
     wts, ctx, parts, x0, st = make_case(cfg, 200, B=B)
     eng = make_engine(cfg, wts, parts, 200, B=B)
@@ -180,7 +184,7 @@ def test_multistream_batch_matches_single_streams(B, check):
         e1 = make_engine(cfg, wts, pb, 200, B=1)
         e1.set_inputs(x0[b:b + 1].cuda())
         e1.run_eager()
-        assert (e1.x.float().cpu() - xb[b:b + 1]).abs().max().item() <= 5e-3
+        assert (e1.x.float().cpu() - xb[b:b + 1]).abs().max().item() <= 1e-2
 
 
 def test_pi0_long_context_full_size():
