@@ -246,12 +246,13 @@ __device__ bool ctr_wait(const ChunkParams& p, int line, unsigned target) {
   }
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
+    // back-to-back polls: each is an L2 round trip (a sleep between them only
+    // delays the hand-off: 7.93 against 7.89 ms per PI0.5 chunk)
     for (int i = 0; i < 16; ++i) {
       if (ld_relaxed_gpu(c) >= target) {
         ld_acquire_gpu(c);  // the success becomes an acquire (one load, no full fence)
         return true;
       }
-      __nanosleep(32);
     }
     if (aborted(p)) return false;
     if (globaltimer_ns() - t0 > p.dep_limit_ns) {
