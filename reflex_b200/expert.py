@@ -356,6 +356,15 @@ class ActionExpertEngine:
                                                  norm_a2=a2(tau, nf), norm_b2=b2(tau, nf), eps=cfg.eps,
                                                  w_out=self.aout_w, b_out=self.aout_b, dt=self.dt, **nxt),
                         ("step", tau)))
+        # split-K workspace of the many-token GEMMs (one, shared: the launches
+        # run in sequence; each tile's counter is reset by its last split)
+        lin = [d for kind, d, _ in ops if kind == "linear"]
+        need_lin = max((K.linear_workspace_bytes(d) for d in lin), default=0)
+        if need_lin and (getattr(self, "split_ws", None) is None or self.split_ws.numel() < need_lin + 256):
+            self.split_ws = K.linear_workspace(need_lin + 256, self.dev)
+        for d in lin:
+            if need_lin:
+                d.workspace, d.workspace_bytes = K.aligned_ptr(self.split_ws, 256), need_lin
         # attention workspaces: one per layer with the dense source (it holds
         # the layer's converted context through the chunk), else one shared by
         # every launch (they run in sequence)
