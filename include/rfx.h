@@ -134,9 +134,11 @@ int rfx_kv_quant_append(const rfx_kv_quant_desc* desc, void* stream);
 #define RFX_EPI_SILU 1     /* y[t][o] = bf16(silu(bf16(acc + bias[o]))) */
 #define RFX_EPI_QKV_ROPE 2 /* q/k/v split of a packed QKV weight (rfx_pack_weight RFX_PACK_QKV_ROPE),
                               RoPE on q and k at positions[t], head-major q, token-major k/v */
-#define RFX_EPI_RESIDUAL 3 /* y[t][o] = bf16(y[t][o] + bf16(gate[b][o] * bf16(acc))); gate null -> 1 */
+#define RFX_EPI_RESIDUAL 3 /* y[t][o] = bf16(y[t][o] + bf16(gate[b][o] * bf16(acc + bias[o])));
+                              gate null -> 1, bias null -> 0 */
 #define RFX_EPI_GEGLU 4    /* y[t][f] = bf16(bf16(gelu_tanh(bf16(gate_f))) * bf16(up_f)) on a weight
                               packed with rfx_pack_weight RFX_PACK_GATE_UP */
+#define RFX_EPI_GELU 5     /* y[t][o] = bf16(gelu_tanh(bf16(acc + bias[o]))) (SigLIP fc1) */
 typedef struct rfx_linear_desc {
   int T;                /* tokens */
   int O;                /* rows of the (packed) weight; multiple of 128 */
@@ -175,8 +177,10 @@ typedef struct rfx_linear_desc {
    * least rfx_linear_workspace_size bytes, a many-token GEMM whose tiles
    * leave SMs idle splits K over more CTAs and the last split of a tile sums
    * the fp32 partials in split order (deterministic) before the epilogue.
-   * Launches sharing a workspace must not run concurrently (one stream, or
-   * ordered by events).  NULL / too small: no split. */
+   * The first 64 KB hold the tile counters for every shape, so GEMMs of
+   * different shapes may share one workspace; launches sharing it must not
+   * run concurrently (one stream, or ordered by events).  NULL / too small:
+   * no split. */
   void* workspace;
   size_t workspace_bytes;
 } rfx_linear_desc;
@@ -408,6 +412,57 @@ typedef struct rfx_embed_cache_desc {
 } rfx_embed_cache_desc;
 int rfx_embed_cache_check(const rfx_embed_cache_desc* desc, void* stream);
 
+/* --------------------------------------------------- vision tower ---- */
+/* The SigLIP vision tower + PaliGemma projector that the reference calls as
+ * the VLM's image embedder (``vlm.model.get_image_features``,
+ * reflex/policies/pi05/modeling_pi05.py:141-158, one call per camera at :244;
+ * transformers' SiglipVisionModel, fork not vendored).  Its projections run on
+ * rfx_linear (RFX_EPI_STORE / RFX_EPI_GELU / RFX_EPI_RESIDUAL with bias); the
+ * three entry points below are the rest. */
+
+/* Patch extraction for the stride-P P x P patch convolution
+ * (SiglipVisionEmbeddings.patch_embedding): out[b*G*G + gy*G + gx][c*P*P + py*P + px]
+ * = bf16(image[b][c][gy*P + py][gx*P + px]), G = H / P (square images), columns
+ * C*P*P .. ldo-1 zero, so that rfx_linear with the [width][C*P*P] convolution
+ * weight (zero-padded to ldo columns) computes the patch embeddings. */
+typedef struct rfx_patches_desc {
+  int B, C, H, W, patch;
+  const float* image; /* fp32 [B][C][H][W], contiguous */
+  void* out;          /* bf16 [B*G*G][ldo] */
+  int ldo;            /* multiple of 64, >= C*patch*patch */
+} rfx_patches_desc;
+int rfx_patches(const rfx_patches_desc* desc, void* stream);
+
+/* LayerNorm of token rows (nn.LayerNorm, SiglipEncoderLayer.layer_norm1/2 and
+ * post_layernorm): y[t][k] = bf16((x[t][k] - mean_t) * rsqrt(var_t + eps) * w[k] + b[k]),
+ * mean and (biased) variance over the C columns in fp32.  C % 64 == 0, C <= 4096. */
+typedef struct rfx_layer_norm_desc {
+  int T, C;
+  const void* x; /* bf16 [T][ldx] */
+  int ldx;
+  const float* w; /* [C] */
+  const float* b; /* [C] */
+  float eps;
+  void* y; /* bf16 [T][ldy] */
+  int ldy;
+} rfx_layer_norm_desc;
+int rfx_layer_norm(const rfx_layer_norm_desc* desc, void* stream);
+
+/* Full (unmasked) multi-head attention within each image (SiglipAttention,
+ * eager): out = softmax(q k^T * scale) v per head, fp32 scores, P in bf16.
+ * qkv holds the q, k and v projections side by side: row b*N + i, columns
+ * h*D .. (q), H*D + h*D .. (k), 2*H*D + h*D .. (v).  N <= 256 tokens per image,
+ * D <= 128 with D % 8 == 0; ld_qkv and ld_out multiples of 8. */
+typedef struct rfx_vit_attn_desc {
+  int B, N, H, D;
+  const void* qkv; /* bf16 [B*N][ld_qkv] */
+  int ld_qkv;
+  void* out; /* bf16 [B*N][ld_out], head h at columns h*D .. h*D+D-1 */
+  int ld_out;
+  float scale;
+} rfx_vit_attn_desc;
+int rfx_vit_attention(const rfx_vit_attn_desc* desc, void* stream);
+
 /* ------------------------------------------------ fused chunk executor ---- */
 /* The whole PI0.5 denoising loop of one chunk (all Euler steps x layers:
  * input norm, QKV+RoPE, partitioned attention over the context ring,
@@ -507,6 +562,9 @@ int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc);
 int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc);
 int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc);
+int rfx_plan_add_patches(rfx_plan* plan, const rfx_patches_desc* desc);
+int rfx_plan_add_layer_norm(rfx_plan* plan, const rfx_layer_norm_desc* desc);
+int rfx_plan_add_vit_attention(rfx_plan* plan, const rfx_vit_attn_desc* desc);
 /* The chunk (not owned by the plan) is run at this point: counter clear + one launch. */
 int rfx_plan_add_chunk(rfx_plan* plan, rfx_chunk* chunk);
 /* The next op added is launched without programmatic dependent launch: it

@@ -38,6 +38,7 @@ RFX_EPI_SILU = 1
 RFX_EPI_QKV_ROPE = 2
 RFX_EPI_RESIDUAL = 3
 RFX_EPI_GEGLU = 4
+RFX_EPI_GELU = 5
 
 RFX_PACK_QKV_ROPE = 0
 RFX_PACK_GATE_UP = 1
@@ -149,6 +150,31 @@ class NormDesc(Structure):
     ]
 
 
+class PatchesDesc(Structure):
+    _fields_ = [
+        ("B", c_int), ("C", c_int), ("H", c_int), ("W", c_int), ("patch", c_int),
+        ("image", c_void_p), ("out", c_void_p), ("ldo", c_int),
+    ]
+
+
+class LayerNormDesc(Structure):
+    _fields_ = [
+        ("T", c_int), ("C", c_int),
+        ("x", c_void_p), ("ldx", c_int),
+        ("w", c_void_p), ("b", c_void_p), ("eps", c_float),
+        ("y", c_void_p), ("ldy", c_int),
+    ]
+
+
+class VitAttnDesc(Structure):
+    _fields_ = [
+        ("B", c_int), ("N", c_int), ("H", c_int), ("D", c_int),
+        ("qkv", c_void_p), ("ld_qkv", c_int),
+        ("out", c_void_p), ("ld_out", c_int),
+        ("scale", c_float),
+    ]
+
+
 class ChunkDesc(Structure):
     _fields_ = [
         ("B", c_int), ("S", c_int), ("num_layers", c_int), ("num_steps", c_int),
@@ -202,6 +228,12 @@ SIGNATURES = {
     "rfx_copy_rows": ([POINTER(CopyRowsDesc), c_void_p], c_int),
     "rfx_rms_norm": ([POINTER(NormDesc), c_void_p], c_int),
     "rfx_plan_add_rms_norm": ([c_void_p, POINTER(NormDesc)], c_int),
+    "rfx_patches": ([POINTER(PatchesDesc), c_void_p], c_int),
+    "rfx_layer_norm": ([POINTER(LayerNormDesc), c_void_p], c_int),
+    "rfx_vit_attention": ([POINTER(VitAttnDesc), c_void_p], c_int),
+    "rfx_plan_add_patches": ([c_void_p, POINTER(PatchesDesc)], c_int),
+    "rfx_plan_add_layer_norm": ([c_void_p, POINTER(LayerNormDesc)], c_int),
+    "rfx_plan_add_vit_attention": ([c_void_p, POINTER(VitAttnDesc)], c_int),
     "rfx_plan_add_chunk": ([c_void_p, c_void_p], c_int),
     "rfx_chunk_workspace_size": ([POINTER(ChunkDesc), POINTER(c_size_t)], c_int),
     "rfx_chunk_create": ([POINTER(ChunkDesc), c_void_p, c_size_t, POINTER(c_void_p)], c_int),

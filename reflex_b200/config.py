@@ -86,3 +86,40 @@ def timestep_schedule(num_steps: int) -> list[float]:
         out.append(float(t))
         t = np.float32(t + dt)
     return out
+
+
+@dataclass(frozen=True)
+class VisionConfig:
+    """The SigLIP vision tower and PaliGemma projector that turn a camera image
+    into the 256 image tokens of the prefix (the ``get_image_features`` call at
+    reflex/policies/pi05/modeling_pi05.py:141-158,244; PaliGemma-3B-224's
+    SigLIP-So400m/14: 27 layers, width 1152, 16 x 72 heads, MLP 4304 with
+    GELU-tanh, LayerNorm eps 1e-6, 14 x 14 patches of a 224 x 224 image, and a
+    1152 -> 2048 projector)."""
+
+    num_layers: int = 27
+    width: int = 1152
+    num_heads: int = 16
+    head_dim: int = 72
+    mlp_dim: int = 4304
+    patch: int = 14
+    image: int = 224
+    channels: int = 3
+    proj_dim: int = 2048
+    eps: float = 1e-6
+
+    @property
+    def grid(self) -> int:
+        return self.image // self.patch
+
+    @property
+    def tokens(self) -> int:
+        """Image tokens (patches) per image."""
+        return self.grid * self.grid
+
+    @property
+    def patch_dim(self) -> int:
+        return self.channels * self.patch * self.patch
+
+    def with_(self, **kw) -> "VisionConfig":
+        return replace(self, **kw)

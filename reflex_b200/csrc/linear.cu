@@ -106,6 +106,7 @@ struct LinParams {
   int ksplit;
   float* part;
   int* ctr;
+  int act;  // activation of the kEpiSilu kernels: 0 SiLU, 1 GELU-tanh (RFX_EPI_GELU)
 };
 
 __device__ __forceinline__ void trace(const LinParams& p, int ev) {
@@ -186,7 +187,8 @@ __device__ __forceinline__ void epilogue_store(const LinParams& p, int m, int i,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (EPI == kEpiResidual) {
-        const float a = bf16_round(v0[j]), c = bf16_round(v1[j]);
+        const float a = bf16_round(p.bias ? v0[j] + p.bias[o0 + j] : v0[j]);
+        const float c = bf16_round(p.bias ? v1[j] + p.bias[o0 + 64 + j] : v1[j]);
         const float ga = p.gate ? bf16_round(__fmul_rn(in.g0[j], a)) : a;
         const float gc = p.gate ? bf16_round(__fmul_rn(in.g1[j], c)) : c;
         r0[j] = __fadd_rn(in.r0[j], ga);
@@ -194,8 +196,8 @@ __device__ __forceinline__ void epilogue_store(const LinParams& p, int m, int i,
       } else {
         float a = v0[j] + in.r0[j], c = v1[j] + in.r1[j];
         if (EPI == kEpiSilu) {
-          a = silu(bf16_round(a));
-          c = silu(bf16_round(c));
+          a = p.act ? gelu_tanh(bf16_round(a)) : silu(bf16_round(a));
+          c = p.act ? gelu_tanh(bf16_round(c)) : silu(bf16_round(c));
         }
         r0[j] = a;
         r1[j] = c;
@@ -1098,12 +1100,15 @@ const void* select_kernel(int nt, int pro, int epi) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// RFX_EPI_GELU runs the SiLU epilogue's kernels with the activation switched
+int kernel_epi(int epi) { return epi == RFX_EPI_GELU ? RFX_EPI_SILU : epi; }
+
 int validate(const rfx_linear_desc& d) {
   if (d.T < 1 || d.O < kBM || d.O % kBM || d.K < kBK || d.K % kBK || d.tokens_per_batch < 1)
     return set_error(RFX_E_INVAL, "rfx_linear: need T>=1, O%%128==0, K%%64==0, tokens_per_batch>=1 (T=%d O=%d K=%d)",
                      d.T, d.O, d.K);
   if (d.prologue != RFX_PRO_LOAD && d.prologue != RFX_PRO_NORM) return set_error(RFX_E_INVAL, "rfx_linear: prologue");
-  if (d.epilogue < RFX_EPI_STORE || d.epilogue > RFX_EPI_GEGLU) return set_error(RFX_E_INVAL, "rfx_linear: epilogue");
+  if (d.epilogue < RFX_EPI_STORE || d.epilogue > RFX_EPI_GELU) return set_error(RFX_E_INVAL, "rfx_linear: epilogue");
   if (!d.w || !d.x || !aligned16(d.w) || !aligned16(d.x) || d.ldx < d.K || d.ldx % 8)
     return set_error(RFX_E_INVAL, "rfx_linear: w/x must be 16-byte aligned and ldx>=K, ldx%%8==0");
   if (d.prologue == RFX_PRO_NORM &&
@@ -1135,9 +1140,11 @@ namespace {
 // (a 400-token o_proj, K = 2048, as 4 x 8: 15.8 us against 17.1 us for the
 // per-tile kernel's in-cluster split; the 8- and 16-stream chunks 2-3 %
 // faster than with a 32-step floor), and the partial slots stay within 64 MB.
+constexpr int kSplitMaxTiles = 16384;  // tiles the fixed counter block serves
 int pick_ksplit(int tiles, int k_chunks, int nt, int nsm) {
   int best = 1;
   double best_t = static_cast<double>((tiles + nsm - 1) / nsm);
+  if (tiles > kSplitMaxTiles) return 1;
   for (int s = 2; s <= 4; ++s) {
     if (k_chunks / s < 8 || static_cast<size_t>(tiles) * s * nt * 128 * 4 > (size_t(64) << 20)) break;
     const double t = static_cast<double>((tiles * s + nsm - 1) / nsm) / s + 0.1;
@@ -1149,9 +1156,12 @@ int pick_ksplit(int tiles, int k_chunks, int nt, int nsm) {
   return best;
 }
 
-// Split-K workspace of the persistent kernel: per-tile arrival counters
-// (int, padded to 256 B) then fp32 partial slots [tile][ksplit][nt][128].
-size_t split_ctr_bytes(int tiles) { return (static_cast<size_t>(tiles) * 4 + 255) & ~size_t(255); }
+// Split-K workspace of the persistent kernel: a fixed 64 KB of per-tile
+// arrival counters (int) then fp32 partial slots [tile][ksplit][nt][128].
+// The counter block has the same place and size for every shape, so GEMMs of
+// different shapes can take turns on one workspace: no launch's partials ever
+// land on another shape's counters (each launch leaves its counters zero).
+size_t split_ctr_bytes(int) { return static_cast<size_t>(kSplitMaxTiles) * 4; }
 size_t split_workspace_bytes(int tiles, int ksplit, int nt) {
   if (ksplit <= 1) return 0;
   return split_ctr_bytes(tiles) + static_cast<size_t>(tiles) * ksplit * nt * 128 * 4;
@@ -1249,13 +1259,14 @@ LinParams lin_params(const rfx_linear_desc& d) {
   p.y_rps = d.y_rows_per_batch > 0 ? d.y_rows_per_batch : d.tokens_per_batch;
   p.y_off = d.y_rows_per_batch > 0 ? d.y_row_offset : 0;
   p.status = device_status_ptr();
+  p.act = d.epilogue == RFX_EPI_GELU ? 1 : 0;
   return p;
 }
 
 int launch_linear_tiles(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, const TilesPlan& tp,
                         int nsm, cudaStream_t stream, bool pdl) {
   const int nt = tp.nt;
-  const void* fn = select_tiles(nt, d.epilogue);
+  const void* fn = select_tiles(nt, kernel_epi(d.epilogue));
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no tile kernel for this epilogue");
   const int smem = tiles_smem(nt);
   int rc = ensure_smem_attr(fn, smem);
@@ -1301,7 +1312,7 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   if (rc) return rc;
   const TilesPlan tp = plan_tiles(d, nsm, false);
   if (tp.nt) return launch_linear_tiles(d, tmW, tmX, tp, nsm, stream, pdl);
-  const void* fn = select_kernel(cfg.nt, d.prologue, d.epilogue);
+  const void* fn = select_kernel(cfg.nt, d.prologue, kernel_epi(d.epilogue));
   if (!fn) return set_error(RFX_E_INVAL, "rfx_linear: no kernel for this configuration");
   rc = ensure_smem_attr(fn, cfg.smem, cfg.splits > 8);
   if (rc) return rc;
@@ -1353,6 +1364,7 @@ int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtens
   p.recv_off = cfg.recv_off;
   p.stage_off = cfg.stage_off;
   p.status = device_status_ptr();
+  p.act = d.epilogue == RFX_EPI_GELU ? 1 : 0;
   p.trace = static_cast<unsigned long long*>(trace_buffer(m_tiles * cfg.splits * n_tiles * 16));
 
   p.n_tiles = n_tiles;

@@ -93,6 +93,9 @@ int launch_action_in(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl)
 int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl);
 int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl);
 int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl);
+int launch_patches(const rfx_patches_desc& d, cudaStream_t stream, bool pdl);
+int launch_layer_norm(const rfx_layer_norm_desc& d, cudaStream_t stream, bool pdl);
+int launch_vit_attention(const rfx_vit_attn_desc& d, cudaStream_t stream, bool pdl);
 int run_chunk_op(rfx_chunk* c, cudaStream_t s);
 
 }  // namespace rfx

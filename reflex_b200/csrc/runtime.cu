@@ -322,11 +322,21 @@ struct CopyOp {
 struct NormOp {
   rfx_norm_desc d;
 };
+struct PatchOp {
+  rfx_patches_desc d;
+};
+struct LayerNormOp {
+  rfx_layer_norm_desc d;
+};
+struct VitAttnOp {
+  rfx_vit_attn_desc d;
+};
 struct BarrierOp {};
 struct ChunkOp {
   rfx_chunk* c;
 };
-using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp, NormOp, BarrierOp, ChunkOp>;
+using Op = std::variant<LinearOp, AttnOp, QuantOp, TimeOp, ModOp, InOp, TailOp, CopyOp, NormOp, BarrierOp, ChunkOp,
+                        PatchOp, LayerNormOp, VitAttnOp>;
 }  // namespace
 
 struct rfx_plan {
@@ -349,6 +359,9 @@ int run_op(const Op& op, cudaStream_t s, bool pdl) {
   if (auto* o = std::get_if<CopyOp>(&op)) return launch_copy_rows(o->d, s, pdl);
   if (auto* o = std::get_if<NormOp>(&op)) return launch_rms_norm(o->d, s, pdl);
   if (auto* o = std::get_if<ChunkOp>(&op)) return run_chunk_op(o->c, s);
+  if (auto* o = std::get_if<PatchOp>(&op)) return launch_patches(o->d, s, pdl);
+  if (auto* o = std::get_if<LayerNormOp>(&op)) return launch_layer_norm(o->d, s, pdl);
+  if (auto* o = std::get_if<VitAttnOp>(&op)) return launch_vit_attention(o->d, s, pdl);
   return set_error(RFX_E_STATE, "plan: unknown op");
 }
 // Launches every op in order; an op that follows a BarrierOp runs without PDL.
@@ -456,6 +469,25 @@ extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* 
 extern "C" int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc) {
   PLAN_GUARD(plan);
   plan->ops.emplace_back(NormOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+
+extern "C" int rfx_plan_add_patches(rfx_plan* plan, const rfx_patches_desc* desc) {
+  PLAN_GUARD(plan);
+  plan->ops.emplace_back(PatchOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+extern "C" int rfx_plan_add_layer_norm(rfx_plan* plan, const rfx_layer_norm_desc* desc) {
+  PLAN_GUARD(plan);
+  plan->ops.emplace_back(LayerNormOp{*desc});
+  plan->launches += 1;
+  return RFX_OK;
+}
+extern "C" int rfx_plan_add_vit_attention(rfx_plan* plan, const rfx_vit_attn_desc* desc) {
+  PLAN_GUARD(plan);
+  plan->ops.emplace_back(VitAttnOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }

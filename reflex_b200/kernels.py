@@ -291,6 +291,43 @@ def rms_norm(**kw) -> None:
     L.call("rfx_rms_norm", ctypes.byref(d), _stream())
 
 
+def patches_desc(*, image, out, patch) -> L.PatchesDesc:
+    """Patch rows of [B, C, H, W] fp32 images for the patch convolution as a GEMM."""
+    _need_cuda(image, out)
+    if image.dtype != torch.float32 or out.dtype != torch.bfloat16 or not image.is_contiguous():
+        raise ValueError("patches: contiguous fp32 images -> bf16 rows")
+    d = L.PatchesDesc()
+    d.B, d.C, d.H, d.W = image.shape
+    d.patch = patch
+    d.image, d.out, d.ldo = image.data_ptr(), out.data_ptr(), out.stride(0)
+    return d
+
+
+def layer_norm_desc(*, x, y, w, b, eps=1e-6, T=None) -> L.LayerNormDesc:
+    _need_cuda(x, y, w, b)
+    if x.dtype != torch.bfloat16 or y.dtype != torch.bfloat16 or w.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("layer_norm maps bf16 rows to bf16 rows with fp32 weight and bias")
+    d = L.LayerNormDesc()
+    d.T = x.shape[0] if T is None else T
+    d.C = x.shape[1]
+    d.x, d.ldx = x.data_ptr(), x.stride(0)
+    d.w, d.b, d.eps = w.data_ptr(), b.data_ptr(), eps
+    d.y, d.ldy = y.data_ptr(), y.stride(0)
+    return d
+
+
+def vit_attention_desc(*, qkv, out, B, N, H, D, scale) -> L.VitAttnDesc:
+    _need_cuda(qkv, out)
+    if qkv.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise ValueError("vit_attention: bf16 q|k|v rows -> bf16 rows")
+    d = L.VitAttnDesc()
+    d.B, d.N, d.H, d.D = B, N, H, D
+    d.qkv, d.ld_qkv = qkv.data_ptr(), qkv.stride(0)
+    d.out, d.ld_out = out.data_ptr(), out.stride(0)
+    d.scale = scale
+    return d
+
+
 def copy_rows_desc(*, dst, src, rows, width, dst_rows_per_group, dst_row_offset=0, group=None,
                    src_ld=None) -> L.CopyRowsDesc:
     _need_cuda(dst, src)
@@ -329,6 +366,9 @@ class Plan:
         L.ModulationDesc: "rfx_plan_add_modulation",
         L.CopyRowsDesc: "rfx_plan_add_copy_rows",
         L.NormDesc: "rfx_plan_add_rms_norm",
+        L.PatchesDesc: "rfx_plan_add_patches",
+        L.LayerNormDesc: "rfx_plan_add_layer_norm",
+        L.VitAttnDesc: "rfx_plan_add_vit_attention",
     }
     # direct (non-plan) entry point of each descriptor kind, for eager execution
     DIRECT = {
@@ -339,6 +379,9 @@ class Plan:
         L.ModulationDesc: "rfx_modulation",
         L.CopyRowsDesc: "rfx_copy_rows",
         L.NormDesc: "rfx_rms_norm",
+        L.PatchesDesc: "rfx_patches",
+        L.LayerNormDesc: "rfx_layer_norm",
+        L.VitAttnDesc: "rfx_vit_attention",
     }
 
     @classmethod

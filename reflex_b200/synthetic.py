@@ -135,3 +135,41 @@ def rope_table(max_pos: int, head_dim: int, base: float) -> torch.Tensor:
     t = torch.arange(max_pos, dtype=torch.float)
     freqs = torch.einsum("i,j -> ij", t, inv_freq)
     return torch.cat((freqs.cos(), freqs.sin()), dim=-1)
+
+
+def vision_weights(cfg, seed: int = 20, device="cpu") -> dict[str, torch.Tensor]:
+    """Random-init SigLIP tower + projector weights (``cfg``: VisionConfig),
+    named as transformers' SiglipVisionModel / PaliGemmaMultiModalProjector
+    state dicts.  Linear and patch weights N(0, 0.02) and biases N(0, 0.02),
+    bf16-representable; position embeddings N(0, 0.02); LayerNorm weight
+    1 + N(0, 0.05) and bias N(0, 0.02), fp32."""
+    r = _Rng(seed, device)
+    W, F = cfg.width, cfg.mlp_dim
+    w: dict[str, torch.Tensor] = {}
+    pre = "vision_model."
+    w[pre + "embeddings.patch_embedding.weight"] = _bf16(r.normal(W, cfg.channels, cfg.patch, cfg.patch, std=0.02))
+    w[pre + "embeddings.patch_embedding.bias"] = _bf16(r.normal(W, std=0.02))
+    w[pre + "embeddings.position_embedding.weight"] = _bf16(r.normal(cfg.tokens, W, std=0.02))
+    for l in range(cfg.num_layers):
+        p = f"{pre}encoder.layers.{l}."
+        for name in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            w[p + f"self_attn.{name}.weight"] = _bf16(r.normal(W, W, std=0.02))
+            w[p + f"self_attn.{name}.bias"] = _bf16(r.normal(W, std=0.02))
+        w[p + "mlp.fc1.weight"] = _bf16(r.normal(F, W, std=0.02))
+        w[p + "mlp.fc1.bias"] = _bf16(r.normal(F, std=0.02))
+        w[p + "mlp.fc2.weight"] = _bf16(r.normal(W, F, std=0.02))
+        w[p + "mlp.fc2.bias"] = _bf16(r.normal(W, std=0.02))
+        for n in ("layer_norm1", "layer_norm2"):
+            w[p + f"{n}.weight"] = 1.0 + r.normal(W, std=0.05)
+            w[p + f"{n}.bias"] = r.normal(W, std=0.02)
+    w[pre + "post_layernorm.weight"] = 1.0 + r.normal(W, std=0.05)
+    w[pre + "post_layernorm.bias"] = r.normal(W, std=0.02)
+    w["projector.linear.weight"] = _bf16(r.normal(cfg.proj_dim, W, std=0.02))
+    w["projector.linear.bias"] = _bf16(r.normal(cfg.proj_dim, std=0.02))
+    return w
+
+
+def images(cfg, B: int = 1, seed: int = 21, device="cpu") -> torch.Tensor:
+    """Normalized camera images [B, 3, H, W] in [-1, 1] (SigLIP's input range),
+    fp32."""
+    return _Rng(seed, device).uniform(B, cfg.channels, cfg.image, cfg.image)

@@ -19,7 +19,8 @@ STRUCTS = {
     "rfx_kv_quant_desc": "KvQuantDesc", "rfx_linear_desc": "LinearDesc", "rfx_norm_desc": "NormDesc",
     "rfx_attn_desc": "AttnDesc", "rfx_time_cond_desc": "TimeCondDesc", "rfx_modulation_desc": "ModulationDesc",
     "rfx_action_io_desc": "ActionIoDesc", "rfx_copy_rows_desc": "CopyRowsDesc", "rfx_chunk_desc": "ChunkDesc",
-    "rfx_embed_cache_desc": "EmbedCacheDesc",
+    "rfx_embed_cache_desc": "EmbedCacheDesc", "rfx_patches_desc": "PatchesDesc",
+    "rfx_layer_norm_desc": "LayerNormDesc", "rfx_vit_attn_desc": "VitAttnDesc",
 }
 
 
@@ -81,12 +82,12 @@ def test_plan_calls_out_of_order():
 
 
 @pytest.mark.parametrize("T,O,K,want", [
-    (768, 2048, 16384, 512 + 96 * 3 * 128 * 128 * 4),  # down_proj of a 768-token frame: 96 tiles, K split 3
+    (768, 2048, 16384, 65536 + 96 * 3 * 128 * 128 * 4),  # down_proj of a 768-token frame: 96 tiles, K split 3
     (768, 32768, 2048, 0),                              # gate/up: 768 tiles fill the SMs
     (50, 2048, 16384, 0),                               # few tokens: the per-tile kernel
 ])
 def test_linear_split_workspace_size(T, O, K, want):
-    """The split-K workspace query needs no device: counters padded to 256 B
+    """The split-K workspace query needs no device: a fixed 64 KB counter block
     plus fp32 partial slots [tile][split][128 tokens][128 rows] (148 SMs
     assumed when no GPU answers)."""
     lib = _lib.load()
@@ -113,3 +114,25 @@ def test_kv_quant_rejects_too_many_rings():
     d.region_base, d.region_off, d.region_len = 0, 0, 1
     assert lib.rfx_kv_quant_append(ctypes.byref(d), None) == _lib.RFX_E_INVAL
     assert b"65535" in lib.rfx_last_error()
+
+
+def test_vision_entry_points_reject_bad_shapes():
+    """Shape checks of the vision tower's entry points run before any launch."""
+    lib = _lib.load()
+    a = _lib.VitAttnDesc()
+    a.B, a.N, a.H, a.D = 1, 257, 16, 72  # more than 256 tokens per image
+    a.qkv = a.out = 1 << 20
+    a.ld_qkv, a.ld_out, a.scale = 3 * 16 * 72, 16 * 72, 0.1
+    assert lib.rfx_vit_attention(ctypes.byref(a), None) == _lib.RFX_E_INVAL
+    a.N, a.D = 256, 76  # head dim not a multiple of 8
+    assert lib.rfx_vit_attention(ctypes.byref(a), None) == _lib.RFX_E_INVAL
+    n = _lib.LayerNormDesc()
+    n.T, n.C = 4, 1000  # C % 64 != 0
+    n.x = n.y = n.w = n.b = 1 << 20
+    n.ldx = n.ldy = 1024
+    assert lib.rfx_layer_norm(ctypes.byref(n), None) == _lib.RFX_E_INVAL
+    p = _lib.PatchesDesc()
+    p.B, p.C, p.H, p.W, p.patch = 1, 3, 224, 224, 14
+    p.image = p.out = 1 << 20
+    p.ldo = 588  # not a multiple of 64
+    assert lib.rfx_patches(ctypes.byref(p), None) == _lib.RFX_E_INVAL

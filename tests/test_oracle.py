@@ -171,3 +171,23 @@ def test_model_18_layers_matches_reference():
     np.testing.assert_allclose([h.abs().max().item() for h in hidden], g["hidden_step0_absmax"], rtol=1e-4)
     np.testing.assert_allclose([h.norm().item() for h in hidden], g["hidden_step0_l2"], rtol=1e-4)
     np.testing.assert_allclose(x.numpy(), g["actions"], atol=FP32_ATOL, rtol=0)
+
+
+def test_vision_tower_matches_transformers_siglip():
+    """The SigLIP tower + projector restatement against the installed
+    transformers' SiglipVisionModel / PaliGemmaMultiModalProjector (2 layers at
+    full widths, seeded weights and image; tests/golden/make_golden_vision.py)."""
+    from oracle import vision as ov
+    from reflex_b200.config import VisionConfig
+
+    g = np.load(os.path.join(GOLD, "vision_l2.npz"))
+    cfg = VisionConfig(num_layers=int(g["layers"]))
+    w = synthetic.vision_weights(cfg, seed=int(g["w_seed"]))
+    img = synthetic.images(cfg, B=1, seed=int(g["img_seed"]))
+    assert sha(*([w[k] for k in sorted(w)] + [img])) == str(g["inputs_sha"])
+    with torch.no_grad():
+        out, hid = ov.image_features(cfg, w, img, return_hidden=True)
+    assert (hid[0, :64] - torch.from_numpy(g["hidden64"])).abs().max().item() < FP32_ATOL
+    assert (out[0, :64] - torch.from_numpy(g["tokens64"])).abs().max().item() < FP32_ATOL
+    assert (out[0].norm(dim=-1) - torch.from_numpy(g["tok_norm"])).abs().max().item() < 1e-3
+    assert (out[0].mean(-1) - torch.from_numpy(g["tok_mean"])).abs().max().item() < FP32_ATOL
