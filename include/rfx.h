@@ -435,7 +435,8 @@ int rfx_patches(const rfx_patches_desc* desc, void* stream);
 
 /* LayerNorm of token rows (nn.LayerNorm, SiglipEncoderLayer.layer_norm1/2 and
  * post_layernorm): y[t][k] = bf16((x[t][k] - mean_t) * rsqrt(var_t + eps) * w[k] + b[k]),
- * mean and (biased) variance over the C columns in fp32.  C % 64 == 0, C <= 4096. */
+ * mean and (biased) variance over the C columns in fp32.  C % 8 == 0, C <= 2048;
+ * rows, w and b 16-byte aligned. */
 typedef struct rfx_layer_norm_desc {
   int T, C;
   const void* x; /* bf16 [T][ldx] */

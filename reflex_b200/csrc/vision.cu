@@ -54,41 +54,68 @@ struct LnParams {
   int ldy, T, C;
 };
 
-// One warp per row; lane j takes column pairs j, j + 32, ... (C % 64 == 0).
-// The row is read three times (sum, squared deviations, output), the second
-// and third time from L1, so nothing is held in a register array.
+// One warp per row; lane j takes the row's 16-byte chunks j, j + 32, ...
+// (C % 8 == 0, C <= 2048: at most eight chunks a lane), all loaded at once and
+// kept in registers for the mean, the variance and the output.
+constexpr int kLnChunks = 8;
 __global__ void __launch_bounds__(256) layernorm_kernel(const LnParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= p.T) return;
-  const int np = p.C / 64;  // pairs per lane
-  const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(p.x + static_cast<long>(t) * p.ldx);
+  const int nch = p.C / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<long>(t) * p.ldx);
+  float v[kLnChunks][8];
   float s = 0.f;
-  for (int i = 0; i < np; ++i) {
-    const float2 v = __bfloat1622float2(xr[i * 32 + lane]);
-    s += v.x + v.y;
+#pragma unroll
+  for (int i = 0; i < kLnChunks; ++i) {
+    const int c = i * 32 + lane;
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    if (c < nch) raw = xr[c];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      v[i][2 * e] = f.x;
+      v[i][2 * e + 1] = f.y;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += v[i][e];
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float mean = s / static_cast<float>(p.C);
   float q = 0.f;
-  for (int i = 0; i < np; ++i) {
-    const float2 v = __bfloat1622float2(xr[i * 32 + lane]);
-    const float a = v.x - mean, c = v.y - mean;
-    q += a * a + c * c;
+#pragma unroll
+  for (int i = 0; i < kLnChunks; ++i) {
+    if (i * 32 + lane >= nch) continue;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = v[i][e] - mean;
+      q += a * a;
+    }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
   const float rstd = rsqrtf(q / static_cast<float>(p.C) + p.eps);
-  uint32_t* yr = reinterpret_cast<uint32_t*>(p.y + static_cast<long>(t) * p.ldy);
-  for (int i = 0; i < np; ++i) {
-    const float2 v = __bfloat1622float2(xr[i * 32 + lane]);
-    const int k = 2 * (i * 32 + lane);
-    const float2 w = *reinterpret_cast<const float2*>(p.w + k);
-    const float2 b = *reinterpret_cast<const float2*>(p.b + k);
-    yr[i * 32 + lane] = pack_bf16x2((v.x - mean) * rstd * w.x + b.x, (v.y - mean) * rstd * w.y + b.y);
+  uint4* yr = reinterpret_cast<uint4*>(p.y + static_cast<long>(t) * p.ldy);
+#pragma unroll
+  for (int i = 0; i < kLnChunks; ++i) {
+    const int c = i * 32 + lane;
+    if (c >= nch) continue;
+    const float4 w0 = *reinterpret_cast<const float4*>(p.w + 8 * c);
+    const float4 w1 = *reinterpret_cast<const float4*>(p.w + 8 * c + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(p.b + 8 * c);
+    const float4 b1 = *reinterpret_cast<const float4*>(p.b + 8 * c + 4);
+    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    uint4 o;
+    o.x = pack_bf16x2((v[i][0] - mean) * rstd * w[0] + b[0], (v[i][1] - mean) * rstd * w[1] + b[1]);
+    o.y = pack_bf16x2((v[i][2] - mean) * rstd * w[2] + b[2], (v[i][3] - mean) * rstd * w[3] + b[3]);
+    o.z = pack_bf16x2((v[i][4] - mean) * rstd * w[4] + b[4], (v[i][5] - mean) * rstd * w[5] + b[5]);
+    o.w = pack_bf16x2((v[i][6] - mean) * rstd * w[6] + b[6], (v[i][7] - mean) * rstd * w[7] + b[7]);
+    yr[c] = o;
   }
 }
 
@@ -169,24 +196,33 @@ __global__ void __launch_bounds__(kVThreads, 1) vit_attention_kernel(const VitPa
   const __nv_bfloat16* qsrc = p.qkv + static_cast<long>(h) * p.D;
   const __nv_bfloat16* ksrc = p.qkv + static_cast<long>(p.H + h) * p.D;
   const __nv_bfloat16* vsrc = p.qkv + static_cast<long>(2 * p.H + h) * p.D;
+  // every 16-byte chunk of data by an asynchronous copy (all of a thread's
+  // copies in flight at once), the padding chunks and rows by plain zero stores
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   for (int i = threadIdx.x; i < kVQ * 16; i += kVThreads) {
     const int r = i >> 4, c = i & 15;
     const int n = qt * kVQ + r;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (n < p.N && c < dch) v = *reinterpret_cast<const uint4*>(qsrc + (row0 + n) * p.ld_qkv + c * 8);
-    *reinterpret_cast<uint4*>(smem + kVOffQ + (c >> 3) * 16384 + sw128_off(r, c & 7)) = v;
+    uint8_t* dst = smem + kVOffQ + (c >> 3) * 16384 + sw128_off(r, c & 7);
+    if (n < p.N && c < dch)
+      cp_async16(dst, qsrc + (row0 + n) * p.ld_qkv + c * 8);
+    else
+      *reinterpret_cast<uint4*>(dst) = zero;
   }
   for (int i = threadIdx.x; i < kVKeys * 16; i += kVThreads) {
     const int r = i >> 4, c = i & 15;
-    uint4 k = make_uint4(0u, 0u, 0u, 0u), v = k;
+    uint8_t* kd = smem + kVOffK + (c >> 3) * 32768 + sw128_off(r, c & 7);
+    uint8_t* vd = smem + kVOffV + (r >> 6) * 16384 + (c >> 3) * 8192 + sw128_off(r & 63, c & 7);
     if (r < p.N && c < dch) {
-      k = *reinterpret_cast<const uint4*>(ksrc + (row0 + r) * p.ld_qkv + c * 8);
-      v = *reinterpret_cast<const uint4*>(vsrc + (row0 + r) * p.ld_qkv + c * 8);
+      cp_async16(kd, ksrc + (row0 + r) * p.ld_qkv + c * 8);
+      cp_async16(vd, vsrc + (row0 + r) * p.ld_qkv + c * 8);
+    } else {
+      *reinterpret_cast<uint4*>(kd) = zero;
+      *reinterpret_cast<uint4*>(vd) = zero;
     }
-    *reinterpret_cast<uint4*>(smem + kVOffK + (c >> 3) * 32768 + sw128_off(r, c & 7)) = k;
-    *reinterpret_cast<uint4*>(smem + kVOffV + (r >> 6) * 16384 + (c >> 3) * 8192 + sw128_off(r & 63, c & 7)) = v;
   }
-  fence_proxy_async_smem();  // generic-proxy stores -> tensor-core operand reads
+  cp_async_commit();
+  cp_async_wait_all();
+  fence_proxy_async_smem();  // shared-memory writes -> tensor-core operand reads
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -322,10 +358,9 @@ int launch_patches(const rfx_patches_desc& d, cudaStream_t stream, bool pdl) {
 }
 
 int launch_layer_norm(const rfx_layer_norm_desc& d, cudaStream_t stream, bool pdl) {
-  if (d.T < 1 || d.C < 64 || d.C % 64 || d.C > 4096 || !d.x || !d.y || !d.w || !d.b || d.ldx < d.C || d.ldx % 8 ||
-      d.ldy < d.C || d.ldy % 8 || !a16v(d.x) || !a16v(d.y) || (reinterpret_cast<uintptr_t>(d.w) & 7u) ||
-      (reinterpret_cast<uintptr_t>(d.b) & 7u))
-    return set_error(RFX_E_INVAL, "rfx_layer_norm: need C %% 64 == 0 (<= 4096), 16-byte aligned rows");
+  if (d.T < 1 || d.C < 8 || d.C % 8 || d.C > 2048 || !d.x || !d.y || !d.w || !d.b || d.ldx < d.C || d.ldx % 8 ||
+      d.ldy < d.C || d.ldy % 8 || !a16v(d.x) || !a16v(d.y) || !a16v(d.w) || !a16v(d.b))
+    return set_error(RFX_E_INVAL, "rfx_layer_norm: need C %% 8 == 0 (<= 2048), 16-byte aligned rows and vectors");
   LnParams p{static_cast<const __nv_bfloat16*>(d.x), d.ldx, d.w, d.b, d.eps, static_cast<__nv_bfloat16*>(d.y),
              d.ldy, d.T, d.C};
   return launch_kernel(reinterpret_cast<const void*>(layernorm_kernel), dim3((d.T + 7) / 8), dim3(256), 0, stream,

@@ -127,7 +127,7 @@ def test_vision_entry_points_reject_bad_shapes():
     a.N, a.D = 256, 76  # head dim not a multiple of 8
     assert lib.rfx_vit_attention(ctypes.byref(a), None) == _lib.RFX_E_INVAL
     n = _lib.LayerNormDesc()
-    n.T, n.C = 4, 1000  # C % 64 != 0
+    n.T, n.C = 4, 1004  # C % 8 != 0
     n.x = n.y = n.w = n.b = 1 << 20
     n.ldx = n.ldy = 1024
     assert lib.rfx_layer_norm(ctypes.byref(n), None) == _lib.RFX_E_INVAL
