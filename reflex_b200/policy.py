@@ -13,11 +13,15 @@ rfx engines (the denoising half of Reflex's PI0.5 / PI0 policies).
   modeling_pi0.py:740-845, 1001-1040 (``sample_actions`` and
   ``predict_action_chunk`` without ``incremental_input``).
 
-What enters where the reference starts from raw observations: the vision
-tower with its projector and the language embedding table are not part of
-this library, so ``images`` are the observation's image embeddings
-[B, frame_len, vlm_width] (one frame: every camera's patch embeddings) and
-``tokens`` are the instruction's token embeddings [B, n_lang, vlm_width].
+What enters where the reference starts from raw observations: ``images``
+are either the cameras' images (a list of [B, 3, 224, 224] tensors, one per
+camera, or one [B, n_cams, 3, 224, 224] tensor), which a model built with a
+``vision`` tower (reflex_b200.vision.VisionTower, the SigLIP tower and
+projector of ``get_image_features``, modeling_pi05.py:141-158,244) turns into
+image tokens, or the image tokens themselves [B, frame_len, vlm_width] (one
+frame: every camera's 256 tokens, cameras in order).  The language embedding
+table is not part of this library: ``tokens`` are the instruction's token
+embeddings [B, n_lang, vlm_width].
 With prefix-layer weights the model runs them through the prefix layers
 into the KV rings (PrefixEngine: the instruction once, each frame into the
 sliding window, the oldest frame evicted); without them the caller fills the
@@ -50,7 +54,8 @@ class PI05Model:
 
     def __init__(self, cfg: ExpertConfig, weights: dict, *, prefix_cfg: ExpertConfig | None = None,
                  prefix_weights: dict | None = None, batch: int = 1, n_lang: int = 0, frame_len: int = 0,
-                 window_frames: int = 2, capacity: int | None = None, device="cuda", fused: bool | None = None):
+                 window_frames: int = 2, capacity: int | None = None, device="cuda", fused: bool | None = None,
+                 vision=None):
         if cfg.variant != self.variant:
             raise ValueError(f"{type(self).__name__} needs a {self.variant} config")
         cap = capacity or max(1, n_lang + window_frames * frame_len)
@@ -74,6 +79,7 @@ class PI05Model:
                                        frame_len=frame_len, window_frames=window_frames, batch=batch, device=device)
         self.frames_seen = 0
         self.has_instruction = False
+        self.vision = vision
 
     # ------------------------------------------------------------ prefix ---
     @property
@@ -93,7 +99,25 @@ class PI05Model:
         if n_tokens != self.prefix_length:
             raise ValueError(f"{n_tokens} prefix tokens, the layout gives {self.prefix_length}")
 
+    def embed_images(self, images):
+        """Camera images -> image tokens [B, n_cams * 256, proj_dim] through the
+        vision tower (cameras batched into one call, in camera order as the
+        reference concatenates them, modeling_pi05.py:236-253); image tokens
+        pass through unchanged."""
+        if images is None:
+            return None
+        if isinstance(images, (list, tuple)):
+            images = torch.stack([torch.as_tensor(im) for im in images], 1)
+        if images.dim() != 5:
+            return images
+        if self.vision is None:
+            raise ValueError("camera images given but the model has no vision tower")
+        B, nc = images.shape[:2]
+        feats = self.vision.get_image_features(images.reshape(B * nc, *images.shape[2:]))
+        return feats.reshape(B, nc * feats.shape[1], feats.shape[2])
+
     def _prefill(self, images, tokens, incremental_input: bool) -> None:
+        images = self.embed_images(images)
         if tokens is not None and (not incremental_input or not self.has_instruction):
             if self.instruction is None:
                 raise ValueError("instruction embeddings given but the model has no prefix-layer weights")

@@ -218,3 +218,33 @@ def test_select_action_queue():
     assert torch.equal(acts[5], chunk[:, 0])
     pol.reset()
     assert len(pol._action_queue) == 0
+
+
+def test_sample_actions_from_camera_images():
+    """Camera images through the model's vision tower (SigLIP + projector,
+    2 layers at full widths) give the same actions as passing that tower's
+    image tokens (the path the other tests check against the oracle), with
+    the cameras' tokens concatenated in camera order."""
+    from reflex_b200.config import VisionConfig
+    from reflex_b200.policy import PI05Model
+    from reflex_b200.vision import VisionTower
+    cfg = pi05_config(num_layers=2, adarms="gate", quant_mode="i8_sym")
+    vcfg = vlm_config(num_layers=2)
+    viscfg = VisionConfig(num_layers=2)
+    tower = VisionTower(viscfg, synthetic.vision_weights(viscfg, seed=40), max_images=2)
+    n_lang, ncam = 16, 2
+    wts = synthetic.expert_weights(cfg, seed=0)
+    pw = synthetic.prefix_weights(vcfg, seed=10)
+    kw = dict(prefix_cfg=vcfg, prefix_weights=pw, n_lang=n_lang, frame_len=ncam * viscfg.tokens, window_frames=2)
+    with_tower = PI05Model(cfg, wts, vision=tower, **kw)
+    plain = PI05Model(cfg, wts, **kw)
+    lang = synthetic.frame_embeddings(vcfg, n_lang, seed=21).cuda()
+    cams = [synthetic.images(viscfg, B=1, seed=50 + i) for i in range(ncam)]
+    x0 = synthetic.noise(cfg, seed=2).cuda()
+    a1 = with_tower.sample_actions([c.cuda() for c in cams], None, lang, None, None, noise=x0).clone()
+    tokens = tower.get_image_features(torch.cat(cams).cuda()).reshape(1, ncam * viscfg.tokens, -1).clone()
+    a2 = plain.sample_actions(tokens, None, lang, None, None, noise=x0)
+    torch.cuda.synchronize()
+    assert torch.equal(a1, a2)
+    with pytest.raises(ValueError):
+        plain.sample_actions(torch.stack(cams, 1).cuda(), None, None, None, None, noise=x0, incremental_input=True)
