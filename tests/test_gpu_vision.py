@@ -164,3 +164,24 @@ def test_tower_plan_counts_and_bad_input():
         t.get_image_features(torch.zeros(3, 3, 224, 224))
     with pytest.raises(ValueError):
         t.get_image_features(torch.zeros(1, 3, 112, 112))
+
+
+def test_tower_small_images_ragged_tokens():
+    """112 x 112 images (8 x 8 = 64 patches, a 64-entry position table): the
+    attention's single query tile is mostly past N and its keys past N are
+    masked.  Two layers, two images, against the oracle's bf16-rounding model
+    within four bf16 steps (2^-8 relative each) at the tokens' largest
+    magnitude."""
+    cfg = VisionConfig(num_layers=2, image=112)
+    w = synthetic.vision_weights(cfg, seed=60)
+    img = synthetic.images(cfg, B=2, seed=61)
+    from reflex_b200.vision import VisionTower
+    t = VisionTower(cfg, w, max_images=2)
+    out = t.get_image_features(img.cuda()).float().cpu()
+    torch.cuda.synchronize()
+    assert K.device_status() == 0
+    assert out.shape == (2, 64, cfg.proj_dim)
+    with torch.no_grad():
+        ref = ov.image_features(cfg, w, img, bf16=True)
+    err = (out - ref).abs().max().item()
+    assert err < 4 * 2 ** -8 * max(1.0, ref.abs().max().item()), err
