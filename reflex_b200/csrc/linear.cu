@@ -772,7 +772,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
             waited = true;
           }
           tma_load_2d(st + kWTileBytes, &tmX, &full[s], kc * kBK, n0);
-          if (issued == 0) trace(p, kTrPdl);
           ++issued;
         }
       }
@@ -796,7 +795,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
         for (int kc = kc0; kc < kc1; ++kc, ++it) {
           const int s = it % kPStages;
           if (!(ok = mbar_wait(&full[s], (it / kPStages) & 1, p.status, kDevTimeoutTmaFull))) break;
-          if (it == 0) trace(p, kTrFirstFull);
           tc_fence_after();
           const uint64_t off = static_cast<uint64_t>((s * kPStage) >> 4);
 #pragma unroll
@@ -805,7 +803,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[buf]);
-        if (tl == 0) trace(p, kTrMmaIssued);
       }
     }
   } else {
@@ -843,7 +840,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
           : "r"(ok ? 1u : 0u)
           : "memory");
       if (!all) break;
-      if (tl == 0 && et == 0) trace(p, kTrAcc);
       tc_fence_after();
       const uint32_t acc = tmem + buf * NT + lane_base;
       bool split_last = false;
@@ -877,7 +873,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
           *last_s = old == p.ksplit - 1 ? 1 : 0;
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (tl == 0 && et == 0) trace(p, kTrRed);
         split_last = *last_s != 0;
         if (!split_last) continue;
         __threadfence();
@@ -912,7 +907,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<float4*>(red + (8 * j + (et >> 5)) * kRedLd + 4 * lane) = sum[j];
-          if (tl == 0 && h == 0 && et == 0) trace(p, kTrCluster);
         } else {
           uint32_t r[2][16];
 #pragma unroll
@@ -956,7 +950,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) cur[u] = nxt[u];
         asm volatile("bar.sync 1, 256;" ::: "memory");  // red is free again
-        if (tl == 0 && h == 0 && et == 0) trace(p, kTrEpi);
       }
     }
   }
@@ -1136,17 +1129,22 @@ int validate(const rfx_linear_desc& d) {
 namespace {
 // K splits of the persistent kernel's tiles: the count (1..4) that finishes
 // the units soonest, waves of units x their length (1 / ksplit) plus a tenth
-// of a unit for the partials' round trip.  A split keeps at least 8 k-steps
-// (a 400-token o_proj, K = 2048, as 4 x 8: 15.8 us against 17.1 us for the
-// per-tile kernel's in-cluster split; the 8- and 16-stream chunks 2-3 %
-// faster than with a 32-step floor), and the partial slots stay within 64 MB.
+// of a unit for the partials' round trip.  A split keeps at least 8 k-steps,
+// and at least 32 when it adds a round of units: a short split unit costs
+// about as much as a long one (its partial store, the sum and the epilogue
+// dominate), so it pays only where it fills idle SMs in the same round (a
+// 400-token o_proj, K = 2048, as 4 x 8 k-steps: 15.8 us against 17.1 us for
+// the per-tile kernel's in-cluster split; the same rule at 1600 tokens would
+// have tripled the rounds).  The partial slots stay within 64 MB.
 constexpr int kSplitMaxTiles = 16384;  // tiles the fixed counter block serves
 int pick_ksplit(int tiles, int k_chunks, int nt, int nsm) {
   int best = 1;
   double best_t = static_cast<double>((tiles + nsm - 1) / nsm);
   if (tiles > kSplitMaxTiles) return 1;
+  const int rounds1 = (tiles + nsm - 1) / nsm;
   for (int s = 2; s <= 4; ++s) {
     if (k_chunks / s < 8 || static_cast<size_t>(tiles) * s * nt * 128 * 4 > (size_t(64) << 20)) break;
+    if (tiles * s > rounds1 * nsm && k_chunks / s < 32) continue;
     const double t = static_cast<double>((tiles * s + nsm - 1) / nsm) / s + 0.1;
     if (t < best_t - 1e-9) {
       best_t = t;
