@@ -87,7 +87,7 @@ enum {
 };
 
 __device__ __forceinline__ void trace(const AttnParams& p, int ev) {
-  if (p.trace)
+  if (kTraceBuilt && p.trace)
     p.trace[((static_cast<long>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 16 + ev] =
         globaltimer_ns();
 }

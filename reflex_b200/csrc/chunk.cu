@@ -330,7 +330,7 @@ __device__ __forceinline__ void workers_publish(const ChunkParams& p, int et, in
 }
 
 __device__ __forceinline__ void stamp(unsigned long long* slot, int k) {
-  if (slot) slot[k] = globaltimer_ns();
+  if (kTraceBuilt && slot) slot[k] = globaltimer_ns();
 }
 
 // ---------------------------------------------------------------- math ---
@@ -1504,13 +1504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d_hint(smem + s * kWBytes, wmap(maps, op), &full[s], (kb0 + j) * kBK, wrow, pol);
               ++armed;
             }
-            if (p.trace && tau == 0 && i < p.trace_tasks)
+            if (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks)
               p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 7] = globaltimer_ns();
             int line;
             unsigned target;
             gemm_input(p, op, use, &line, &target);
             if (ok) ok = ctr_wait(p, line, target);
-            if (p.trace && tau == 0 && i < p.trace_tasks)
+            if (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks)
               p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 3] = globaltimer_ns();
             fence_proxy_async_global();
             // armed stages get their activation tile even after a failed wait,
@@ -1520,7 +1520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(smem + kOffX + s * kXBytes, xmap(maps, op), &full[s], (kb0 + j) * kBK, 0);
             }
             issued += armed;
-            if (p.trace && tau == 0 && i < p.trace_tasks && nw == nkb)
+            if (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks && nw == nkb)
               p.trace[(static_cast<long>(cta) * p.trace_tasks + i) * 16 + 13] = globaltimer_ns();
             for (int j = nw; j < nkb && ok; ++j) {
               const uint32_t ii = issued;
@@ -1539,7 +1539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = bar_wait(p, &empty[ii % kStages], (ii / kStages) & 1, kDevTimeoutStageEmpty);
             if (!ok) break;
             unsigned long long* pts =
-                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                            : nullptr;
             stamp(pts, 12);
             const int b = tk.y, qt = tk.z;
@@ -1619,7 +1619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++tmem_uses;
             tc_fence_after();
             unsigned long long* mts =
-                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                            : nullptr;
             unsigned long long waited = 0;
             for (int j = 0; j < nkb && ok; ++j) {
@@ -1657,7 +1657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = bar_wait(p, q_full, q_cnt & 1, kDevTimeoutTmaFull);
             ++q_cnt;
             unsigned long long* mts =
-                (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+                (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                            : nullptr;
             stamp(mts, 14);
             for (int jl = 0; jl < nbl && ok; ++jl) {
@@ -1703,7 +1703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ty = task_type(tk), layer = task_layer(tk);
         const unsigned use = static_cast<unsigned>(tau * p.NL + layer);
         unsigned long long* ts =
-            (p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
+            (kTraceBuilt && p.trace && tau == 0 && i < p.trace_tasks) ? p.trace + (static_cast<long>(cta) * p.trace_tasks + i) * 16
                                                        : nullptr;
         if (et == 0) {
           stamp(ts, 0);

@@ -110,7 +110,7 @@ struct LinParams {
 };
 
 __device__ __forceinline__ void trace(const LinParams& p, int ev) {
-  if (p.trace) p.trace[static_cast<long>(blockIdx.x) * 16 + ev] = globaltimer_ns();
+  if (kTraceBuilt && p.trace) p.trace[static_cast<long>(blockIdx.x) * 16 + ev] = globaltimer_ns();
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {

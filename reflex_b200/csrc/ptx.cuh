@@ -33,6 +33,16 @@ enum DeviceError : int {
 // A wait gives up after this many nanoseconds (about one second).
 constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 
+// The %globaltimer phase stamps behind rfx_set_trace are compiled only into a
+// library built with -DRFX_TRACE (make EXTRA_NVFLAGS=-DRFX_TRACE): even
+// untaken, the stamp code in the executor's and the GEMMs' loops cost 2-3 %
+// of a chunk.
+#ifdef RFX_TRACE
+constexpr bool kTraceBuilt = true;
+#else
+constexpr bool kTraceBuilt = false;
+#endif
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

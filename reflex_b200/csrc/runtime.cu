@@ -207,6 +207,10 @@ extern "C" const char* rfx_last_error(void) { return g_last_error; }
 
 extern "C" int rfx_set_trace(void* buf, size_t bytes) {
   if (buf && (reinterpret_cast<uintptr_t>(buf) & 7u)) return set_error(RFX_E_INVAL, "rfx_set_trace: 8-byte alignment");
+  if (buf && !kTraceBuilt)
+    return set_error(RFX_E_UNSUPPORTED,
+                     "rfx_set_trace: this library was built without the phase stamps; rebuild it with "
+                     "make -C reflex_b200/csrc EXTRA_NVFLAGS=-DRFX_TRACE");
   g_trace_bytes.store(buf ? bytes : 0);
   g_trace_buf.store(buf);
   return RFX_OK;

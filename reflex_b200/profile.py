@@ -39,7 +39,8 @@ def main():
     ap.add_argument("--chunk", action="store_true", help="run whole chunks instead of single ops")
     ap.add_argument("--fused", action="store_true", help="with --chunk: the persistent chunk executor")
     ap.add_argument("--trace", action="store_true",
-                    help="with --chunk --fused: %%globaltimer stamps of every task of the first Euler step")
+                    help="with --chunk --fused: %%globaltimer stamps of every task of the first Euler step "
+                         "(needs a library built with make -C reflex_b200/csrc EXTRA_NVFLAGS=-DRFX_TRACE)")
     ap.add_argument("--trace-out", default=None, help="with --trace: also save the raw stamps (.npy)")
     ap.add_argument("--frame", action="store_true",
                     help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
