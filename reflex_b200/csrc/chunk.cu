@@ -708,7 +708,7 @@ __device__ __forceinline__ void convert16r(uint4 raw, uint8_t* tile_base, int ke
   *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-template <int V>
+template <int V, bool DBG>
 __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int layer,
                             unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, uint32_t& kvn_cnt,
                             uint32_t& stg_cnt, unsigned long long* ts) {
@@ -1074,7 +1074,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
             w8[e] = pack_bf16x2(__uint_as_float(rr[q][2 * e]) * inv_l, __uint_as_float(rr[q][2 * e + 1]) * inv_l);
           *reinterpret_cast<uint4*>(orow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
           *reinterpret_cast<uint4*>(orow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-          if (p.dbg_attn && use < static_cast<unsigned>(p.NL)) {
+          if (DBG && p.dbg_attn && use < static_cast<unsigned>(p.NL)) {
             __nv_bfloat16* drow = p.dbg_attn + static_cast<long>(use) * p.T * p.Hq * kD + (orow - p.attn_out);
             *reinterpret_cast<uint4*>(drow + c * 16) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
             *reinterpret_cast<uint4*>(drow + c * 16 + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
@@ -1105,6 +1105,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
 }
 
 // ------------------------------------------------------ worker: combine ---
+template <bool DBG>
 __device__ __forceinline__ bool worker_comb(const ChunkParams& p, uint8_t* smem, int et, unsigned use, int b, int qt,
                                             int r0, int r1, unsigned long long* ts) {
   if (!workers_ctr_wait(p, et, kCAttn, static_cast<unsigned>(p.n_attn) * (use + 1))) return false;
@@ -1182,7 +1183,7 @@ __device__ __forceinline__ bool worker_comb(const ChunkParams& p, uint8_t* smem,
     const uint4 packed = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
                                     pack_bf16x2(y[6], y[7]));
     *reinterpret_cast<uint4*>(orow) = packed;
-    if (p.dbg_attn && use < static_cast<unsigned>(p.NL))
+    if (DBG && p.dbg_attn && use < static_cast<unsigned>(p.NL))
       *reinterpret_cast<uint4*>(p.dbg_attn + static_cast<long>(use) * p.T * p.Hq * kD + (orow - p.attn_out)) = packed;
   }
   workers_sync();  // the buffer is read before any later use of it
@@ -1265,7 +1266,7 @@ __device__ __noinline__ bool worker_fin_at(const ChunkParams& p, uint8_t* small,
 // PI0's kTFinAt1 (action_time_mlp_in: bias + SiLU) and kTFinAt2
 // (action_time_mlp_out: bias, or the state token's embedding, then the first
 // layer's input norm).
-template <int V>
+template <int V, bool DBG>
 __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small, int et, int kind, int tau, int layer, int t,
                            unsigned long long* ts) {
   const int lane = et & 31, wq = et >> 5;
@@ -1313,7 +1314,7 @@ __device__ __forceinline__ bool worker_fin(const ChunkParams& p, uint8_t* small,
       hv[e] = bf16_round(__fadd_rn(hres[e], ga));
     }
   }
-  if (kind == kTFinD && tau == 0 && p.dbg_h)
+  if (DBG && kind == kTFinD && tau == 0 && p.dbg_h)
     *reinterpret_cast<uint2*>(p.dbg_h + (static_cast<long>(layer) * p.T + t) * p.W + f0) = pack4_bf16(hv);
   if (tail) {
     if (sa < 0) {
@@ -1409,8 +1410,10 @@ __device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigne
   }
 }
 
-// V: kPi05 or kPi0 (PI0's code paths are compiled only into its instantiation)
-template <int V>
+// V: kPi05 or kPi0 (PI0's code paths are compiled only into its instantiation);
+// DBG: the instantiation that also writes the per-layer debug outputs
+// (debug_hidden / debug_attn), kept out of the other one's loops
+template <int V, bool DBG>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_kernel(const __grid_constant__ Maps maps, const __grid_constant__ ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -1696,7 +1699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < n_init && ok; ++i)
       ok = V == kPi0 ? worker_fin_at(p, small, et, kTInit, 0, itasks[i].y, nullptr)
-                     : worker_fin<V>(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
+                     : worker_fin<V, DBG>(p, small, et, kTInit, 0, 0, itasks[i].y, nullptr);
     for (int tau = 0; tau < p.steps && ok; ++tau) {
       for (int i = 0; i < n_step && ok; ++i) {
         const int4 tk = stasks[i];
@@ -1719,10 +1722,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = worker_gemm(p, smem, small, tmem, et, gemm_op(ty), layer, tk.y, tk.z, acc_cnt, pair_cnt, ts);
             break;
           case kTAttn:
-            ok = worker_attn<V>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
+            ok = worker_attn<V, DBG>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
             break;
-          case kTComb: ok = worker_comb(p, smem, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
-          case kTFinO: case kTFinD: ok = worker_fin<V>(p, small, et, ty, tau, layer, tk.y, ts); break;
+          case kTComb: ok = worker_comb<DBG>(p, smem, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
+          case kTFinO: case kTFinD: ok = worker_fin<V, DBG>(p, small, et, ty, tau, layer, tk.y, ts); break;
           case kTFinAt1: case kTFinAt2:
             if (V == kPi0) ok = worker_fin_at(p, small, et, ty, tau, tk.y, ts);
             break;
@@ -1773,6 +1776,13 @@ constexpr int kSplitsQkv = 2, kSplitsO = 8, kSplitsGu = 2, kSplitsDown = 8;
 constexpr int kMaxSplits = 64;  // attention key-range splits (the combine holds two per lane)
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// The executor instantiation of a variant, with or without the debug outputs.
+using ChunkFn = void (*)(const Maps, const ChunkParams);
+ChunkFn chunk_fn(int variant, bool dbg) {
+  if (variant == kPi0) return dbg ? chunk_kernel<kPi0, true> : chunk_kernel<kPi0, false>;
+  return dbg ? chunk_kernel<kPi05, true> : chunk_kernel<kPi05, false>;
+}
 
 struct Layout {
   int T, S, q_tiles, n_ctx_blocks, n_blocks, splits, n_attn, n_comb;
@@ -2187,8 +2197,8 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
     rc = make_tmap_2d(&c->maps.q, p.q, 2, kD, static_cast<uint64_t>(d.B) * d.num_q_heads * L.S, kD * 2, 64, kQR, true);
   if (!rc) rc = make_tmap_2d(&c->maps.kn, p.kn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
   if (!rc) rc = make_tmap_2d(&c->maps.vn, p.vn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
-  const void* kfn = d.variant == RFX_CHUNK_PI0 ? reinterpret_cast<const void*>(chunk_kernel<kPi0>)
-                                                : reinterpret_cast<const void*>(chunk_kernel<kPi05>);
+  const void* kfn = reinterpret_cast<const void*>(
+      chunk_fn(d.variant == RFX_CHUNK_PI0 ? kPi0 : kPi05, d.debug_hidden != nullptr || d.debug_attn != nullptr));
   if (!rc) rc = ensure_smem_attr(kfn, kSmemBytes);
   // the smallest shared-memory carveout that holds the kernel (164 of 228 KB),
   // so the rest of the unified L1 caches local memory and global loads
@@ -2236,9 +2246,8 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (c->params.variant == kPi0)
-    return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel<kPi0>, c->maps, c->params), "rfx_chunk_run: launch");
-  return check_cuda(cudaLaunchKernelEx(&cfg, chunk_kernel<kPi05>, c->maps, c->params), "rfx_chunk_run: launch");
+  const ChunkFn fn = chunk_fn(c->params.variant, c->params.dbg_h != nullptr || c->params.dbg_attn != nullptr);
+  return check_cuda(cudaLaunchKernelEx(&cfg, fn, c->maps, c->params), "rfx_chunk_run: launch");
 }
 
 extern "C" int rfx_chunk_destroy(rfx_chunk* c) {
