@@ -708,7 +708,14 @@ __device__ __forceinline__ void convert16r(uint4 raw, uint8_t* tile_base, int ke
   *reinterpret_cast<uint4*>(atom + sw128_offset(key, c0 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-template <int V, bool DBG>
+// Context-scheme instantiations of the attention worker: any scheme (read
+// from the parameters) or int8 with fp32 scales fixed at compile time.  The
+// fixed one is used for PI0, whose items walk 2-3 staged blocks each (its
+// chunk 10.63 -> 10.38 ms); for PI0.5 (one block per item) the register
+// allocation of the generic one came out 0.4 % faster.
+constexpr int kScAny = 0, kScI8F32 = 1;
+
+template <int V, bool DBG, int SC>
 __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem, uint8_t* small, uint32_t tmem, int et, int layer,
                             unsigned use, int b, int qt, int sp, uint32_t& blk_cnt, uint32_t& kvn_cnt,
                             uint32_t& stg_cnt, unsigned long long* ts) {
@@ -744,7 +751,8 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
   // block of this query row among the new tokens: new key j is visible iff
   // new_block[j] <= it (PI0's state token does not see the action tokens)
   const int my_block = (V == kPi0 && row_valid && p.new_block) ? p.new_block[s_row] : 0;
-  const bool sbf16 = p.scale_bf16 != 0;
+  const bool sbf16 = SC == kScI8F32 ? false : p.scale_bf16 != 0;
+  const int mode = SC == kScI8F32 ? static_cast<int>(kQuantI8Sym) : p.mode;
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
@@ -763,7 +771,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     if (et >= 64 || j >= p.n_ctx_blocks || !async_sc) return;
     const long slot = static_cast<long>(j) * kKB + et;
     const long gi = static_cast<long>(b) * p.cap + (slot < p.cap ? slot : p.cap - 1);
-    if (p.mode == kQuantI8Sym) {
+    if (mode == kQuantI8Sym) {
       cp_async4(sc + et, static_cast<const float*>(p.k_scale[layer]) + gi);
       cp_async4(sc + 64 + et, static_cast<const float*>(p.v_scale[layer]) + gi);
     } else {
@@ -789,7 +797,7 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
         sc[384 + et] = load_scalar(p.k_zp[layer], gi, true);
         sc[448 + et] = load_scalar(p.v_zp[layer], gi, true);
       }
-      if (p.mode == kQuantI8Sym) {
+      if (mode == kQuantI8Sym) {
         sc[et] = valid ? sc[et] * p.scale_log2 : 0.f;
         sc[64 + et] = valid ? sc[64 + et] : 0.f;
       } else {
@@ -823,13 +831,13 @@ __device__ __forceinline__ bool worker_attn(const ChunkParams& p, uint8_t* smem,
     if (j < p.n_ctx_blocks) {
       const float* dq = sc + 256 + half * 64;
       const float* zq = sc + 384 + half * 64;
-      const bool u8 = p.mode != kQuantI8Sym;
+      const bool u8 = mode != kQuantI8Sym;
 #pragma unroll 4
       for (int q = 0; q < 4; ++q) {
         const int it = et + q * kWorkers;  // 0..1023: 16 chunks of 16 bytes per key
         const int key = it >> 4, g = it & 15;
         const uint4 raw = *reinterpret_cast<const uint4*>(stg + half * kStgBytes + key * kD + g * 16);
-        convert16r(raw, tile, key, g, p.mode, sbf16, u8 ? dq[key] : 0.f, u8 ? zq[key] : 0.f);
+        convert16r(raw, tile, key, g, mode, sbf16, u8 ? dq[key] : 0.f, u8 ? zq[key] : 0.f);
       }
     } else {
       const int nb0 = (j - p.n_ctx_blocks) * kKB;
@@ -1412,8 +1420,9 @@ __device__ __forceinline__ void gemm_input(const ChunkParams& p, int op, unsigne
 
 // V: kPi05 or kPi0 (PI0's code paths are compiled only into its instantiation);
 // DBG: the instantiation that also writes the per-layer debug outputs
-// (debug_hidden / debug_attn), kept out of the other one's loops
-template <int V, bool DBG>
+// (debug_hidden / debug_attn), kept out of the other one's loops; SC: the
+// attention worker's context scheme (kScAny or kScI8F32)
+template <int V, bool DBG, int SC>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_kernel(const __grid_constant__ Maps maps, const __grid_constant__ ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -1722,7 +1731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = worker_gemm(p, smem, small, tmem, et, gemm_op(ty), layer, tk.y, tk.z, acc_cnt, pair_cnt, ts);
             break;
           case kTAttn:
-            ok = worker_attn<V, DBG>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
+            ok = worker_attn<V, DBG, SC>(p, smem, small, tmem, et, layer, use, tk.y, tk.z, tk.w, blk_cnt, kvn_cnt, stg_cnt, ts);
             break;
           case kTComb: ok = worker_comb<DBG>(p, smem, et, use, tk.y, tk.z, tk.w >> 16, tk.w & 0xffff, ts); break;
           case kTFinO: case kTFinD: ok = worker_fin<V, DBG>(p, small, et, ty, tau, layer, tk.y, ts); break;
@@ -1779,9 +1788,12 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // The executor instantiation of a variant, with or without the debug outputs.
 using ChunkFn = void (*)(const Maps, const ChunkParams);
-ChunkFn chunk_fn(int variant, bool dbg) {
-  if (variant == kPi0) return dbg ? chunk_kernel<kPi0, true> : chunk_kernel<kPi0, false>;
-  return dbg ? chunk_kernel<kPi05, true> : chunk_kernel<kPi05, false>;
+ChunkFn chunk_fn(int variant, bool dbg, bool i8_f32) {
+  if (variant == kPi0) {
+    if (i8_f32) return dbg ? chunk_kernel<kPi0, true, kScI8F32> : chunk_kernel<kPi0, false, kScI8F32>;
+    return dbg ? chunk_kernel<kPi0, true, kScAny> : chunk_kernel<kPi0, false, kScAny>;
+  }
+  return dbg ? chunk_kernel<kPi05, true, kScAny> : chunk_kernel<kPi05, false, kScAny>;
 }
 
 struct Layout {
@@ -2198,7 +2210,8 @@ extern "C" int rfx_chunk_create(const rfx_chunk_desc* desc, void* workspace, siz
   if (!rc) rc = make_tmap_2d(&c->maps.kn, p.kn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
   if (!rc) rc = make_tmap_2d(&c->maps.vn, p.vn, 2, kD, static_cast<uint64_t>(T), kD * 2, 64, kKB, true);
   const void* kfn = reinterpret_cast<const void*>(
-      chunk_fn(d.variant == RFX_CHUNK_PI0 ? kPi0 : kPi05, d.debug_hidden != nullptr || d.debug_attn != nullptr));
+      chunk_fn(d.variant == RFX_CHUNK_PI0 ? kPi0 : kPi05, d.debug_hidden != nullptr || d.debug_attn != nullptr,
+               d.quant_mode == RFX_QUANT_I8_SYM && d.scale_dtype == RFX_DTYPE_F32));
   if (!rc) rc = ensure_smem_attr(kfn, kSmemBytes);
   // the smallest shared-memory carveout that holds the kernel (164 of 228 KB),
   // so the rest of the unified L1 caches local memory and global loads
@@ -2246,7 +2259,8 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const ChunkFn fn = chunk_fn(c->params.variant, c->params.dbg_h != nullptr || c->params.dbg_attn != nullptr);
+  const ChunkFn fn = chunk_fn(c->params.variant, c->params.dbg_h != nullptr || c->params.dbg_attn != nullptr,
+                              c->params.mode == kQuantI8Sym && !c->params.scale_bf16);
   return check_cuda(cudaLaunchKernelEx(&cfg, fn, c->maps, c->params), "rfx_chunk_run: launch");
 }
 
