@@ -78,9 +78,19 @@ int rfx_set_wait_limit_ns(unsigned long long ns);
  * launched afterwards by this process. Default: enabled. */
 int rfx_set_pdl(int enable);
 
+/* Diagnostics: 0 launches the chunk executor (rfx_chunk_run) without the
+ * cooperative attribute, for profilers that cannot replay a cooperative
+ * launch; 1 (the default) restores it.  The executor still needs all of its
+ * CTAs (one per SM) resident at once, which a launch on an otherwise idle GPU
+ * gets; when they are not, its bounded waits (rfx_set_wait_limit_ns) end the
+ * launch with a device status.  No counterpart in the reference. */
+int rfx_set_chunk_cooperative(int enable);
+
 /* Diagnostics: when `buf` (device, 8-byte aligned, `bytes` long) is set, the
- * linear and attention kernels record a %globaltimer stamp (ns) per phase per
- * CTA at buf[cta * 16 + event]; NULL turns tracing off. */
+ * linear, attention and chunk-executor kernels record a %globaltimer stamp
+ * (ns) per phase per CTA (the executor: per task) at buf[cta * 16 + event];
+ * NULL turns tracing off.  The stamps exist only in a library built with
+ * -DRFX_TRACE; without them a non-NULL `buf` returns RFX_E_UNSUPPORTED. */
 int rfx_set_trace(void* buf, size_t bytes);
 
 /* Number of streaming multiprocessors of the current device. */

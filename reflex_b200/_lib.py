@@ -213,6 +213,7 @@ SIGNATURES = {
     "rfx_embed_cache_check": ([POINTER(EmbedCacheDesc), c_void_p], c_int),
     "rfx_set_wait_limit_ns": ([ctypes.c_ulonglong], c_int),
     "rfx_set_trace": ([c_void_p, c_size_t], c_int),
+    "rfx_set_chunk_cooperative": ([c_int], c_int),
     "rfx_num_sms": ([POINTER(c_int)], c_int),
     "rfx_kv_quant_append": ([POINTER(KvQuantDesc), c_void_p], c_int),
     "rfx_linear": ([POINTER(LinearDesc), c_void_p], c_int),

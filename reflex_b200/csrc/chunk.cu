@@ -2257,8 +2257,12 @@ extern "C" int rfx_chunk_run(rfx_chunk* c, void* stream) {
   attr[1].val.clusterDim.x = 2;
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  // without the cooperative attribute (rfx_set_chunk_cooperative(0), for
+  // profilers that cannot replay a cooperative launch) only the cluster shape
+  // is given
+  const bool coop = chunk_cooperative();
+  cfg.attrs = coop ? attr : attr + 1;
+  cfg.numAttrs = coop ? 2 : 1;
   const ChunkFn fn = chunk_fn(c->params.variant, c->params.dbg_h != nullptr || c->params.dbg_attn != nullptr,
                               c->params.mode == kQuantI8Sym && !c->params.scale_bf16);
   return check_cuda(cudaLaunchKernelEx(&cfg, fn, c->maps, c->params), "rfx_chunk_run: launch");

@@ -24,6 +24,7 @@ void* trace_buffer(size_t n_events);
 
 // Whether kernels are launched with programmatic dependent launch.
 bool pdl_enabled();
+bool chunk_cooperative();
 
 // Bound (ns) of device waits on work of other CTAs (rfx_set_wait_limit_ns).
 unsigned long long dependency_wait_limit_ns();

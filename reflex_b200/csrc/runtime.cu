@@ -17,6 +17,7 @@ namespace rfx {
 namespace {
 thread_local char g_last_error[512] = "";
 std::atomic<bool> g_pdl{true};
+std::atomic<bool> g_chunk_coop{true};
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -33,6 +34,7 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+bool chunk_cooperative() { return g_chunk_coop.load(std::memory_order_relaxed); }
 
 namespace {
 std::atomic<unsigned long long> g_dep_wait_ns{kWaitLimitNs};
@@ -218,6 +220,11 @@ extern "C" int rfx_set_trace(void* buf, size_t bytes) {
 
 extern "C" int rfx_set_wait_limit_ns(unsigned long long ns) {
   g_dep_wait_ns.store(ns == 0 ? kWaitLimitNs : ns);
+  return RFX_OK;
+}
+
+extern "C" int rfx_set_chunk_cooperative(int enable) {
+  g_chunk_coop.store(enable != 0);
   return RFX_OK;
 }
 

@@ -42,6 +42,9 @@ def main():
                     help="with --chunk --fused: %%globaltimer stamps of every task of the first Euler step "
                          "(needs a library built with make -C reflex_b200/csrc EXTRA_NVFLAGS=-DRFX_TRACE)")
     ap.add_argument("--trace-out", default=None, help="with --trace: also save the raw stamps (.npy)")
+    ap.add_argument("--noncoop", action="store_true",
+                    help="with --chunk --fused: launch the executor without the cooperative attribute (profilers "
+                         "that cannot replay cooperative launches) and with 20 ms bounds on its cross-CTA waits")
     ap.add_argument("--frame", action="store_true",
                     help="the ops of one prefix layer of the streaming frame update (768 new tokens over a 48-token "
                          "pinned prefix and a 2-frame window)")
@@ -51,6 +54,10 @@ def main():
     if args.quant_bulk:
         quant_bulk(args.reps)
         return
+    if args.noncoop:
+        from . import _lib as L
+        L.call("rfx_set_chunk_cooperative", 0)
+        L.call("rfx_set_wait_limit_ns", 20_000_000)
     if args.frame:
         frame_ops(args.ops, args.reps)
         return
