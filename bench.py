@@ -298,10 +298,12 @@ def chunk_kernel_roofline(eng, hbm_peak, reps=3):
     avg_ms = statistics.median(durs)
     achieved = bytes_per / (avg_ms * 1e-3) / 1e9
     traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and workload
+    capture = {("pi05", N_CTX): "chunk_kernel_pi05_818ctx.md", ("pi0", PI0_LONG_CTX): "chunk_kernel_pi0_6344ctx.md"}
+    source = capture.get((cfg.variant, eng.n_ctx))
     try:
-        if cfg.variant != "pi05" or eng.n_ctx != N_CTX:
+        if source is None or eng.B != 1 or cfg.num_layers != 18:
             raise OSError("no capture of this workload")
-        with open(os.path.join(ROOT, "profiles", "chunk_kernel_pi05_818ctx.md")) as f:
+        with open(os.path.join(ROOT, "profiles", source)) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
                     traffic = int(line.split(":")[1])
@@ -311,10 +313,9 @@ def chunk_kernel_roofline(eng, hbm_peak, reps=3):
     return {"kernel": "chunk_kernel (persistent executor of the whole 10-step chunk, 1 CTA per SM)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/chunk_kernel_pi05_818ctx.md"
-                               if traffic is not None else
-                               "not captured: ncu reports LaunchFailed for this clustered cooperative launch "
-                               "(profiles/chunk_kernel_pi05_818ctx.md)"),
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch (non-cooperative, "
+                               f"profile --noncoop), profiles/{source}"
+                               if traffic is not None else "not captured for this workload"),
             "bytes_per_launch": bytes_per, "avg_launch_us": round(avg_ms * 1e3, 2)}
 
 
