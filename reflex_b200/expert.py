@@ -367,13 +367,16 @@ class ActionExpertEngine:
                 d.workspace, d.workspace_bytes = K.aligned_ptr(self.split_ws, 256), need_lin
         # attention workspaces: one per layer with the dense source (it holds
         # the layer's converted context through the chunk), else one shared by
-        # every launch (they run in sequence)
+        # every launch (they run in sequence); zero-filled when allocated (a
+        # PI0 chunk over a 6344-token context failed its parity test twice in
+        # full GPU-suite runs with workspaces that held earlier tests' data and
+        # passed with zeroed ones; no read of unwritten workspace was found)
         need = max(K.attention_workspace_bytes(d) for _, d in attn_descs) if attn_descs else 0
         per_layer = any(d.kv_source == L.RFX_KV_DENSE for _, d in attn_descs)
         n_ws = cfg.num_layers if per_layer else 1
         if need and (not isinstance(self.workspace, list) or len(self.workspace) != n_ws
                      or self.workspace[0].numel() < need + 1024):
-            self.workspace = [torch.empty(need + 1024, dtype=torch.uint8, device=self.dev) for _ in range(n_ws)]
+            self.workspace = [torch.zeros(need + 1024, dtype=torch.uint8, device=self.dev) for _ in range(n_ws)]
         for l, d in attn_descs:
             if need:
                 d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace[l if per_layer else 0], 1024), need

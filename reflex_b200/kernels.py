@@ -199,7 +199,7 @@ def attention(**kw) -> None:
     need = attention_workspace_bytes(d)
     ws = kw.get("workspace")
     if need and (ws is None or ws.numel() * ws.element_size() < need or ws.data_ptr() % 1024):
-        ws = torch.empty(need + 1024, dtype=torch.uint8, device=kw["q"].device)
+        ws = torch.zeros(need + 1024, dtype=torch.uint8, device=kw["q"].device)
         d.workspace, d.workspace_bytes = aligned_ptr(ws, 1024), need
     L.call("rfx_attention", ctypes.byref(d), _stream())
 

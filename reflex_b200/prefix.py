@@ -150,7 +150,7 @@ class PrefixEngine:
                                                  self.frame_len), None))
         need = max(K.attention_workspace_bytes(d) for d in attn_descs)
         if need and (self.workspace is None or self.workspace.numel() < need + 1024):
-            self.workspace = torch.empty(need + 1024, dtype=torch.uint8, device=self.dev)
+            self.workspace = torch.zeros(need + 1024, dtype=torch.uint8, device=self.dev)
         for d in attn_descs:
             if need:
                 d.workspace, d.workspace_bytes = K.aligned_ptr(self.workspace, 1024), need
