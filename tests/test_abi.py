@@ -136,3 +136,17 @@ def test_vision_entry_points_reject_bad_shapes():
     p.image = p.out = 1 << 20
     p.ldo = 588  # not a multiple of 64
     assert lib.rfx_patches(ctypes.byref(p), None) == _lib.RFX_E_INVAL
+
+
+def test_diagnostic_switches():
+    """The phase stamps are left out of the default build, so asking for a
+    trace buffer is refused (RFX_E_UNSUPPORTED) rather than silently ignored;
+    turning tracing off and toggling the executor's cooperative launch need
+    no device."""
+    lib = _lib.load()
+    assert lib.rfx_set_trace(None, 0) == _lib.RFX_OK
+    assert lib.rfx_set_trace(1 << 20, 4096) == _lib.RFX_E_UNSUPPORTED
+    assert b"RFX_TRACE" in lib.rfx_last_error()
+    assert lib.rfx_set_trace(None, 0) == _lib.RFX_OK
+    assert lib.rfx_set_chunk_cooperative(0) == _lib.RFX_OK
+    assert lib.rfx_set_chunk_cooperative(1) == _lib.RFX_OK
