@@ -191,3 +191,20 @@ def test_vision_tower_matches_transformers_siglip():
     assert (out[0, :64] - torch.from_numpy(g["tokens64"])).abs().max().item() < FP32_ATOL
     assert (out[0].norm(dim=-1) - torch.from_numpy(g["tok_norm"])).abs().max().item() < 1e-3
     assert (out[0].mean(-1) - torch.from_numpy(g["tok_mean"])).abs().max().item() < FP32_ATOL
+
+
+def test_vision_patch_rows_are_the_convolution():
+    """The patch rows the CUDA path feeds to its GEMM, times the reshaped
+    convolution weight, equal the stride-14 14 x 14 convolution itself (the
+    order of pixels within a row matches the weight's (channel, y, x) order)."""
+    from oracle import vision as ov
+    from reflex_b200.config import VisionConfig
+
+    cfg = VisionConfig(num_layers=1, image=56)
+    w = synthetic.vision_weights(cfg, seed=3)
+    img = synthetic.images(cfg, B=2, seed=4)
+    pw = w["vision_model.embeddings.patch_embedding.weight"]
+    conv = torch.nn.functional.conv2d(img, pw, w["vision_model.embeddings.patch_embedding.bias"], stride=cfg.patch)
+    ref = conv.flatten(2).transpose(1, 2)
+    got = ov.patches(cfg, img) @ pw.reshape(cfg.width, -1).T + w["vision_model.embeddings.patch_embedding.bias"]
+    assert (got - ref).abs().max().item() < 1e-4
