@@ -474,6 +474,8 @@ IoParams io_params(const rfx_action_io_desc& d) {
 
 bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+}  // namespace
+
 int validate_io(const rfx_action_io_desc& d, bool tail) {
   if (d.B < 1 || d.S < 1 || d.action_dim < 8 || d.action_dim % 8 || d.action_dim > 256 || d.width < 256 ||
       d.width % 256 || !d.x)
@@ -491,14 +493,21 @@ int validate_io(const rfx_action_io_desc& d, bool tail) {
   return RFX_OK;
 }
 
-}  // namespace
-
-int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl) {
+int validate_time_cond(const rfx_time_cond_desc& d) {
   const bool embed_only = d.w_in == nullptr;
   if (d.n_t < 1 || d.n_t > kMaxRows || d.width < 256 || d.width % 256 || !d.t || !d.cond ||
       !a16(d.cond) || (!embed_only && (!d.w_out || !d.hidden || !a16(d.w_in) || !a16(d.w_out) || !a16(d.hidden))))
     return set_error(RFX_E_INVAL, "rfx_time_cond: need 1<=n_t<=16, width%%256==0, aligned weights");
   if (!(d.min_period > 0.0) || !(d.max_period > 0.0)) return set_error(RFX_E_INVAL, "rfx_time_cond: periods");
+  if (!embed_only && static_cast<size_t>(d.n_t) * d.width * sizeof(float) > 200 * 1024)
+    return set_error(RFX_E_UNSUPPORTED, "rfx_time_cond: n_t*width too large");
+  return RFX_OK;
+}
+
+int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl) {
+  const bool embed_only = d.w_in == nullptr;
+  int rc0 = validate_time_cond(d);
+  if (rc0) return rc0;
   __nv_bfloat16* emb = static_cast<__nv_bfloat16*>(d.cond);  // the embedding is staged in `cond`
   const int half = d.width / 2;
   const float* t = d.t;
@@ -511,7 +520,6 @@ int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl)
   const void* gemv = reinterpret_cast<const void*>(gemv_bf16_silu_kernel);
   rc = ensure_smem_attr(gemv, 200 * 1024);
   if (rc) return rc;
-  if (smem > 200 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_time_cond: n_t*width too large");
   const __nv_bfloat16* in0 = emb;
   const __nv_bfloat16* w_in = static_cast<const __nv_bfloat16*>(d.w_in);
   const __nv_bfloat16* b_in = static_cast<const __nv_bfloat16*>(d.b_in);
@@ -527,24 +535,35 @@ int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl)
   return launch_kernel(gemv, grid, dim3(256), smem, stream, pdl, 1, in1, n_t, width, w_out, b_out, n_out, cond);
 }
 
-int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pdl) {
+// conditioning rows padded to the next instantiated count
+static int modulation_rows(int n_rows) { return n_rows <= 4 ? 4 : n_rows <= 8 ? 8 : n_rows <= 10 ? 10 : 16; }
+
+int validate_modulation(const rfx_modulation_desc& d) {
   const int out = d.mode == RFX_ADARMS_SSG ? 3 * d.width : d.width;
   if ((d.mode != RFX_ADARMS_GATE && d.mode != RFX_ADARMS_SSG) || d.n_rows < 1 || d.n_rows > kMaxRows ||
       d.n_norms < 1 || d.width < 128 || d.width % 128 || !d.w || !d.b || !d.cond || !d.a2 || !d.gate ||
       (d.mode == RFX_ADARMS_SSG && !d.b2) || !a16(d.w) || !a16(d.cond) || !a16(d.a2) || !a16(d.gate) ||
       (d.b2 && !a16(d.b2)))
     return set_error(RFX_E_INVAL, "rfx_modulation: bad descriptor");
+  if (static_cast<long>(d.n_norms) * out > (1L << 30))
+    return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: too many output rows");
+  if (static_cast<size_t>(modulation_rows(d.n_rows)) * d.width * sizeof(float) > 100 * 1024)
+    return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
+  return RFX_OK;
+}
+
+int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_modulation(d);
+  if (rc) return rc;
+  const int out = d.mode == RFX_ADARMS_SSG ? 3 * d.width : d.width;
   const long rows = static_cast<long>(d.n_norms) * out;
-  if (rows > (1L << 30)) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: too many output rows");
-  // conditioning rows padded to the next instantiated count
-  const int kr = d.n_rows <= 4 ? 4 : d.n_rows <= 8 ? 8 : d.n_rows <= 10 ? 10 : 16;
+  const int kr = modulation_rows(d.n_rows);
   const void* fn = kr == 4   ? reinterpret_cast<const void*>(modulation_kernel<4>)
                    : kr == 8 ? reinterpret_cast<const void*>(modulation_kernel<8>)
                    : kr == 10 ? reinterpret_cast<const void*>(modulation_kernel<10>)
                               : reinterpret_cast<const void*>(modulation_kernel<16>);
   const size_t smem = static_cast<size_t>(kr) * d.width * sizeof(float);
-  if (smem > 100 * 1024) return set_error(RFX_E_UNSUPPORTED, "rfx_modulation: n_rows*width too large");
-  int rc = ensure_smem_attr(fn, 100 * 1024);
+  rc = ensure_smem_attr(fn, 100 * 1024);
   if (rc) return rc;
   int nsm = 148;
   rfx_num_sms(&nsm);
@@ -580,23 +599,34 @@ int launch_euler_tail(const rfx_action_io_desc& d, cudaStream_t stream, bool pdl
   return launch_kernel(fn, dim3(d.B * d.S), dim3(256), smem, stream, pdl, 1, p);
 }
 
-int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl) {
+int validate_rms_norm(const rfx_norm_desc& d) {
   if (d.T < 1 || d.K < 8 || d.K % 8 || d.K > 4096 || d.tokens_per_batch < 1 || !d.x || !d.y || !d.norm_a1 ||
       d.ldx < d.K || d.ldx % 8 || d.ldy < d.K || d.ldy % 8 || !a16(d.x) || !a16(d.y) || !a16(d.norm_a1) ||
       (d.norm_a2 && !a16(d.norm_a2)) || (d.norm_b2 && !a16(d.norm_b2)) || d.norm_ab_stride % 4)
     return set_error(RFX_E_INVAL, "rfx_rms_norm: need K%%8==0 (<=4096), 16-byte aligned rows and vectors");
+  return RFX_OK;
+}
+
+int launch_rms_norm(const rfx_norm_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_rms_norm(d);
+  if (rc) return rc;
   NormParams p{static_cast<const __nv_bfloat16*>(d.x), d.ldx, d.T, d.K, d.tokens_per_batch, d.norm_a1, d.norm_a2,
                d.norm_b2, d.norm_ab_stride, d.eps, static_cast<__nv_bfloat16*>(d.y), d.ldy};
   return launch_kernel(reinterpret_cast<const void*>(rmsnorm_kernel), dim3(d.T), dim3(128), 0, stream, pdl, 1, p);
 }
 
-int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl) {
+int validate_copy_rows(const rfx_copy_rows_desc& d) {
   if (!d.dst || !d.src || d.rows < 0 || d.width < 8 || d.width % 8 || d.group < 1 || d.dst_rows_per_group < 1 ||
       d.dst_row_offset < 0 || d.dst_row_offset + d.group > d.dst_rows_per_group || d.dst_ld < d.width ||
       d.dst_ld % 8 || d.src_ld < 0 || d.src_ld % 8 || (d.src_ld > 0 && d.src_ld < d.width) || !a16(d.dst) ||
       !a16(d.src))
     return set_error(RFX_E_INVAL, "rfx_copy_rows: bad layout (16-byte aligned rows of width%%8==0 required)");
-  if (d.rows == 0) return RFX_OK;
+  return RFX_OK;
+}
+
+int launch_copy_rows(const rfx_copy_rows_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_copy_rows(d);
+  if (rc || d.rows == 0) return rc;
   CopyRowsParams p{static_cast<__nv_bfloat16*>(d.dst), d.dst_ld, d.dst_rows_per_group, d.dst_row_offset, d.group,
                    static_cast<const __nv_bfloat16*>(d.src), d.src_ld, d.rows, d.width};
   const long total = static_cast<long>(d.rows) * (d.width / 8);

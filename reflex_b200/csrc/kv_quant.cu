@@ -273,12 +273,15 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) kv_quant_append_kernel
   }
 }
 
+// V pointers all null: quantize K alone (fused_quantize_store of one tensor)
+bool kv_quant_k_only(const KvQuantDesc& d) { return !d.x[1] && !d.q[1] && !d.scale[1] && !d.zp[1]; }
+
 }  // namespace
 
-int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) {
+int validate_kv_quant(const KvQuantDesc& d) {
   if (d.D != kD) return set_error(RFX_E_INVAL, "kv_quant_append: head_dim must be 256");
   if (d.B <= 0 || d.H <= 0 || d.L < 0) return set_error(RFX_E_INVAL, "kv_quant_append: bad B/H/L");
-  if (d.L == 0) return RFX_OK;
+  if (d.L == 0) return RFX_OK;  // nothing to append: the call is a no-op
   if (d.region_len <= 0 || d.region_base < 0 || d.region_off < 0 || d.L > d.region_len)
     return set_error(RFX_E_INVAL, "kv_quant_append: bad ring region");
   if (static_cast<long>(d.region_base) + d.region_len > d.capacity)
@@ -286,9 +289,7 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   if (d.mode != kQuantI8Sym && d.mode != kQuantU8Ref) return set_error(RFX_E_INVAL, "kv_quant_append: bad mode");
   if (d.in_dtype != kDtypeBF16 && d.in_dtype != kDtypeF32)
     return set_error(RFX_E_INVAL, "kv_quant_append: input dtype must be bf16 or f32");
-  // V pointers all null: quantize K alone (fused_quantize_store of one tensor)
-  const bool k_only = !d.x[1] && !d.q[1] && !d.scale[1] && !d.zp[1];
-  const int nw = k_only ? 1 : 2;
+  const int nw = kv_quant_k_only(d) ? 1 : 2;
   for (int w = 0; w < nw; ++w) {
     if (!d.x[w] || !d.q[w] || !d.scale[w] || (d.mode == kQuantU8Ref && !d.zp[w]))
       return set_error(RFX_E_INVAL, "kv_quant_append: null pointer");
@@ -298,6 +299,15 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   const int esz = d.in_dtype == kDtypeBF16 ? 2 : 4;
   if (((d.xs_b | d.xs_h | d.xs_l) * esz) % 16 || (d.qs_b | d.qs_h | d.qs_c) % 8)
     return set_error(RFX_E_INVAL, "kv_quant_append: strides must keep 16-byte rows");
+  if (static_cast<long>(d.B) * d.H > 65535)
+    return set_error(RFX_E_INVAL, "kv_quant_append: B * H must be at most 65535");
+  return RFX_OK;
+}
+
+int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_kv_quant(d);
+  if (rc || d.L == 0) return rc;
+  const int nw = kv_quant_k_only(d) ? 1 : 2;
 
   QuantArgs a{};
   for (int w = 0; w < 2; ++w) {
@@ -312,8 +322,6 @@ int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl) 
   a.B = d.B; a.H = d.H; a.L = d.L;
   a.region_base = d.region_base; a.region_off = d.region_off; a.region_len = d.region_len;
 
-  if (static_cast<long>(d.B) * d.H > 65535)
-    return set_error(RFX_E_INVAL, "kv_quant_append: B * H must be at most 65535");
   constexpr int kRowsPerBlock = kWarpsPerBlock * kRowsPerWarp;
   dim3 grid(static_cast<unsigned>((d.L + kRowsPerBlock - 1) / kRowsPerBlock), static_cast<unsigned>(d.B * d.H), nw);
   dim3 block(kWarpsPerBlock * 32);

@@ -77,6 +77,7 @@ struct KvQuantDesc {
   long ss_b, ss_h, ss_c;
   int region_base, region_off, region_len;
 };
+KvQuantDesc kv_quant_internal(const rfx_kv_quant_desc& d);
 int launch_kv_quant_append(const KvQuantDesc& d, cudaStream_t stream, bool pdl);
 
 int launch_linear(const rfx_linear_desc& d, const CUtensorMap* tmW, const CUtensorMap* tmX, cudaStream_t stream,
@@ -87,6 +88,18 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
                      cudaStream_t stream, bool pdl);
 int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV);
 size_t attention_workspace_bytes(const rfx_attn_desc& d);
+
+// Descriptor checks of the launchers below, host-only (no CUDA call): each
+// launcher runs its check first, and the plan adds run it when an op is added.
+int validate_kv_quant(const KvQuantDesc& d);
+int validate_time_cond(const rfx_time_cond_desc& d);
+int validate_modulation(const rfx_modulation_desc& d);
+int validate_io(const rfx_action_io_desc& d, bool tail);
+int validate_copy_rows(const rfx_copy_rows_desc& d);
+int validate_rms_norm(const rfx_norm_desc& d);
+int validate_patches(const rfx_patches_desc& d);
+int validate_layer_norm(const rfx_layer_norm_desc& d);
+int validate_vit_attention(const rfx_vit_attn_desc& d);
 
 int launch_time_cond(const rfx_time_cond_desc& d, cudaStream_t stream, bool pdl);
 int launch_modulation(const rfx_modulation_desc& d, cudaStream_t stream, bool pdl);

@@ -269,37 +269,43 @@ extern "C" int rfx_device_status(void* stream, int* out) {
   return RFX_OK;
 }
 
+namespace rfx {
+KvQuantDesc kv_quant_internal(const rfx_kv_quant_desc& d) {
+  KvQuantDesc k{};
+  k.mode = d.mode;
+  k.in_dtype = d.in_dtype;
+  k.x[0] = d.k;
+  k.x[1] = d.v;
+  k.xs_b = d.xs_b;
+  k.xs_h = d.xs_h;
+  k.xs_l = d.xs_l;
+  k.B = d.B;
+  k.H = d.H;
+  k.L = d.L;
+  k.D = d.D;
+  k.q[0] = d.k_q;
+  k.q[1] = d.v_q;
+  k.qs_b = d.qs_b;
+  k.qs_h = d.qs_h;
+  k.qs_c = d.qs_c;
+  k.capacity = d.capacity;
+  k.scale[0] = d.k_scale;
+  k.scale[1] = d.v_scale;
+  k.zp[0] = d.k_zp;
+  k.zp[1] = d.v_zp;
+  k.ss_b = d.ss_b;
+  k.ss_h = d.ss_h;
+  k.ss_c = d.ss_c;
+  k.region_base = d.region_base;
+  k.region_off = d.region_off;
+  k.region_len = d.region_len;
+  return k;
+}
+}  // namespace rfx
+
 extern "C" int rfx_kv_quant_append(const rfx_kv_quant_desc* d, void* stream) {
   if (!d) return set_error(RFX_E_INVAL, "rfx_kv_quant_append: null descriptor");
-  KvQuantDesc k{};
-  k.mode = d->mode;
-  k.in_dtype = d->in_dtype;
-  k.x[0] = d->k;
-  k.x[1] = d->v;
-  k.xs_b = d->xs_b;
-  k.xs_h = d->xs_h;
-  k.xs_l = d->xs_l;
-  k.B = d->B;
-  k.H = d->H;
-  k.L = d->L;
-  k.D = d->D;
-  k.q[0] = d->k_q;
-  k.q[1] = d->v_q;
-  k.qs_b = d->qs_b;
-  k.qs_h = d->qs_h;
-  k.qs_c = d->qs_c;
-  k.capacity = d->capacity;
-  k.scale[0] = d->k_scale;
-  k.scale[1] = d->v_scale;
-  k.zp[0] = d->k_zp;
-  k.zp[1] = d->v_zp;
-  k.ss_b = d->ss_b;
-  k.ss_h = d->ss_h;
-  k.ss_c = d->ss_c;
-  k.region_base = d->region_base;
-  k.region_off = d->region_off;
-  k.region_len = d->region_len;
-  return launch_kv_quant_append(k, static_cast<cudaStream_t>(stream), pdl_enabled());
+  return launch_kv_quant_append(kv_quant_internal(*d), static_cast<cudaStream_t>(stream), pdl_enabled());
 }
 
 // ================================================================ plans ====
@@ -362,7 +368,7 @@ namespace {
 int run_op(const Op& op, cudaStream_t s, bool pdl) {
   if (auto* o = std::get_if<LinearOp>(&op)) return launch_linear(o->d, &o->w, &o->x, s, pdl);
   if (auto* o = std::get_if<AttnOp>(&op)) return launch_attention(o->d, &o->q, &o->k, &o->v, s, pdl);
-  if (auto* o = std::get_if<QuantOp>(&op)) return rfx_kv_quant_append(&o->d, s);
+  if (auto* o = std::get_if<QuantOp>(&op)) return launch_kv_quant_append(kv_quant_internal(o->d), s, pdl);
   if (auto* o = std::get_if<TimeOp>(&op)) return launch_time_cond(o->d, s, pdl);
   if (auto* o = std::get_if<ModOp>(&op)) return launch_modulation(o->d, s, pdl);
   if (auto* o = std::get_if<InOp>(&op)) return launch_action_in(o->d, s, pdl);
@@ -441,30 +447,40 @@ extern "C" int rfx_plan_add_attention(rfx_plan* plan, const rfx_attn_desc* desc)
 }
 extern "C" int rfx_plan_add_kv_quant(rfx_plan* plan, const rfx_kv_quant_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_kv_quant(kv_quant_internal(*desc));
+  if (rc) return rc;
   plan->ops.emplace_back(QuantOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_time_cond(rfx_plan* plan, const rfx_time_cond_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_time_cond(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(TimeOp{*desc});
   plan->launches += desc->w_in ? 3 : 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_modulation(rfx_plan* plan, const rfx_modulation_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_modulation(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(ModOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_action_in(rfx_plan* plan, const rfx_action_io_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_io(*desc, false);
+  if (rc) return rc;
   plan->ops.emplace_back(InOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_io(*desc, true);
+  if (rc) return rc;
   plan->ops.emplace_back(TailOp{*desc});
   plan->launches += 1;
   return RFX_OK;
@@ -472,6 +488,8 @@ extern "C" int rfx_plan_add_euler_tail(rfx_plan* plan, const rfx_action_io_desc*
 
 extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_copy_rows(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(CopyOp{*desc});
   plan->launches += 1;
   return RFX_OK;
@@ -479,6 +497,8 @@ extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* 
 
 extern "C" int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_rms_norm(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(NormOp{*desc});
   plan->launches += 1;
   return RFX_OK;
@@ -486,18 +506,24 @@ extern "C" int rfx_plan_add_rms_norm(rfx_plan* plan, const rfx_norm_desc* desc) 
 
 extern "C" int rfx_plan_add_patches(rfx_plan* plan, const rfx_patches_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_patches(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(PatchOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_layer_norm(rfx_plan* plan, const rfx_layer_norm_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_layer_norm(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(LayerNormOp{*desc});
   plan->launches += 1;
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_vit_attention(rfx_plan* plan, const rfx_vit_attn_desc* desc) {
   PLAN_GUARD(plan);
+  const int rc = validate_vit_attention(*desc);
+  if (rc) return rc;
   plan->ops.emplace_back(VitAttnOp{*desc});
   plan->launches += 1;
   return RFX_OK;

@@ -346,10 +346,16 @@ bool a16v(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
 }  // namespace
 
-int launch_patches(const rfx_patches_desc& d, cudaStream_t stream, bool pdl) {
+int validate_patches(const rfx_patches_desc& d) {
   if (d.B < 1 || d.C < 1 || d.patch < 1 || d.H != d.W || d.H % d.patch || !d.image || !d.out || !a16v(d.out) ||
       d.ldo % 64 || d.ldo < d.C * d.patch * d.patch)
     return set_error(RFX_E_INVAL, "rfx_patches: square image with H %% patch == 0, ldo %% 64 == 0 and >= C*P*P");
+  return RFX_OK;
+}
+
+int launch_patches(const rfx_patches_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_patches(d);
+  if (rc) return rc;
   PatchParams p{d.image, static_cast<__nv_bfloat16*>(d.out), d.B, d.C, d.H, d.W, d.patch, d.H / d.patch, d.ldo,
                 d.C * d.patch * d.patch};
   const long total = static_cast<long>(d.B) * p.G * p.G * (d.ldo / 2);
@@ -357,24 +363,36 @@ int launch_patches(const rfx_patches_desc& d, cudaStream_t stream, bool pdl) {
                        dim3(256), 0, stream, pdl, 1, p);
 }
 
-int launch_layer_norm(const rfx_layer_norm_desc& d, cudaStream_t stream, bool pdl) {
+int validate_layer_norm(const rfx_layer_norm_desc& d) {
   if (d.T < 1 || d.C < 8 || d.C % 8 || d.C > 2048 || !d.x || !d.y || !d.w || !d.b || d.ldx < d.C || d.ldx % 8 ||
       d.ldy < d.C || d.ldy % 8 || !a16v(d.x) || !a16v(d.y) || !a16v(d.w) || !a16v(d.b))
     return set_error(RFX_E_INVAL, "rfx_layer_norm: need C %% 8 == 0 (<= 2048), 16-byte aligned rows and vectors");
+  return RFX_OK;
+}
+
+int launch_layer_norm(const rfx_layer_norm_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_layer_norm(d);
+  if (rc) return rc;
   LnParams p{static_cast<const __nv_bfloat16*>(d.x), d.ldx, d.w, d.b, d.eps, static_cast<__nv_bfloat16*>(d.y),
              d.ldy, d.T, d.C};
   return launch_kernel(reinterpret_cast<const void*>(layernorm_kernel), dim3((d.T + 7) / 8), dim3(256), 0, stream,
                        pdl, 1, p);
 }
 
-int launch_vit_attention(const rfx_vit_attn_desc& d, cudaStream_t stream, bool pdl) {
+int validate_vit_attention(const rfx_vit_attn_desc& d) {
   if (d.B < 1 || d.B > 65535 || d.N < 1 || d.N > kVKeys || d.H < 1 || d.H > 65535 || d.D < 8 || d.D > 128 ||
       d.D % 8 || !d.qkv || !d.out || !a16v(d.qkv) || !a16v(d.out) || d.ld_qkv % 8 || d.ld_qkv < 3 * d.H * d.D ||
       d.ld_out % 8 || d.ld_out < d.H * d.D)
     return set_error(RFX_E_INVAL,
                      "rfx_vit_attention: need N <= 256, D %% 8 == 0 (<= 128), 16-byte aligned rows of q|k|v");
+  return RFX_OK;
+}
+
+int launch_vit_attention(const rfx_vit_attn_desc& d, cudaStream_t stream, bool pdl) {
+  int rc = validate_vit_attention(d);
+  if (rc) return rc;
   const void* fn = reinterpret_cast<const void*>(vit_attention_kernel);
-  int rc = ensure_smem_attr(fn, kVSmem);
+  rc = ensure_smem_attr(fn, kVSmem);
   if (rc) return rc;
   VitParams p{static_cast<const __nv_bfloat16*>(d.qkv), d.ld_qkv, static_cast<__nv_bfloat16*>(d.out), d.ld_out,
               d.N, d.H, d.D, d.scale * 1.4426950408889634f, device_status_ptr()};

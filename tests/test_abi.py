@@ -81,6 +81,82 @@ def test_plan_calls_out_of_order():
         assert lib.rfx_plan_destroy(plan) == _lib.RFX_OK
 
 
+def test_plan_adds_check_descriptors():
+    """Every plan add runs its op's descriptor check when the op is added (no
+    device needed for the ops without tensor maps): a bad descriptor is
+    refused with RFX_E_INVAL and leaves the plan as it was; good ones are
+    counted by their launches (time conditioning with its MLP: three)."""
+    lib = _lib.load()
+    plan = ctypes.c_void_p()
+    assert lib.rfx_plan_create(ctypes.byref(plan)) == _lib.RFX_OK
+    n = ctypes.c_int(-1)
+    try:
+        norm = _lib.NormDesc()
+        norm.T, norm.K, norm.tokens_per_batch = 50, 1024, 50
+        norm.x = norm.y = norm.norm_a1 = 1 << 20  # aligned, never dereferenced
+        norm.ldx = norm.ldy = 1024
+        assert lib.rfx_plan_add_rms_norm(plan, ctypes.byref(norm)) == _lib.RFX_OK
+        norm.K = norm.ldx = norm.ldy = 1020  # K % 8 != 0
+        assert lib.rfx_plan_add_rms_norm(plan, ctypes.byref(norm)) == _lib.RFX_E_INVAL
+        assert b"rfx_rms_norm" in lib.rfx_last_error()
+
+        cp = _lib.CopyRowsDesc()
+        cp.dst = cp.src = 1 << 20
+        cp.rows, cp.width, cp.group, cp.dst_rows_per_group, cp.dst_row_offset = 50, 1024, 50, 51, 1
+        cp.dst_ld = cp.src_ld = 1024
+        assert lib.rfx_plan_add_copy_rows(plan, ctypes.byref(cp)) == _lib.RFX_OK
+        cp.dst_row_offset = 2  # group of 50 from row 2 overruns 51 rows
+        assert lib.rfx_plan_add_copy_rows(plan, ctypes.byref(cp)) == _lib.RFX_E_INVAL
+
+        tc = _lib.TimeCondDesc()
+        tc.n_t, tc.width, tc.min_period, tc.max_period = 10, 1024, 4e-3, 4.0
+        tc.t = 1 << 20
+        tc.w_in = tc.b_in = tc.w_out = tc.b_out = tc.hidden = tc.cond = 1 << 20
+        assert lib.rfx_plan_add_time_cond(plan, ctypes.byref(tc)) == _lib.RFX_OK
+        tc.min_period = 0.0
+        assert lib.rfx_plan_add_time_cond(plan, ctypes.byref(tc)) == _lib.RFX_E_INVAL
+
+        md = _lib.ModulationDesc()
+        md.mode, md.n_rows, md.n_norms, md.width = _lib.RFX_ADARMS_GATE, 10, 37, 1024
+        md.w = md.b = md.cond = md.a2 = md.gate = 1 << 20
+        assert lib.rfx_plan_add_modulation(plan, ctypes.byref(md)) == _lib.RFX_OK
+        md.mode = 7
+        assert lib.rfx_plan_add_modulation(plan, ctypes.byref(md)) == _lib.RFX_E_INVAL
+
+        q = _lib.KvQuantDesc()
+        q.mode, q.in_dtype = _lib.RFX_QUANT_I8_SYM, _lib.RFX_DTYPE_BF16
+        q.k = q.v = q.k_q = q.v_q = q.k_scale = q.v_scale = 1 << 20
+        q.B, q.H, q.L, q.D, q.capacity = 1, 1, 768, 256, 2048
+        q.xs_b, q.xs_h, q.xs_l = 768 * 256, 768 * 256, 256
+        q.qs_b, q.qs_h, q.qs_c = 2048 * 256, 2048 * 256, 256
+        q.ss_b, q.ss_h, q.ss_c = 2048, 2048, 1
+        q.region_base, q.region_off, q.region_len = 0, 1280, 2048
+        assert lib.rfx_plan_add_kv_quant(plan, ctypes.byref(q)) == _lib.RFX_OK
+        q.region_len = 4096  # the region runs past the ring's capacity
+        assert lib.rfx_plan_add_kv_quant(plan, ctypes.byref(q)) == _lib.RFX_E_INVAL
+
+        ln = _lib.LayerNormDesc()
+        ln.T, ln.C = 768, 1004  # C % 8 != 0
+        ln.x = ln.y = ln.w = ln.b = 1 << 20
+        ln.ldx = ln.ldy = 1024
+        assert lib.rfx_plan_add_layer_norm(plan, ctypes.byref(ln)) == _lib.RFX_E_INVAL
+        va = _lib.VitAttnDesc()
+        va.B, va.N, va.H, va.D = 3, 300, 16, 72  # more than 256 tokens per image
+        va.qkv = va.out = 1 << 20
+        va.ld_qkv, va.ld_out, va.scale = 3 * 16 * 72, 16 * 72, 72 ** -0.5
+        assert lib.rfx_plan_add_vit_attention(plan, ctypes.byref(va)) == _lib.RFX_E_INVAL
+        pd = _lib.PatchesDesc()
+        pd.B, pd.C, pd.H, pd.W, pd.patch = 3, 3, 224, 220, 14  # not square
+        pd.image = pd.out = 1 << 20
+        pd.ldo = 640
+        assert lib.rfx_plan_add_patches(plan, ctypes.byref(pd)) == _lib.RFX_E_INVAL
+
+        assert lib.rfx_plan_num_launches(plan, ctypes.byref(n)) == _lib.RFX_OK
+        assert n.value == 1 + 1 + 3 + 1 + 1
+    finally:
+        assert lib.rfx_plan_destroy(plan) == _lib.RFX_OK
+
+
 @pytest.mark.parametrize("T,O,K,want", [
     (768, 2048, 16384, 65536 + 96 * 3 * 128 * 128 * 4),  # down_proj of a 768-token frame: 96 tiles, K split 3
     (768, 32768, 2048, 0),                              # gate/up: 768 tiles fill the SMs
