@@ -2,8 +2,9 @@
 `pip install --target baseline/_ref` copy of Reflex, driven through the
 harness the arm uses, reproduces the golden 2-layer PI0.5 chunk that
 tests/golden/make_golden.py computed from the reference checkout (same seeded
-weights, context, noise and state).  CPU only; skipped where the install is
-absent (it is git-ignored).
+weights, context, noise and state); that test is skipped where the install
+is absent (it is git-ignored).  The arm's JSON line carries the contract's
+keys either way (without the install it times the oracle port).  CPU only.
 """
 import os
 
@@ -40,3 +41,23 @@ def test_reference_arm_reproduces_golden_chunk():
             x = H.run_reference_chunk(R, model, cfg, x0, st, n_ctx)
     err = (x - torch.from_numpy(g["actions"])).abs().max().item()
     assert err <= 1e-5, err
+
+
+def test_reference_arm_json_line():
+    """`bench.py --impl reference` prints one JSON line with the contract's
+    keys (here with 2 layers and one chunk, to keep the CPU suite short)."""
+    import json
+    import subprocess
+    import sys
+
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--layers", "2"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "ms" and d["higher_is_better"] is False
+    assert d["value"] > 0 and d["n_gpus"] == 1 and d["steps"] == 1
+    assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"] == {"value": d["value"], "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"]
