@@ -1141,6 +1141,12 @@ size_t attention_workspace_bytes(const rfx_attn_desc& d) {
   return ws_layout(d, g).total;
 }
 
+int attention_launches(const rfx_attn_desc& d) {
+  Geometry g;
+  if (geometry(d, &g) != RFX_OK) return 0;
+  return (d.kv_source == RFX_KV_DENSE ? 1 : 0) + 1 + (g.splits > 1 ? 1 : 0);
+}
+
 int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV) {
   Geometry g;
   int rc = geometry(d, &g);

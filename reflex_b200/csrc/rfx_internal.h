@@ -88,6 +88,9 @@ int launch_attention(const rfx_attn_desc& d, const CUtensorMap* tmQ, const CUten
                      cudaStream_t stream, bool pdl);
 int build_attention_maps(const rfx_attn_desc& d, CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV);
 size_t attention_workspace_bytes(const rfx_attn_desc& d);
+// Kernel launches of one rfx_attention call: the dense conversion (dense
+// source), the attention, and the split-KV combine (more than one split).
+int attention_launches(const rfx_attn_desc& d);
 
 // Descriptor checks of the launchers below, host-only (no CUDA call): each
 // launcher runs its check first, and the plan adds run it when an op is added.

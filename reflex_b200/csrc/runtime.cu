@@ -442,7 +442,7 @@ extern "C" int rfx_plan_add_attention(rfx_plan* plan, const rfx_attn_desc* desc)
   if (ws > 0 && (!desc->workspace || desc->workspace_bytes < ws))
     return set_error(RFX_E_INVAL, "plan: attention needs %zu bytes of workspace", ws);
   plan->ops.emplace_back(op);
-  plan->launches += ws > 0 ? 2 : 1;
+  plan->launches += attention_launches(op.d);
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_kv_quant(rfx_plan* plan, const rfx_kv_quant_desc* desc) {
@@ -450,7 +450,7 @@ extern "C" int rfx_plan_add_kv_quant(rfx_plan* plan, const rfx_kv_quant_desc* de
   const int rc = validate_kv_quant(kv_quant_internal(*desc));
   if (rc) return rc;
   plan->ops.emplace_back(QuantOp{*desc});
-  plan->launches += 1;
+  plan->launches += desc->L > 0 ? 1 : 0;  // an empty append launches nothing
   return RFX_OK;
 }
 extern "C" int rfx_plan_add_time_cond(rfx_plan* plan, const rfx_time_cond_desc* desc) {
@@ -491,7 +491,7 @@ extern "C" int rfx_plan_add_copy_rows(rfx_plan* plan, const rfx_copy_rows_desc* 
   const int rc = validate_copy_rows(*desc);
   if (rc) return rc;
   plan->ops.emplace_back(CopyOp{*desc});
-  plan->launches += 1;
+  plan->launches += desc->rows > 0 ? 1 : 0;  // no rows: nothing is launched
   return RFX_OK;
 }
 

@@ -153,6 +153,15 @@ def test_plan_adds_check_descriptors():
 
         assert lib.rfx_plan_num_launches(plan, ctypes.byref(n)) == _lib.RFX_OK
         assert n.value == 1 + 1 + 3 + 1 + 1
+        # empty ops are accepted and launch nothing
+        q.region_len, q.L = 2048, 0
+        assert lib.rfx_plan_add_kv_quant(plan, ctypes.byref(q)) == _lib.RFX_OK
+        assert lib.rfx_kv_quant_append(ctypes.byref(q), None) == _lib.RFX_OK
+        cp.dst_row_offset, cp.rows = 1, 0
+        assert lib.rfx_plan_add_copy_rows(plan, ctypes.byref(cp)) == _lib.RFX_OK
+        assert lib.rfx_copy_rows(ctypes.byref(cp), None) == _lib.RFX_OK
+        assert lib.rfx_plan_num_launches(plan, ctypes.byref(n)) == _lib.RFX_OK
+        assert n.value == 1 + 1 + 3 + 1 + 1
     finally:
         assert lib.rfx_plan_destroy(plan) == _lib.RFX_OK
 
