@@ -1,0 +1,84 @@
+"""The int8 quantize-append kernel's rounding path, restated in numpy float32,
+gives the oracle's q = clamp(rne(x / scale), -127, 127) for every bf16 input
+of a row and for random fp32 inputs.
+
+The kernel (reflex_b200/csrc/kv_quant.cu, quant8_i8) does not divide: with
+scale = fl(absmax / 127) and rcp = fl(1 / scale), it takes y = fl(x * rcp),
+rounds it by adding and subtracting 1.5 * 2^23, and divides only the values
+whose y lies within 2^-14 of a half-integer (and every value of a row whose
+scale is below the smallest normal float).  Its source argues that the two
+agree.  The GPU tests check bit-exactness on the inputs they draw; this test
+checks the argument itself over every bf16 value of a row, at 640 row
+maxima across the normal range, without a GPU.  Every numpy float32
+operation here rounds to nearest even, as the kernel's explicit .rn
+instructions do.
+"""
+import numpy as np
+
+from oracle import quant as oq
+
+MAGIC = np.float32(1.5 * 2 ** 23)
+FAR = np.float32(0.5 - 2 ** -14)
+TINY = np.float32(2 ** -126)
+
+
+def kernel_q(x, amax):
+    """The kernel's int8 value of each x (float32) of a row with maximum |x| = amax."""
+    x = x.astype(np.float32)
+    scale = np.float32(amax) / np.float32(127.0)
+    exact = np.clip(np.rint(x / scale), -127, 127)
+    if scale < TINY:  # denormal scale: every value is divided
+        return exact.astype(np.int32), None
+    rcp = np.float32(1.0) / scale
+    y = x * rcp
+    t = y + MAGIC
+    r = t - MAGIC
+    d = np.abs(y - r)
+    near = ~(d <= FAR)
+    # the low byte of t is rne(y) in two's complement; |y| < 127.5 keeps it in range
+    fast = r.astype(np.int32)
+    return np.where(near, exact.astype(np.int32), fast), (y, near)
+
+
+def all_bf16():
+    bits = np.arange(1 << 16, dtype=np.uint32) << 16
+    v = bits.view(np.float32)
+    return v[np.isfinite(v)]
+
+
+def oracle_q(x, amax):
+    """oracle/quant.py on one row whose maximum |x| is amax (appended to the row)."""
+    row = np.concatenate([x.astype(np.float32), np.array([amax], dtype=np.float32)])
+    q, scale = oq.quant_i8_sym(row[None, :])
+    return q[0, :-1].astype(np.int32), scale[0, 0]
+
+
+def test_every_bf16_value_rounds_like_the_oracle():
+    xs = all_bf16()
+    pos = np.sort(np.unique(np.abs(xs[xs != 0])))
+    # 640 row maxima from the smallest bf16 up to 2^127, log-spaced over the patterns
+    amaxes = pos[np.linspace(0, len(pos) - 1, 640).astype(int)]
+    n_near = n_vals = 0
+    for a in amaxes:
+        x = xs[np.abs(xs) <= a]
+        got, info = kernel_q(x, a)
+        want, scale = oracle_q(x, a)
+        assert scale == np.float32(a) / np.float32(127.0)
+        assert np.array_equal(got, want), (a, x[got != want][:4], got[got != want][:4], want[got != want][:4])
+        if info is not None:
+            y, near = info
+            assert np.abs(y).max() < 127.5
+            n_near += int(near.sum())
+            n_vals += len(x)
+    # the slow path is rare: most rows' values are far from every half-integer
+    assert 0 < n_near < 0.05 * n_vals
+
+
+def test_random_fp32_rows_round_like_the_oracle():
+    g = np.random.default_rng(5)
+    for scale_exp in (-100, -20, -3, 0, 4, 30, 100):
+        x = (g.standard_normal((2000, 256)) * 2.0 ** scale_exp).astype(np.float32)
+        q, scale = oq.quant_i8_sym(x)
+        for r in range(0, 2000, 97):
+            got, _ = kernel_q(x[r], np.abs(x[r]).max())
+            assert np.array_equal(got, q[r].astype(np.int32))
