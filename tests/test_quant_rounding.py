@@ -1,6 +1,8 @@
-"""The int8 quantize-append kernel's rounding path, restated in numpy float32,
-gives the oracle's q = clamp(rne(x / scale), -127, 127) for every bf16 input
-of a row and for random fp32 inputs.
+"""Integer tricks of the int8 kernels, restated in numpy and checked without a
+GPU: the quantize-append kernel's rounding path gives the oracle's
+q = clamp(rne(x / scale), -127, 127) for every bf16 input of a row and for
+random fp32 inputs, and the attention's int8 -> f16 byte-permute conversion is
+exact for every int8 value.
 
 The kernel (reflex_b200/csrc/kv_quant.cu, quant8_i8) does not divide: with
 scale = fl(absmax / 127) and rcp = fl(1 / scale), it takes y = fl(x * rcp),
@@ -82,3 +84,29 @@ def test_random_fp32_rows_round_like_the_oracle():
         for r in range(0, 2000, 97):
             got, _ = kernel_q(x[r], np.abs(x[r]).max())
             assert np.array_equal(got, q[r].astype(np.int32))
+
+
+def byte_perm(x, y, s):
+    """CUDA's __byte_perm(x, y, s): byte i of the result is byte (s >> 4i) & 7
+    of the 8-byte value y:x (bytes 0-3 from x, 4-7 from y)."""
+    src = [(x >> (8 * i)) & 0xFF for i in range(4)] + [(y >> (8 * i)) & 0xFF for i in range(4)]
+    return sum(src[(s >> (4 * i)) & 7] << (8 * i) for i in range(4))
+
+
+def test_int8_to_f16_byte_permute_is_exact():
+    """The attention workers' int8 -> f16 conversion (i8x4_to_f16x4 in
+    csrc/chunk.cu): bytes offset to unsigned become the low mantissa bytes of
+    f16 1024 + u, and one f16 subtraction of 1152 leaves the signed value.
+    Every int8 value in every byte position converts exactly."""
+    bias = np.float16(1152.0)
+    assert np.array([0x6480], dtype=np.uint16).view(np.float16)[0] == bias
+    for v in range(-128, 128):
+        for pos in range(4):
+            x = ((v & 0xFF) << (8 * pos)) | (0x11 << (8 * ((pos + 1) % 4)))  # a neighbour byte as well
+            x ^= 0x80808080
+            a = byte_perm(x, 0x64646464, 0x4140)
+            b = byte_perm(x, 0x64646464, 0x4342)
+            halves = np.array([a & 0xFFFF, a >> 16, b & 0xFFFF, b >> 16], dtype=np.uint16).view(np.float16)
+            out = (halves - bias).astype(np.float32)
+            assert out[pos] == v, (v, pos, out)
+            assert out[(pos + 1) % 4] == 0x11
