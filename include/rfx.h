@@ -242,7 +242,13 @@ int rfx_pack_weight(int kind, const void* src, void* dst, int rows, int K, void*
  *     the workspace, then the attention streams those tiles by TMA with two
  *     key blocks in flight (right for many query tiles, e.g. a 768-token
  *     frame through the prefix layers, where every query tile visits every
- *     block).  Same results as the ring path (new_block included). */
+ *     block).  Same results as the ring path (new_block included).
+ *
+ * Numerics: scores in fp32; P (times each context token's value scale) and V
+ * are f16 in P·V with fp32 accumulation, and O is rescaled only when the
+ * running maximum moves by more than 2^8, so results are exact to the stated
+ * tolerance while a context token's value absmax stays below about 32,000
+ * and new-key values below 65504 in magnitude (larger ones overflow). */
 #define RFX_KV_RING_TILES 0
 #define RFX_KV_DENSE 1
 typedef struct rfx_attn_desc {
